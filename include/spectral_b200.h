@@ -1,0 +1,199 @@
+/*
+ * spectral_b200.h — C ABI of libspectral_b200.so (B200 / sm_100a).
+ *
+ * The drop-in boundary for SpectralAI's MoE inference hot path:
+ *   - the BVH expert router (eval forward of BVHRouter, python/bvh_router.py:269-329),
+ *   - the ternary {-1,0,+1} SwiGLU expert (ternary_gated_mlp,
+ *     cuda/v5/ternary_torch_ext.cu:123-191, 284-339) and its grouped MoE form.
+ *
+ * Conventions
+ *   - Plain pointers and sizes only.  Device pointers are CUDA device addresses
+ *     on the handle's device; `stream` is a cudaStream_t passed as void*.
+ *   - Every entry point returns an int status: SB_OK (0) or a negative SB_ERR_*.
+ *     The message of the last failure on the calling thread is available from
+ *     sb_last_error().  Nothing here calls exit/abort or traps on the device.
+ *   - Forward calls are asynchronous on `stream` (like the reference's
+ *     bvh_router_ext.route, cuda/v5/bvh_torch_ext.cu:310-357).
+ *   - The caller owns all input/output buffers and the workspace; a handle owns
+ *     only its device-resident weights.  Handles are independent (no process-
+ *     global tree, unlike the reference's __constant__ tree,
+ *     cuda/v5/bvh_torch_ext.cu:51-55), so one process may hold many routers.
+ *   - Device kernels bound every wait; a wait that runs out sets a status word
+ *     that the next call returns as SB_ERR_DEVICE_TIMEOUT.
+ */
+#ifndef SPECTRAL_B200_H
+#define SPECTRAL_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SB_ABI_VERSION 1
+
+enum sb_status {
+  SB_OK = 0,
+  SB_ERR_INVALID = -1,        /* bad argument (null, shape, dtype, mode)          */
+  SB_ERR_CUDA = -2,           /* CUDA runtime / driver error                       */
+  SB_ERR_UNSUPPORTED = -3,    /* valid but not supported by this build           */
+  SB_ERR_DEVICE_TIMEOUT = -4, /* a bounded device-side wait expired              */
+  SB_ERR_NOMEM = -5,          /* device allocation failed                        */
+  SB_ERR_WORKSPACE = -6       /* workspace smaller than *_workspace_bytes()       */
+};
+
+enum sb_dtype { SB_F32 = 0, SB_BF16 = 1, SB_F16 = 2 };
+
+/* Level selection rule.  HARD = the reference eval branch (argmax + one_hot,
+ * bvh_router.py:190-193).  SOFT = the training branch with the Gumbel noise
+ * removed, softmax(logits / clamp(T, 0.01)) (bvh_router.py:200-202). */
+enum sb_select { SB_SELECT_HARD = 0, SB_SELECT_SOFT = 1 };
+
+/* Arithmetic of the encoder GEMMs.  FAST = bf16 tcgen05 tensor cores with fp32
+ * accumulation (input must be bf16); EXACT = fp32 FFMA (input fp32 or bf16),
+ * matching the reference's fp32 PyTorch math to rounding. */
+enum sb_precision { SB_PREC_FAST = 0, SB_PREC_EXACT = 1 };
+
+/* Version of this ABI (SB_ABI_VERSION). */
+int sb_abi_version(void);
+
+/* Copies the calling thread's last error message (NUL-terminated) into buf.
+ * Returns the full message length. */
+int sb_last_error(char* buf, size_t len);
+
+/* Reads and clears the device status word of `device` (synchronous).  Returns
+ * SB_OK or SB_ERR_DEVICE_TIMEOUT if a kernel gave up a bounded wait. */
+int sb_device_status(int device);
+
+/* ------------------------------------------------------------------------ */
+/* BVH router                                                                */
+/* ------------------------------------------------------------------------ */
+
+#define SB_MAX_LEVELS 8
+
+typedef struct sb_router sb_router;
+
+/* Router shape.  Replaces RouterConfig (python/bvh_router.py:28-65), with the
+ * three hard-coded levels generalised to n_levels (1..8). */
+typedef struct {
+  int32_t hidden;                    /* embed_dim H                         */
+  int32_t spectral;                  /* spectral_dim S                      */
+  int32_t n_levels;                  /* L (reference: 3)                    */
+  int32_t branching[SB_MAX_LEVELS];  /* children per node at each level     */
+} sb_router_desc;
+
+/* Host fp32 parameters in the reference state_dict layout
+ * (python/bvh_router.py:227-255).  Level l (0-based) has N_l = prod(branching[0..l]) nodes.
+ * Null biases read as zero.  portals[l] is required for l < n_levels-1. */
+typedef struct {
+  const float* to3d_w;                      /* to_3d.weight            [3,H]     */
+  const float* to3d_b;                      /* to_3d.bias              [3]       */
+  const float* enc1_w;                      /* spectral.net.0.weight   [H,H]     */
+  const float* enc1_b;                      /* spectral.net.0.bias     [H]       */
+  const float* enc2_w;                      /* spectral.net.2.weight   [S,H]     */
+  const float* enc2_b;                      /* spectral.net.2.bias     [S]       */
+  const float* centers[SB_MAX_LEVELS];      /* level{l+1}.centers      [N_l,3]   */
+  const float* refract_w[SB_MAX_LEVELS];    /* refract{l+1}.W_dispersion.weight [N_l,S] */
+  const float* refract_b[SB_MAX_LEVELS];    /* refract{l+1}.W_dispersion.bias   [N_l]   */
+  const float* portals[SB_MAX_LEVELS];      /* portal{l+1}.transform   [N_l,3,4] */
+  float temperature;                        /* buffer `temperature`              */
+} sb_router_weights;
+
+/* Output buffers of one forward (device pointers; any may be NULL to skip).
+ * Mirrors RoutingResult (bvh_router.py:72-77) plus the MoE top-k pair. */
+typedef struct {
+  int32_t* topk_ids;      /* [B,k]   top-k experts, larger prob first, ties -> lower id */
+  float* topk_weights;    /* [B,k]   softmax over the k selected probabilities          */
+  int64_t* expert_id;     /* [B]     argmax of the last level                           */
+  float* expert_probs;    /* [B,N_L] last-level probabilities                           */
+  int64_t* route_path;    /* [B,L]   level-global chosen node per level                 */
+  float* confidence;      /* [B]     max of the last level                              */
+} sb_router_outputs;
+
+/* Creates a router on `device`.  Replaces BVHRouter.__init__ (bvh_router.py:227-255)
+ * and the reference C-ABI's bvh_alloc_buffers (cuda/v5/bvh_router_kernel.cu:378-717). */
+int sb_router_create(const sb_router_desc* desc, int device, sb_router** out);
+
+/* Copies host fp32 parameters into handle-owned device memory (synchronous).
+ * Replaces bvh_router_ext.upload_tree (cuda/v5/bvh_torch_ext.cu:270-303). */
+int sb_router_upload(sb_router* h, const sb_router_weights* w);
+
+/* Bytes of caller-provided device workspace that sb_router_forward needs. */
+size_t sb_router_workspace_bytes(const sb_router* h, int64_t batch, int precision);
+
+/* Router forward over x [B,H] (device, row-major, dtype SB_F32 or SB_BF16).
+ * Replaces BVHRouter.forward in eval mode (bvh_router.py:269-329) and the
+ * reference kernel launch bvh_router_ext.route (cuda/v5/bvh_torch_ext.cu:310-357).
+ * No batch cap (the reference caps B at 1024). */
+int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64_t batch,
+                      int precision, int select, int top_k,
+                      const sb_router_outputs* out,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+int sb_router_destroy(sb_router* h);
+
+/* ------------------------------------------------------------------------ */
+/* Ternary experts                                                           */
+/* ------------------------------------------------------------------------ */
+
+/* Host packer in the reference layout: int8 w[K,N] in {-1,0,+1} -> int32
+ * packed[ceil(K/16), N], 2-bit codes 00=0, 01=+1, 10=-1, bit pair i of word
+ * [p,c] = row p*16+i.  Replaces pack_ternary_impl (ternary_torch_ext.cu:197-231). */
+int sb_ternary_pack_ref(const int8_t* w, int64_t K, int64_t N, int32_t* packed);
+
+/* Bytes of one matrix in the device layout used by the B200 kernels: row-major
+ * [N, ceil(K/64)*4] uint32 words, one word per 16 consecutive K of one output
+ * row n.  Inside a word, element 2j (j=0..7) has its non-zero flag at bit j and
+ * its sign at bit 8+j, element 2j+1 has them at bits 16+j and 24+j, so that two
+ * elements expand to two 16-bit floats with one AND, one multiply and one shift. */
+size_t sb_ternary_matrix_bytes(int64_t K, int64_t N);
+
+/* Converts a reference-layout packed matrix (device int32 [ceil(K/16), N]) into
+ * the device layout above (device buffer of sb_ternary_matrix_bytes(K,N)). */
+int sb_ternary_repack(const int32_t* packed_ref, int64_t K, int64_t N,
+                      uint32_t* dst, void* stream);
+
+/* Fused ternary gated MLP for one expert: y[M,H] = s_d * (T_d (silu(s_g*(T_g x)) * (s_u*(T_u x)))).
+ * x: device [M,H] (SB_F32 or SB_BF16); weights in the device layout
+ * (gate/up: K=H, N=I; down: K=I, N=H); scales fp32 [I],[I],[H]; y: fp32 [M,H].
+ * Replaces ternary_gated_mlp (ternary_torch_ext.cu:284-339). */
+int sb_ternary_gated_mlp(const void* x, int x_dtype, int64_t M, int64_t H, int64_t I,
+                         const uint32_t* gate, const uint32_t* up, const uint32_t* down,
+                         const float* gate_scale, const float* up_scale, const float* down_scale,
+                         float* y, void* workspace, size_t workspace_bytes, void* stream);
+
+size_t sb_ternary_gated_mlp_workspace_bytes(int64_t M, int64_t H, int64_t I);
+
+/* y[M,N] = scale * (x @ T) + bias with x [M,K] (SB_F32/SB_BF16) and T in the device layout.
+ * Replaces ternary_linear (ternary_torch_ext.cu:237-278). */
+int sb_ternary_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
+                      const uint32_t* w, const float* scale, const float* bias,
+                      float* y, void* workspace, size_t workspace_bytes, void* stream);
+
+size_t sb_ternary_linear_workspace_bytes(int64_t M, int64_t K, int64_t N);
+
+/* Grouped MoE SwiGLU over E experts with top-k routing:
+ *   out[t] = sum_j weights[t,j] * expert_{ids[t,j]}(x[t])   (j in fixed order 0..k-1)
+ * Replaces the reference's per-(slot, expert) Python loop OLMoELayer.forward_topk
+ * (python/olmoe_extract.py:126-157) over CUDATernaryExpertModule experts.
+ * x: device [B,H] (SB_F32/SB_BF16); ids int32 [B,k] (each in [0,E)); weights fp32 [B,k];
+ * gate/up/down: device arrays of E matrices in the device layout, contiguous per kind
+ * (expert e at offset e*sb_ternary_matrix_bytes); scales fp32 [E,I],[E,I],[E,H];
+ * out: device [B,H] of out_dtype (SB_F32 or SB_BF16). */
+int sb_ternary_moe_swiglu(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I,
+                          int32_t n_experts, int32_t top_k,
+                          const int32_t* ids, const float* weights,
+                          const uint32_t* gate, const uint32_t* up, const uint32_t* down,
+                          const float* gate_scale, const float* up_scale, const float* down_scale,
+                          void* out, int out_dtype,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+size_t sb_ternary_moe_workspace_bytes(int64_t B, int64_t H, int64_t I,
+                                      int32_t n_experts, int32_t top_k);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPECTRAL_B200_H */

@@ -1,0 +1,51 @@
+"""Build the reference's own ternary torch extension into oracle/_ref/ (checker only).
+
+Compiles cuda/v5/ternary_torch_ext.cu from the reference tree, where it lies,
+with torch.utils.cpp_extension for sm_100a.  The resulting module
+(``oracle/_ref/ternary_expert_ext_ref*.so``) is used only by tests as a second
+pin for the packing restatement (its ``pack_ternary`` is host code and runs
+without a GPU) and, on a GPU box, as the timed reference-GPU kernel.  Nothing
+in the product loads it.  Sources are never copied into this repository.
+
+Usage: python oracle/build_ref.py [--reference /path/to/reference]
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+OUT = HERE / "_ref"
+
+
+def build(reference: Path, verbose: bool = False) -> bool:
+    src = reference / "cuda" / "v5" / "ternary_torch_ext.cu"
+    if not src.is_file():
+        print(f"[oracle/_ref] reference source not found: {src}")
+        return False
+    OUT.mkdir(exist_ok=True)
+    from torch.utils.cpp_extension import load
+    load(
+        name="ternary_expert_ext_ref",
+        sources=[str(src)],
+        build_directory=str(OUT),
+        extra_cuda_cflags=["-O3", "-gencode", "arch=compute_100a,code=sm_100a"],
+        verbose=verbose,
+        is_python_module=True,
+    )
+    return True
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--reference", default=os.environ.get("SB_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("-v", action="store_true")
+    a = ap.parse_args()
+    return 0 if build(Path(a.reference), a.v) else 1
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,44 @@
+// common.cuh — host-side helpers shared by the library's translation units:
+// error reporting, CUDA checks, tensor-map creation and device properties.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdint.h>
+#include <stdio.h>
+
+#include <string>
+
+#include "../../include/spectral_b200.h"
+
+namespace sb {
+
+// Records the calling thread's last error message and returns `code`.
+int fail(int code, const char* fmt, ...);
+
+#define SB_CUDA_TRY(expr)                                                              \
+  do {                                                                                 \
+    cudaError_t _e = (expr);                                                           \
+    if (_e != cudaSuccess)                                                             \
+      return ::sb::fail(SB_ERR_CUDA, "%s failed: %s (%s:%d)", #expr,                   \
+                        cudaGetErrorString(_e), __FILE__, __LINE__);                   \
+  } while (0)
+
+#define SB_REQUIRE(cond, ...)                                                          \
+  do {                                                                                 \
+    if (!(cond)) return ::sb::fail(SB_ERR_INVALID, __VA_ARGS__);                       \
+  } while (0)
+
+// Number of SMs of the current device (cached per device).
+int num_sms();
+
+// 2-D tiled tensor map over a row-major [rows, cols] matrix of `elem_bytes`
+// elements with a box of box_cols x box_rows and the given swizzle.
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
+                 int elem_bytes, uint64_t rows, uint64_t cols, uint64_t row_stride_elems,
+                 uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle);
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace sb

@@ -1,0 +1,156 @@
+"""Seeded synthetic inputs and random-init weights for the router and the
+ternary expert layer.
+
+There are no trained checkpoints or datasets for this path, so every workload
+is generated from a fixed recipe.  The recipe is written once here and shared
+by the golden-fixture script, the tests and the benchmark, so that no part of
+the code depends on matching another RNG stream by accident.
+
+Router recipe (state_dict names follow ``BVHRouter``, python/bvh_router.py:227-255):
+  * Weights use a generator seeded with ``WEIGHT_STREAM + seed``.
+  * Linears whose in_features is the hidden size (``to_3d``, ``spectral.net.0``,
+    ``spectral.net.2``) get W ~ N(0, 1/H); the refraction Linears (in = S) get
+    W ~ N(0, 1/S); biases are 0; centers ~ U[-1, 1]^3; log_radii = 0; portals
+    are the identity; temperature = 1.0.  Draw order is fixed (see
+    ``router_weights``).
+  * ``perturb=True`` additionally draws non-zero biases, non-identity portals
+    and a temperature != 1 so that every term of the forward is exercised.
+
+Ternary recipe (ternary SwiGLU, python/real_model_demo.py:85-98 container):
+  * T in {-1, 0, +1} with P = 1/3 each, one fp32 scale per expert matrix
+    (``c / sqrt(fan_in)`` with c ~ U[0.5, 1.5)), broadcast to the per-channel
+    scale vectors the reference kernel API takes.
+Inputs (``hidden_states``) use a generator seeded with ``seed`` itself, so equal
+seeds never give correlated router weights and inputs.
+Routing recipe (MoE layer): each token picks ``k`` distinct experts by
+Gumbel-top-k over Zipf(1.1) probabilities on a seeded expert permutation;
+weights are the softmax of N(0, 1) logits.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Sequence
+
+import numpy as np
+import torch
+
+
+WEIGHT_STREAM = 0x5B200000
+
+
+def level_sizes(branching: Sequence[int]) -> List[int]:
+    """Number of nodes on each level: level l has prod(branching[:l+1]) nodes."""
+    out, n = [], 1
+    for b in branching:
+        n *= int(b)
+        out.append(n)
+    return out
+
+
+def router_weights(hidden: int, spectral: int, branching: Sequence[int] = (4, 4, 4),
+                   seed: int = 0, perturb: bool = False,
+                   temperature: float = 1.0) -> Dict[str, np.ndarray]:
+    """fp32 router parameters keyed by ``BVHRouter`` state_dict names."""
+    # weights draw from their own stream: with the same seed as the inputs the
+    # first weight rows would equal the first input rows
+    g = torch.Generator().manual_seed(WEIGHT_STREAM + seed)
+    H, S = hidden, spectral
+    sizes = level_sizes(branching)
+    L = len(sizes)
+    w: Dict[str, np.ndarray] = {}
+
+    def randn(*shape, std):
+        return (torch.randn(*shape, generator=g) * std).numpy().astype(np.float32)
+
+    w["to_3d.weight"] = randn(3, H, std=1.0 / math.sqrt(H))
+    w["spectral.net.0.weight"] = randn(H, H, std=1.0 / math.sqrt(H))
+    w["spectral.net.2.weight"] = randn(S, H, std=1.0 / math.sqrt(H))
+    for l in range(L):
+        w[f"refract{l + 1}.W_dispersion.weight"] = randn(sizes[l], S, std=1.0 / math.sqrt(S))
+    for l in range(L):
+        c = torch.rand(sizes[l], 3, generator=g) * 2.0 - 1.0
+        w[f"level{l + 1}.centers"] = c.numpy().astype(np.float32)
+    if perturb:
+        w["to_3d.bias"] = randn(3, std=0.1)
+        w["spectral.net.0.bias"] = randn(H, std=0.1)
+        w["spectral.net.2.bias"] = randn(S, std=0.1)
+        for l in range(L):
+            w[f"refract{l + 1}.W_dispersion.bias"] = randn(sizes[l], std=0.5)
+        for l in range(L - 1):
+            eye = np.zeros((sizes[l], 3, 4), np.float32)
+            for i in range(3):
+                eye[:, i, i] = 1.0
+            w[f"portal{l + 1}.transform"] = eye + randn(sizes[l], 3, 4, std=0.2)
+    else:
+        w["to_3d.bias"] = np.zeros(3, np.float32)
+        w["spectral.net.0.bias"] = np.zeros(H, np.float32)
+        w["spectral.net.2.bias"] = np.zeros(S, np.float32)
+        for l in range(L):
+            w[f"refract{l + 1}.W_dispersion.bias"] = np.zeros(sizes[l], np.float32)
+        for l in range(L - 1):
+            eye = np.zeros((sizes[l], 3, 4), np.float32)
+            for i in range(3):
+                eye[:, i, i] = 1.0
+            w[f"portal{l + 1}.transform"] = eye
+    for l in range(L):
+        w[f"level{l + 1}.log_radii"] = np.zeros(sizes[l], np.float32)
+    w["temperature"] = np.array(temperature, np.float32)
+    w["expert_counts"] = np.zeros(sizes[-1], np.float32)
+    return w
+
+
+def unit_rms_rows(x: torch.Tensor) -> torch.Tensor:
+    """Divide each row by its root-mean-square (fp32)."""
+    rms = x.float().pow(2).mean(dim=-1, keepdim=True).sqrt()
+    return x.float() / rms
+
+
+def hidden_states(batch: int, hidden: int, seed: int, dtype=torch.float32,
+                  device="cpu") -> torch.Tensor:
+    """Unit-RMS Gaussian rows; generated on ``device`` with a seeded generator."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    x = torch.randn(batch, hidden, generator=g, device=device, dtype=torch.float32)
+    return unit_rms_rows(x).to(dtype)
+
+
+def ternary_experts(n_experts: int, hidden: int, inter: int, seed: int = 2):
+    """Ternary SwiGLU experts in the reference container layout.
+
+    Returns a list of dicts with ``gate_ternary [I,H]``, ``up_ternary [I,H]``,
+    ``down_ternary [H,I]`` (int8) and per-channel fp32 scale vectors holding one
+    constant per matrix.
+    """
+    rng = np.random.default_rng(seed)
+    out = []
+    for e in range(n_experts):
+        d = {"expert_id": e}
+        for name, shape, fan_in in (("gate", (inter, hidden), hidden),
+                                    ("up", (inter, hidden), hidden),
+                                    ("down", (hidden, inter), inter)):
+            t = rng.integers(-1, 2, size=shape, dtype=np.int8)
+            c = rng.uniform(0.5, 1.5)
+            d[f"{name}_ternary"] = t
+            d[f"{name}_scale"] = np.full(shape[0], c / math.sqrt(fan_in), np.float32)
+        out.append(d)
+    return out
+
+
+def zipf_routing(n_tokens: int, n_experts: int, k: int, seed: int, alpha: float = 1.1):
+    """Top-k expert ids (int32 [B,k], distinct per row) and weights (fp32 [B,k]).
+
+    Experts are ranked by a seeded permutation and drawn without replacement
+    with Zipf(alpha) probabilities through the Gumbel-top-k trick; weights are
+    softmax(N(0,1)) over the k slots.
+    """
+    rng = np.random.default_rng(seed)
+    perm = rng.permutation(n_experts)
+    p = 1.0 / np.arange(1, n_experts + 1, dtype=np.float64) ** alpha
+    logp = np.log(p / p.sum())
+    keys = logp[None, :] + rng.gumbel(size=(n_tokens, n_experts))
+    ranks = np.argsort(-keys, axis=1, kind="stable")[:, :k]
+    ids = perm[ranks].astype(np.int32)
+    logits = rng.standard_normal((n_tokens, k))
+    wts = np.exp(logits - logits.max(axis=1, keepdims=True))
+    wts = (wts / wts.sum(axis=1, keepdims=True)).astype(np.float32)
+    return ids, wts

@@ -1,0 +1,121 @@
+"""Pins the CPU oracle against the reference's own outputs (tests/golden/*.npz).
+
+The fixtures were produced by tests/golden/make_golden.py, which runs the
+reference modules (BVHRouter, OLMoELayer.forward_topk, quantize_ternary and
+the reference extension's pack_ternary).  These tests need no GPU.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import ROUTER_GOLDENS, golden_router_case, load_golden
+from oracle import router as orouter
+from oracle import ternary as otern
+from parity import compare_paths, rel_err, topk_ids_match
+
+
+@pytest.mark.parametrize("name", ROUTER_GOLDENS)
+def test_encoder_matches_reference(name):
+    w, x, g = golden_router_case(name)
+    pos, spec = orouter.encode(w, x)
+    np.testing.assert_allclose(pos, g["pos"], rtol=1e-4, atol=2e-6)
+    np.testing.assert_allclose(spec, g["spec"], rtol=1e-4, atol=2e-6)
+
+
+@pytest.mark.parametrize("mode", ["hard", "soft"])
+@pytest.mark.parametrize("name", ROUTER_GOLDENS)
+def test_router_matches_reference(name, mode):
+    w, x, g = golden_router_case(name)
+    br = tuple(int(b) for b in g["branching"])
+    out = orouter.router_forward(w, x, br, mode=mode, k=min(8, int(np.prod(br))))
+    bad, excused = compare_paths(g[f"{mode}_route_path"], out["route_path"], out["level_margins"])
+    assert bad == 0, f"{bad} route paths differ beyond ties"
+    assert excused.sum() <= max(1, len(excused) // 50)
+    keep = ~excused
+    assert np.array_equal(g[f"{mode}_expert_id"][keep], out["expert_id"][keep])
+    # level probabilities: 1e-4 relative + 1e-8 absolute (soft-mode logits reach |40|
+    # at T=0.5, where one fp32 ulp already moves exp() by 4e-6 relative).  The
+    # routing weights are held to the 1e-5 of the contract below.
+    np.testing.assert_allclose(out["expert_probs"][keep], g[f"{mode}_expert_probs"][keep],
+                               rtol=1e-4, atol=1e-8)
+    np.testing.assert_allclose(out["confidence"][keep], g[f"{mode}_confidence"][keep], rtol=1e-5)
+    # top-k: ids equal up to ties, weights within 1e-5 relative
+    n_bad = topk_ids_match(g[f"{mode}_expert_probs"][keep], g[f"{mode}_topk_ids"][keep],
+                           out["topk_ids"][keep], tol=1e-6)
+    assert n_bad == 0
+    np.testing.assert_allclose(out["topk_weights"][keep], g[f"{mode}_topk_weights"][keep], rtol=1e-5)
+
+
+def test_hard_mode_is_one_hot():
+    """Reference eval property (tests/test_bvh_router.py:111-117): one non-zero per row."""
+    w, x, g = golden_router_case("router_small")
+    out = orouter.router_forward(w, x, (4, 4, 4), mode="hard")
+    assert ((out["expert_probs"] > 0).sum(axis=1) == 1).all()
+    assert np.array_equal(out["expert_id"], out["route_path"][:, -1])
+
+
+def test_level_chain_generalises_to_L_levels():
+    """At L=3 the L-level recurrence is the reference; L=4 runs the same recurrence."""
+    from sb200 import synth
+    w = synth.router_weights(32, 16, (2, 3, 2, 2), seed=3, perturb=True)
+    x = synth.hidden_states(20, 32, seed=4).numpy()
+    out = orouter.router_forward(w, x, (2, 3, 2, 2), mode="soft", k=4)
+    assert out["expert_probs"].shape == (20, 24)
+    assert out["route_path"].shape == (20, 4)
+    np.testing.assert_allclose(out["topk_weights"].sum(axis=1), 1.0, rtol=1e-6)
+
+
+def test_pack_matches_reference_extension():
+    g = load_golden("ternary_small")
+    if "pack/in" not in g:
+        pytest.skip("golden made without the reference extension")
+    got = otern.pack_ternary(g["pack/in"])
+    assert got.dtype == np.int32
+    assert np.array_equal(got, g["pack/out"])
+    back = otern.unpack_ternary(got, g["pack/in"].shape[0])
+    assert np.array_equal(back, g["pack/in"])
+
+
+def test_quantizer_matches_reference():
+    g = load_golden("ternary_small")
+    t, s = otern.quantize_ternary_per_matrix(g["q_latent"])
+    assert np.array_equal(t, g["q_ternary"])
+    np.testing.assert_allclose(s, g["q_scale"], rtol=1e-6)
+
+
+def test_expert_swiglu_matches_reference():
+    g = load_golden("ternary_small")
+    y = otern.gated_mlp(g["e/x"], g["e/gate_ternary"], g["e/up_ternary"], g["e/down_ternary"],
+                        g["e/gate_scale"], g["e/up_scale"], g["e/down_scale"])
+    np.testing.assert_allclose(y, g["e/y"], rtol=1e-4, atol=1e-6)
+    # the packed (reference-kernel) formulation is the same math
+    gp = otern.pack_ternary(g["e/gate_ternary"].T)
+    up = otern.pack_ternary(g["e/up_ternary"].T)
+    dp = otern.pack_ternary(g["e/down_ternary"].T)
+    y2 = otern.gated_mlp_packed(g["e/x"], gp, up, dp, g["e/gate_scale"], g["e/up_scale"],
+                                g["e/down_scale"])
+    np.testing.assert_allclose(y2, y, rtol=1e-12, atol=1e-12)
+
+
+def test_moe_combine_matches_reference():
+    g = load_golden("ternary_small")
+    experts = []
+    for e in range(6):
+        experts.append({k: g[f"moe/{e}/{k}"] for k in ("gate_ternary", "up_ternary", "down_ternary",
+                                                        "gate_scale", "up_scale", "down_scale")})
+    y = otern.moe_combine(g["moe/x"], g["moe/ids"], g["moe/probs"], experts)
+    np.testing.assert_allclose(y, g["moe/y"], rtol=1e-4, atol=1e-6)
+
+
+def test_int8_accumulator_is_exact():
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((5, 64)).astype(np.float32)
+    q, s = otern.quantize_int8_rows(x)
+    T = rng.integers(-1, 2, (7, 64)).astype(np.int8)
+    acc = otern.int8_accumulate(q, T)
+    ref = np.array([[sum(int(q[i, k]) * int(T[j, k]) for k in range(64)) for j in range(7)]
+                    for i in range(5)])
+    assert np.array_equal(acc, ref)
+    assert np.abs(q).max() <= 127
