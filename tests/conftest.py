@@ -57,3 +57,19 @@ def cuda_device():
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     return torch.device("cuda:0")
+
+
+@pytest.fixture(autouse=True)
+def _device_status_clean(request):
+    """After every GPU test, the library's device status word must be clean
+    (no kernel gave up a bounded wait)."""
+    yield
+    if request.node.get_closest_marker("gpu") is None:
+        return
+    import torch
+    if not torch.cuda.is_available():
+        return
+    from sb200 import _lib
+    torch.cuda.synchronize()
+    rc = _lib.load().sb_device_status(0)
+    assert rc == 0, f"device status: {_lib.last_error()}"
