@@ -1,0 +1,365 @@
+"""Benchmark of the B200 hot path; prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload router|moe_layer] [--batch B]
+
+Workloads (seeded synthetic inputs with BASELINE.json's shapes; no datasets):
+  router     BVH router forward, hidden 2048, spectral 256, 4x4x4 = 64 experts,
+             top-8 + softmax, bf16 unit-RMS tokens (config 1; default B = 262144).
+             A step routes B tokens resident in HBM (1 GiB > L2, no flush needed).
+
+One process per GPU (torchrun for N > 1).  Router work shards by token with no
+collective: every rank routes its own B tokens (weak scaling).  Timing: W
+warm-up steps, then exactly K steps between CUDA events on the launching
+stream, bracketed by barrier + synchronize, max over ranks.
+
+--impl reference times the reference's CPU path on the host cores: the
+restated oracle (oracle/, a numpy port of python/bvh_router.py) on a bounded
+sample per step, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO / "spectral-ai_b200"))
+sys.path.insert(0, str(REPO))
+
+H, S, BRANCHING, TOPK = 2048, 256, (4, 4, 4), 8
+ROUTER_FLOP_PER_TOKEN = 2 * (H * H + H * S + 3 * H + S * 84)   # 9,492,480 (hard mode evaluates 3 refraction rows)
+ROUTER_BYTES_PER_TOKEN = 2 * H + TOPK * 8                       # bf16 in + ids/weights out
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"],
+                "bf16_tflops_sustained": d.get("bf16_tflops_sustained", d["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+# ---------------------------------------------------------------------------
+# clocks sampler (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.t0 = self.t1 = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+        time.sleep(0.3)
+
+    def mark(self, begin: bool):
+        if begin:
+            self.t0 = time.time()
+        else:
+            self.t1 = time.time()
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        rows = [r.split(",") for r in out.strip().splitlines() if r.strip()]
+        sm, mx, reasons = [], [], set()
+        for r in rows:
+            r = [c.strip() for c in r]
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        # samples under load: the upper half of observed clocks are the timed region
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_setup(n_gpus: int):
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    import torch.distributed as dist
+    if world > 1:
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    import torch
+    import torch.distributed as dist
+    if world == 1:
+        return v
+    t = torch.tensor([v], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline (oracle port of the reference path)
+# ---------------------------------------------------------------------------
+def blas_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 1) for i in threadpool_info() if i.get("user_api") == "blas"]
+        return max(n) if n else 1
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_router_rate(sample_tokens: int, budget_s: float = 12.0):
+    """Tokens/s of the oracle router (numpy fp32) on the host cores."""
+    import numpy as np
+    from oracle import router as orouter
+    from sb200 import synth
+    w = synth.router_weights(H, S, BRANCHING, seed=0)
+    x = synth.hidden_states(sample_tokens, H, seed=1).numpy()
+    for _ in range(2):   # warm the BLAS and thread pools
+        orouter.router_forward(w, x, BRANCHING, mode="hard", k=TOPK)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        orouter.router_forward(w, x, BRANCHING, mode="hard", k=TOPK)
+        done += sample_tokens
+        el = time.perf_counter() - t0
+        if el >= budget_s or done >= 8 * sample_tokens:
+            break
+    return done / el, done, el
+
+
+# ---------------------------------------------------------------------------
+# workloads
+# ---------------------------------------------------------------------------
+def router_workload(batch: int, device):
+    import numpy as np
+    import torch
+    from bvh_router import BVHRouter, RouterConfig
+    from sb200 import synth
+    w = synth.router_weights(H, S, BRANCHING, seed=0)
+    r = BVHRouter(RouterConfig(embed_dim=H, spectral_dim=S))
+    r.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in w.items()})
+    r = r.to(device).eval()
+    x = synth.hidden_states(batch, H, seed=1, dtype=torch.bfloat16, device=device)
+    eng = r.sync_weights(device)
+    outs = {"topk_ids": torch.empty(batch, TOPK, dtype=torch.int32, device=device),
+            "topk_weights": torch.empty(batch, TOPK, dtype=torch.float32, device=device)}
+
+    def step():
+        eng.forward(x, precision="fast", select="hard", k=TOPK, outputs=outs)
+
+    x_host = x.cpu().pin_memory()
+    ids_host = torch.empty(batch, TOPK, dtype=torch.int32).pin_memory()
+    w_host = torch.empty(batch, TOPK, dtype=torch.float32).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        # public API: BVHRouter.forward_topk on a host batch copied in, results copied out
+        x_dev.copy_(x_host, non_blocking=True)
+        ids, wts = r.forward_topk(x_dev, k=TOPK)
+        ids_host.copy_(ids, non_blocking=True)
+        w_host.copy_(wts, non_blocking=True)
+
+    meta = {"tokens_per_step": batch,
+            "h2d": batch * H * 2, "d2h": batch * TOPK * 8,
+            "dominant": "router_enc1_gelu_tc", "dominant_flop": 2.0 * batch * H * H,
+            "dominant_bytes": batch * H * 2 * 2 + H * H * 2,
+            "config": {"workload": "router_fwd_bvh_4x4x4_top8", "hidden": H, "spectral_dim": S,
+                       "experts": 64, "top_k": TOPK, "batch_tokens_per_gpu": batch,
+                       "select": "hard", "precision": "bf16 tcgen05 encoder, fp32 descent",
+                       "l2": "inputs 1 GiB per GPU > 126 MB L2 (no flush)"}}
+    return step, e2e_step, meta
+
+
+def time_steps(step, steps, warmup, world, sampler=None, profile=False):
+    import torch
+    from sb200 import _lib
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    if profile:
+        _lib.profile_enable(True)
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if sampler:
+        sampler.mark(True)
+    e0.record(s)
+    for _ in range(steps):
+        step()
+    e1.record(s)
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.mark(False)
+    barrier(world)
+    ms = e0.elapsed_time(e1)
+    prof = _lib.profile_read() if profile else {}
+    if profile:
+        _lib.profile_enable(False)
+    return max_over_ranks(ms, world), prof
+
+
+def run_ours(a):
+    import torch
+    rank, world, local = dist_setup(a.gpus)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    batch = a.batch or 262144
+    step, e2e_step, meta = router_workload(batch, dev)
+    sampler = ClockSampler(local) if rank == 0 or True else None
+    sampler.start()
+    total_ms, prof = time_steps(step, a.steps, a.warmup, world, sampler, profile=True)
+    clocks = sampler.stop()
+    e2e_ms, _ = time_steps(e2e_step, a.steps, a.warmup, world)
+    tokens = meta["tokens_per_step"] * a.steps * world
+    value = tokens / (total_ms / 1e3)
+    e2e_value = tokens / (e2e_ms / 1e3)
+    pk = peaks()
+    dom = prof.get(meta["dominant"], (0, 0.0))
+    launches = sum(n for n, _ in prof.values())
+    roof = None
+    if dom[0]:
+        avg_s = dom[1] / dom[0] / 1e3
+        achieved = meta["dominant_flop"] / avg_s / 1e12
+        roof = {"kernel": meta["dominant"], "bound": "tensor", "achieved": round(achieved, 1),
+                "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": round(achieved / pk["bf16_tflops"], 4),
+                "peak_source": f"{pk['source']} bf16 burst (cuBLAS)",
+                "traffic": traffic_for(meta),
+                "avg_launch_ms": round(dom[1] / dom[0], 4),
+                "hbm_frac_of_step": round(meta["tokens_per_step"] * ROUTER_BYTES_PER_TOKEN /
+                                          (total_ms / a.steps / 1e3) / 1e9 / pk["hbm_gbs"], 4)}
+    out = {"metric": "router Mq/s (BVH route, top-8) — MoE layer pending",
+           "value": round(value / 1e6, 3), "unit": "Mq/s", "n_gpus": world, "steps": a.steps,
+           "warmup": a.warmup, "ms_per_step": round(total_ms / a.steps, 4),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+           "data": "synthetic (seeded unit-RMS Gaussian tokens, random-init router)",
+           "config": dict(meta["config"], parallelism=f"token-shard x{world}, no collective"),
+           "e2e": {"value": round(e2e_value / 1e6, 3), "unit": "Mq/s",
+                   "h2d_bytes_per_step": meta["h2d"], "d2h_bytes_per_step": meta["d2h"],
+                   "api": "bvh_router.BVHRouter.forward_topk"},
+           "gpu_launches": launches,
+           "kernels": {k: {"launches": n, "avg_ms": round(t / max(n, 1), 4)} for k, (n, t) in prof.items()},
+           "roofline": roof, "clocks": clocks}
+    if rank == 0 and world == 1 and not a.no_cpu_baseline:
+        rate, done, el = cpu_router_rate(4096)
+        out["cpu_baseline"] = {"value": round(rate / 1e6, 6), "unit": "Mq/s", "cores": blas_threads(),
+                               "kind": "port",
+                               "sample": f"{done} tokens of the same workload through the numpy "
+                                         f"oracle (fp32) in {el:.1f} s"}
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def traffic_for(meta):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary
+    (profiles/<kernel>.json, bytes per token measured on a smaller case), or None."""
+    p = REPO / "profiles" / f"{meta['dominant']}.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    return int(d["dram_bytes_per_token"] * meta["tokens_per_step"])
+
+
+def run_reference(a):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    sample = 4096
+    # each step: the reference CPU router path on a bounded token sample
+    from oracle import router as orouter
+    from sb200 import synth
+    cores = blas_threads()
+    w = synth.router_weights(H, S, BRANCHING, seed=0)
+    x = synth.hidden_states(sample, H, seed=1).numpy()
+    for _ in range(max(a.warmup, 1)):
+        orouter.router_forward(w, x, BRANCHING, mode="hard", k=TOPK)
+    t0 = time.perf_counter()
+    for _ in range(a.steps):
+        orouter.router_forward(w, x, BRANCHING, mode="hard", k=TOPK)
+    el = time.perf_counter() - t0
+    value = sample * a.steps / el / 1e6
+    out = {"impl": "reference", "metric": "router Mq/s (BVH route, top-8) — MoE layer pending",
+           "value": round(value, 6), "unit": "Mq/s", "n_gpus": 0, "steps": a.steps,
+           "warmup": a.warmup, "ms_per_step": round(el / a.steps * 1e3, 3),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+           "data": "synthetic (seeded unit-RMS Gaussian tokens, random-init router)",
+           "config": {"workload": "router_fwd_bvh_4x4x4_top8", "hidden": H, "spectral_dim": S,
+                      "experts": 64, "top_k": TOPK, "batch_tokens_per_step": sample},
+           "cpu_baseline": {"value": round(value, 6), "unit": "Mq/s", "cores": cores, "kind": "port",
+                            "sample": f"{sample} tokens per step through the numpy port of "
+                                      "python/bvh_router.py (fp32), host cores"},
+           "e2e": {"value": round(value, 6), "unit": "Mq/s", "h2d_bytes_per_step": 0,
+                   "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="router", choices=["router"])
+    ap.add_argument("--batch", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    a = ap.parse_args()
+    a.warmup = max(a.warmup, 3) if a.impl == "ours" else a.warmup
+    if a.impl == "reference":
+        a.steps = min(a.steps, 10)
+        run_reference(a)
+    else:
+        run_ours(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -66,6 +66,15 @@ int sb_last_error(char* buf, size_t len);
  * SB_OK or SB_ERR_DEVICE_TIMEOUT if a kernel gave up a bounded wait. */
 int sb_device_status(int device);
 
+/* Per-kernel timing with CUDA events recorded on each launch's stream (the
+ * reference times host-side with perf_counter + synchronize,
+ * python/benchmark_cuda_pipeline.py:110-146).  Enabling clears the counters. */
+int sb_profile_enable(int on);
+/* Number of distinct kernels timed so far (waits for the recorded events). */
+int sb_profile_count(void);
+/* Name, launch count and summed milliseconds of timed kernel i. */
+int sb_profile_entry(int i, char* name, size_t len, int64_t* launches, double* total_ms);
+
 /* ------------------------------------------------------------------------ */
 /* BVH router                                                                */
 /* ------------------------------------------------------------------------ */

@@ -77,7 +77,98 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype, 
   return SB_OK;
 }
 
+// ---------------------------------------------------------------------------
+// per-kernel event profiler
+// ---------------------------------------------------------------------------
+namespace {
+struct ProfEntry {
+  std::string name;
+  int64_t launches = 0;
+  double total_ms = 0.0;
+};
+struct Pending {
+  const char* name;
+  cudaEvent_t start, stop;
+};
+std::mutex g_prof_mu;
+bool g_prof_on = false;
+std::vector<ProfEntry> g_prof_entries;
+std::vector<Pending> g_prof_pending;
+std::vector<cudaEvent_t> g_prof_free;
+
+void prof_resolve_locked() {
+  for (const Pending& p : g_prof_pending) {
+    float ms = 0.f;
+    if (cudaEventSynchronize(p.stop) == cudaSuccess &&
+        cudaEventElapsedTime(&ms, p.start, p.stop) == cudaSuccess) {
+      ProfEntry* e = nullptr;
+      for (auto& x : g_prof_entries)
+        if (x.name == p.name) e = &x;
+      if (!e) {
+        g_prof_entries.push_back(ProfEntry{p.name, 0, 0.0});
+        e = &g_prof_entries.back();
+      }
+      e->launches += 1;
+      e->total_ms += ms;
+    }
+    g_prof_free.push_back(p.start);
+    g_prof_free.push_back(p.stop);
+  }
+  g_prof_pending.clear();
+}
+}  // namespace
+
+bool prof_enabled() { return g_prof_on; }
+
+cudaEvent_t prof_event() {
+  std::lock_guard<std::mutex> g(g_prof_mu);
+  if (!g_prof_free.empty()) {
+    cudaEvent_t e = g_prof_free.back();
+    g_prof_free.pop_back();
+    return e;
+  }
+  cudaEvent_t e = nullptr;
+  if (cudaEventCreate(&e) != cudaSuccess) return nullptr;
+  return e;
+}
+
+void prof_record(const char* name, cudaEvent_t start, cudaEvent_t stop) {
+  std::lock_guard<std::mutex> g(g_prof_mu);
+  g_prof_pending.push_back(Pending{name, start, stop});
+  if (g_prof_pending.size() > 4096) prof_resolve_locked();
+}
+
 }  // namespace sb
+
+extern "C" int sb_profile_enable(int on) {
+  std::lock_guard<std::mutex> g(sb::g_prof_mu);
+  sb::prof_resolve_locked();
+  sb::g_prof_entries.clear();
+  sb::g_prof_on = on != 0;
+  return SB_OK;
+}
+
+extern "C" int sb_profile_count(void) {
+  std::lock_guard<std::mutex> g(sb::g_prof_mu);
+  sb::prof_resolve_locked();
+  return (int)sb::g_prof_entries.size();
+}
+
+extern "C" int sb_profile_entry(int i, char* name, size_t len, int64_t* launches, double* total_ms) {
+  std::lock_guard<std::mutex> g(sb::g_prof_mu);
+  sb::prof_resolve_locked();
+  if (i < 0 || i >= (int)sb::g_prof_entries.size())
+    return sb::fail(SB_ERR_INVALID, "profile entry %d out of range", i);
+  const auto& e = sb::g_prof_entries[i];
+  if (name && len) {
+    size_t n = e.name.size() < len - 1 ? e.name.size() : len - 1;
+    memcpy(name, e.name.data(), n);
+    name[n] = 0;
+  }
+  if (launches) *launches = e.launches;
+  if (total_ms) *total_ms = e.total_ms;
+  return SB_OK;
+}
 
 extern "C" int sb_abi_version(void) { return SB_ABI_VERSION; }
 

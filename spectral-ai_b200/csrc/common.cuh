@@ -41,4 +41,32 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
+// Per-kernel CUDA-event timing (off by default).  A ProfScope records an event
+// pair around one launch on its stream; sb_profile_count()/sb_profile_entry()
+// resolve them.
+bool prof_enabled();
+void prof_record(const char* name, cudaEvent_t start, cudaEvent_t stop);
+cudaEvent_t prof_event();
+
+struct ProfScope {
+  const char* name;
+  cudaStream_t stream;
+  cudaEvent_t start = nullptr;
+  ProfScope(const char* n, cudaStream_t s) : name(n), stream(s) {
+    if (prof_enabled()) {
+      start = prof_event();
+      if (start) cudaEventRecord(start, stream);
+    }
+  }
+  ~ProfScope() {
+    if (start) {
+      cudaEvent_t stop = prof_event();
+      if (stop) {
+        cudaEventRecord(stop, stream);
+        prof_record(name, start, stop);
+      }
+    }
+  }
+};
+
 }  // namespace sb

@@ -682,8 +682,8 @@ size_t ws_spec_bytes(const sb_router* h, int64_t B) {
 }
 
 template <int BN, int STAGES, class Epi>
-int launch_gemm_tc(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, Epi epi,
-                   cudaStream_t stream) {
+int launch_gemm_tc(const char* name, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
+                   int K, Epi epi, cudaStream_t stream) {
   using C = GemmCfg<BN, STAGES>;
   auto kern = gemm_tc_kernel<BN, STAGES, Epi>;
   static bool attr_done[64] = {};
@@ -695,6 +695,7 @@ int launch_gemm_tc(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, i
   }
   const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN);
   const int grid = tiles < num_sms() ? tiles : num_sms();
+  ProfScope prof(name, stream);
   kern<<<grid, GEMM_THREADS, C::SMEM_BYTES, stream>>>(ta, tb, M, N, K, idesc_f16(1, GEMM_BM, BN), epi);
   SB_CUDA_TRY(cudaGetLastError());
   return SB_OK;
@@ -749,25 +750,31 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
                            CU_TENSOR_MAP_SWIZZLE_128B)))
       return rc;
     EpiGeluBf16 e1{h->b1, static_cast<__nv_bfloat16*>(G), H, H};
-    if ((rc = launch_gemm_tc<256, 4>(ta, h->tm_w1, M, H, H, e1, stream))) return rc;
+    if ((rc = launch_gemm_tc<256, 4>("router_enc1_gelu_tc", ta, h->tm_w1, M, H, H, e1, stream))) return rc;
     EpiTanhF32 e2{h->b2, spec, S, S};
     if (S <= 128) {  // tm_w2's box height matches this tile width (set at upload)
-      if ((rc = launch_gemm_tc<128, 4>(tg, h->tm_w2, M, S, H, e2, stream))) return rc;
+      if ((rc = launch_gemm_tc<128, 4>("router_enc2_tanh_tc", tg, h->tm_w2, M, S, H, e2, stream))) return rc;
     } else {
-      if ((rc = launch_gemm_tc<256, 4>(tg, h->tm_w2, M, S, H, e2, stream))) return rc;
+      if ((rc = launch_gemm_tc<256, 4>("router_enc2_tanh_tc", tg, h->tm_w2, M, S, H, e2, stream))) return rc;
     }
   } else {
     dim3 grid1((H + 127) / 128, (M + 127) / 128), grid2((S + 127) / 128, (M + 127) / 128);
     float* G32 = static_cast<float*>(G);
-    if (x_dtype == SB_BF16)
-      sgemm_nt_kernel<__nv_bfloat16, ACT_GELU><<<grid1, 256, 0, stream>>>(
-          static_cast<const __nv_bfloat16*>(x), h->w1_f32, h->b1, G32, M, H, H);
-    else
-      sgemm_nt_kernel<float, ACT_GELU><<<grid1, 256, 0, stream>>>(static_cast<const float*>(x),
-                                                                 h->w1_f32, h->b1, G32, M, H, H);
-    SB_CUDA_TRY(cudaGetLastError());
-    sgemm_nt_kernel<float, ACT_TANH><<<grid2, 256, 0, stream>>>(G32, h->w2_f32, h->b2, spec, M, S, H);
-    SB_CUDA_TRY(cudaGetLastError());
+    {
+      ProfScope prof1("router_enc1_gelu_f32", stream);
+      if (x_dtype == SB_BF16)
+        sgemm_nt_kernel<__nv_bfloat16, ACT_GELU><<<grid1, 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(x), h->w1_f32, h->b1, G32, M, H, H);
+      else
+        sgemm_nt_kernel<float, ACT_GELU><<<grid1, 256, 0, stream>>>(static_cast<const float*>(x),
+                                                                   h->w1_f32, h->b1, G32, M, H, H);
+      SB_CUDA_TRY(cudaGetLastError());
+    }
+    {
+      ProfScope prof2("router_enc2_tanh_f32", stream);
+      sgemm_nt_kernel<float, ACT_TANH><<<grid2, 256, 0, stream>>>(G32, h->w2_f32, h->b2, spec, M, S, H);
+      SB_CUDA_TRY(cudaGetLastError());
+    }
   }
   TreeDev t{};
   t.L = L;
@@ -802,6 +809,7 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
   int64_t blocks = (batch + DESC_WARPS - 1) / DESC_WARPS;
   const int64_t cap = (int64_t)num_sms() * 8;
   if (blocks > cap) blocks = cap;
+  ProfScope prof("router_descent", stream);
   if (x_dtype == SB_BF16)
     descent_kernel<__nv_bfloat16><<<(unsigned)blocks, DESC_WARPS * 32, dsm, stream>>>(
         static_cast<const __nv_bfloat16*>(x), spec, batch, t, select == SB_SELECT_SOFT, o);

@@ -55,6 +55,10 @@ SIGNATURES = [
     ("sb_abi_version", C.c_int, []),
     ("sb_last_error", C.c_int, [C.c_char_p, C.c_size_t]),
     ("sb_device_status", C.c_int, [C.c_int]),
+    ("sb_profile_enable", C.c_int, [C.c_int]),
+    ("sb_profile_count", C.c_int, []),
+    ("sb_profile_entry", C.c_int, [C.c_int, C.c_char_p, C.c_size_t, C.POINTER(C.c_int64),
+                                   C.POINTER(C.c_double)]),
     ("sb_router_create", C.c_int, [C.POINTER(RouterDesc), C.c_int, C.POINTER(C.c_void_p)]),
     ("sb_router_upload", C.c_int, [C.c_void_p, C.POINTER(RouterWeights)]),
     ("sb_router_workspace_bytes", C.c_size_t, [C.c_void_p, C.c_int64, C.c_int]),
@@ -118,6 +122,23 @@ def last_error() -> str:
 def check(rc: int, what: str) -> None:
     if rc != SB_OK:
         raise RuntimeError(f"{what}: {SB_ERR.get(rc, rc)}: {last_error()}")
+
+
+def profile_enable(on: bool = True) -> None:
+    load().sb_profile_enable(1 if on else 0)
+
+
+def profile_read():
+    """{kernel name: (launches, total_ms)} of the library's event profiler."""
+    lib = load()
+    out = {}
+    for i in range(lib.sb_profile_count()):
+        name = C.create_string_buffer(128)
+        n = C.c_int64()
+        ms = C.c_double()
+        check(lib.sb_profile_entry(i, name, 128, C.byref(n), C.byref(ms)), "sb_profile_entry")
+        out[name.value.decode()] = (int(n.value), float(ms.value))
+    return out
 
 
 def exported_symbols():
