@@ -241,33 +241,76 @@ __device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
 constexpr int DESC_WARPS = 8;
 constexpr int SPL_MAX = 8;  // spectral dims per lane: S <= 256
 
+// Loads 4 consecutive input features as fp32 (8-byte / 16-byte aligned).
+__device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&v)[4]) {
+  const uint2 u = *reinterpret_cast<const uint2*>(p);
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
+  const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+  v[0] = a.x; v[1] = a.y; v[2] = b.x; v[3] = b.y;
+}
+__device__ __forceinline__ void load4(const float* p, float (&v)[4]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+}
+
+constexpr int DESC_TPW = 4;  // tokens per warp iteration sharing the to_3d weight reads
+
+// Shared memory: to_3d weights [3][H] fp32, then (soft mode) two probability
+// buffers of max_nodes floats per warp.
 template <typename TX>
 __global__ void __launch_bounds__(DESC_WARPS * 32)
     descent_kernel(const TX* __restrict__ x, const float* __restrict__ spec, int64_t B, TreeDev t,
                    int soft, DescentOut o) {
   extern __shared__ float dsm[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float* pa = dsm + (size_t)warp * 2 * t.max_nodes;  // previous level probs (soft)
-  float* pb = pa + t.max_nodes;                      // current level probs (soft)
   const int H = t.H, S = t.S, L = t.L;
-  for (int64_t tok = (int64_t)blockIdx.x * DESC_WARPS + warp; tok < B;
-       tok += (int64_t)gridDim.x * DESC_WARPS) {
-    // ---- pos = to_3d(x) in fp32 (bvh_router.py:285)
-    float p0 = 0.f, p1 = 0.f, p2 = 0.f;
-    const TX* xr = x + tok * (int64_t)H;
-    for (int i = lane * 8; i < H; i += 256) {
-      float v[8];
-      load8(xr + i, v);
+  float* w3 = dsm;
+  for (int i = threadIdx.x; i < 3 * H; i += blockDim.x) w3[i] = t.w3d[i];
+  __syncthreads();
+  float* pa0 = dsm + 3 * H + (size_t)warp * 2 * t.max_nodes;  // previous level probs (soft)
+  float* pb0 = pa0 + t.max_nodes;                              // current level probs (soft)
+  const float b3x = __ldg(t.b3d + 0), b3y = __ldg(t.b3d + 1), b3z = __ldg(t.b3d + 2);
+  for (int64_t tok0 = ((int64_t)blockIdx.x * DESC_WARPS + warp) * DESC_TPW; tok0 < B;
+       tok0 += (int64_t)gridDim.x * DESC_WARPS * DESC_TPW) {
+    // ---- pos = to_3d(x) in fp32 for DESC_TPW tokens (bvh_router.py:285)
+    float acc[DESC_TPW][3];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        p0 = fmaf(v[j], __ldg(t.w3d + i + j), p0);
-        p1 = fmaf(v[j], __ldg(t.w3d + H + i + j), p1);
-        p2 = fmaf(v[j], __ldg(t.w3d + 2 * H + i + j), p2);
+    for (int u = 0; u < DESC_TPW; ++u) acc[u][0] = acc[u][1] = acc[u][2] = 0.f;
+    for (int i = lane * 4; i < H; i += 128) {
+      const float4 wa = *reinterpret_cast<const float4*>(w3 + i);
+      const float4 wb = *reinterpret_cast<const float4*>(w3 + H + i);
+      const float4 wc = *reinterpret_cast<const float4*>(w3 + 2 * H + i);
+#pragma unroll
+      for (int u = 0; u < DESC_TPW; ++u) {
+        if (tok0 + u >= B) break;
+        float v[4];
+        load4(x + (tok0 + u) * (int64_t)H + i, v);
+        acc[u][0] = fmaf(v[0], wa.x, fmaf(v[1], wa.y, fmaf(v[2], wa.z, fmaf(v[3], wa.w, acc[u][0]))));
+        acc[u][1] = fmaf(v[0], wb.x, fmaf(v[1], wb.y, fmaf(v[2], wb.z, fmaf(v[3], wb.w, acc[u][1]))));
+        acc[u][2] = fmaf(v[0], wc.x, fmaf(v[1], wc.y, fmaf(v[2], wc.z, fmaf(v[3], wc.w, acc[u][2]))));
       }
     }
-    float cx = warp_sum(p0) + __ldg(t.b3d + 0);
-    float cy = warp_sum(p1) + __ldg(t.b3d + 1);
-    float cz = warp_sum(p2) + __ldg(t.b3d + 2);
+#pragma unroll
+    for (int u = 0; u < DESC_TPW; ++u) {
+      acc[u][0] = warp_sum(acc[u][0]);
+      acc[u][1] = warp_sum(acc[u][1]);
+      acc[u][2] = warp_sum(acc[u][2]);
+    }
+#pragma unroll 1
+    for (int u = 0; u < DESC_TPW; ++u) {
+    const int64_t tok = tok0 + u;
+    if (tok >= B) break;
+    float* pa = pa0;
+    float* pb = pb0;
+    float cx = acc[0][0] + b3x, cy = acc[0][1] + b3y, cz = acc[0][2] + b3z;
+    // select this token's sums without dynamic register indexing
+#pragma unroll
+    for (int v = 1; v < DESC_TPW; ++v)
+      if (u == v) {
+        cx = acc[v][0] + b3x;
+        cy = acc[v][1] + b3y;
+        cz = acc[v][2] + b3z;
+      }
 
     float spec_r[SPL_MAX];
 #pragma unroll
@@ -481,6 +524,7 @@ __global__ void __launch_bounds__(DESC_WARPS * 32)
       if (o.expert_id) o.expert_id[tok] = eid;
       if (o.confidence) o.confidence[tok] = conf;
     }
+    }  // tokens of the group
   }
 }
 
@@ -797,7 +841,8 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
   t.portals = h->portals;
   DescentOut o{out->topk_ids, out->topk_weights, out->expert_id, out->expert_probs,
                out->route_path, out->confidence, top_k};
-  const size_t dsm = select == SB_SELECT_SOFT ? (size_t)DESC_WARPS * 2 * h->max_nodes * sizeof(float) : 0;
+  const size_t dsm = (size_t)3 * H * sizeof(float) +
+                     (select == SB_SELECT_SOFT ? (size_t)DESC_WARPS * 2 * h->max_nodes * sizeof(float) : 0);
   if (dsm > 48 * 1024) {
     static bool attr[2] = {false, false};
     auto k0 = descent_kernel<float>;
@@ -806,7 +851,7 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
     if (!attr[0]) { SB_CUDA_TRY(cudaFuncSetAttribute(k0, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)); attr[0] = true; }
     if (!attr[1]) { SB_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)); attr[1] = true; }
   }
-  int64_t blocks = (batch + DESC_WARPS - 1) / DESC_WARPS;
+  int64_t blocks = (batch + DESC_WARPS * DESC_TPW - 1) / (DESC_WARPS * DESC_TPW);
   const int64_t cap = (int64_t)num_sms() * 8;
   if (blocks > cap) blocks = cap;
   ProfScope prof("router_descent", stream);

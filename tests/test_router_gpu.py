@@ -39,7 +39,9 @@ def check_against(ref, got, mode, wtol, ptol=None):
     probs = got["expert_probs"].cpu().numpy()
     np.testing.assert_allclose(probs[keep], ref["expert_probs"][keep],
                                rtol=ptol or wtol, atol=1e-8 if ptol is None else 1e-6)
-    np.testing.assert_allclose(got["confidence"].cpu().numpy()[keep], ref["confidence"][keep], rtol=wtol)
+    # confidence is a level probability: same tolerance as expert_probs
+    np.testing.assert_allclose(got["confidence"].cpu().numpy()[keep], ref["confidence"][keep],
+                               rtol=ptol or wtol)
     if "topk_ids" in got:
         ids = got["topk_ids"].cpu().numpy()
         tol = 1e-6 if wtol <= 1e-5 else wtol
