@@ -14,6 +14,7 @@
 //   ((w & (0x00010001 << j)) * (M << (P - j))) | ((w & (0x01000100 << j)) << (7 - j))
 // where M << P is the magnitude pattern of 1.0 (bf16: 0x7F << 7, fp16: 0xF << 10).
 #include "common.cuh"
+#include "ternary_gemm.cuh"
 
 namespace sb {
 
@@ -91,26 +92,411 @@ extern "C" int sb_ternary_repack(const int32_t* packed_ref, int64_t K, int64_t N
   return SB_OK;
 }
 
+// ===========================================================================
+// MoE dispatch / combine and the host entry points
+// ===========================================================================
+namespace sb {
+
+// expert histogram of the (token, slot) pairs; out-of-range ids are reported
+// through the status word and dropped
+__global__ void moe_hist_kernel(const int32_t* __restrict__ ids, int64_t R, int E,
+                                int* __restrict__ counts) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < R;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int e = ids[i];
+    if (e >= 0 && e < E)
+      atomicAdd(&counts[e], 1);
+    else
+      set_status(ST_BAD_ARGUMENT);
+  }
+}
+
+// expert offsets (exclusive scan), scatter cursors and the m-tile table
+__global__ void moe_scan_kernel(const int* __restrict__ counts, int E, int* __restrict__ offsets,
+                                int* __restrict__ cursor, MTile* __restrict__ mtiles,
+                                int* __restrict__ num_mtiles, int max_mtiles) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  int off = 0, nt = 0;
+  for (int e = 0; e < E; ++e) {
+    const int c = counts[e];
+    offsets[e] = off;
+    cursor[e] = 0;
+    for (int r = 0; r < c && nt < max_mtiles; r += 128) {
+      MTile t;
+      t.expert = e;
+      t.row0 = off + r;
+      t.rows = (c - r) < 128 ? (c - r) : 128;
+      t.pad = 0;
+      mtiles[nt++] = t;
+    }
+    off += c;
+  }
+  *num_mtiles = nt;
+}
+
+template <typename TX, typename TA>
+__device__ __forceinline__ TA cvt_act(TX v);
+template <> __device__ __forceinline__ __nv_bfloat16 cvt_act<float, __nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <> __device__ __forceinline__ __half cvt_act<float, __half>(float v) { return __float2half_rn(v); }
+template <> __device__ __forceinline__ __nv_bfloat16 cvt_act<__nv_bfloat16, __nv_bfloat16>(__nv_bfloat16 v) { return v; }
+template <> __device__ __forceinline__ __half cvt_act<__nv_bfloat16, __half>(__nv_bfloat16 v) { return __float2half_rn(__bfloat162float(v)); }
+
+// One warp per (token, slot) pair: claim a row of the expert's segment, record
+// the routing weight and the inverse map, and copy the token's activations.
+template <typename TX, typename TA>
+__global__ void moe_scatter_kernel(const TX* __restrict__ x, const int32_t* __restrict__ ids,
+                                   const float* __restrict__ wts, int64_t B, int k, int H, int E,
+                                   const int* __restrict__ offsets, int* __restrict__ cursor,
+                                   TA* __restrict__ xp, int64_t ldx, float* __restrict__ row_w,
+                                   int* __restrict__ inv) {
+  const int lane = threadIdx.x & 31;
+  const int64_t R = B * k;
+  for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < R;
+       i += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int e = ids[i];
+    int pos = -1;
+    if (lane == 0 && e >= 0 && e < E) pos = offsets[e] + atomicAdd(&cursor[e], 1);
+    pos = __shfl_sync(0xffffffffu, pos, 0);
+    if (lane == 0) inv[i] = pos;
+    if (pos < 0) continue;
+    if (lane == 0) row_w[pos] = wts ? wts[i] : 1.0f;
+    const TX* src = x + (i / k) * (int64_t)H;
+    TA* dst = xp + (int64_t)pos * ldx;
+    for (int c = lane; c < H; c += 32) dst[c] = cvt_act<TX, TA>(src[c]);
+  }
+}
+
+// out[t] = sum_j y[inv[t*k+j]] in slot order (fixed, so results are reproducible)
+template <typename TO>
+__device__ __forceinline__ TO cvt_out(float v);
+template <> __device__ __forceinline__ float cvt_out<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 cvt_out<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+template <typename TO>
+__global__ void moe_combine_kernel(const float* __restrict__ y, const int* __restrict__ inv, int64_t B,
+                                   int k, int H, TO* __restrict__ out) {
+  const int64_t total = B * (int64_t)H;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t t = i / H;
+    const int c = (int)(i % H);
+    float acc = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int pos = inv[t * k + j];
+      if (pos >= 0) acc += y[(int64_t)pos * H + c];
+    }
+    out[i] = cvt_out<TO>(acc);
+  }
+}
+
+template <typename TX, typename TA>
+__global__ void rows_convert_kernel(const TX* __restrict__ x, int64_t M, int K, TA* __restrict__ xp,
+                                    int64_t ldx) {
+  const int64_t total = M * (int64_t)K;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / K;
+    const int c = (int)(i % K);
+    xp[r * ldx + c] = cvt_act<TX, TA>(x[i]);
+  }
+}
+
+__global__ void fill_i32_kernel(int32_t* p, int64_t n, int32_t v) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    p[i] = v;
+}
+
+namespace {
+
+inline int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+struct MoeLayout {
+  int64_t R, ldx, ldh, max_mt;
+  size_t off_counts, off_offsets, off_cursor, off_nmt, off_mtiles, off_roww, off_inv, off_ids, off_xp,
+      off_hp, off_yp, total;
+};
+
+MoeLayout moe_layout(int64_t B, int64_t H, int64_t I, int32_t E, int32_t k) {
+  MoeLayout L{};
+  L.R = B * k;
+  L.ldx = round_up(H, 64);
+  L.ldh = round_up(I, 64);
+  L.max_mt = L.R / 128 + E + 1;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    size_t at = o;
+    o = align_up(o + bytes, 1024);
+    return at;
+  };
+  L.off_counts = take(sizeof(int) * E);
+  L.off_offsets = take(sizeof(int) * E);
+  L.off_cursor = take(sizeof(int) * E);
+  L.off_nmt = take(sizeof(int));
+  L.off_mtiles = take(sizeof(MTile) * L.max_mt);
+  L.off_roww = take(sizeof(float) * L.R);
+  L.off_inv = take(sizeof(int) * L.R);
+  L.off_ids = take(sizeof(int) * L.R);
+  L.off_xp = take((size_t)L.R * L.ldx * 2);
+  L.off_hp = take((size_t)L.R * L.ldh * 2);
+  L.off_yp = take((size_t)L.R * H * 4);
+  L.total = o;
+  return L;
+}
+
+template <int MODE, int FMT>
+int launch_tgemm(const char* name, const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1,
+                 const TernGemmParams& p, cudaStream_t stream) {
+  auto kern = ternary_gemm_kernel<MODE, FMT>;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TG_SMEM_BYTES));
+    attr_done[dev] = true;
+  }
+  ProfScope prof(name, stream);
+  kern<<<num_sms(), TG_THREADS, TG_SMEM_BYTES, stream>>>(ta, tb0, tb1, p);
+  SB_CUDA_TRY(cudaGetLastError());
+  return SB_OK;
+}
+
+int check_ternary_shapes(int64_t H, int64_t I) {
+  SB_REQUIRE(H > 0 && I > 0, "hidden=%lld and intermediate=%lld must be positive", (long long)H, (long long)I);
+  SB_REQUIRE(H <= (1 << 20) && I <= (1 << 20), "dimensions too large");
+  return SB_OK;
+}
+
+// The grouped SwiGLU pipeline shared by the MoE layer and the single-expert API.
+int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int32_t E, int32_t k,
+                const int32_t* ids, const float* weights, const uint32_t* gate, const uint32_t* up,
+                const uint32_t* down, const float* gs, const float* us, const float* ds, void* out,
+                int out_dtype, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  int rc;
+  if ((rc = check_ternary_shapes(H, I))) return rc;
+  SB_REQUIRE(E >= 1 && E <= 65536, "n_experts=%d out of range", E);
+  SB_REQUIRE(k >= 1 && k <= 64, "top_k=%d out of range", k);
+  SB_REQUIRE(x_dtype == SB_F32 || x_dtype == SB_BF16, "x dtype must be SB_F32 or SB_BF16");
+  SB_REQUIRE(out_dtype == SB_F32 || out_dtype == SB_BF16, "out dtype must be SB_F32 or SB_BF16");
+  if (B == 0) return SB_OK;
+  SB_REQUIRE(x && ids && gate && up && down && gs && us && ds && out, "null pointer argument");
+  SB_REQUIRE(B * k <= (int64_t)INT32_MAX / 2, "too many (token, slot) pairs");
+  const MoeLayout L = moe_layout(B, H, I, E, k);
+  if (!workspace || workspace_bytes < L.total)
+    return fail(SB_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, L.total);
+  SB_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 1023u) == 0, "workspace must be 1024-byte aligned");
+  SB_REQUIRE((reinterpret_cast<uintptr_t>(gate) & 15u) == 0 && (reinterpret_cast<uintptr_t>(up) & 15u) == 0 &&
+                 (reinterpret_cast<uintptr_t>(down) & 15u) == 0,
+             "packed weights must be 16-byte aligned");
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* counts = reinterpret_cast<int*>(ws + L.off_counts);
+  int* offsets = reinterpret_cast<int*>(ws + L.off_offsets);
+  int* cursor = reinterpret_cast<int*>(ws + L.off_cursor);
+  int* nmt = reinterpret_cast<int*>(ws + L.off_nmt);
+  MTile* mtiles = reinterpret_cast<MTile*>(ws + L.off_mtiles);
+  float* row_w = reinterpret_cast<float*>(ws + L.off_roww);
+  int* inv = reinterpret_cast<int*>(ws + L.off_inv);
+  void* xp = ws + L.off_xp;
+  __half* hp = reinterpret_cast<__half*>(ws + L.off_hp);
+  float* yp = reinterpret_cast<float*>(ws + L.off_yp);
+  const int fmt_gu = (x_dtype == SB_BF16) ? 1 : 0;  // bf16 inputs stay bf16; fp32 inputs go to fp16
+
+  {
+    ProfScope prof("moe_dispatch", stream);
+    SB_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int) * E, stream));
+    const int64_t R = L.R;
+    int64_t blocks = (R + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    moe_hist_kernel<<<(unsigned)blocks, 256, 0, stream>>>(ids, R, E, counts);
+    moe_scan_kernel<<<1, 32, 0, stream>>>(counts, E, offsets, cursor, mtiles, nmt, (int)L.max_mt);
+    int64_t wblocks = (R * 32 + 255) / 256;
+    if (wblocks > (int64_t)num_sms() * 16) wblocks = (int64_t)num_sms() * 16;
+    if (x_dtype == SB_BF16)
+      moe_scatter_kernel<__nv_bfloat16, __nv_bfloat16><<<(unsigned)wblocks, 256, 0, stream>>>(
+          static_cast<const __nv_bfloat16*>(x), ids, weights, B, k, (int)H, E, offsets, cursor,
+          static_cast<__nv_bfloat16*>(xp), L.ldx, row_w, inv);
+    else
+      moe_scatter_kernel<float, __half><<<(unsigned)wblocks, 256, 0, stream>>>(
+          static_cast<const float*>(x), ids, weights, B, k, (int)H, E, offsets, cursor,
+          static_cast<__half*>(xp), L.ldx, row_w, inv);
+    SB_CUDA_TRY(cudaGetLastError());
+  }
+
+  // tensor maps: activations (SW128, 64 x 128 box) and packed weights (16 B x rows box)
+  CUtensorMap tmx, tmg, tmu, tmh, tmd;
+  const CUtensorMapDataType adt = fmt_gu ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int64_t KWh = ternary_row_words(H), KWi = ternary_row_words(I);
+  if ((rc = make_tmap_2d(&tmx, xp, adt, 2, L.R, H, L.ldx, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&tmg, gate, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, 4, 128,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+      (rc = make_tmap_2d(&tmu, up, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, 4, 128,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+      (rc = make_tmap_2d(&tmh, hp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.R, I, L.ldh, 64, 128,
+                         CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&tmd, down, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * H, KWi, KWi, 4, 256,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+
+  TernGemmParams pg{};
+  pg.mtiles = mtiles;
+  pg.num_mtiles = nmt;
+  pg.n_ntiles = (int)((I + 127) / 128);
+  pg.N = (int)I;
+  pg.K = (int)H;
+  pg.b_rows = (int)I;
+  pg.s0 = gs;
+  pg.s1 = us;
+  pg.out = hp;
+  pg.ldo = L.ldh;
+  if (fmt_gu)
+    rc = launch_tgemm<TG_GATEUP, 1>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream);
+  else
+    rc = launch_tgemm<TG_GATEUP, 0>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream);
+  if (rc) return rc;
+
+  TernGemmParams pd{};
+  pd.mtiles = mtiles;
+  pd.num_mtiles = nmt;
+  pd.n_ntiles = (int)((H + 255) / 256);
+  pd.N = (int)H;
+  pd.K = (int)I;
+  pd.b_rows = (int)H;
+  pd.s0 = ds;
+  pd.row_w = row_w;
+  pd.out = yp;
+  pd.ldo = H;
+  if ((rc = launch_tgemm<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, pd, stream))) return rc;
+
+  {
+    ProfScope prof("moe_combine", stream);
+    int64_t blocks = (B * H + 255) / 256;
+    if (blocks > (int64_t)num_sms() * 32) blocks = (int64_t)num_sms() * 32;
+    if (out_dtype == SB_F32)
+      moe_combine_kernel<float><<<(unsigned)blocks, 256, 0, stream>>>(yp, inv, B, k, (int)H, static_cast<float*>(out));
+    else
+      moe_combine_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, stream>>>(yp, inv, B, k, (int)H,
+                                                                               static_cast<__nv_bfloat16*>(out));
+    SB_CUDA_TRY(cudaGetLastError());
+  }
+  return SB_OK;
+}
+
+}  // namespace
+}  // namespace sb
+
+extern "C" size_t sb_ternary_moe_workspace_bytes(int64_t B, int64_t H, int64_t I, int32_t E, int32_t k) {
+  if (B < 0 || H <= 0 || I <= 0 || E <= 0 || k <= 0) return 0;
+  return sb::moe_layout(B, H, I, E, k).total;
+}
+
+extern "C" int sb_ternary_moe_swiglu(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I,
+                                     int32_t n_experts, int32_t top_k, const int32_t* ids,
+                                     const float* weights, const uint32_t* gate, const uint32_t* up,
+                                     const uint32_t* down, const float* gate_scale, const float* up_scale,
+                                     const float* down_scale, void* out, int out_dtype, void* workspace,
+                                     size_t workspace_bytes, void* stream) {
+  SB_REQUIRE(weights != nullptr || B == 0, "weights is null");
+  return sb::moe_forward(x, x_dtype, B, H, I, n_experts, top_k, ids, weights, gate, up, down, gate_scale,
+                         up_scale, down_scale, out, out_dtype, workspace, workspace_bytes,
+                         reinterpret_cast<cudaStream_t>(stream));
+}
+
+// Single expert = the grouped path with one expert and one slot per token;
+// the slot ids live at the end of the workspace.
 extern "C" size_t sb_ternary_gated_mlp_workspace_bytes(int64_t M, int64_t H, int64_t I) {
-  (void)M; (void)H; (void)I;
-  return 0;
+  if (M < 0 || H <= 0 || I <= 0) return 0;
+  return sb::moe_layout(M, H, I, 1, 1).total + sb::align_up(sizeof(int32_t) * (size_t)(M > 0 ? M : 1), 1024);
 }
-extern "C" int sb_ternary_gated_mlp(const void*, int, int64_t, int64_t, int64_t, const uint32_t*,
-                                    const uint32_t*, const uint32_t*, const float*, const float*,
-                                    const float*, float*, void*, size_t, void*) {
-  return sb::fail(SB_ERR_UNSUPPORTED, "sb_ternary_gated_mlp: not built yet");
+
+extern "C" int sb_ternary_gated_mlp(const void* x, int x_dtype, int64_t M, int64_t H, int64_t I,
+                                    const uint32_t* gate, const uint32_t* up, const uint32_t* down,
+                                    const float* gate_scale, const float* up_scale, const float* down_scale,
+                                    float* y, void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace sb;
+  int rc;
+  if ((rc = check_ternary_shapes(H, I))) return rc;
+  if (M == 0) return SB_OK;
+  const size_t need = sb_ternary_gated_mlp_workspace_bytes(M, H, I);
+  if (!workspace || workspace_bytes < need)
+    return fail(SB_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, need);
+  const size_t base = moe_layout(M, H, I, 1, 1).total;
+  int32_t* ids = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + base);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int64_t blocks = (M + 255) / 256;
+  if (blocks > 4096) blocks = 4096;
+  fill_i32_kernel<<<(unsigned)blocks, 256, 0, st>>>(ids, M, 0);
+  SB_CUDA_TRY(cudaGetLastError());
+  return moe_forward(x, x_dtype, M, H, I, 1, 1, ids, nullptr, gate, up, down, gate_scale, up_scale,
+                     down_scale, y, SB_F32, workspace, base, st);
 }
-extern "C" size_t sb_ternary_linear_workspace_bytes(int64_t, int64_t, int64_t) { return 0; }
-extern "C" int sb_ternary_linear(const void*, int, int64_t, int64_t, int64_t, const uint32_t*,
-                                 const float*, const float*, float*, void*, size_t, void*) {
-  return sb::fail(SB_ERR_UNSUPPORTED, "sb_ternary_linear: not built yet");
+
+// y = scale * (x @ T) + bias: the dispatch copies x into the activation layout
+// (one expert, identity rows), then one grouped GEMM with the linear epilogue.
+extern "C" size_t sb_ternary_linear_workspace_bytes(int64_t M, int64_t K, int64_t N) {
+  if (M < 0 || K <= 0 || N <= 0) return 0;
+  return sb::moe_layout(M, K, 64, 1, 1).total + sb::align_up(sizeof(int32_t) * (size_t)(M > 0 ? M : 1), 1024);
 }
-extern "C" size_t sb_ternary_moe_workspace_bytes(int64_t, int64_t, int64_t, int32_t, int32_t) {
-  return 0;
-}
-extern "C" int sb_ternary_moe_swiglu(const void*, int, int64_t, int64_t, int64_t, int32_t, int32_t,
-                                     const int32_t*, const float*, const uint32_t*,
-                                     const uint32_t*, const uint32_t*, const float*, const float*,
-                                     const float*, void*, int, void*, size_t, void*) {
-  return sb::fail(SB_ERR_UNSUPPORTED, "sb_ternary_moe_swiglu: not built yet");
+
+extern "C" int sb_ternary_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t N,
+                                 const uint32_t* w, const float* scale, const float* bias, float* y,
+                                 void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace sb;
+  SB_REQUIRE(K > 0 && N > 0, "shape must be positive");
+  SB_REQUIRE(x_dtype == SB_F32 || x_dtype == SB_BF16, "x dtype must be SB_F32 or SB_BF16");
+  if (M == 0) return SB_OK;
+  SB_REQUIRE(x && w && scale && y, "null pointer argument");
+  const size_t need = sb_ternary_linear_workspace_bytes(M, K, N);
+  if (!workspace || workspace_bytes < need)
+    return fail(SB_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, need);
+  SB_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 1023u) == 0, "workspace must be 1024-byte aligned");
+  const MoeLayout L = moe_layout(M, K, 64, 1, 1);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* counts = reinterpret_cast<int*>(ws + L.off_counts);
+  int* offsets = reinterpret_cast<int*>(ws + L.off_offsets);
+  int* cursor = reinterpret_cast<int*>(ws + L.off_cursor);
+  int* nmt = reinterpret_cast<int*>(ws + L.off_nmt);
+  MTile* mtiles = reinterpret_cast<MTile*>(ws + L.off_mtiles);
+  void* xp = ws + L.off_xp;
+  int32_t* ids = reinterpret_cast<int32_t*>(ws + L.total);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int fmt = (x_dtype == SB_BF16) ? 1 : 0;
+  // one expert holding every row in token order: the m-tile table comes from
+  // the histogram + scan of all-zero ids, and x is converted row for row
+  int64_t blocks = (M + 255) / 256;
+  if (blocks > 4096) blocks = 4096;
+  fill_i32_kernel<<<(unsigned)blocks, 256, 0, st>>>(ids, M, 0);
+  SB_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int), st));
+  moe_hist_kernel<<<(unsigned)blocks, 256, 0, st>>>(ids, M, 1, counts);
+  moe_scan_kernel<<<1, 32, 0, st>>>(counts, 1, offsets, cursor, mtiles, nmt, (int)L.max_mt);
+  {
+    int64_t cb = (M * K + 255) / 256;
+    if (cb > (int64_t)num_sms() * 32) cb = (int64_t)num_sms() * 32;
+    if (fmt)
+      rows_convert_kernel<__nv_bfloat16, __nv_bfloat16><<<(unsigned)cb, 256, 0, st>>>(
+          static_cast<const __nv_bfloat16*>(x), M, (int)K, static_cast<__nv_bfloat16*>(xp), L.ldx);
+    else
+      rows_convert_kernel<float, __half><<<(unsigned)cb, 256, 0, st>>>(static_cast<const float*>(x), M, (int)K,
+                                                                         static_cast<__half*>(xp), L.ldx);
+    SB_CUDA_TRY(cudaGetLastError());
+  }
+  CUtensorMap tmx, tmw;
+  int rc;
+  const int64_t KW = ternary_row_words(K);
+  if ((rc = make_tmap_2d(&tmx, xp, fmt ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, M,
+                         K, L.ldx, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&tmw, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)N, KW, KW, 4, 256,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  TernGemmParams pl{};
+  pl.mtiles = mtiles;
+  pl.num_mtiles = nmt;
+  pl.n_ntiles = (int)((N + 255) / 256);
+  pl.N = (int)N;
+  pl.K = (int)K;
+  pl.b_rows = (int)N;
+  pl.s0 = scale;
+  pl.bias = bias;
+  pl.out = y;
+  pl.ldo = N;
+  if (fmt) return launch_tgemm<TG_LINEAR, 1>("ternary_linear_tc", tmx, tmw, tmw, pl, st);
+  return launch_tgemm<TG_LINEAR, 0>("ternary_linear_tc", tmx, tmw, tmw, pl, st);
 }

@@ -1,0 +1,175 @@
+"""Torch-facing wrappers of the ternary C-ABI entry points.
+
+Weights live on the device in the B200 layout: uint32 [N, KW], KW =
+ceil(K/64)*4, one word per 16 consecutive K of an output row; element 2j of a
+word has its non-zero flag at bit j and its sign at bit 8+j, element 2j+1 at
+bits 16+j and 24+j.  ``pack_device`` builds it on the host from int8 ternary
+matrices in the PyTorch [out, in] layout; ``repack_reference`` converts the
+reference extension's packed layout (int32 [ceil(K/16), N],
+cuda/v5/ternary_torch_ext.cu:197-231) on the device.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional, Sequence
+
+import numpy as np
+import torch
+
+from . import _lib
+
+
+def row_words(K: int) -> int:
+    return (K + 63) // 64 * 4
+
+
+def pack_device(T: np.ndarray) -> np.ndarray:
+    """int8 ternary [N, K] ({-1,0,+1}) -> uint32 [N, ceil(K/64)*4] device layout."""
+    T = np.asarray(T)
+    N, K = T.shape
+    KW = row_words(K)
+    pad = np.zeros((N, KW * 16), np.int8)
+    pad[:, :K] = T
+    g = pad.reshape(N, KW, 8, 2)          # [n, word, pair j, element e]
+    nz = (g != 0).astype(np.uint32)
+    sg = (g < 0).astype(np.uint32)
+    j = np.arange(8, dtype=np.uint32)[None, None, :]
+    w = ((nz[..., 0] << j) | (sg[..., 0] << (8 + j)) |
+         (nz[..., 1] << (16 + j)) | (sg[..., 1] << (24 + j)))
+    return np.bitwise_or.reduce(w, axis=2).astype(np.uint32)
+
+
+def _stream(dev) -> C.c_void_p:
+    return C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+
+def _ws(nbytes: int, device) -> tuple:
+    buf = torch.empty(nbytes + 1024, dtype=torch.uint8, device=device)
+    base = buf.data_ptr()
+    aligned = (base + 1023) // 1024 * 1024
+    return buf, aligned, buf.numel() - (aligned - base)
+
+
+def repack_reference(packed: torch.Tensor, K: int) -> torch.Tensor:
+    """Reference-layout packed int32 [ceil(K/16), N] (CUDA) -> device layout (CUDA)."""
+    lib = _lib.load()
+    if not packed.is_cuda:
+        raise RuntimeError("packed weights must be a CUDA tensor")
+    packed = packed.contiguous()
+    N = packed.shape[1]
+    out = torch.empty(N, row_words(K), dtype=torch.int32, device=packed.device)
+    with torch.cuda.device(packed.device):
+        _lib.check(lib.sb_ternary_repack(C.c_void_p(packed.data_ptr()), K, N, C.c_void_p(out.data_ptr()),
+                                         _stream(packed.device)), "sb_ternary_repack")
+    return out
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.float32:
+        return _lib.SB_F32
+    if t.dtype == torch.bfloat16:
+        return _lib.SB_BF16
+    raise RuntimeError(f"activation dtype {t.dtype} must be float32 or bfloat16")
+
+
+def gated_mlp(x: torch.Tensor, gate: torch.Tensor, up: torch.Tensor, down: torch.Tensor,
+              gate_scale: torch.Tensor, up_scale: torch.Tensor, down_scale: torch.Tensor,
+              hidden: int, inter: int) -> torch.Tensor:
+    """One expert: y fp32 [M, H]; weights already in the device layout."""
+    lib = _lib.load()
+    M = x.shape[0]
+    y = torch.empty(M, hidden, dtype=torch.float32, device=x.device)
+    need = int(lib.sb_ternary_gated_mlp_workspace_bytes(M, hidden, inter))
+    buf, ws, wsb = _ws(need, x.device)
+    with torch.cuda.device(x.device):
+        rc = lib.sb_ternary_gated_mlp(
+            C.c_void_p(x.data_ptr()), _dtype_code(x), M, hidden, inter,
+            C.c_void_p(gate.data_ptr()), C.c_void_p(up.data_ptr()), C.c_void_p(down.data_ptr()),
+            C.c_void_p(gate_scale.data_ptr()), C.c_void_p(up_scale.data_ptr()),
+            C.c_void_p(down_scale.data_ptr()), C.c_void_p(y.data_ptr()), C.c_void_p(ws), wsb,
+            _stream(x.device))
+    _lib.check(rc, "sb_ternary_gated_mlp")
+    return y
+
+
+def linear(x: torch.Tensor, w: torch.Tensor, scale: torch.Tensor, bias: Optional[torch.Tensor],
+           K: int, N: int) -> torch.Tensor:
+    lib = _lib.load()
+    M = x.shape[0]
+    y = torch.empty(M, N, dtype=torch.float32, device=x.device)
+    need = int(lib.sb_ternary_linear_workspace_bytes(M, K, N))
+    buf, ws, wsb = _ws(need, x.device)
+    with torch.cuda.device(x.device):
+        rc = lib.sb_ternary_linear(C.c_void_p(x.data_ptr()), _dtype_code(x), M, K, N,
+                                   C.c_void_p(w.data_ptr()), C.c_void_p(scale.data_ptr()),
+                                   C.c_void_p(bias.data_ptr()) if bias is not None else None,
+                                   C.c_void_p(y.data_ptr()), C.c_void_p(ws), wsb, _stream(x.device))
+    _lib.check(rc, "sb_ternary_linear")
+    return y
+
+
+class TernaryExperts:
+    """E ternary SwiGLU experts resident on one device, in the B200 layout.
+
+    ``experts`` is a sequence of containers with the reference fields
+    (python/real_model_demo.py:85-98): gate_ternary [I,H], up_ternary [I,H],
+    down_ternary [H,I] (values in {-1,0,+1}) and gate_scale [I], up_scale [I],
+    down_scale [H]; dicts or attribute objects both work.
+    """
+
+    def __init__(self, experts: Sequence, device):
+        def get(e, k):
+            return e[k] if isinstance(e, dict) else getattr(e, k)
+
+        self.device = torch.device(device)
+        self.E = len(experts)
+        g0 = np.asarray(get(experts[0], "gate_ternary"))
+        self.I, self.H = g0.shape
+        gate = np.concatenate([pack_device(np.asarray(get(e, "gate_ternary"), np.int8)) for e in experts])
+        up = np.concatenate([pack_device(np.asarray(get(e, "up_ternary"), np.int8)) for e in experts])
+        down = np.concatenate([pack_device(np.asarray(get(e, "down_ternary"), np.int8)) for e in experts])
+        to = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(self.device)
+        self.gate = to(gate.view(np.int32))
+        self.up = to(up.view(np.int32))
+        self.down = to(down.view(np.int32))
+        self.gate_scale = to(np.stack([np.asarray(get(e, "gate_scale"), np.float32) for e in experts]))
+        self.up_scale = to(np.stack([np.asarray(get(e, "up_scale"), np.float32) for e in experts]))
+        self.down_scale = to(np.stack([np.asarray(get(e, "down_scale"), np.float32) for e in experts]))
+        self._ws = None
+
+    def memory_bytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in (self.gate, self.up, self.down, self.gate_scale,
+                                                            self.up_scale, self.down_scale))
+
+    def workspace_bytes(self, B: int, k: int) -> int:
+        return int(_lib.load().sb_ternary_moe_workspace_bytes(B, self.H, self.I, self.E, k))
+
+    def forward(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
+                out_dtype=torch.float32, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """out[t] = sum_j weights[t,j] * expert_{ids[t,j]}(x[t])."""
+        lib = _lib.load()
+        if not x.is_cuda:
+            raise RuntimeError("activations must be CUDA tensors (there is no CPU path)")
+        x = x.contiguous()
+        ids = ids.to(torch.int32).contiguous()
+        weights = weights.to(torch.float32).contiguous()
+        B, k = ids.shape
+        if out is None:
+            out = torch.empty(B, self.H, dtype=out_dtype, device=x.device)
+        need = self.workspace_bytes(B, k)
+        if self._ws is None or self._ws[0].numel() < need + 1024:
+            self._ws = _ws(need, x.device)
+        buf, ws, wsb = self._ws
+        with torch.cuda.device(x.device):
+            rc = lib.sb_ternary_moe_swiglu(
+                C.c_void_p(x.data_ptr()), _dtype_code(x), B, self.H, self.I, self.E, k,
+                C.c_void_p(ids.data_ptr()), C.c_void_p(weights.data_ptr()),
+                C.c_void_p(self.gate.data_ptr()), C.c_void_p(self.up.data_ptr()),
+                C.c_void_p(self.down.data_ptr()), C.c_void_p(self.gate_scale.data_ptr()),
+                C.c_void_p(self.up_scale.data_ptr()), C.c_void_p(self.down_scale.data_ptr()),
+                C.c_void_p(out.data_ptr()),
+                _lib.SB_BF16 if out.dtype == torch.bfloat16 else _lib.SB_F32,
+                C.c_void_p(ws), wsb, _stream(x.device))
+        _lib.check(rc, "sb_ternary_moe_swiglu")
+        return out

@@ -55,3 +55,15 @@ def topk_ids_match(ref_probs: np.ndarray, ref_ids: np.ndarray, got_ids: np.ndarr
     same = ref_ids == got_ids
     close = np.abs(pr - pg) <= tol * np.maximum(np.abs(pr), np.abs(pg))
     return int((~same & ~(close & valid)).sum())
+
+
+def ternary_errors(got, ref):
+    """(row-normwise relative error max, elementwise error relative to |ref| + row rms max)."""
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    diff = got - ref
+    rn = np.sqrt((ref * ref).sum(axis=1)) + 1e-30
+    norm = np.sqrt((diff * diff).sum(axis=1)) / rn
+    rms = rn / np.sqrt(ref.shape[1])
+    elem = np.abs(diff) / (np.abs(ref) + rms[:, None])
+    return float(norm.max()), float(elem.max())

@@ -1,0 +1,69 @@
+"""Ternary packing: host packer against the reference extension, device layout round trip (no GPU)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+
+
+def decode_device(words: np.ndarray, K: int) -> np.ndarray:
+    """Inverse of the split-plane device layout (test-side restatement)."""
+    w = np.asarray(words).view(np.uint32)
+    N, KW = w.shape
+    j = np.arange(8, dtype=np.uint32)
+    out = np.zeros((N, KW, 8, 2), np.int8)
+    for e in range(2):
+        nz = (w[:, :, None] >> (16 * e + j)) & 1
+        sg = (w[:, :, None] >> (16 * e + 8 + j)) & 1
+        out[..., e] = (nz.astype(np.int8) * (1 - 2 * sg.astype(np.int8)))
+    return out.reshape(N, KW * 16)[:, :K]
+
+
+def test_pack_ternary_matches_reference_extension():
+    import ternary_expert_ext as ext
+    g = load_golden("ternary_small")
+    if "pack/in" not in g:
+        pytest.skip("golden made without the reference extension")
+    got = ext.pack_ternary(torch.from_numpy(g["pack/in"]))
+    assert got.dtype == torch.int32
+    assert np.array_equal(got.numpy(), g["pack/out"])
+
+
+def test_pack_ternary_rejects_non_cpu_int8():
+    import ternary_expert_ext as ext
+    with pytest.raises(RuntimeError):
+        ext.pack_ternary(torch.zeros(4, 4, dtype=torch.float32))
+
+
+@pytest.mark.parametrize("shape", [(7, 5), (128, 64), (40, 72), (256, 2048), (3, 1)])
+def test_device_layout_round_trip(shape):
+    from sb200.ternary import pack_device, row_words
+    rng = np.random.default_rng(shape[0] * 1000 + shape[1])
+    T = rng.integers(-1, 2, size=shape, dtype=np.int8)
+    w = pack_device(T)
+    assert w.shape == (shape[0], row_words(shape[1])) and w.dtype == np.uint32
+    assert np.array_equal(decode_device(w, shape[1]), T)
+
+
+def test_device_layout_pair_expansion_formula():
+    """Two elements per word expand to 16-bit +-1/0 with and/mul/shift (bf16 and fp16)."""
+    from sb200.ternary import pack_device
+    rng = np.random.default_rng(5)
+    T = rng.integers(-1, 2, size=(1, 16), dtype=np.int8)
+    w = int(pack_device(T)[0, 0])
+    for fmt, (mul, top) in {"bf16": (0x7F, 7), "f16": (0xF, 10)}.items():
+        for j in range(8):
+            nz = w & (0x00010001 << j)
+            sg = w & (0x01000100 << j)
+            v = ((nz * (mul << (top - j))) | (sg << (7 - j))) & 0xFFFFFFFF
+            for e in range(2):
+                half = (v >> (16 * e)) & 0xFFFF
+                dt = np.float16 if fmt == "f16" else None
+                if fmt == "f16":
+                    val = float(np.array([half], np.uint16).view(np.float16)[0])
+                else:
+                    val = float(np.array([half << 16], np.uint32).view(np.float32)[0])
+                assert val == T[0, 2 * j + e]

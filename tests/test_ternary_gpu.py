@@ -1,0 +1,181 @@
+"""Ternary SwiGLU kernels against the CPU oracle (needs a B200).
+
+Contract: outputs after the fp32 scales within 1e-3 relative — held here
+row-normwise (||y - y_ref|| / ||y_ref|| <= 1e-3 per token); the elementwise
+error relative to |y_ref| + rms(row) is bounded too.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import load_golden
+from oracle import ternary as otern
+from parity import ternary_errors
+
+pytestmark = pytest.mark.gpu
+
+NORM_TOL = 1e-3
+ELEM_TOL = 5e-3
+
+
+def experts_from_golden(g, prefix, n):
+    keys = ("gate_ternary", "up_ternary", "down_ternary", "gate_scale", "up_scale", "down_scale")
+    return [{k: g[f"{prefix}{e}/{k}"] for k in keys} for e in range(n)]
+
+
+def assert_close(got, ref, what):
+    norm, elem = ternary_errors(got, ref)
+    print(f"{what}: normwise {norm:.3e} elementwise {elem:.3e}")
+    assert norm <= NORM_TOL, f"{what}: normwise {norm}"
+    assert elem <= ELEM_TOL, f"{what}: elementwise {elem}"
+
+
+def test_repack_matches_host_layout(cuda_device):
+    from sb200.ternary import pack_device, repack_reference
+    rng = np.random.default_rng(1)
+    for K, N in [(72, 40), (2048, 1024), (1024, 2048), (37, 29)]:
+        T = rng.integers(-1, 2, size=(N, K), dtype=np.int8)     # [out, in]
+        ref_packed = torch.from_numpy(otern.pack_ternary(T.T.copy())).to(cuda_device)
+        dev = repack_reference(ref_packed, K).cpu().numpy().view(np.uint32)
+        assert np.array_equal(dev, pack_device(T))
+
+
+@pytest.mark.parametrize("xdtype", [torch.float32, torch.bfloat16])
+def test_gated_mlp_matches_reference_golden(cuda_device, xdtype):
+    """Reference API ternary_gated_mlp on the golden expert (H=72, I=40: ragged K and N)."""
+    import ternary_expert_ext as ext
+    g = load_golden("ternary_small")
+    gp = torch.from_numpy(otern.pack_ternary(g["e/gate_ternary"].T.copy())).to(cuda_device)
+    up = torch.from_numpy(otern.pack_ternary(g["e/up_ternary"].T.copy())).to(cuda_device)
+    dp = torch.from_numpy(otern.pack_ternary(g["e/down_ternary"].T.copy())).to(cuda_device)
+    s = [torch.from_numpy(g[f"e/{n}_scale"]).to(cuda_device) for n in ("gate", "up", "down")]
+    x = torch.from_numpy(g["e/x"]).to(xdtype).to(cuda_device)
+    y = ext.ternary_gated_mlp(x, gp, up, dp, *s)
+    assert y.dtype == torch.float32 and y.shape == (24, 72)
+    ref = otern.gated_mlp(x.float().cpu().numpy(), g["e/gate_ternary"], g["e/up_ternary"],
+                          g["e/down_ternary"], g["e/gate_scale"], g["e/up_scale"], g["e/down_scale"])
+    assert_close(y.cpu().numpy(), ref, "golden expert")
+    if xdtype == torch.float32:   # the reference's own output (torch fallback math)
+        assert_close(y.cpu().numpy(), g["e/y"], "golden expert vs reference")
+
+
+@pytest.mark.parametrize("M", [1, 3, 130, 512])
+def test_gated_mlp_olmoe_shape(cuda_device, M):
+    from sb200 import synth
+    import ternary_expert_ext as ext
+    ex = synth.ternary_experts(1, 2048, 1024, seed=21)[0]
+    gp = torch.from_numpy(otern.pack_ternary(ex["gate_ternary"].T.copy())).to(cuda_device)
+    up = torch.from_numpy(otern.pack_ternary(ex["up_ternary"].T.copy())).to(cuda_device)
+    dp = torch.from_numpy(otern.pack_ternary(ex["down_ternary"].T.copy())).to(cuda_device)
+    s = [torch.from_numpy(ex[f"{n}_scale"]).to(cuda_device) for n in ("gate", "up", "down")]
+    x = synth.hidden_states(M, 2048, seed=22, dtype=torch.bfloat16, device=cuda_device)
+    y = ext.ternary_gated_mlp(x, gp, up, dp, *s)
+    ref = otern.gated_mlp(x.float().cpu().numpy(), ex["gate_ternary"], ex["up_ternary"],
+                          ex["down_ternary"], ex["gate_scale"], ex["up_scale"], ex["down_scale"])
+    assert_close(y.cpu().numpy(), ref, f"expert M={M}")
+
+
+def test_ternary_linear(cuda_device):
+    import ternary_expert_ext as ext
+    rng = np.random.default_rng(3)
+    for K, N, M in [(72, 40, 5), (2048, 1024, 300), (1000, 300, 129)]:
+        T = rng.integers(-1, 2, size=(K, N), dtype=np.int8)   # reference packs [in, out]
+        packed = torch.from_numpy(otern.pack_ternary(T)).to(cuda_device)
+        scale = torch.from_numpy(rng.uniform(0.01, 0.1, N).astype(np.float32)).to(cuda_device)
+        bias = torch.from_numpy(rng.standard_normal(N).astype(np.float32)).to(cuda_device)
+        x = torch.from_numpy(rng.standard_normal((M, K)).astype(np.float32)).to(cuda_device)
+        y = ext.ternary_linear(x, packed, scale, bias)
+        ref = otern.ternary_linear(x.cpu().numpy(), otern.pack_ternary(T), scale.cpu().numpy(),
+                                   bias.cpu().numpy())
+        assert_close(y.cpu().numpy(), ref, f"linear {K}x{N}")
+
+
+def test_moe_combine_golden(cuda_device):
+    """Grouped MoE SwiGLU against the reference OLMoE forward_topk golden (6 experts, top-3)."""
+    from sb200.ternary import TernaryExperts
+    g = load_golden("ternary_small")
+    experts = experts_from_golden(g, "moe/", 6)
+    te = TernaryExperts(experts, cuda_device)
+    x = torch.from_numpy(g["moe/x"]).to(cuda_device)
+    ids = torch.from_numpy(g["moe/ids"]).to(cuda_device)
+    w = torch.from_numpy(g["moe/probs"]).to(cuda_device)
+    y = te.forward(x, ids, w)
+    assert_close(y.cpu().numpy(), g["moe/y"], "moe golden vs reference")
+    ref = otern.moe_combine(g["moe/x"], g["moe/ids"], g["moe/probs"], experts)
+    assert_close(y.cpu().numpy(), ref, "moe golden vs oracle")
+
+
+def test_moe_config2_sampled(cuda_device):
+    """Config 2: 64 experts, 2048->1024->2048, 4096 tokens x top-8 with Zipf(1.1) loads."""
+    from sb200 import synth
+    from sb200.ternary import TernaryExperts
+    E, H, I, B, k = 64, 2048, 1024, 4096, 8
+    experts = synth.ternary_experts(E, H, I, seed=2)
+    te = TernaryExperts(experts, cuda_device)
+    x = synth.hidden_states(B, H, seed=2, dtype=torch.bfloat16, device=cuda_device)
+    ids_np, w_np = synth.zipf_routing(B, E, k, seed=2)
+    ids = torch.from_numpy(ids_np).to(cuda_device)
+    w = torch.from_numpy(w_np).to(cuda_device)
+    y = te.forward(x, ids, w)
+    y2 = te.forward(x, ids, w)
+    assert torch.equal(y, y2), "not reproducible"
+    rows = np.linspace(0, B - 1, 96).astype(np.int64)
+    ref = otern.moe_combine(x[rows].float().cpu().numpy(), ids_np[rows], w_np[rows], experts)
+    assert_close(y.cpu().numpy()[rows], ref, "config-2 sampled rows")
+    # bf16 output path
+    yb = te.forward(x, ids, w, out_dtype=torch.bfloat16)
+    torch.testing.assert_close(yb.float(), y, rtol=8e-3, atol=1e-5)
+
+
+def test_moe_edge_cases(cuda_device):
+    """Experts with no tokens, one token, duplicate ids in a row, B not a tile multiple."""
+    from sb200 import synth
+    from sb200.ternary import TernaryExperts
+    E, H, I = 5, 256, 128
+    experts = synth.ternary_experts(E, H, I, seed=9)
+    te = TernaryExperts(experts, cuda_device)
+    B, k = 131, 2
+    x = synth.hidden_states(B, H, seed=10, device=cuda_device)
+    ids = torch.zeros(B, k, dtype=torch.int32)
+    ids[:, 1] = 3
+    ids[0, 0] = 1        # expert 1: one token; experts 2 and 4: none
+    ids[1, 1] = 0        # duplicate expert in one row
+    w = torch.rand(B, k)
+    y = te.forward(x, ids.to(cuda_device), w.to(cuda_device))
+    ref = otern.moe_combine(x.cpu().numpy(), ids.numpy(), w.numpy(), experts)
+    assert_close(y.cpu().numpy(), ref, "edge cases")
+    empty = te.forward(x[:0], ids[:0].to(cuda_device), w[:0].to(cuda_device))
+    assert empty.shape == (0, H)
+
+
+def test_bridge_module(cuda_device):
+    """CUDATernaryExpertModule: reference module API and buffers."""
+    from dataclasses import dataclass
+    import ternary_expert_ext_bridge as bridge
+    from sb200 import synth
+    assert bridge.HAS_TERNARY_EXT
+    ex = synth.ternary_experts(1, 256, 512, seed=4)[0]
+
+    @dataclass
+    class FakeExpert:
+        expert_id: int
+        gate_ternary: np.ndarray
+        up_ternary: np.ndarray
+        down_ternary: np.ndarray
+        gate_scale: np.ndarray
+        up_scale: np.ndarray
+        down_scale: np.ndarray
+
+    fe = FakeExpert(0, ex["gate_ternary"].astype(np.float32), ex["up_ternary"].astype(np.float32),
+                    ex["down_ternary"].astype(np.float32), ex["gate_scale"], ex["up_scale"], ex["down_scale"])
+    m = bridge.create_expert_module(fe).cuda()
+    x = torch.randn(2, 8, 256, device=cuda_device)
+    out = m(x)
+    assert out.shape == (2, 8, 256)
+    ref = otern.gated_mlp(x.reshape(16, 256).cpu().numpy(), ex["gate_ternary"], ex["up_ternary"],
+                          ex["down_ternary"], ex["gate_scale"], ex["up_scale"], ex["down_scale"])
+    assert_close(out.reshape(16, 256).cpu().numpy(), ref, "bridge module")
+    assert m.memory_bytes() == (16 * 512 + 16 * 512 + 32 * 256) * 4 + (512 + 512 + 256) * 4
