@@ -19,6 +19,7 @@ to fp16 before the down projection.
 
 from __future__ import annotations
 
+import weakref
 from typing import Optional
 
 import torch
@@ -26,18 +27,18 @@ import torch
 from sb200 import _lib
 from sb200 import ternary as _t
 
-_cache = {}
+# repacked weights per packed tensor object (weak keys: an entry dies with its
+# tensor, so a later tensor at the same address never sees a stale layout)
+_cache: "weakref.WeakKeyDictionary[torch.Tensor, tuple]" = weakref.WeakKeyDictionary()
 
 
 def _device_layout(packed: torch.Tensor, K: int) -> torch.Tensor:
-    key = (packed.data_ptr(), tuple(packed.shape), packed._version, K, packed.device)
-    hit = _cache.get(key)
-    if hit is not None:
-        return hit
-    if len(_cache) > 256:
-        _cache.clear()
-    out = _t.repack_reference(packed, K)
-    _cache[key] = out
+    stamp = (packed.data_ptr(), tuple(packed.shape), packed._version, K, packed.device)
+    hit = _cache.get(packed)
+    if hit is not None and hit[0] == stamp:
+        return hit[1]
+    out = _t.repack_reference(packed.contiguous(), K)
+    _cache[packed] = (stamp, out)
     return out
 
 
@@ -83,8 +84,8 @@ def ternary_gated_mlp(input: torch.Tensor, gate_packed: torch.Tensor, up_packed:
     out_dim = down_packed.shape[1]
     if out_dim != H:
         raise RuntimeError(f"down projection out_dim {out_dim} must equal in_dim {H}")
-    g = _device_layout(gate_packed.contiguous(), H)
-    u = _device_layout(up_packed.contiguous(), H)
-    d = _device_layout(down_packed.contiguous(), I)
+    g = _device_layout(gate_packed, H)
+    u = _device_layout(up_packed, H)
+    d = _device_layout(down_packed, I)
     return _t.gated_mlp(input, g, u, d, gate_scale.float().contiguous(), up_scale.float().contiguous(),
                         down_scale.float().contiguous(), H, I)
