@@ -4,18 +4,26 @@
                     [--workload router|moe_layer] [--batch B]
 
 Workloads (seeded synthetic inputs with BASELINE.json's shapes; no datasets):
-  router     BVH router forward, hidden 2048, spectral 256, 4x4x4 = 64 experts,
-             top-8 + softmax, bf16 unit-RMS tokens (config 1; default B = 262144).
-             A step routes B tokens resident in HBM (1 GiB > L2, no flush needed).
+  moe_layer  (default, the headline) one OLMoE-shaped MoE layer: BVH router
+             (hidden 2048, spectral 256, 4x4x4 = 64 experts, top-8, soft
+             level selection so the top-8 is not degenerate) followed by the
+             grouped ternary SwiGLU (64 experts, 2048 -> 1024 -> 2048, 2-bit
+             weights) over 4096 bf16 tokens per GPU (config 2).  L2 is flushed
+             (256 MiB write) before every timed step; each step is timed with
+             its own CUDA event pair and the flush stays outside them.
+  router     BVH router forward alone at B = 262144 bf16 tokens (config 1);
+             1 GiB of input per GPU > L2, so no flush.  Reported inside the
+             moe_layer line as "router".
 
 One process per GPU (torchrun for N > 1).  Router work shards by token with no
-collective: every rank routes its own B tokens (weak scaling).  Timing: W
-warm-up steps, then exactly K steps between CUDA events on the launching
-stream, bracketed by barrier + synchronize, max over ranks.
+collective; every rank runs its own token shard (weak scaling).  Timing: W
+warm-up steps, then exactly K timed steps on the launching stream, bracketed
+by barrier + synchronize, max over ranks.
 
 --impl reference times the reference's CPU path on the host cores: the
-restated oracle (oracle/, a numpy port of python/bvh_router.py) on a bounded
-sample per step, rank 0 only.
+restated oracle (oracle/: numpy ports of python/bvh_router.py and of the
+TernaryExpertModule fp32 fallback, python/real_model_demo.py:360-403) on a
+bounded token sample per step, rank 0 only.
 """
 
 from __future__ import annotations
@@ -34,6 +42,7 @@ sys.path.insert(0, str(REPO / "spectral-ai_b200"))
 sys.path.insert(0, str(REPO))
 
 H, S, BRANCHING, TOPK = 2048, 256, (4, 4, 4), 8
+E_EXPERTS, I_INTER = 64, 1024
 ROUTER_FLOP_PER_TOKEN = 2 * (H * H + H * S + 3 * H + S * 84)   # 9,492,480 (hard mode evaluates 3 refraction rows)
 ROUTER_BYTES_PER_TOKEN = 2 * H + TOPK * 8                       # bf16 in + ids/weights out
 
@@ -217,10 +226,56 @@ def router_workload(batch: int, device):
     return step, e2e_step, meta
 
 
-def time_steps(step, steps, warmup, world, sampler=None, profile=False):
+def moe_workload(batch: int, device, select: str = "soft"):
+    import numpy as np
+    import torch
+    from bvh_router import BVHRouter, RouterConfig
+    from sb200 import synth
+    from sb200.moe import BVHMoELayer
+    from sb200.ternary import TernaryExperts
+    w = synth.router_weights(H, S, BRANCHING, seed=0)
+    r = BVHRouter(RouterConfig(embed_dim=H, spectral_dim=S))
+    r.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in w.items()})
+    r = r.to(device).eval()
+    experts = TernaryExperts(synth.ternary_experts(E_EXPERTS, H, I_INTER, seed=2), device)
+    layer = BVHMoELayer(r, experts, top_k=TOPK, select=select)
+    x = synth.hidden_states(batch, H, seed=2, dtype=torch.bfloat16, device=device)
+    out = torch.empty(batch, H, dtype=torch.bfloat16, device=device)
+    ids, _ = layer.route(x)
+    counts = torch.bincount(ids.long().flatten(), minlength=E_EXPERTS).float()
+
+    def step():
+        layer.forward(x, out=out)
+
+    x_host = x.cpu().pin_memory()
+    out_host = torch.empty(batch, H, dtype=torch.bfloat16).pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        y = layer(x_dev)
+        out_host.copy_(y, non_blocking=True)
+
+    pairs = batch * TOPK
+    meta = {"tokens_per_step": batch, "h2d": batch * H * 2, "d2h": batch * H * 2,
+            "dominant": "ternary_gateup_tc", "dominant_flop": 2.0 * pairs * H * 2 * I_INTER,
+            "config": {"workload": "moe_layer_bvh_route_ternary_swiglu", "hidden": H,
+                       "intermediate": I_INTER, "experts": E_EXPERTS, "top_k": TOPK,
+                       "tokens_per_gpu": batch, "router_select": select,
+                       "expert_load_max_over_mean": round(float(counts.max() / counts.mean()), 3),
+                       "experts_with_tokens": int((counts > 0).sum()),
+                       "precision": "router bf16 tcgen05 + fp32 descent; ternary bf16 x {-1,0,1} "
+                                    "tcgen05, fp16 hidden, fp32 accumulate; bf16 out",
+                       "l2": "flushed (256 MiB write) before every timed step, outside the events"}}
+    return step, e2e_step, meta
+
+
+def time_steps(step, steps, warmup, world, sampler=None, profile=False, flush=None):
     import torch
     from sb200 import _lib
     for _ in range(warmup):
+        if flush is not None:
+            flush()
         step()
     torch.cuda.synchronize()
     barrier(world)
@@ -228,76 +283,138 @@ def time_steps(step, steps, warmup, world, sampler=None, profile=False):
     if profile:
         _lib.profile_enable(True)
     s = torch.cuda.current_stream()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if sampler:
         sampler.mark(True)
-    e0.record(s)
-    for _ in range(steps):
-        step()
-    e1.record(s)
-    torch.cuda.synchronize()
+    if flush is None:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        for _ in range(steps):
+            step()
+        e1.record(s)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1)
+    else:
+        ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in range(steps)]
+        for a, b in ev:
+            flush()
+            a.record(s)
+            step()
+            b.record(s)
+        torch.cuda.synchronize()
+        ms = sum(a.elapsed_time(b) for a, b in ev)
     if sampler:
         sampler.mark(False)
     barrier(world)
-    ms = e0.elapsed_time(e1)
     prof = _lib.profile_read() if profile else {}
     if profile:
         _lib.profile_enable(False)
     return max_over_ranks(ms, world), prof
 
 
+def roofline_tensor(meta, prof, pk, steps_ms, steps):
+    dom = prof.get(meta["dominant"], (0, 0.0))
+    if not dom[0]:
+        return None
+    avg_s = dom[1] / dom[0] / 1e3
+    achieved = meta["dominant_flop"] / avg_s / 1e12
+    return {"kernel": meta["dominant"], "bound": "tensor", "achieved": round(achieved, 1),
+            "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4),
+            "peak_source": f"{pk['source']} bf16 burst (cuBLAS)",
+            "traffic": traffic_for(meta), "avg_launch_ms": round(dom[1] / dom[0], 4),
+            "algorithmic_flop_per_launch": meta["dominant_flop"]}
+
+
 def run_ours(a):
     import torch
     rank, world, local = dist_setup(a.gpus)
     dev = torch.device("cuda", torch.cuda.current_device())
-    batch = a.batch or 262144
-    step, e2e_step, meta = router_workload(batch, dev)
-    sampler = ClockSampler(local) if rank == 0 or True else None
+    pk = peaks()
+    sampler = ClockSampler(local)
     sampler.start()
-    total_ms, prof = time_steps(step, a.steps, a.warmup, world, sampler, profile=True)
+    # ---- headline: the MoE layer
+    batch = a.batch or 4096
+    flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush = lambda: flush_buf.fill_(1)
+    step, e2e_step, meta = moe_workload(batch, dev)
+    total_ms, prof = time_steps(step, a.steps, a.warmup, world, sampler, profile=True, flush=flush)
     clocks = sampler.stop()
-    e2e_ms, _ = time_steps(e2e_step, a.steps, a.warmup, world)
+    e2e_ms, _ = time_steps(e2e_step, a.steps, a.warmup, world, flush=flush)
     tokens = meta["tokens_per_step"] * a.steps * world
     value = tokens / (total_ms / 1e3)
     e2e_value = tokens / (e2e_ms / 1e3)
-    pk = peaks()
-    dom = prof.get(meta["dominant"], (0, 0.0))
     launches = sum(n for n, _ in prof.values())
-    roof = None
-    if dom[0]:
-        avg_s = dom[1] / dom[0] / 1e3
-        achieved = meta["dominant_flop"] / avg_s / 1e12
-        roof = {"kernel": meta["dominant"], "bound": "tensor", "achieved": round(achieved, 1),
-                "peak": pk["bf16_tflops"], "unit": "TFLOP/s",
-                "frac": round(achieved / pk["bf16_tflops"], 4),
-                "peak_source": f"{pk['source']} bf16 burst (cuBLAS)",
-                "traffic": traffic_for(meta),
-                "avg_launch_ms": round(dom[1] / dom[0], 4),
-                "hbm_frac_of_step": round(meta["tokens_per_step"] * ROUTER_BYTES_PER_TOKEN /
-                                          (total_ms / a.steps / 1e3) / 1e9 / pk["hbm_gbs"], 4)}
-    out = {"metric": "router Mq/s (BVH route, top-8) — MoE layer pending",
-           "value": round(value / 1e6, 3), "unit": "Mq/s", "n_gpus": world, "steps": a.steps,
+    out = {"metric": "MoE-layer tokens/s (BVH route + ternary SwiGLU)",
+           "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
            "warmup": a.warmup, "ms_per_step": round(total_ms / a.steps, 4),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-           "data": "synthetic (seeded unit-RMS Gaussian tokens, random-init router)",
-           "config": dict(meta["config"], parallelism=f"token-shard x{world}, no collective"),
-           "e2e": {"value": round(e2e_value / 1e6, 3), "unit": "Mq/s",
+           "data": "synthetic (seeded unit-RMS Gaussian tokens, random-init router and ternary experts)",
+           "config": dict(meta["config"], parallelism=f"token-shard x{world}, experts replicated, no collective"),
+           "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                    "h2d_bytes_per_step": meta["h2d"], "d2h_bytes_per_step": meta["d2h"],
-                   "api": "bvh_router.BVHRouter.forward_topk"},
+                   "api": "sb200.moe.BVHMoELayer.__call__ (BVHRouter.forward_topk + TernaryExperts)"},
            "gpu_launches": launches,
-           "kernels": {k: {"launches": n, "avg_ms": round(t / max(n, 1), 4)} for k, (n, t) in prof.items()},
-           "roofline": roof, "clocks": clocks}
+           "kernels": {k: {"launches": n, "avg_ms": round(t / max(n, 1), 4),
+                           "share": round(t / max(sum(v[1] for v in prof.values()), 1e-9), 4)}
+                       for k, (n, t) in prof.items()},
+           "roofline": roofline_tensor(meta, prof, pk, total_ms, a.steps), "clocks": clocks}
+    # ---- router alone (config 1), same process
+    if not a.skip_router:
+        rstep, _, rmeta = router_workload(a.router_batch, dev)
+        r_ms, rprof = time_steps(rstep, a.router_steps, a.warmup, world, profile=True)
+        rtok = rmeta["tokens_per_step"] * a.router_steps * world
+        out["router"] = {"metric": "router Mq/s", "value": round(rtok / (r_ms / 1e3) / 1e6, 3),
+                         "unit": "Mq/s", "batch_per_gpu": a.router_batch,
+                         "ms_per_step": round(r_ms / a.router_steps, 4),
+                         "hbm_frac": round(rmeta["tokens_per_step"] * ROUTER_BYTES_PER_TOKEN /
+                                           (r_ms / a.router_steps / 1e3) / 1e9 / pk["hbm_gbs"], 4),
+                         "tensor_frac_of_step": round(rmeta["tokens_per_step"] * ROUTER_FLOP_PER_TOKEN /
+                                                      (r_ms / a.router_steps / 1e3) / 1e12 /
+                                                      pk["bf16_tflops"], 4),
+                         "kernels": {k: {"launches": n, "avg_ms": round(t / max(n, 1), 4)}
+                                     for k, (n, t) in rprof.items()},
+                         "roofline": roofline_tensor(rmeta, rprof, pk, r_ms, a.router_steps)}
+        if rank == 0 and world == 1 and not a.no_cpu_baseline:
+            rate, done, el = cpu_router_rate(4096)
+            out["router"]["cpu_baseline"] = {
+                "value": round(rate / 1e6, 6), "unit": "Mq/s", "cores": blas_threads(), "kind": "port",
+                "sample": f"{done} tokens through the numpy port of python/bvh_router.py (fp32) in {el:.1f} s"}
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        rate, done, el = cpu_router_rate(4096)
-        out["cpu_baseline"] = {"value": round(rate / 1e6, 6), "unit": "Mq/s", "cores": blas_threads(),
+        rate, done, el = cpu_moe_rate(a.cpu_sample)
+        out["cpu_baseline"] = {"value": round(rate, 2), "unit": "tokens/s", "cores": blas_threads(),
                                "kind": "port",
-                               "sample": f"{done} tokens of the same workload through the numpy "
-                                         f"oracle (fp32) in {el:.1f} s"}
+                               "sample": f"{done} tokens of the same workload (router soft top-8 + "
+                                         f"64 ternary experts, fp32 numpy port of the reference CPU "
+                                         f"path) in {el:.1f} s"}
     if rank == 0:
         print(json.dumps(out), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+def cpu_moe_rate(sample_tokens: int, budget_s: float = 15.0):
+    """Tokens/s of the CPU path: oracle router (soft, top-8) + fp32 ternary experts."""
+    from oracle import router as orouter
+    from oracle import ternary as otern
+    from sb200 import synth
+    w = synth.router_weights(H, S, BRANCHING, seed=0)
+    experts = synth.ternary_experts(E_EXPERTS, H, I_INTER, seed=2)
+    x = synth.hidden_states(sample_tokens, H, seed=2).numpy()
+
+    def one():
+        o = orouter.router_forward(w, x, BRANCHING, mode="soft", k=TOPK)
+        otern.moe_combine(x, o["topk_ids"], o["topk_weights"], experts, fp32=True)
+
+    one()   # warm the BLAS and thread pools
+    done, t0 = 0, time.perf_counter()
+    while True:
+        one()
+        done += sample_tokens
+        el = time.perf_counter() - t0
+        if el >= budget_s or done >= 16 * sample_tokens:
+            break
+    return done / el, done, el
 
 
 def traffic_for(meta):
@@ -314,31 +431,38 @@ def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    sample = 4096
-    # each step: the reference CPU router path on a bounded token sample
+    sample = a.cpu_sample
     from oracle import router as orouter
+    from oracle import ternary as otern
     from sb200 import synth
     cores = blas_threads()
     w = synth.router_weights(H, S, BRANCHING, seed=0)
-    x = synth.hidden_states(sample, H, seed=1).numpy()
+    experts = synth.ternary_experts(E_EXPERTS, H, I_INTER, seed=2)
+    x = synth.hidden_states(sample, H, seed=2).numpy()
+
+    def one():
+        o = orouter.router_forward(w, x, BRANCHING, mode="soft", k=TOPK)
+        otern.moe_combine(x, o["topk_ids"], o["topk_weights"], experts, fp32=True)
+
     for _ in range(max(a.warmup, 1)):
-        orouter.router_forward(w, x, BRANCHING, mode="hard", k=TOPK)
+        one()
     t0 = time.perf_counter()
     for _ in range(a.steps):
-        orouter.router_forward(w, x, BRANCHING, mode="hard", k=TOPK)
+        one()
     el = time.perf_counter() - t0
-    value = sample * a.steps / el / 1e6
-    out = {"impl": "reference", "metric": "router Mq/s (BVH route, top-8) — MoE layer pending",
-           "value": round(value, 6), "unit": "Mq/s", "n_gpus": 0, "steps": a.steps,
+    value = sample * a.steps / el
+    out = {"impl": "reference", "metric": "MoE-layer tokens/s (BVH route + ternary SwiGLU)",
+           "value": round(value, 2), "unit": "tokens/s", "n_gpus": 0, "steps": a.steps,
            "warmup": a.warmup, "ms_per_step": round(el / a.steps * 1e3, 3),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-           "data": "synthetic (seeded unit-RMS Gaussian tokens, random-init router)",
-           "config": {"workload": "router_fwd_bvh_4x4x4_top8", "hidden": H, "spectral_dim": S,
-                      "experts": 64, "top_k": TOPK, "batch_tokens_per_step": sample},
-           "cpu_baseline": {"value": round(value, 6), "unit": "Mq/s", "cores": cores, "kind": "port",
-                            "sample": f"{sample} tokens per step through the numpy port of "
-                                      "python/bvh_router.py (fp32), host cores"},
-           "e2e": {"value": round(value, 6), "unit": "Mq/s", "h2d_bytes_per_step": 0,
+           "data": "synthetic (seeded unit-RMS Gaussian tokens, random-init router and ternary experts)",
+           "config": {"workload": "moe_layer_bvh_route_ternary_swiglu", "hidden": H,
+                      "intermediate": I_INTER, "experts": E_EXPERTS, "top_k": TOPK,
+                      "tokens_per_step": sample, "router_select": "soft"},
+           "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
+                            "sample": f"{sample} tokens per step through the numpy ports of "
+                                      "python/bvh_router.py and TernaryExpertModule (fp32), host cores"},
+           "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
@@ -346,16 +470,20 @@ def run_reference(a):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="router", choices=["router"])
-    ap.add_argument("--batch", type=int, default=0)
+    ap.add_argument("--batch", type=int, default=0, help="MoE-layer tokens per GPU (default 4096)")
+    ap.add_argument("--router-batch", type=int, default=262144)
+    ap.add_argument("--router-steps", type=int, default=100)
+    ap.add_argument("--skip-router", action="store_true")
+    ap.add_argument("--cpu-sample", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3) if a.impl == "ours" else a.warmup
     if a.impl == "reference":
-        a.steps = min(a.steps, 10)
+        a.steps = min(a.steps, 8)
+        a.warmup = min(a.warmup, 1)
         run_reference(a)
     else:
         run_ours(a)

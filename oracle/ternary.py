@@ -104,21 +104,35 @@ def gated_mlp_packed(x, gate_packed, up_packed, down_packed, gs, us, ds):
     return gated_mlp(x, Tg, Tu, Td, gs, us, ds)
 
 
-def moe_combine(x, ids, weights, experts):
-    """out[t] = sum_k weights[t,k] * expert_{ids[t,k]}(x[t]) (float64).
+def gated_mlp_f32(x, T_gate, T_up, T_down, s_gate, s_up, s_down):
+    """fp32 restatement of TernaryExpertModule.forward_hidden (real_model_demo.py:379-398),
+    including its per-call dequantization W = T * s; used to time the CPU path."""
+    x = np.asarray(x, np.float32)
+    gw = T_gate.astype(np.float32) * np.asarray(s_gate, np.float32)[:, None]
+    uw = T_up.astype(np.float32) * np.asarray(s_up, np.float32)[:, None]
+    dw = T_down.astype(np.float32) * np.asarray(s_down, np.float32)[:, None]
+    g = x @ gw.T
+    h = (g / (np.float32(1) + np.exp(-g))) * (x @ uw.T)
+    return h @ dw.T
+
+
+def moe_combine(x, ids, weights, experts, fp32: bool = False):
+    """out[t] = sum_k weights[t,k] * expert_{ids[t,k]}(x[t]) (float64, or fp32 with ``fp32``).
 
     ``experts`` is a list of dicts in the container layout of
     python/real_model_demo.py:85-98.
     """
-    x = np.asarray(x, np.float64)
+    dt = np.float32 if fp32 else np.float64
+    x = np.asarray(x, dt)
     ids = np.asarray(ids)
-    weights = np.asarray(weights, np.float64)
+    weights = np.asarray(weights, dt)
     out = np.zeros_like(x)
+    f = gated_mlp_f32 if fp32 else gated_mlp
     for e in np.unique(ids):
         rows, slots = np.nonzero(ids == e)
         ex = experts[int(e)]
-        y = gated_mlp(x[rows], ex["gate_ternary"], ex["up_ternary"], ex["down_ternary"],
-                      ex["gate_scale"], ex["up_scale"], ex["down_scale"])
+        y = f(x[rows], ex["gate_ternary"], ex["up_ternary"], ex["down_ternary"],
+              ex["gate_scale"], ex["up_scale"], ex["down_scale"])
         np.add.at(out, rows, weights[rows, slots][:, None] * y)
     return out
 
