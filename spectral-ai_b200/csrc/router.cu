@@ -168,6 +168,8 @@ struct TreeDev {
   const float* b3d;      // [3]
   const float* centers;  // [total,3]
   const float* refw;     // [total,S]
+  const float* refwT;    // [S,total]
+  int total_nodes;
   const float* refb;     // [total]
   const float* portals;  // [total,12]
 };
@@ -267,8 +269,9 @@ __global__ void __launch_bounds__(DESC_WARPS * 32)
   float* w3 = dsm;
   for (int i = threadIdx.x; i < 3 * H; i += blockDim.x) w3[i] = t.w3d[i];
   __syncthreads();
-  float* pa0 = dsm + 3 * H + (size_t)warp * 2 * t.max_nodes;  // previous level probs (soft)
-  float* pb0 = pa0 + t.max_nodes;                              // current level probs (soft)
+  float* pa0 = dsm + 3 * H + (size_t)warp * (2 * t.max_nodes + t.S);  // previous level probs (soft)
+  float* pb0 = pa0 + t.max_nodes;                                      // current level probs (soft)
+  float* spec_s = pb0 + t.max_nodes;                                   // this token's spectral row (soft)
   const float b3x = __ldg(t.b3d + 0), b3y = __ldg(t.b3d + 1), b3z = __ldg(t.b3d + 2);
   for (int64_t tok0 = ((int64_t)blockIdx.x * DESC_WARPS + warp) * DESC_TPW; tok0 < B;
        tok0 += (int64_t)gridDim.x * DESC_WARPS * DESC_TPW) {
@@ -276,18 +279,26 @@ __global__ void __launch_bounds__(DESC_WARPS * 32)
     float acc[DESC_TPW][3];
 #pragma unroll
     for (int u = 0; u < DESC_TPW; ++u) acc[u][0] = acc[u][1] = acc[u][2] = 0.f;
+    // four 128-wide chunks per iteration keep 4 x DESC_TPW independent loads in flight
+#pragma unroll 4
     for (int i = lane * 4; i < H; i += 128) {
       const float4 wa = *reinterpret_cast<const float4*>(w3 + i);
       const float4 wb = *reinterpret_cast<const float4*>(w3 + H + i);
       const float4 wc = *reinterpret_cast<const float4*>(w3 + 2 * H + i);
+      float v[DESC_TPW][4];
 #pragma unroll
       for (int u = 0; u < DESC_TPW; ++u) {
-        if (tok0 + u >= B) break;
-        float v[4];
-        load4(x + (tok0 + u) * (int64_t)H + i, v);
-        acc[u][0] = fmaf(v[0], wa.x, fmaf(v[1], wa.y, fmaf(v[2], wa.z, fmaf(v[3], wa.w, acc[u][0]))));
-        acc[u][1] = fmaf(v[0], wb.x, fmaf(v[1], wb.y, fmaf(v[2], wb.z, fmaf(v[3], wb.w, acc[u][1]))));
-        acc[u][2] = fmaf(v[0], wc.x, fmaf(v[1], wc.y, fmaf(v[2], wc.z, fmaf(v[3], wc.w, acc[u][2]))));
+        if (tok0 + u < B) {
+          load4(x + (tok0 + u) * (int64_t)H + i, v[u]);
+        } else {
+          v[u][0] = v[u][1] = v[u][2] = v[u][3] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < DESC_TPW; ++u) {
+        acc[u][0] = fmaf(v[u][0], wa.x, fmaf(v[u][1], wa.y, fmaf(v[u][2], wa.z, fmaf(v[u][3], wa.w, acc[u][0]))));
+        acc[u][1] = fmaf(v[u][0], wb.x, fmaf(v[u][1], wb.y, fmaf(v[u][2], wb.z, fmaf(v[u][3], wb.w, acc[u][1]))));
+        acc[u][2] = fmaf(v[u][0], wc.x, fmaf(v[u][1], wc.y, fmaf(v[u][2], wc.z, fmaf(v[u][3], wc.w, acc[u][2]))));
       }
     }
 #pragma unroll
@@ -317,7 +328,9 @@ __global__ void __launch_bounds__(DESC_WARPS * 32)
     for (int j = 0; j < SPL_MAX; ++j) {
       const int s = lane + 32 * j;
       spec_r[j] = (s < S) ? spec[tok * (int64_t)S + s] : 0.f;
+      if (soft && s < S) spec_s[s] = spec_r[j];
     }
+    if (soft) __syncwarp();
 
     int prev_choice = 0;
     float prev_pc = 1.f;  // HARD: probability of the chosen parent
@@ -383,16 +396,22 @@ __global__ void __launch_bounds__(DESC_WARPS * 32)
         warp_argmax(best, bi);
         choice = bi;
         __syncwarp();
-        // p_j = probs_j * n_j with n_j = sigmoid(W_j . spec + b_j)
+        // p_j = probs_j * n_j with n_j = sigmoid(W_j . spec + b_j): one node per lane,
+        // refraction weights read transposed ([S][nodes]) so a warp's loads coalesce
         float tot = 0.f;
-        for (int j = 0; j < Nl; ++j) {
-          const float n = sigmoidf_(refract_dot<SPL_MAX>(t.refw + (size_t)(off + j) * S, spec_r, S, lane) +
-                                    __ldg(t.refb + off + j));
-          if (lane == (j & 31)) {
-            const float v = pb[j] * n;
-            pb[j] = v;
-            tot += v;
+        for (int j = lane; j < Nl; j += 32) {
+          const float* wt = t.refwT + off + j;
+          float d0 = 0.f, d1 = 0.f;
+          int s = 0;
+          for (; s + 1 < S; s += 2) {
+            d0 = fmaf(spec_s[s], __ldg(wt + (size_t)s * t.total_nodes), d0);
+            d1 = fmaf(spec_s[s + 1], __ldg(wt + (size_t)(s + 1) * t.total_nodes), d1);
           }
+          if (s < S) d0 = fmaf(spec_s[s], __ldg(wt + (size_t)s * t.total_nodes), d0);
+          const float n = sigmoidf_((d0 + d1) + __ldg(t.refb + off + j));
+          const float v = pb[j] * n;
+          pb[j] = v;
+          tot += v;
         }
         tot = warp_sum(tot);
         __syncwarp();
@@ -553,6 +572,7 @@ struct sb_router {
   float* b3d = nullptr;              // [3]
   float* centers = nullptr;          // [total,3]
   float* refw = nullptr;             // [total,S]
+  float* refwT = nullptr;            // [S,total] (soft-mode layout)
   float* refb = nullptr;             // [total]
   float* portals = nullptr;          // [total,12]
   CUtensorMap tm_w1{}, tm_w2{};
@@ -574,12 +594,12 @@ struct DeviceGuard {
 
 void free_router_buffers(sb_router* h) {
   void* ptrs[] = {h->w1_bf16, h->w2_bf16, h->w1_f32, h->w2_f32, h->b1,   h->b2,
-                  h->w3d,     h->b3d,     h->centers, h->refw,  h->refb, h->portals};
+                  h->w3d,     h->b3d,     h->centers, h->refw,  h->refb, h->portals, h->refwT};
   for (void* p : ptrs)
     if (p) cudaFree(p);
   h->w1_bf16 = h->w2_bf16 = nullptr;
   h->w1_f32 = h->w2_f32 = h->b1 = h->b2 = h->w3d = h->b3d = nullptr;
-  h->centers = h->refw = h->refb = h->portals = nullptr;
+  h->centers = h->refw = h->refb = h->portals = h->refwT = nullptr;
 }
 
 template <typename T>
@@ -592,6 +612,16 @@ int dev_alloc(T** p, size_t count) {
 __global__ void f32_to_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* __restrict__ out, int64_t n) {
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     out[i] = __float2bfloat16_rn(in[i]);
+}
+
+// out[c, r] = in[r, c] for a rows x cols matrix
+__global__ void transpose_f32_kernel(const float* __restrict__ in, float* __restrict__ out, int64_t rows,
+                                     int64_t cols) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * cols;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / cols, c = i % cols;
+    out[c * rows + r] = in[i];
+  }
 }
 
 int upload_f32(float* dst, const float* src, size_t count, float fill_if_null) {
@@ -672,6 +702,7 @@ extern "C" int sb_router_upload(sb_router* h, const sb_router_weights* w) {
       (rc = dev_alloc(&h->b1, (size_t)H)) || (rc = dev_alloc(&h->b2, (size_t)S)) ||
       (rc = dev_alloc(&h->w3d, (size_t)3 * H)) || (rc = dev_alloc(&h->b3d, (size_t)3)) ||
       (rc = dev_alloc(&h->centers, T * 3)) || (rc = dev_alloc(&h->refw, T * S)) ||
+      (rc = dev_alloc(&h->refwT, T * S)) ||
       (rc = dev_alloc(&h->refb, T)) || (rc = dev_alloc(&h->portals, T * 12))) {
     free_router_buffers(h);
     return rc;
@@ -699,6 +730,7 @@ extern "C" int sb_router_upload(sb_router* h, const sb_router_weights* w) {
       SB_CUDA_TRY(cudaMemset(h->portals + off * 12, 0, n * 12 * sizeof(float)));
     }
   }
+  transpose_f32_kernel<<<256, 256>>>(h->refw, h->refwT, (int64_t)T, (int64_t)S);
   f32_to_bf16_kernel<<<1024, 256>>>(h->w1_f32, h->w1_bf16, (int64_t)HH);
   f32_to_bf16_kernel<<<256, 256>>>(h->w2_f32, h->w2_bf16, (int64_t)SH);
   SB_CUDA_TRY(cudaGetLastError());
@@ -837,12 +869,14 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
   t.b3d = h->b3d;
   t.centers = h->centers;
   t.refw = h->refw;
+  t.refwT = h->refwT;
+  t.total_nodes = h->total_nodes;
   t.refb = h->refb;
   t.portals = h->portals;
   DescentOut o{out->topk_ids, out->topk_weights, out->expert_id, out->expert_probs,
                out->route_path, out->confidence, top_k};
   const size_t dsm = (size_t)3 * H * sizeof(float) +
-                     (select == SB_SELECT_SOFT ? (size_t)DESC_WARPS * 2 * h->max_nodes * sizeof(float) : 0);
+                     (select == SB_SELECT_SOFT ? (size_t)DESC_WARPS * (2 * h->max_nodes + S) * sizeof(float) : 0);
   if (dsm > 48 * 1024) {
     static bool attr[2] = {false, false};
     auto k0 = descent_kernel<float>;

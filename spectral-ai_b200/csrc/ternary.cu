@@ -143,12 +143,28 @@ template <> __device__ __forceinline__ __half cvt_act<__nv_bfloat16, __half>(__n
 
 // One warp per (token, slot) pair: claim a row of the expert's segment, record
 // the routing weight and the inverse map, and copy the token's activations.
+// 16-byte vector row copies (bf16 -> bf16: 8 values per lane step; fp32 -> fp16: 4)
+__device__ __forceinline__ void copy_row_vec(const __nv_bfloat16* src, __nv_bfloat16* dst, int H, int lane) {
+  const uint4* s4 = reinterpret_cast<const uint4*>(src);
+  uint4* d4 = reinterpret_cast<uint4*>(dst);
+  for (int c = lane; c < H / 8; c += 32) d4[c] = __ldg(s4 + c);
+}
+__device__ __forceinline__ void copy_row_vec(const float* src, __half* dst, int H, int lane) {
+  const float4* s4 = reinterpret_cast<const float4*>(src);
+  uint2* d2 = reinterpret_cast<uint2*>(dst);
+  for (int c = lane; c < H / 4; c += 32) {
+    const float4 v = __ldg(s4 + c);
+    __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+    d2[c] = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+  }
+}
+
 template <typename TX, typename TA>
 __global__ void moe_scatter_kernel(const TX* __restrict__ x, const int32_t* __restrict__ ids,
                                    const float* __restrict__ wts, int64_t B, int k, int H, int E,
                                    const int* __restrict__ offsets, int* __restrict__ cursor,
                                    TA* __restrict__ xp, int64_t ldx, float* __restrict__ row_w,
-                                   int* __restrict__ inv) {
+                                   int* __restrict__ inv, int vec) {
   const int lane = threadIdx.x & 31;
   const int64_t R = B * k;
   for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < R;
@@ -162,7 +178,11 @@ __global__ void moe_scatter_kernel(const TX* __restrict__ x, const int32_t* __re
     if (lane == 0) row_w[pos] = wts ? wts[i] : 1.0f;
     const TX* src = x + (i / k) * (int64_t)H;
     TA* dst = xp + (int64_t)pos * ldx;
-    for (int c = lane; c < H; c += 32) dst[c] = cvt_act<TX, TA>(src[c]);
+    if (vec) {
+      copy_row_vec(src, dst, H, lane);
+    } else {
+      for (int c = lane; c < H; c += 32) dst[c] = cvt_act<TX, TA>(src[c]);
+    }
   }
 }
 
@@ -173,8 +193,42 @@ template <> __device__ __forceinline__ float cvt_out<float>(float v) { return v;
 template <> __device__ __forceinline__ __nv_bfloat16 cvt_out<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
 
 template <typename TO>
+__device__ __forceinline__ void store4(TO* p, float4 v);
+template <>
+__device__ __forceinline__ void store4<float>(float* p, float4 v) { *reinterpret_cast<float4*>(p) = v; }
+template <>
+__device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* p, float4 v) {
+  __nv_bfloat162 a = __floats2bfloat162_rn(v.x, v.y), b = __floats2bfloat162_rn(v.z, v.w);
+  *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
+}
+
+// out[t] = sum_j y[inv[t*k+j]] in slot order (fixed, so results are reproducible).
+// Vector path: one thread per 4 columns (needs H % 4 == 0).
+template <typename TO>
 __global__ void moe_combine_kernel(const float* __restrict__ y, const int* __restrict__ inv, int64_t B,
                                    int k, int H, TO* __restrict__ out) {
+  if ((H & 3) == 0) {
+    const int H4 = H >> 2;
+    const int64_t total = B * (int64_t)H4;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+      const int64_t t = i / H4;
+      const int c = (int)(i % H4) * 4;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < k; ++j) {
+        const int pos = __ldg(inv + t * k + j);
+        if (pos >= 0) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(y + (int64_t)pos * H + c));
+          acc.x += v.x;
+          acc.y += v.y;
+          acc.z += v.z;
+          acc.w += v.w;
+        }
+      }
+      store4<TO>(out + t * H + c, acc);
+    }
+    return;
+  }
   const int64_t total = B * (int64_t)H;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -310,14 +364,15 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
     moe_scan_kernel<<<1, 32, 0, stream>>>(counts, E, offsets, cursor, mtiles, nmt, (int)L.max_mt);
     int64_t wblocks = (R * 32 + 255) / 256;
     if (wblocks > (int64_t)num_sms() * 16) wblocks = (int64_t)num_sms() * 16;
+    const bool x16 = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
     if (x_dtype == SB_BF16)
       moe_scatter_kernel<__nv_bfloat16, __nv_bfloat16><<<(unsigned)wblocks, 256, 0, stream>>>(
           static_cast<const __nv_bfloat16*>(x), ids, weights, B, k, (int)H, E, offsets, cursor,
-          static_cast<__nv_bfloat16*>(xp), L.ldx, row_w, inv);
+          static_cast<__nv_bfloat16*>(xp), L.ldx, row_w, inv, x16 && (H % 8) == 0);
     else
       moe_scatter_kernel<float, __half><<<(unsigned)wblocks, 256, 0, stream>>>(
           static_cast<const float*>(x), ids, weights, B, k, (int)H, E, offsets, cursor,
-          static_cast<__half*>(xp), L.ldx, row_w, inv);
+          static_cast<__half*>(xp), L.ldx, row_w, inv, x16 && (H % 4) == 0);
     SB_CUDA_TRY(cudaGetLastError());
   }
 
