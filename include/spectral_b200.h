@@ -142,6 +142,29 @@ int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64_t batch,
 
 int sb_router_destroy(sb_router* h);
 
+/* Size of the fixed device array behind sb_router_forward_noalloc (32 MiB per GPU). */
+#define SB_ROUTER_NOALLOC_SCRATCH_BYTES (32u << 20)
+
+/* Router forward that allocates nothing; no counterpart in the reference.
+ * Same arguments and outputs as sb_router_forward minus the workspace: its
+ * scratch is a fixed 32 MiB device array inside the library, for callers that
+ * cannot allocate device memory when they route (a serving process whose HBM
+ * is all reserved by its own pool, or a language runtime binding this ABI with
+ * no device allocator).  Limits and sharing:
+ *   - batch is limited to sb_router_workspace_bytes(h, batch, precision) below
+ *     the array size minus up to 768 bytes of alignment (about 6500 tokens at
+ *     hidden 2048 in SB_PREC_FAST); larger batches fail with SB_ERR_INVALID;
+ *   - every GPU that loads the library holds the array until the process exits;
+ *   - the first call on a device looks up the array's device address (once per
+ *     device, with that device current); make that first call before any
+ *     stream capture;
+ *   - all calls share the one array per device and it keeps the last call's
+ *     contents (nothing needs clearing: each call writes every scratch element
+ *     it reads); calls that overlap on the GPU, e.g. on two streams, race. */
+int sb_router_forward_noalloc(sb_router* h, const void* x, int x_dtype, int64_t batch,
+                              int precision, int select, int top_k,
+                              const sb_router_outputs* out, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Ternary experts                                                           */
 /* ------------------------------------------------------------------------ */

@@ -15,6 +15,7 @@
 #include "gemm_tc.cuh"
 
 #include <math.h>
+#include <mutex>
 #include <new>
 
 namespace sb {
@@ -897,4 +898,61 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
         static_cast<const float*>(x), spec, batch, t, select == SB_SELECT_SOFT, o);
   SB_CUDA_TRY(cudaGetLastError());
   return SB_OK;
+}
+
+// ===========================================================================
+// Allocation-free router forward
+// ===========================================================================
+// Some callers cannot allocate device memory at the point where they route a
+// batch: a serving process that reserved all of HBM for its own pool at
+// start-up (the router then runs inside a request with no allocator to turn
+// to), or a host that binds this C ABI from a language runtime that has no
+// device allocator at all.  For them sb_router_forward_noalloc takes its
+// scratch (the GELU activations and the spectral rows) from this fixed array
+// instead of a caller-provided workspace.  Every GPU that loads the library
+// holds the array until the process exits.
+static __device__ __align__(256) unsigned char g_router_noalloc_scratch[SB_ROUTER_NOALLOC_SCRATCH_BYTES];
+
+namespace sb {
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};  // device address of the array, per device ordinal
+}  // namespace
+}  // namespace sb
+
+extern "C" int sb_router_forward_noalloc(sb_router* h, const void* x, int x_dtype, int64_t batch,
+                                         int precision, int select, int top_k,
+                                         const sb_router_outputs* out, void* stream) {
+  using namespace sb;
+  SB_REQUIRE(h != nullptr, "sb_router_forward_noalloc: null handle");
+  SB_REQUIRE(h->device >= 0 && h->device < 64, "device ordinal %d out of range", h->device);
+  DeviceGuard g(h->device);
+  void* base = nullptr;
+  {
+    // In host code the array's name is only a host-side stand-in; the device
+    // address comes from the runtime, once per device, with that device current.
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[h->device]) {
+      void* p = nullptr;
+      cudaError_t e = cudaGetSymbolAddress(&p, g_router_noalloc_scratch);
+      if (e != cudaSuccess || p == nullptr)
+        return fail(SB_ERR_CUDA, "cudaGetSymbolAddress of the router scratch failed: %s",
+                    cudaGetErrorString(e));
+      g_noalloc_ptr[h->device] = p;
+    }
+    base = g_noalloc_ptr[h->device];
+  }
+  // the forward wants 1024-byte-aligned scratch; the array is 256-byte aligned
+  const uintptr_t b = reinterpret_cast<uintptr_t>(base);
+  const uintptr_t aligned = (b + 1023u) & ~static_cast<uintptr_t>(1023u);
+  const size_t usable = SB_ROUTER_NOALLOC_SCRATCH_BYTES - (size_t)(aligned - b);
+  if (batch < 0) return fail(SB_ERR_INVALID, "batch=%lld must be >= 0", (long long)batch);
+  const size_t need = sb_router_workspace_bytes(h, batch, precision);
+  if (need > usable)
+    return fail(SB_ERR_INVALID,
+                "sb_router_forward_noalloc: batch %lld needs %zu bytes of scratch, more than the "
+                "%zu bytes of its fixed array (split the batch or use sb_router_forward)",
+                (long long)batch, need, usable);
+  return sb_router_forward(h, x, x_dtype, batch, precision, select, top_k, out,
+                           reinterpret_cast<void*>(aligned), usable, stream);
 }

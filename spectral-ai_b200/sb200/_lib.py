@@ -66,6 +66,9 @@ SIGNATURES = [
      [C.c_void_p, C.c_void_p, C.c_int, C.c_int64, C.c_int, C.c_int, C.c_int,
       C.POINTER(RouterOutputs), C.c_void_p, C.c_size_t, C.c_void_p]),
     ("sb_router_destroy", C.c_int, [C.c_void_p]),
+    ("sb_router_forward_noalloc", C.c_int,
+     [C.c_void_p, C.c_void_p, C.c_int, C.c_int64, C.c_int, C.c_int, C.c_int,
+      C.POINTER(RouterOutputs), C.c_void_p]),
     ("sb_ternary_pack_ref", C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p]),
     ("sb_ternary_matrix_bytes", C.c_size_t, [C.c_int64, C.c_int64]),
     ("sb_ternary_repack", C.c_int, [C.c_void_p, C.c_int64, C.c_int64, C.c_void_p, C.c_void_p]),
