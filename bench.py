@@ -217,7 +217,7 @@ def router_workload(batch: int, device):
 
     meta = {"tokens_per_step": batch,
             "h2d": batch * H * 2, "d2h": batch * TOPK * 8,
-            "dominant": "router_enc1_gelu_tc", "dominant_flop": 2.0 * batch * H * H,
+            "dominant": "router_enc1_gelu_tc", "dominant_flop": 2.0 * batch * H * (H + 3),
             "dominant_bytes": batch * H * 2 * 2 + H * H * 2,
             "config": {"workload": "router_fwd_bvh_4x4x4_top8", "hidden": H, "spectral_dim": S,
                        "experts": 64, "top_k": TOPK, "batch_tokens_per_gpu": batch,

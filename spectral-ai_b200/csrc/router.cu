@@ -1,22 +1,27 @@
 // router.cu — BVH router forward for B200 (sm_100a).
 //
 // Restates BVHRouter.forward (python/bvh_router.py:269-329) in eval mode as
-// three kernels:
-//   1. G    = GELU_erf(x W1^T + b1)        tcgen05 bf16 GEMM (FAST) or fp32 FFMA (EXACT)
-//   2. spec = tanh(G W2^T + b2)            same engines          (SpectralEncoder, :84-97)
-//   3. per token, one warp: pos = x W3^T + b3 (fp32), then the level chain of
-//      RouterLevel.forward (:156-204) with the parent log-mask over all nodes of
-//      each level, refraction sigmoid(W_l spec + b_l) (:117-125), portals
-//      (:100-114), normalisation p = p*n/(sum+1e-8) (:291-311), and the MoE
-//      top-k + softmax (python/olmoe_extract.py:105-118).
-// In HARD mode only the chosen node of each level has non-zero probability,
-// so only its refraction row is evaluated (the others multiply a zero).
+// four kernels (FAST engine; the EXACT engine swaps 1-3 for fp32 FFMA kernels):
+//   1. G = GELU_erf(x W1^T + b1) (bf16) and, in an extra 16-column tail tile of
+//      the same tcgen05 GEMM over the same x tiles, pos = x W3^T + b3 with W3
+//      split into three bf16 terms so the positions keep fp32 accuracy
+//      (SpectralEncoder :84-97, to_3d :232, :285).
+//   2. spec = tanh(G W2^T + b2)                      tcgen05 GEMM, bf16 out
+//   3. n = sigmoid(spec Wr^T + br) for every node    tcgen05 GEMM (PrismaticRefraction :117-125)
+//   4. the level chain of RouterLevel.forward (:156-204): d^2 to every node of
+//      the level, logits -d^2 / (2T^2 + 1e-8) plus the parent log-mask
+//      log(p_parent + 1e-10), argmax (HARD, :190-193) or softmax(logits/tau)
+//      (SOFT, :200-202 without the Gumbel noise), p = p*n / (sum + 1e-8)
+//      (:291-311), portals (:100-114), then the MoE top-k + softmax
+//      (python/olmoe_extract.py:105-118).  HARD runs one thread per token,
+//      SOFT one warp per token.
 #include "common.cuh"
 #include "gemm_tc.cuh"
 
 #include <math.h>
 #include <mutex>
 #include <new>
+#include <vector>
 
 namespace sb {
 
@@ -26,12 +31,16 @@ namespace sb {
 __device__ __forceinline__ float gelu_erf(float v) {
   return 0.5f * v * (1.0f + erff(v * 0.70710678118654752440f));
 }
+__device__ __forceinline__ float sigmoidf_(float z) { return 1.0f / (1.0f + expf(-z)); }
 
+// G = GELU(acc + b1) as bf16; tail tile: pos[row] = hi + (mid + lo) + b3.
 struct EpiGeluBf16 {
   const float* bias;
   __nv_bfloat16* out;
   int64_t ldo;
   int N;
+  const float* b3d;  // [3]
+  float* pos;        // [B, 4]
   __device__ __forceinline__ void apply(int64_t row, int col0, const uint32_t (&r)[32]) const {
     __nv_bfloat16* dst = out + row * ldo + col0;
     if (col0 + 32 <= N && (ldo & 7) == 0) {
@@ -54,39 +63,74 @@ struct EpiGeluBf16 {
           dst[j] = __float2bfloat16_rn(gelu_erf(__uint_as_float(r[j]) + __ldg(bias + col0 + j)));
     }
   }
+  __device__ __forceinline__ void tail(int64_t row, const uint32_t (&r)[32]) const {
+    float4 v;
+    v.x = __uint_as_float(r[0]) + (__uint_as_float(r[3]) + __uint_as_float(r[6])) + __ldg(b3d + 0);
+    v.y = __uint_as_float(r[1]) + (__uint_as_float(r[4]) + __uint_as_float(r[7])) + __ldg(b3d + 1);
+    v.z = __uint_as_float(r[2]) + (__uint_as_float(r[5]) + __uint_as_float(r[8])) + __ldg(b3d + 2);
+    v.w = 0.f;
+    reinterpret_cast<float4*>(pos)[row] = v;
+  }
 };
 
-struct EpiTanhF32 {
+// spec = tanh(acc + b2) as bf16 (the A operand of the refraction GEMM).
+struct EpiTanhBf16 {
   const float* bias;
-  float* out;
+  __nv_bfloat16* out;
   int64_t ldo;
   int N;
   __device__ __forceinline__ void apply(int64_t row, int col0, const uint32_t (&r)[32]) const {
-    float* dst = out + row * ldo + col0;
-    if (col0 + 32 <= N && (ldo & 3) == 0) {
-      float4* d4 = reinterpret_cast<float4*>(dst);
+    __nv_bfloat16* dst = out + row * ldo + col0;
+    if (col0 + 32 <= N && (ldo & 7) == 0) {
+      uint32_t packed[16];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        float4 v;
-        v.x = tanhf(__uint_as_float(r[4 * j + 0]) + __ldg(bias + col0 + 4 * j + 0));
-        v.y = tanhf(__uint_as_float(r[4 * j + 1]) + __ldg(bias + col0 + 4 * j + 1));
-        v.z = tanhf(__uint_as_float(r[4 * j + 2]) + __ldg(bias + col0 + 4 * j + 2));
-        v.w = tanhf(__uint_as_float(r[4 * j + 3]) + __ldg(bias + col0 + 4 * j + 3));
-        d4[j] = v;
+      for (int j = 0; j < 16; ++j) {
+        const float a = tanhf(__uint_as_float(r[2 * j]) + __ldg(bias + col0 + 2 * j));
+        const float b = tanhf(__uint_as_float(r[2 * j + 1]) + __ldg(bias + col0 + 2 * j + 1));
+        __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+        packed[j] = *reinterpret_cast<uint32_t*>(&h);
       }
+      uint4* d4 = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+        d4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
     } else {
 #pragma unroll
       for (int j = 0; j < 32; ++j)
-        if (col0 + j < N) dst[j] = tanhf(__uint_as_float(r[j]) + __ldg(bias + col0 + j));
+        if (col0 + j < N) dst[j] = __float2bfloat16_rn(tanhf(__uint_as_float(r[j]) + __ldg(bias + col0 + j)));
     }
   }
+  __device__ __forceinline__ void tail(int64_t, const uint32_t (&)[32]) const {}
+};
+
+// n = sigmoid(acc + br) in fp32, row-major [B, ldn] (SOFT) or node-major
+// [nodes, ldn] (HARD, one thread per token reads its own column coalesced).
+struct EpiSigmoidN {
+  const float* bias;
+  float* out;
+  int64_t ldn;
+  int N;
+  int node_major;
+  __device__ __forceinline__ void apply(int64_t row, int col0, const uint32_t (&r)[32]) const {
+    if (node_major) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) out[(int64_t)(col0 + j) * ldn + row] = sigmoidf_(__uint_as_float(r[j]) + __ldg(bias + col0 + j));
+    } else {
+      float* dst = out + row * ldn + col0;
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) dst[j] = sigmoidf_(__uint_as_float(r[j]) + __ldg(bias + col0 + j));
+    }
+  }
+  __device__ __forceinline__ void tail(int64_t, const uint32_t (&)[32]) const {}
 };
 
 // ---------------------------------------------------------------------------
 // EXACT engine: fp32 FFMA GEMM, C = act(A B^T + bias), A [M,K] fp32|bf16, B [N,K] fp32.
 // 128x128 tile, K-step 8, 256 threads, 8x8 outputs per thread.
 // ---------------------------------------------------------------------------
-enum { ACT_GELU = 0, ACT_TANH = 1 };
+enum { ACT_GELU = 0, ACT_TANH = 1, ACT_SIGMOID = 2 };
 
 template <typename TA>
 __device__ __forceinline__ float to_f32(TA v);
@@ -97,11 +141,13 @@ __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) {
   return __bfloat162float(v);
 }
 
+// C element (m, n) is stored at C[m * ldc + n], or at C[n * ldc + m] when transposed.
 template <typename TA, int ACT>
 __global__ void __launch_bounds__(256) sgemm_nt_kernel(const TA* __restrict__ A,
                                                        const float* __restrict__ B,
                                                        const float* __restrict__ bias,
-                                                       float* __restrict__ C, int M, int N, int K) {
+                                                       float* __restrict__ C, int M, int N, int K,
+                                                       int64_t ldc, int transposed) {
   __shared__ float As[8][128 + 4];
   __shared__ float Bs[8][128 + 4];
   const int tid = threadIdx.x;
@@ -147,43 +193,14 @@ __global__ void __launch_bounds__(256) sgemm_nt_kernel(const TA* __restrict__ A,
       const int n = n0 + tc * 8 + j;
       if (n >= N) continue;
       const float v = acc[i][j] + bias[n];
-      C[(int64_t)m * N + n] = ACT == ACT_GELU ? gelu_erf(v) : tanhf(v);
+      const float y = ACT == ACT_GELU ? gelu_erf(v) : (ACT == ACT_TANH ? tanhf(v) : sigmoidf_(v));
+      if (transposed)
+        C[(int64_t)n * ldc + m] = y;
+      else
+        C[(int64_t)m * ldc + n] = y;
     }
   }
 }
-
-// ---------------------------------------------------------------------------
-// Descent: one warp per token.
-// ---------------------------------------------------------------------------
-struct TreeDev {
-  int L;
-  int S;
-  int H;
-  int branching[SB_MAX_LEVELS];
-  int nodes[SB_MAX_LEVELS];   // N_l
-  int offset[SB_MAX_LEVELS];  // first node of level l in the flat arrays
-  int max_nodes;
-  float denom;  // 2 T^2 + 1e-8 in fp32
-  float tau;    // clamp(T, 0.01)
-  const float* w3d;      // [3,H]
-  const float* b3d;      // [3]
-  const float* centers;  // [total,3]
-  const float* refw;     // [total,S]
-  const float* refwT;    // [S,total]
-  int total_nodes;
-  const float* refb;     // [total]
-  const float* portals;  // [total,12]
-};
-
-struct DescentOut {
-  int32_t* topk_ids;
-  float* topk_w;
-  int64_t* expert_id;
-  float* expert_probs;
-  int64_t* route_path;
-  float* confidence;
-  int k;
-};
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -208,43 +225,6 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
   }
 }
 
-__device__ __forceinline__ float sigmoidf_(float z) { return 1.0f / (1.0f + expf(-z)); }
-
-// dot(spec, refw[node]) over S with spec distributed as spec_r[j] = spec[lane + 32 j]
-template <int SPL>
-__device__ __forceinline__ float refract_dot(const float* __restrict__ w, const float (&spec_r)[SPL],
-                                             int S, int lane) {
-  float acc = 0.f;
-#pragma unroll
-  for (int j = 0; j < SPL; ++j) {
-    const int s = lane + 32 * j;
-    if (s < S) acc = fmaf(spec_r[j], __ldg(w + s), acc);
-  }
-  return warp_sum(acc);
-}
-
-// Loads 8 consecutive input features as fp32.
-__device__ __forceinline__ void load8(const __nv_bfloat16* p, float (&v)[8]) {
-  const uint4 u = *reinterpret_cast<const uint4*>(p);
-  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const float2 f = __bfloat1622float2(h[j]);
-    v[2 * j] = f.x;
-    v[2 * j + 1] = f.y;
-  }
-}
-__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
-  const float4 a = *reinterpret_cast<const float4*>(p);
-  const float4 b = *reinterpret_cast<const float4*>(p + 4);
-  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
-  v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
-}
-
-constexpr int DESC_WARPS = 8;
-constexpr int SPL_MAX = 8;  // spectral dims per lane: S <= 256
-
-// Loads 4 consecutive input features as fp32 (8-byte / 16-byte aligned).
 __device__ __forceinline__ void load4(const __nv_bfloat16* p, float (&v)[4]) {
   const uint2 u = *reinterpret_cast<const uint2*>(p);
   const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&u);
@@ -256,295 +236,264 @@ __device__ __forceinline__ void load4(const float* p, float (&v)[4]) {
   v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
 }
 
-constexpr int DESC_TPW = 4;  // tokens per warp iteration sharing the to_3d weight reads
-
-// Shared memory: to_3d weights [3][H] fp32, then (soft mode) two probability
-// buffers of max_nodes floats per warp.
+// EXACT engine: pos = x W3^T + b3 in fp32, one warp per token.
 template <typename TX>
-__global__ void __launch_bounds__(DESC_WARPS * 32)
-    descent_kernel(const TX* __restrict__ x, const float* __restrict__ spec, int64_t B, TreeDev t,
-                   int soft, DescentOut o) {
-  extern __shared__ float dsm[];
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int H = t.H, S = t.S, L = t.L;
-  float* w3 = dsm;
-  for (int i = threadIdx.x; i < 3 * H; i += blockDim.x) w3[i] = t.w3d[i];
-  __syncthreads();
-  float* pa0 = dsm + 3 * H + (size_t)warp * (2 * t.max_nodes + t.S);  // previous level probs (soft)
-  float* pb0 = pa0 + t.max_nodes;                                      // current level probs (soft)
-  float* spec_s = pb0 + t.max_nodes;                                   // this token's spectral row (soft)
-  const float b3x = __ldg(t.b3d + 0), b3y = __ldg(t.b3d + 1), b3z = __ldg(t.b3d + 2);
-  for (int64_t tok0 = ((int64_t)blockIdx.x * DESC_WARPS + warp) * DESC_TPW; tok0 < B;
-       tok0 += (int64_t)gridDim.x * DESC_WARPS * DESC_TPW) {
-    // ---- pos = to_3d(x) in fp32 for DESC_TPW tokens (bvh_router.py:285)
-    float acc[DESC_TPW][3];
-#pragma unroll
-    for (int u = 0; u < DESC_TPW; ++u) acc[u][0] = acc[u][1] = acc[u][2] = 0.f;
-    // four 128-wide chunks per iteration keep 4 x DESC_TPW independent loads in flight
-#pragma unroll 4
+__global__ void __launch_bounds__(256) pos_f32_kernel(const TX* __restrict__ x, const float* __restrict__ w3d,
+                                                      const float* __restrict__ b3d, int64_t B, int H,
+                                                      float* __restrict__ pos) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t tok = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; tok < B;
+       tok += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f;
+    const TX* xr = x + tok * (int64_t)H;
     for (int i = lane * 4; i < H; i += 128) {
-      const float4 wa = *reinterpret_cast<const float4*>(w3 + i);
-      const float4 wb = *reinterpret_cast<const float4*>(w3 + H + i);
-      const float4 wc = *reinterpret_cast<const float4*>(w3 + 2 * H + i);
-      float v[DESC_TPW][4];
+      float v[4];
+      load4(xr + i, v);
 #pragma unroll
-      for (int u = 0; u < DESC_TPW; ++u) {
-        if (tok0 + u < B) {
-          load4(x + (tok0 + u) * (int64_t)H + i, v[u]);
-        } else {
-          v[u][0] = v[u][1] = v[u][2] = v[u][3] = 0.f;
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < DESC_TPW; ++u) {
-        acc[u][0] = fmaf(v[u][0], wa.x, fmaf(v[u][1], wa.y, fmaf(v[u][2], wa.z, fmaf(v[u][3], wa.w, acc[u][0]))));
-        acc[u][1] = fmaf(v[u][0], wb.x, fmaf(v[u][1], wb.y, fmaf(v[u][2], wb.z, fmaf(v[u][3], wb.w, acc[u][1]))));
-        acc[u][2] = fmaf(v[u][0], wc.x, fmaf(v[u][1], wc.y, fmaf(v[u][2], wc.z, fmaf(v[u][3], wc.w, acc[u][2]))));
+      for (int u = 0; u < 4; ++u) {
+        a0 = fmaf(v[u], __ldg(w3d + i + u), a0);
+        a1 = fmaf(v[u], __ldg(w3d + H + i + u), a1);
+        a2 = fmaf(v[u], __ldg(w3d + 2 * H + i + u), a2);
       }
     }
-#pragma unroll
-    for (int u = 0; u < DESC_TPW; ++u) {
-      acc[u][0] = warp_sum(acc[u][0]);
-      acc[u][1] = warp_sum(acc[u][1]);
-      acc[u][2] = warp_sum(acc[u][2]);
-    }
-#pragma unroll 1
-    for (int u = 0; u < DESC_TPW; ++u) {
-    const int64_t tok = tok0 + u;
-    if (tok >= B) break;
-    float* pa = pa0;
-    float* pb = pb0;
-    float cx = acc[0][0] + b3x, cy = acc[0][1] + b3y, cz = acc[0][2] + b3z;
-    // select this token's sums without dynamic register indexing
-#pragma unroll
-    for (int v = 1; v < DESC_TPW; ++v)
-      if (u == v) {
-        cx = acc[v][0] + b3x;
-        cy = acc[v][1] + b3y;
-        cz = acc[v][2] + b3z;
-      }
+    a0 = warp_sum(a0);
+    a1 = warp_sum(a1);
+    a2 = warp_sum(a2);
+    if (lane == 0)
+      reinterpret_cast<float4*>(pos)[tok] =
+          make_float4(a0 + __ldg(b3d + 0), a1 + __ldg(b3d + 1), a2 + __ldg(b3d + 2), 0.f);
+  }
+}
 
-    float spec_r[SPL_MAX];
-#pragma unroll
-    for (int j = 0; j < SPL_MAX; ++j) {
-      const int s = lane + 32 * j;
-      spec_r[j] = (s < S) ? spec[tok * (int64_t)S + s] : 0.f;
-      if (soft && s < S) spec_s[s] = spec_r[j];
-    }
-    if (soft) __syncwarp();
+// ---------------------------------------------------------------------------
+// Descent
+// ---------------------------------------------------------------------------
+struct TreeDev {
+  int L;
+  int branching[SB_MAX_LEVELS];
+  int nodes[SB_MAX_LEVELS];   // N_l
+  int offset[SB_MAX_LEVELS];  // first node of level l in the flat arrays
+  int total_nodes;
+  int max_nodes;
+  float denom;  // 2 T^2 + 1e-8 in fp32
+  float tau;    // clamp(T, 0.01)
+  const float* centers;  // [total,3]
+  const float* portals;  // [total,12]
+};
 
-    int prev_choice = 0;
-    float prev_pc = 1.f;  // HARD: probability of the chosen parent
+struct DescentOut {
+  int32_t* topk_ids;
+  float* topk_w;
+  int64_t* expert_id;
+  float* expert_probs;
+  int64_t* route_path;
+  float* confidence;
+  int k;
+};
+
+// HARD: one thread per token.  Only the chosen node of a level carries
+// probability, so the parent mask is log(p_c + 1e-10) inside the chosen
+// parent and log(1e-10) elsewhere, and only n at the chosen node is read.
+// n is node-major: n[node * B + tok].
+__global__ void __launch_bounds__(256) descent_hard_kernel(const float* __restrict__ pos,
+                                                           const float* __restrict__ n, int64_t B,
+                                                           TreeDev t, DescentOut o) {
+  const float m_out = logf(0.0f + 1e-10f);
+  for (int64_t tok = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; tok < B;
+       tok += (int64_t)gridDim.x * blockDim.x) {
+    const float4 p4 = reinterpret_cast<const float4*>(pos)[tok];
+    float cx = p4.x, cy = p4.y, cz = p4.z;
+    int prev = 0;
+    float pc = 1.f;
     int choice = 0;
-    float pc = 0.f;
-    for (int l = 0; l < L; ++l) {
+    for (int l = 0; l < t.L; ++l) {
       const int Nl = t.nodes[l], off = t.offset[l], nb = t.branching[l];
+      const float m_in = logf(pc + 1e-10f);
+      const int lo = prev * nb, hi = lo + nb;
       const float* cen = t.centers + (size_t)off * 3;
-      if (!soft) {
-        // argmax over all Nl logits with the parent log-mask (bvh_router.py:176-192)
-        float best = -INFINITY;
-        int bi = 0x7fffffff;
-        for (int j = lane; j < Nl; j += 32) {
-          const float dx = cx - __ldg(cen + 3 * j), dy = cy - __ldg(cen + 3 * j + 1),
-                      dz = cz - __ldg(cen + 3 * j + 2);
-          const float d2 = (dx * dx + dy * dy) + dz * dz;
-          float lg = -d2 / t.denom;
-          if (l > 0) {
-            const float parent = (j / nb == prev_choice) ? prev_pc : 0.f;
-            lg = lg + logf(parent + 1e-10f);
-          }
-          if (lg > best || (lg == best && j < bi)) {
-            best = lg;
-            bi = j;
-          }
-        }
-        warp_argmax(best, bi);
-        choice = bi;
-        const float n = sigmoidf_(refract_dot<SPL_MAX>(t.refw + (size_t)(off + choice) * S, spec_r, S, lane) +
-                                  __ldg(t.refb + off + choice));
-        pc = n / (n + 1e-8f);
-      } else {
-        // logits, softmax(logits / tau), refraction of every node, normalisation
-        float mx = -INFINITY;
-        for (int j = lane; j < Nl; j += 32) {
-          const float dx = cx - __ldg(cen + 3 * j), dy = cy - __ldg(cen + 3 * j + 1),
-                      dz = cz - __ldg(cen + 3 * j + 2);
-          const float d2 = (dx * dx + dy * dy) + dz * dz;
-          float lg = -d2 / t.denom;
-          if (l > 0) lg = lg + logf(pa[j / nb] + 1e-10f);
-          lg = lg / t.tau;
-          pb[j] = lg;
-          mx = fmaxf(mx, lg);
-        }
-        mx = warp_max(mx);
-        float sum = 0.f;
-        for (int j = lane; j < Nl; j += 32) {
-          const float e = expf(pb[j] - mx);
-          pb[j] = e;
-          sum += e;
-        }
-        sum = warp_sum(sum);
-        float best = -INFINITY;
-        int bi = 0x7fffffff;
-        for (int j = lane; j < Nl; j += 32) {
-          const float pr = pb[j] / sum;
-          if (pr > best || (pr == best && j < bi)) {
-            best = pr;
-            bi = j;
-          }
-          pb[j] = pr;
-        }
-        warp_argmax(best, bi);
-        choice = bi;
-        __syncwarp();
-        // p_j = probs_j * n_j with n_j = sigmoid(W_j . spec + b_j): one node per lane,
-        // refraction weights read transposed ([S][nodes]) so a warp's loads coalesce
-        float tot = 0.f;
-        for (int j = lane; j < Nl; j += 32) {
-          const float* wt = t.refwT + off + j;
-          float d0 = 0.f, d1 = 0.f;
-          int s = 0;
-          for (; s + 1 < S; s += 2) {
-            d0 = fmaf(spec_s[s], __ldg(wt + (size_t)s * t.total_nodes), d0);
-            d1 = fmaf(spec_s[s + 1], __ldg(wt + (size_t)(s + 1) * t.total_nodes), d1);
-          }
-          if (s < S) d0 = fmaf(spec_s[s], __ldg(wt + (size_t)s * t.total_nodes), d0);
-          const float n = sigmoidf_((d0 + d1) + __ldg(t.refb + off + j));
-          const float v = pb[j] * n;
-          pb[j] = v;
-          tot += v;
-        }
-        tot = warp_sum(tot);
-        __syncwarp();
-        const float inv_den = tot + 1e-8f;
-        for (int j = lane; j < Nl; j += 32) pb[j] = pb[j] / inv_den;
-        __syncwarp();
-      }
-      // route_path holds the level-global node index (bvh_router.py:322)
-      if (o.route_path && lane == 0) o.route_path[tok * L + l] = choice;
-      if (l < L - 1) {
-        const float* A = t.portals + (size_t)off * 12;
-        if (!soft) {
-          const float* a = A + (size_t)choice * 12;
-          const float lx = fmaf(__ldg(a + 0), cx, fmaf(__ldg(a + 1), cy, fmaf(__ldg(a + 2), cz, __ldg(a + 3))));
-          const float ly = fmaf(__ldg(a + 4), cx, fmaf(__ldg(a + 5), cy, fmaf(__ldg(a + 6), cz, __ldg(a + 7))));
-          const float lz = fmaf(__ldg(a + 8), cx, fmaf(__ldg(a + 9), cy, fmaf(__ldg(a + 10), cz, __ldg(a + 11))));
-          cx = lx * pc;
-          cy = ly * pc;
-          cz = lz * pc;
-        } else {
-          float sx = 0.f, sy = 0.f, sz = 0.f;
-          for (int j = lane; j < Nl; j += 32) {
-            const float* a = A + (size_t)j * 12;
-            const float pj = pb[j];
-            sx += pj * fmaf(__ldg(a + 0), cx, fmaf(__ldg(a + 1), cy, fmaf(__ldg(a + 2), cz, __ldg(a + 3))));
-            sy += pj * fmaf(__ldg(a + 4), cx, fmaf(__ldg(a + 5), cy, fmaf(__ldg(a + 6), cz, __ldg(a + 7))));
-            sz += pj * fmaf(__ldg(a + 8), cx, fmaf(__ldg(a + 9), cy, fmaf(__ldg(a + 10), cz, __ldg(a + 11))));
-          }
-          cx = warp_sum(sx);
-          cy = warp_sum(sy);
-          cz = warp_sum(sz);
-        }
-      }
-      prev_choice = choice;
-      prev_pc = pc;
-      if (soft) {
-        float* tmp = pa;
-        pa = pb;
-        pb = tmp;
-      }
-    }
-    // ---- outputs of the last level
-    const int NL = t.nodes[L - 1];
-    float conf;
-    int eid;
-    if (!soft) {
-      conf = pc;
-      eid = choice;
-      if (!(pc > 0.f)) {  // all-zero (or NaN) row: argmax returns the first index
-        eid = 0;
-        conf = pc > 0.f ? pc : 0.f;
-      }
-      if (o.expert_probs)
-        for (int j = lane; j < NL; j += 32) o.expert_probs[tok * NL + j] = (j == choice) ? pc : 0.f;
-      if (o.topk_ids) {
-        // top-k of a one-hot row: the chosen expert, then the lowest other ids
-        const int k = o.k;
-        if (lane < k) {
-          int id;
-          float v;
-          if (pc > 0.f) {
-            if (lane == 0) {
-              id = choice;
-              v = pc;
-            } else {
-              id = (lane - 1 < choice) ? lane - 1 : lane;
-              v = 0.f;
-            }
-          } else {
-            id = lane;
-            v = pc > 0.f ? pc : 0.f;
-          }
-          const float v0 = (pc > 0.f) ? pc : 0.f;
-          const float e = expf(v - v0);
-          const float denom = (pc > 0.f) ? 1.f + (float)(k - 1) * expf(-v0) : (float)k;
-          o.topk_ids[tok * k + lane] = id;
-          if (o.topk_w) o.topk_w[tok * k + lane] = e / denom;
-        }
-      }
-    } else {
-      // expert_probs = pa (swapped above)
       float best = -INFINITY;
-      int bi = 0x7fffffff;
-      for (int j = lane; j < NL; j += 32) {
-        const float v = pa[j];
-        if (o.expert_probs) o.expert_probs[tok * NL + j] = v;
-        if (v > best || (v == best && j < bi)) {
-          best = v;
+      int bi = 0;
+      for (int j = 0; j < Nl; ++j) {
+        const float dx = cx - __ldg(cen + 3 * j), dy = cy - __ldg(cen + 3 * j + 1),
+                    dz = cz - __ldg(cen + 3 * j + 2);
+        const float d2 = (dx * dx + dy * dy) + dz * dz;
+        float lg = -d2 / t.denom;
+        if (l > 0) lg = lg + ((j >= lo && j < hi) ? m_in : m_out);
+        if (lg > best) {  // strict: the first maximum wins, like torch.argmax
+          best = lg;
           bi = j;
         }
       }
-      warp_argmax(best, bi);
-      eid = bi;
-      conf = best;
-      if (o.topk_ids) {
-        const int k = o.k;
-        float top0 = best, wsum = 0.f, myv = 0.f;
-        int myid = 0;
-        for (int r = 0; r < k; ++r) {
-          float bv = -INFINITY;
-          int bj = 0x7fffffff;
-          for (int j = lane; j < NL; j += 32) {
-            const float v = pa[j];
-            if (v > bv || (v == bv && j < bj)) {
-              bv = v;
-              bj = j;
-            }
-          }
-          warp_argmax(bv, bj);
-          if (r == 0) top0 = bv;
-          const float e = expf(bv - top0);
-          wsum += e;
-          if (lane == r) {
-            myv = e;
-            myid = bj;
-          }
-          __syncwarp();
-          if (lane == (bj & 31)) pa[bj] = -INFINITY;
-          __syncwarp();
-        }
-        if (lane < k) {
-          o.topk_ids[tok * k + lane] = myid;
-          if (o.topk_w) o.topk_w[tok * k + lane] = myv / wsum;
-        }
+      choice = bi;
+      const float nv = __ldg(n + (int64_t)(off + choice) * B + tok);
+      pc = nv / (nv + 1e-8f);
+      if (o.route_path) o.route_path[tok * t.L + l] = choice;
+      if (l < t.L - 1) {
+        const float* a = t.portals + (size_t)(off + choice) * 12;
+        const float lx = fmaf(__ldg(a + 0), cx, fmaf(__ldg(a + 1), cy, fmaf(__ldg(a + 2), cz, __ldg(a + 3))));
+        const float ly = fmaf(__ldg(a + 4), cx, fmaf(__ldg(a + 5), cy, fmaf(__ldg(a + 6), cz, __ldg(a + 7))));
+        const float lz = fmaf(__ldg(a + 8), cx, fmaf(__ldg(a + 9), cy, fmaf(__ldg(a + 10), cz, __ldg(a + 11))));
+        cx = lx * pc;
+        cy = ly * pc;
+        cz = lz * pc;
       }
+      prev = choice;
+    }
+    const int NL = t.nodes[t.L - 1];
+    const bool live = pc > 0.f;  // an all-zero row: argmax returns index 0
+    if (o.expert_id) o.expert_id[tok] = live ? choice : 0;
+    if (o.confidence) o.confidence[tok] = live ? pc : 0.f;
+    if (o.expert_probs)
+      for (int j = 0; j < NL; ++j) o.expert_probs[tok * NL + j] = (j == choice) ? pc : 0.f;
+    if (o.topk_ids) {
+      // top-k of a one-hot row: the chosen expert, then the lowest other ids
+      const int k = o.k;
+      const float v0 = live ? pc : 0.f;
+      const float e0 = 1.f, ez = expf(0.f - v0);
+      const float den = live ? e0 + (float)(k - 1) * ez : (float)k;
+      for (int i = 0; i < k; ++i) {
+        int id;
+        float w;
+        if (live) {
+          id = (i == 0) ? choice : ((i - 1 < choice) ? i - 1 : i);
+          w = (i == 0 ? e0 : ez) / den;
+        } else {
+          id = i;
+          w = 1.f / den;
+        }
+        o.topk_ids[tok * k + i] = id;
+        if (o.topk_w) o.topk_w[tok * k + i] = w;
+      }
+    }
+  }
+}
+
+constexpr int SOFT_WARPS = 8;
+
+// SOFT: one warp per token.  n is row-major: n[tok * total + node].
+// Shared memory: two probability buffers of max_nodes floats per warp.
+__global__ void __launch_bounds__(SOFT_WARPS * 32)
+    descent_soft_kernel(const float* __restrict__ pos, const float* __restrict__ n, int64_t B, TreeDev t,
+                        DescentOut o) {
+  extern __shared__ float dsm[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float* const pa0 = dsm + (size_t)warp * 2 * t.max_nodes;
+  float* const pb0 = pa0 + t.max_nodes;
+  for (int64_t tok = (int64_t)blockIdx.x * SOFT_WARPS + warp; tok < B; tok += (int64_t)gridDim.x * SOFT_WARPS) {
+    const float4 p4 = reinterpret_cast<const float4*>(pos)[tok];
+    float cx = p4.x, cy = p4.y, cz = p4.z;
+    const float* nrow = n + tok * (int64_t)t.total_nodes;
+    float* pa = pa0;
+    float* pb = pb0;
+    for (int l = 0; l < t.L; ++l) {
+      const int Nl = t.nodes[l], off = t.offset[l], nb = t.branching[l];
+      const float* cen = t.centers + (size_t)off * 3;
+      float mx = -INFINITY;
+      for (int j = lane; j < Nl; j += 32) {
+        const float dx = cx - __ldg(cen + 3 * j), dy = cy - __ldg(cen + 3 * j + 1),
+                    dz = cz - __ldg(cen + 3 * j + 2);
+        const float d2 = (dx * dx + dy * dy) + dz * dz;
+        float lg = -d2 / t.denom;
+        if (l > 0) lg = lg + logf(pa[j / nb] + 1e-10f);
+        lg = lg / t.tau;
+        pb[j] = lg;
+        mx = fmaxf(mx, lg);
+      }
+      mx = warp_max(mx);
+      float sum = 0.f;
+      for (int j = lane; j < Nl; j += 32) {
+        const float e = expf(pb[j] - mx);
+        pb[j] = e;
+        sum += e;
+      }
+      sum = warp_sum(sum);
+      float best = -INFINITY;
+      int bi = 0x7fffffff;
+      float tot = 0.f;
+      for (int j = lane; j < Nl; j += 32) {
+        const float pr = pb[j] / sum;
+        if (pr > best || (pr == best && j < bi)) {
+          best = pr;
+          bi = j;
+        }
+        const float v = pr * __ldg(nrow + off + j);
+        pb[j] = v;
+        tot += v;
+      }
+      warp_argmax(best, bi);
+      tot = warp_sum(tot);
+      const float den = tot + 1e-8f;
+      for (int j = lane; j < Nl; j += 32) pb[j] = pb[j] / den;
       __syncwarp();
+      // route_path holds the level-global node index (bvh_router.py:322)
+      if (o.route_path && lane == 0) o.route_path[tok * t.L + l] = bi;
+      if (l < t.L - 1) {
+        const float* A = t.portals + (size_t)off * 12;
+        float sx = 0.f, sy = 0.f, sz = 0.f;
+        for (int j = lane; j < Nl; j += 32) {
+          const float* a = A + (size_t)j * 12;
+          const float pj = pb[j];
+          sx += pj * fmaf(__ldg(a + 0), cx, fmaf(__ldg(a + 1), cy, fmaf(__ldg(a + 2), cz, __ldg(a + 3))));
+          sy += pj * fmaf(__ldg(a + 4), cx, fmaf(__ldg(a + 5), cy, fmaf(__ldg(a + 6), cz, __ldg(a + 7))));
+          sz += pj * fmaf(__ldg(a + 8), cx, fmaf(__ldg(a + 9), cy, fmaf(__ldg(a + 10), cz, __ldg(a + 11))));
+        }
+        cx = warp_sum(sx);
+        cy = warp_sum(sy);
+        cz = warp_sum(sz);
+      }
+      float* tmp = pa;
+      pa = pb;
+      pb = tmp;
+    }
+    // last level probabilities are in pa
+    const int NL = t.nodes[t.L - 1];
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int j = lane; j < NL; j += 32) {
+      const float v = pa[j];
+      if (o.expert_probs) o.expert_probs[tok * NL + j] = v;
+      if (v > best || (v == best && j < bi)) {
+        best = v;
+        bi = j;
+      }
+    }
+    warp_argmax(best, bi);
+    if (o.topk_ids) {
+      const int k = o.k;
+      float top0 = best, wsum = 0.f, myv = 0.f;
+      int myid = 0;
+      for (int r = 0; r < k; ++r) {
+        float bv = -INFINITY;
+        int bj = 0x7fffffff;
+        for (int j = lane; j < NL; j += 32) {
+          const float v = pa[j];
+          if (v > bv || (v == bv && j < bj)) {
+            bv = v;
+            bj = j;
+          }
+        }
+        warp_argmax(bv, bj);
+        if (r == 0) top0 = bv;
+        const float e = expf(bv - top0);
+        wsum += e;
+        if (lane == r) {
+          myv = e;
+          myid = bj;
+        }
+        __syncwarp();
+        if (lane == (bj & 31)) pa[bj] = -INFINITY;
+        __syncwarp();
+      }
+      if (lane < k) {
+        o.topk_ids[tok * k + lane] = myid;
+        if (o.topk_w) o.topk_w[tok * k + lane] = myv / wsum;
+      }
     }
     if (lane == 0) {
-      if (o.expert_id) o.expert_id[tok] = eid;
-      if (o.confidence) o.confidence[tok] = conf;
+      if (o.expert_id) o.expert_id[tok] = bi;
+      if (o.confidence) o.confidence[tok] = best;
     }
-    }  // tokens of the group
+    __syncwarp();
   }
 }
 
@@ -560,11 +509,14 @@ struct sb_router {
   int nodes[SB_MAX_LEVELS] = {};
   int offset[SB_MAX_LEVELS] = {};
   int max_nodes = 0;
+  int bn_ref = 32;  // tile width of the refraction GEMM
   float temperature = 1.f;
   bool uploaded = false;
   // device-resident parameters
   __nv_bfloat16* w1_bf16 = nullptr;  // [H,H]
   __nv_bfloat16* w2_bf16 = nullptr;  // [S,H]
+  __nv_bfloat16* w3s_bf16 = nullptr; // [16,H]: to_3d weights split hi, mid, lo (rows 0-8)
+  __nv_bfloat16* wr_bf16 = nullptr;  // [total,S] refraction weights
   float* w1_f32 = nullptr;           // [H,H]
   float* w2_f32 = nullptr;           // [S,H]
   float* b1 = nullptr;               // [H]
@@ -573,10 +525,9 @@ struct sb_router {
   float* b3d = nullptr;              // [3]
   float* centers = nullptr;          // [total,3]
   float* refw = nullptr;             // [total,S]
-  float* refwT = nullptr;            // [S,total] (soft-mode layout)
   float* refb = nullptr;             // [total]
   float* portals = nullptr;          // [total,12]
-  CUtensorMap tm_w1{}, tm_w2{};
+  CUtensorMap tm_w1{}, tm_w2{}, tm_w3s{}, tm_wr{};
 };
 
 namespace sb {
@@ -594,13 +545,13 @@ struct DeviceGuard {
 };
 
 void free_router_buffers(sb_router* h) {
-  void* ptrs[] = {h->w1_bf16, h->w2_bf16, h->w1_f32, h->w2_f32, h->b1,   h->b2,
-                  h->w3d,     h->b3d,     h->centers, h->refw,  h->refb, h->portals, h->refwT};
+  void* ptrs[] = {h->w1_bf16, h->w2_bf16, h->w3s_bf16, h->wr_bf16, h->w1_f32, h->w2_f32, h->b1,
+                  h->b2,      h->w3d,     h->b3d,      h->centers, h->refw,   h->refb,   h->portals};
   for (void* p : ptrs)
     if (p) cudaFree(p);
-  h->w1_bf16 = h->w2_bf16 = nullptr;
+  h->w1_bf16 = h->w2_bf16 = h->w3s_bf16 = h->wr_bf16 = nullptr;
   h->w1_f32 = h->w2_f32 = h->b1 = h->b2 = h->w3d = h->b3d = nullptr;
-  h->centers = h->refw = h->refb = h->portals = h->refwT = nullptr;
+  h->centers = h->refw = h->refb = h->portals = nullptr;
 }
 
 template <typename T>
@@ -615,13 +566,22 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ in, __nv_bfloat16* 
     out[i] = __float2bfloat16_rn(in[i]);
 }
 
-// out[c, r] = in[r, c] for a rows x cols matrix
-__global__ void transpose_f32_kernel(const float* __restrict__ in, float* __restrict__ out, int64_t rows,
-                                     int64_t cols) {
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < rows * cols;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = i / cols, c = i % cols;
-    out[c * rows + r] = in[i];
+// w [3,H] fp32 -> out [16,H] bf16 with rows c, 3+c, 6+c = hi, mid, lo of row c
+// (w = hi + mid + lo to within 2^-24 relative); rows 9..15 are zero.
+__global__ void split3_bf16_kernel(const float* __restrict__ w, int H, __nv_bfloat16* __restrict__ out) {
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < 16 * H; i += gridDim.x * blockDim.x) {
+    const int r = i / H, col = i % H;
+    __nv_bfloat16 v = __float2bfloat16_rn(0.f);
+    if (r < 9) {
+      const int c = r % 3, part = r / 3;
+      const float x = w[c * H + col];
+      const __nv_bfloat16 hi = __float2bfloat16_rn(x);
+      const float r1 = x - __bfloat162float(hi);
+      const __nv_bfloat16 mid = __float2bfloat16_rn(r1);
+      const float r2 = r1 - __bfloat162float(mid);
+      v = part == 0 ? hi : (part == 1 ? mid : __float2bfloat16_rn(r2));
+    }
+    out[i] = v;
   }
 }
 
@@ -636,17 +596,15 @@ int upload_f32(float* dst, const float* src, size_t count, float fill_if_null) {
 }
 
 }  // namespace
-
 }  // namespace sb
-
 
 extern "C" int sb_router_create(const sb_router_desc* desc, int device, sb_router** out) {
   SB_REQUIRE(desc && out, "sb_router_create: null argument");
   *out = nullptr;
   SB_REQUIRE(desc->hidden > 0 && desc->hidden % 8 == 0,
              "hidden=%d must be a positive multiple of 8", desc->hidden);
-  SB_REQUIRE(desc->spectral > 0 && desc->spectral <= 32 * sb::SPL_MAX,
-             "spectral=%d must be in [1, %d]", desc->spectral, 32 * sb::SPL_MAX);
+  SB_REQUIRE(desc->spectral > 0 && desc->spectral % 8 == 0 && desc->spectral <= 4096,
+             "spectral=%d must be a positive multiple of 8 (at most 4096)", desc->spectral);
   SB_REQUIRE(desc->n_levels >= 1 && desc->n_levels <= SB_MAX_LEVELS, "n_levels=%d must be in [1,%d]",
              desc->n_levels, SB_MAX_LEVELS);
   sb_router* h = new (std::nothrow) sb_router();
@@ -660,9 +618,9 @@ extern "C" int sb_router_create(const sb_router_desc* desc, int device, sb_route
       return sb::fail(SB_ERR_INVALID, "branching[%d]=%d must be >= 1", l, desc->branching[l]);
     }
     n *= desc->branching[l];
-    if (n > (1 << 20)) {
+    if (n > (1 << 16)) {
       delete h;
-      return sb::fail(SB_ERR_INVALID, "level %d has %d nodes (max 1048576)", l, n);
+      return sb::fail(SB_ERR_INVALID, "level %d has %d nodes (max 65536)", l, n);
     }
     h->nodes[l] = n;
     h->offset[l] = total;
@@ -670,6 +628,7 @@ extern "C" int sb_router_create(const sb_router_desc* desc, int device, sb_route
     if (n > h->max_nodes) h->max_nodes = n;
   }
   h->total_nodes = total;
+  h->bn_ref = total >= 256 ? 256 : (total + 31) / 32 * 32;
   *out = h;
   return SB_OK;
 }
@@ -700,10 +659,10 @@ extern "C" int sb_router_upload(sb_router* h, const sb_router_weights* w) {
   const size_t HH = (size_t)H * H, SH = (size_t)S * H, T = (size_t)h->total_nodes;
   if ((rc = dev_alloc(&h->w1_f32, HH)) || (rc = dev_alloc(&h->w2_f32, SH)) ||
       (rc = dev_alloc(&h->w1_bf16, HH)) || (rc = dev_alloc(&h->w2_bf16, SH)) ||
+      (rc = dev_alloc(&h->w3s_bf16, (size_t)16 * H)) || (rc = dev_alloc(&h->wr_bf16, T * S)) ||
       (rc = dev_alloc(&h->b1, (size_t)H)) || (rc = dev_alloc(&h->b2, (size_t)S)) ||
       (rc = dev_alloc(&h->w3d, (size_t)3 * H)) || (rc = dev_alloc(&h->b3d, (size_t)3)) ||
       (rc = dev_alloc(&h->centers, T * 3)) || (rc = dev_alloc(&h->refw, T * S)) ||
-      (rc = dev_alloc(&h->refwT, T * S)) ||
       (rc = dev_alloc(&h->refb, T)) || (rc = dev_alloc(&h->portals, T * 12))) {
     free_router_buffers(h);
     return rc;
@@ -731,15 +690,20 @@ extern "C" int sb_router_upload(sb_router* h, const sb_router_weights* w) {
       SB_CUDA_TRY(cudaMemset(h->portals + off * 12, 0, n * 12 * sizeof(float)));
     }
   }
-  transpose_f32_kernel<<<256, 256>>>(h->refw, h->refwT, (int64_t)T, (int64_t)S);
   f32_to_bf16_kernel<<<1024, 256>>>(h->w1_f32, h->w1_bf16, (int64_t)HH);
   f32_to_bf16_kernel<<<256, 256>>>(h->w2_f32, h->w2_bf16, (int64_t)SH);
+  f32_to_bf16_kernel<<<256, 256>>>(h->refw, h->wr_bf16, (int64_t)(T * S));
+  split3_bf16_kernel<<<64, 256>>>(h->w3d, H, h->w3s_bf16);
   SB_CUDA_TRY(cudaGetLastError());
   SB_CUDA_TRY(cudaDeviceSynchronize());
   if ((rc = make_tmap_2d(&h->tm_w1, h->w1_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, H, H,
                          GEMM_BK, 256, CU_TENSOR_MAP_SWIZZLE_128B)) ||
       (rc = make_tmap_2d(&h->tm_w2, h->w2_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, S, H, H,
-                         GEMM_BK, S <= 128 ? 128 : 256, CU_TENSOR_MAP_SWIZZLE_128B))) {
+                         GEMM_BK, S <= 128 ? 128 : 256, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&h->tm_w3s, h->w3s_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 16, H, H,
+                         GEMM_BK, TAIL_N, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&h->tm_wr, h->wr_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, S, S,
+                         GEMM_BK, (uint32_t)h->bn_ref, CU_TENSOR_MAP_SWIZZLE_128B))) {
     free_router_buffers(h);
     return rc;
   }
@@ -750,19 +714,27 @@ extern "C" int sb_router_upload(sb_router* h, const sb_router_weights* w) {
 
 namespace sb {
 namespace {
-size_t ws_g_bytes(const sb_router* h, int64_t B, int precision) {
+
+struct RouterWs {
+  size_t g, spec, pos, n, total;
+};
+
+RouterWs router_ws(const sb_router* h, int64_t B, int precision) {
+  RouterWs w{};
   const size_t el = precision == SB_PREC_FAST ? 2 : 4;
-  return align_up((size_t)B * h->desc.hidden * el, 1024);
-}
-size_t ws_spec_bytes(const sb_router* h, int64_t B) {
-  return align_up((size_t)B * h->desc.spectral * 4, 1024);
+  w.g = 0;
+  w.spec = align_up((size_t)B * h->desc.hidden * el, 1024);
+  w.pos = w.spec + align_up((size_t)B * h->desc.spectral * el, 1024);
+  w.n = w.pos + align_up((size_t)B * 16, 1024);
+  w.total = w.n + align_up((size_t)B * h->total_nodes * 4, 1024);
+  return w;
 }
 
-template <int BN, int STAGES, class Epi>
-int launch_gemm_tc(const char* name, const CUtensorMap& ta, const CUtensorMap& tb, int M, int N,
-                   int K, Epi epi, cudaStream_t stream) {
+template <int BN, int STAGES, class Epi, bool TAIL = false>
+int launch_gemm_tc(const char* name, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2,
+                   int M, int N, int K, Epi epi, cudaStream_t stream) {
   using C = GemmCfg<BN, STAGES>;
-  auto kern = gemm_tc_kernel<BN, STAGES, Epi>;
+  auto kern = gemm_tc_kernel<BN, STAGES, Epi, TAIL>;
   static bool attr_done[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -770,19 +742,21 @@ int launch_gemm_tc(const char* name, const CUtensorMap& ta, const CUtensorMap& t
     SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
     attr_done[dev] = true;
   }
-  const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN);
+  const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN + (TAIL ? 1 : 0));
   const int grid = tiles < num_sms() ? tiles : num_sms();
   ProfScope prof(name, stream);
-  kern<<<grid, GEMM_THREADS, C::SMEM_BYTES, stream>>>(ta, tb, M, N, K, idesc_f16(1, GEMM_BM, BN), epi);
+  kern<<<grid, GEMM_THREADS, C::SMEM_BYTES, stream>>>(ta, tb, tb2, M, N, K, idesc_f16(1, GEMM_BM, BN),
+                                                      idesc_f16(1, GEMM_BM, TAIL_N), epi);
   SB_CUDA_TRY(cudaGetLastError());
   return SB_OK;
 }
+
 }  // namespace
 }  // namespace sb
 
 extern "C" size_t sb_router_workspace_bytes(const sb_router* h, int64_t batch, int precision) {
   if (!h || batch < 0) return 0;
-  return sb::ws_g_bytes(h, batch, precision) + sb::ws_spec_bytes(h, batch);
+  return sb::router_ws(h, batch, precision).total;
 }
 
 extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64_t batch,
@@ -805,97 +779,134 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
   if (batch == 0) return SB_OK;
   SB_REQUIRE(x != nullptr, "x is null");
   SB_REQUIRE((reinterpret_cast<uintptr_t>(x) & 15u) == 0, "x must be 16-byte aligned");
-  const size_t need = sb_router_workspace_bytes(h, batch, precision);
-  if (!workspace || workspace_bytes < need)
-    return fail(SB_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, need);
+  const RouterWs W = router_ws(h, batch, precision);
+  if (!workspace || workspace_bytes < W.total)
+    return fail(SB_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, W.total);
   SB_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 1023u) == 0, "workspace must be 1024-byte aligned");
   SB_REQUIRE(batch <= (int64_t)INT32_MAX / 2, "batch=%lld too large", (long long)batch);
+  const size_t dsm_soft = (size_t)SOFT_WARPS * 2 * h->max_nodes * sizeof(float);
+  SB_REQUIRE(select != SB_SELECT_SOFT || dsm_soft <= 227 * 1024,
+             "SOFT selection with %d nodes per level exceeds shared memory", h->max_nodes);
   DeviceGuard g(h->device);
   cudaStream_t stream = reinterpret_cast<cudaStream_t>(stream_);
-  const int H = h->desc.hidden, S = h->desc.spectral;
+  const int H = h->desc.hidden, S = h->desc.spectral, T = h->total_nodes;
   const int M = (int)batch;
   uint8_t* ws = static_cast<uint8_t*>(workspace);
-  void* G = ws;
-  float* spec = reinterpret_cast<float*>(ws + ws_g_bytes(h, batch, precision));
+  void* G = ws + W.g;
+  void* spec = ws + W.spec;
+  float* pos = reinterpret_cast<float*>(ws + W.pos);
+  float* nbuf = reinterpret_cast<float*>(ws + W.n);
+  const int node_major = select == SB_SELECT_HARD;
+  const int64_t ldn = node_major ? batch : T;
   int rc;
   if (precision == SB_PREC_FAST) {
-    CUtensorMap ta, tg;
+    CUtensorMap ta, tg, ts;
     if ((rc = make_tmap_2d(&ta, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, H, H, GEMM_BK, GEMM_BM,
+                           CU_TENSOR_MAP_SWIZZLE_128B)) ||
+        (rc = make_tmap_2d(&tg, G, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, H, H, GEMM_BK, GEMM_BM,
+                           CU_TENSOR_MAP_SWIZZLE_128B)) ||
+        (rc = make_tmap_2d(&ts, spec, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, S, S, GEMM_BK, GEMM_BM,
                            CU_TENSOR_MAP_SWIZZLE_128B)))
       return rc;
-    if ((rc = make_tmap_2d(&tg, G, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, H, H, GEMM_BK, GEMM_BM,
-                           CU_TENSOR_MAP_SWIZZLE_128B)))
+    EpiGeluBf16 e1{h->b1, static_cast<__nv_bfloat16*>(G), H, H, h->b3d, pos};
+    if ((rc = launch_gemm_tc<256, 4, EpiGeluBf16, true>("router_enc1_gelu_tc", ta, h->tm_w1, h->tm_w3s, M, H,
+                                                         H, e1, stream)))
       return rc;
-    EpiGeluBf16 e1{h->b1, static_cast<__nv_bfloat16*>(G), H, H};
-    if ((rc = launch_gemm_tc<256, 4>("router_enc1_gelu_tc", ta, h->tm_w1, M, H, H, e1, stream))) return rc;
-    EpiTanhF32 e2{h->b2, spec, S, S};
+    EpiTanhBf16 e2{h->b2, static_cast<__nv_bfloat16*>(spec), S, S};
     if (S <= 128) {  // tm_w2's box height matches this tile width (set at upload)
-      if ((rc = launch_gemm_tc<128, 4>("router_enc2_tanh_tc", tg, h->tm_w2, M, S, H, e2, stream))) return rc;
+      if ((rc = launch_gemm_tc<128, 4>("router_enc2_tanh_tc", tg, h->tm_w2, h->tm_w2, M, S, H, e2, stream)))
+        return rc;
     } else {
-      if ((rc = launch_gemm_tc<256, 4>("router_enc2_tanh_tc", tg, h->tm_w2, M, S, H, e2, stream))) return rc;
+      if ((rc = launch_gemm_tc<256, 4>("router_enc2_tanh_tc", tg, h->tm_w2, h->tm_w2, M, S, H, e2, stream)))
+        return rc;
     }
+    EpiSigmoidN e3{h->refb, nbuf, ldn, T, node_major};
+    switch (h->bn_ref) {  // tm_wr's box height matches this tile width (set at create)
+      case 32: rc = launch_gemm_tc<32, 4>("router_refract_tc", ts, h->tm_wr, h->tm_wr, M, T, S, e3, stream); break;
+      case 64: rc = launch_gemm_tc<64, 4>("router_refract_tc", ts, h->tm_wr, h->tm_wr, M, T, S, e3, stream); break;
+      case 96: rc = launch_gemm_tc<96, 4>("router_refract_tc", ts, h->tm_wr, h->tm_wr, M, T, S, e3, stream); break;
+      case 128: rc = launch_gemm_tc<128, 4>("router_refract_tc", ts, h->tm_wr, h->tm_wr, M, T, S, e3, stream); break;
+      case 160: rc = launch_gemm_tc<160, 4>("router_refract_tc", ts, h->tm_wr, h->tm_wr, M, T, S, e3, stream); break;
+      case 192: rc = launch_gemm_tc<192, 4>("router_refract_tc", ts, h->tm_wr, h->tm_wr, M, T, S, e3, stream); break;
+      case 224: rc = launch_gemm_tc<224, 4>("router_refract_tc", ts, h->tm_wr, h->tm_wr, M, T, S, e3, stream); break;
+      default: rc = launch_gemm_tc<256, 4>("router_refract_tc", ts, h->tm_wr, h->tm_wr, M, T, S, e3, stream); break;
+    }
+    if (rc) return rc;
   } else {
-    dim3 grid1((H + 127) / 128, (M + 127) / 128), grid2((S + 127) / 128, (M + 127) / 128);
+    dim3 grid1((H + 127) / 128, (M + 127) / 128), grid2((S + 127) / 128, (M + 127) / 128),
+        grid3((T + 127) / 128, (M + 127) / 128);
     float* G32 = static_cast<float*>(G);
+    float* S32 = static_cast<float*>(spec);
     {
       ProfScope prof1("router_enc1_gelu_f32", stream);
       if (x_dtype == SB_BF16)
         sgemm_nt_kernel<__nv_bfloat16, ACT_GELU><<<grid1, 256, 0, stream>>>(
-            static_cast<const __nv_bfloat16*>(x), h->w1_f32, h->b1, G32, M, H, H);
+            static_cast<const __nv_bfloat16*>(x), h->w1_f32, h->b1, G32, M, H, H, H, 0);
       else
-        sgemm_nt_kernel<float, ACT_GELU><<<grid1, 256, 0, stream>>>(static_cast<const float*>(x),
-                                                                   h->w1_f32, h->b1, G32, M, H, H);
+        sgemm_nt_kernel<float, ACT_GELU><<<grid1, 256, 0, stream>>>(static_cast<const float*>(x), h->w1_f32,
+                                                                   h->b1, G32, M, H, H, H, 0);
       SB_CUDA_TRY(cudaGetLastError());
     }
     {
       ProfScope prof2("router_enc2_tanh_f32", stream);
-      sgemm_nt_kernel<float, ACT_TANH><<<grid2, 256, 0, stream>>>(G32, h->w2_f32, h->b2, spec, M, S, H);
+      sgemm_nt_kernel<float, ACT_TANH><<<grid2, 256, 0, stream>>>(G32, h->w2_f32, h->b2, S32, M, S, H, S, 0);
+      SB_CUDA_TRY(cudaGetLastError());
+    }
+    {
+      ProfScope prof3("router_refract_f32", stream);
+      sgemm_nt_kernel<float, ACT_SIGMOID><<<grid3, 256, 0, stream>>>(S32, h->refw, h->refb, nbuf, M, T, S,
+                                                                     ldn, node_major);
+      SB_CUDA_TRY(cudaGetLastError());
+    }
+    {
+      ProfScope prof4("router_pos_f32", stream);
+      int64_t blocks = (batch * 32 + 255) / 256;
+      if (blocks > (int64_t)num_sms() * 16) blocks = (int64_t)num_sms() * 16;
+      if (x_dtype == SB_BF16)
+        pos_f32_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(x), h->w3d, h->b3d, batch, H, pos);
+      else
+        pos_f32_kernel<float><<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const float*>(x), h->w3d,
+                                                                    h->b3d, batch, H, pos);
       SB_CUDA_TRY(cudaGetLastError());
     }
   }
   TreeDev t{};
   t.L = L;
-  t.S = S;
-  t.H = H;
   for (int l = 0; l < L; ++l) {
     t.branching[l] = h->desc.branching[l];
     t.nodes[l] = h->nodes[l];
     t.offset[l] = h->offset[l];
   }
+  t.total_nodes = T;
   t.max_nodes = h->max_nodes;
-  const float T = h->temperature;
-  t.denom = 2.0f * (T * T) + 1e-8f;
-  t.tau = T < 0.01f ? 0.01f : T;
-  t.w3d = h->w3d;
-  t.b3d = h->b3d;
+  const float Tm = h->temperature;
+  t.denom = 2.0f * (Tm * Tm) + 1e-8f;
+  t.tau = Tm < 0.01f ? 0.01f : Tm;
   t.centers = h->centers;
-  t.refw = h->refw;
-  t.refwT = h->refwT;
-  t.total_nodes = h->total_nodes;
-  t.refb = h->refb;
   t.portals = h->portals;
   DescentOut o{out->topk_ids, out->topk_weights, out->expert_id, out->expert_probs,
                out->route_path, out->confidence, top_k};
-  const size_t dsm = (size_t)3 * H * sizeof(float) +
-                     (select == SB_SELECT_SOFT ? (size_t)DESC_WARPS * (2 * h->max_nodes + S) * sizeof(float) : 0);
-  if (dsm > 48 * 1024) {
-    static bool attr[2] = {false, false};
-    auto k0 = descent_kernel<float>;
-    auto k1 = descent_kernel<__nv_bfloat16>;
-    SB_REQUIRE(dsm <= 227 * 1024, "soft mode with %d nodes per level exceeds shared memory", h->max_nodes);
-    if (!attr[0]) { SB_CUDA_TRY(cudaFuncSetAttribute(k0, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)); attr[0] = true; }
-    if (!attr[1]) { SB_CUDA_TRY(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024)); attr[1] = true; }
-  }
-  int64_t blocks = (batch + DESC_WARPS * DESC_TPW - 1) / (DESC_WARPS * DESC_TPW);
-  const int64_t cap = (int64_t)num_sms() * 8;
-  if (blocks > cap) blocks = cap;
   ProfScope prof("router_descent", stream);
-  if (x_dtype == SB_BF16)
-    descent_kernel<__nv_bfloat16><<<(unsigned)blocks, DESC_WARPS * 32, dsm, stream>>>(
-        static_cast<const __nv_bfloat16*>(x), spec, batch, t, select == SB_SELECT_SOFT, o);
-  else
-    descent_kernel<float><<<(unsigned)blocks, DESC_WARPS * 32, dsm, stream>>>(
-        static_cast<const float*>(x), spec, batch, t, select == SB_SELECT_SOFT, o);
+  if (select == SB_SELECT_HARD) {
+    int64_t blocks = (batch + 255) / 256;
+    const int64_t cap = (int64_t)num_sms() * 16;
+    if (blocks > cap) blocks = cap;
+    descent_hard_kernel<<<(unsigned)blocks, 256, 0, stream>>>(pos, nbuf, batch, t, o);
+  } else {
+    if (dsm_soft > 48 * 1024) {
+      static bool attr = false;
+      if (!attr) {
+        SB_CUDA_TRY(cudaFuncSetAttribute(descent_soft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         227 * 1024));
+        attr = true;
+      }
+    }
+    int64_t blocks = (batch + SOFT_WARPS - 1) / SOFT_WARPS;
+    const int64_t cap = (int64_t)num_sms() * 8;
+    if (blocks > cap) blocks = cap;
+    descent_soft_kernel<<<(unsigned)blocks, SOFT_WARPS * 32, dsm_soft, stream>>>(pos, nbuf, batch, t, o);
+  }
   SB_CUDA_TRY(cudaGetLastError());
   return SB_OK;
 }
