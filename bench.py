@@ -11,12 +11,17 @@ Workloads (seeded synthetic inputs with BASELINE.json's shapes; no datasets):
              weights) over 4096 bf16 tokens per GPU (config 2).  L2 is flushed
              (256 MiB write) before every timed step; each step is timed with
              its own CUDA event pair and the flush stays outside them.
+  ep         (N > 1) the same layer expert-parallel: 64/N experts per GPU,
+             NCCL all-to-all dispatch of bf16 token rows and combine of fp32
+             expert outputs.  Reported inside the line as "ep".
   router     BVH router forward alone at B = 262144 bf16 tokens (config 1);
              1 GiB of input per GPU > L2, so no flush.  Reported inside the
              moe_layer line as "router".
 
-One process per GPU (torchrun for N > 1).  Router work shards by token with no
-collective; every rank runs its own token shard (weak scaling).  Timing: W
+One process per GPU (torchrun for N > 1).  The headline shards tokens with no
+collective: every rank routes its own 4096 tokens and runs them through its
+own copy of the 64 experts (100 MB of 2-bit weights, replicated; weak
+scaling).  Timing: W
 warm-up steps, then exactly K timed steps on the launching stream, bracketed
 by barrier + synchronize, max over ranks.
 
@@ -270,6 +275,33 @@ def moe_workload(batch: int, device, select: str = "soft"):
     return step, e2e_step, meta
 
 
+def ep_workload(batch: int, device, world: int, select: str = "soft"):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from bvh_router import BVHRouter, RouterConfig
+    from sb200 import synth
+    from sb200.ep import ExpertParallelMoE
+    from sb200.ternary import TernaryExperts
+    rank = dist.get_rank()
+    w = synth.router_weights(H, S, BRANCHING, seed=0)
+    r = BVHRouter(RouterConfig(embed_dim=H, spectral_dim=S))
+    r.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in w.items()})
+    r = r.to(device).eval()
+    e_local = E_EXPERTS // world
+    allx = synth.ternary_experts(E_EXPERTS, H, I_INTER, seed=2)
+    local = TernaryExperts(allx[rank * e_local:(rank + 1) * e_local], device)
+    layer = ExpertParallelMoE(lambda rows, ids, ww: local.forward(rows, ids, ww, out_dtype=torch.float32),
+                              E_EXPERTS)
+    x = synth.hidden_states(batch, H, seed=2 + 1000 * rank, dtype=torch.bfloat16, device=device)
+
+    def step():
+        ids, wts = r.forward_topk(x, k=TOPK, select=select)
+        layer(x, ids, wts, out_dtype=torch.bfloat16)
+
+    return step, {}
+
+
 def time_steps(step, steps, warmup, world, sampler=None, profile=False, flush=None):
     import torch
     from sb200 import _lib
@@ -358,6 +390,16 @@ def run_ours(a):
                            "share": round(t / max(sum(v[1] for v in prof.values()), 1e-9), 4)}
                        for k, (n, t) in prof.items()},
            "roofline": roofline_tensor(meta, prof, pk, total_ms, a.steps), "clocks": clocks}
+    # ---- expert-parallel form of the same layer (N > 1): E/N experts per GPU,
+    #      NCCL all-to-all dispatch and combine
+    if world > 1 and not a.skip_ep:
+        estep, emeta = ep_workload(batch, dev, world)
+        ep_ms, eprof = time_steps(estep, a.steps, a.warmup, world, profile=True, flush=flush)
+        out["ep"] = {"metric": "MoE-layer tokens/s, expert parallel", "unit": "tokens/s",
+                     "value": round(tokens / (ep_ms / 1e3), 1), "ms_per_step": round(ep_ms / a.steps, 4),
+                     "experts_per_gpu": E_EXPERTS // world,
+                     "parallelism": f"ep{world}: NCCL all_to_all_single dispatch (bf16 rows) + combine (fp32)",
+                     "kernels": {k: {"launches": n, "avg_ms": round(t / max(n, 1), 4)} for k, (n, t) in eprof.items()}}
     # ---- router alone (config 1), same process
     if not a.skip_router:
         rstep, _, rmeta = router_workload(a.router_batch, dev)
@@ -477,6 +519,7 @@ def main():
     ap.add_argument("--router-batch", type=int, default=262144)
     ap.add_argument("--router-steps", type=int, default=100)
     ap.add_argument("--skip-router", action="store_true")
+    ap.add_argument("--skip-ep", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     a = ap.parse_args()
