@@ -49,3 +49,14 @@ def test_anneal_and_balance_bookkeeping():
     r.anneal_temperature()
     assert abs(r.temperature.item() - 0.95) < 1e-6
     assert r.load_balancing_loss().item() == 0.0
+
+
+def test_facade_and_hybrid_router_surface():
+    import spectral_ai
+    from bvh_router_bridge import HybridBVHRouter
+    for name in ("BVHRouter", "RouterConfig", "RoutingResult", "HybridBVHRouter", "BVHMoELayer"):
+        assert hasattr(spectral_ai, name)
+    h = HybridBVHRouter(spectral_ai.RouterConfig(embed_dim=64, spectral_dim=16))
+    assert all(k.startswith("pytorch_router.") for k in h.state_dict())
+    h.anneal_temperature()
+    assert h.load_balancing_loss().item() == 0.0
