@@ -15,6 +15,10 @@
 // where M << P is the magnitude pattern of 1.0 (bf16: 0x7F << 7, fp16: 0xF << 10).
 #include "common.cuh"
 #include "ternary_gemm.cuh"
+#include "ternary_ts.cuh"
+
+#include <cstdlib>
+#include <cstring>
 
 namespace sb {
 
@@ -314,6 +318,30 @@ int launch_tgemm(const char* name, const CUtensorMap& ta, const CUtensorMap& tb0
   return SB_OK;
 }
 
+template <int MODE, int FMT>
+int launch_ts(const char* name, const CUtensorMap& tx, const CUtensorMap& tw0, const CUtensorMap& tw1,
+              const TernGemmParams& p, cudaStream_t stream) {
+  auto kern = ternary_ts_kernel<MODE, FMT>;
+  static bool attr_done[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && !attr_done[dev]) {
+    SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TS_SMEM_BYTES));
+    attr_done[dev] = true;
+  }
+  ProfScope prof(name, stream);
+  kern<<<num_sms(), TS_THREADS, TS_SMEM_BYTES, stream>>>(tx, tw0, tw1, p);
+  SB_CUDA_TRY(cudaGetLastError());
+  return SB_OK;
+}
+
+// Which grouped ternary GEMM runs: "ts" (weights in TMEM, the default) or
+// "ss" (weights unpacked into shared memory), from SB_TERNARY_ENGINE.
+bool use_ts_engine() {
+  const char* e = getenv("SB_TERNARY_ENGINE");
+  return !(e && strcmp(e, "ss") == 0);
+}
+
 int check_ternary_shapes(int64_t H, int64_t I) {
   SB_REQUIRE(H > 0 && I > 0, "hidden=%lld and intermediate=%lld must be positive", (long long)H, (long long)I);
   SB_REQUIRE(H <= (1 << 20) && I <= (1 << 20), "dimensions too large");
@@ -377,24 +405,26 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   }
 
   // tensor maps: activations (SW128, 64 x 128 box) and packed weights (16 B x rows box)
+  const bool ts = use_ts_engine();
   CUtensorMap tmx, tmg, tmu, tmh, tmd;
   const CUtensorMapDataType adt = fmt_gu ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const int64_t KWh = ternary_row_words(H), KWi = ternary_row_words(I);
+  const uint32_t gu_box = ts ? 64 : 128, d_box = ts ? 128 : 256;
   if ((rc = make_tmap_2d(&tmx, xp, adt, 2, L.R, H, L.ldx, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) ||
-      (rc = make_tmap_2d(&tmg, gate, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, 4, 128,
+      (rc = make_tmap_2d(&tmg, gate, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, 4, gu_box,
                          CU_TENSOR_MAP_SWIZZLE_NONE)) ||
-      (rc = make_tmap_2d(&tmu, up, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, 4, 128,
+      (rc = make_tmap_2d(&tmu, up, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, 4, gu_box,
                          CU_TENSOR_MAP_SWIZZLE_NONE)) ||
       (rc = make_tmap_2d(&tmh, hp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.R, I, L.ldh, 64, 128,
                          CU_TENSOR_MAP_SWIZZLE_128B)) ||
-      (rc = make_tmap_2d(&tmd, down, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * H, KWi, KWi, 4, 256,
+      (rc = make_tmap_2d(&tmd, down, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * H, KWi, KWi, 4, d_box,
                          CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
 
   TernGemmParams pg{};
   pg.mtiles = mtiles;
   pg.num_mtiles = nmt;
-  pg.n_ntiles = (int)((I + 127) / 128);
+  pg.n_ntiles = ts ? (int)((I + 63) / 64) : (int)((I + 127) / 128);
   pg.N = (int)I;
   pg.K = (int)H;
   pg.b_rows = (int)I;
@@ -402,16 +432,18 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   pg.s1 = us;
   pg.out = hp;
   pg.ldo = L.ldh;
-  if (fmt_gu)
-    rc = launch_tgemm<TG_GATEUP, 1>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream);
+  if (ts)
+    rc = fmt_gu ? launch_ts<TG_GATEUP, 1>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream)
+                : launch_ts<TG_GATEUP, 0>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream);
   else
-    rc = launch_tgemm<TG_GATEUP, 0>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream);
+    rc = fmt_gu ? launch_tgemm<TG_GATEUP, 1>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream)
+                : launch_tgemm<TG_GATEUP, 0>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream);
   if (rc) return rc;
 
   TernGemmParams pd{};
   pd.mtiles = mtiles;
   pd.num_mtiles = nmt;
-  pd.n_ntiles = (int)((H + 255) / 256);
+  pd.n_ntiles = ts ? (int)((H + 127) / 128) : (int)((H + 255) / 256);
   pd.N = (int)H;
   pd.K = (int)I;
   pd.b_rows = (int)H;
@@ -419,7 +451,11 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   pd.row_w = row_w;
   pd.out = yp;
   pd.ldo = H;
-  if ((rc = launch_tgemm<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, pd, stream))) return rc;
+  if (ts)
+    rc = launch_ts<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, pd, stream);
+  else
+    rc = launch_tgemm<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, pd, stream);
+  if (rc) return rc;
 
   {
     ProfScope prof("moe_combine", stream);
@@ -538,13 +574,13 @@ extern "C" int sb_ternary_linear(const void* x, int x_dtype, int64_t M, int64_t 
   const int64_t KW = ternary_row_words(K);
   if ((rc = make_tmap_2d(&tmx, xp, fmt ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, M,
                          K, L.ldx, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) ||
-      (rc = make_tmap_2d(&tmw, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)N, KW, KW, 4, 256,
-                         CU_TENSOR_MAP_SWIZZLE_NONE)))
+      (rc = make_tmap_2d(&tmw, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)N, KW, KW, 4,
+                         use_ts_engine() ? 128 : 256, CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
   TernGemmParams pl{};
   pl.mtiles = mtiles;
   pl.num_mtiles = nmt;
-  pl.n_ntiles = (int)((N + 255) / 256);
+  pl.n_ntiles = use_ts_engine() ? (int)((N + 127) / 128) : (int)((N + 255) / 256);
   pl.N = (int)N;
   pl.K = (int)K;
   pl.b_rows = (int)N;
@@ -552,6 +588,10 @@ extern "C" int sb_ternary_linear(const void* x, int x_dtype, int64_t M, int64_t 
   pl.bias = bias;
   pl.out = y;
   pl.ldo = N;
+  if (use_ts_engine()) {
+    if (fmt) return launch_ts<TG_LINEAR, 1>("ternary_linear_tc", tmx, tmw, tmw, pl, st);
+    return launch_ts<TG_LINEAR, 0>("ternary_linear_tc", tmx, tmw, tmw, pl, st);
+  }
   if (fmt) return launch_tgemm<TG_LINEAR, 1>("ternary_linear_tc", tmx, tmw, tmw, pl, st);
   return launch_tgemm<TG_LINEAR, 0>("ternary_linear_tc", tmx, tmw, tmw, pl, st);
 }

@@ -1,0 +1,304 @@
+// ternary_ts.cuh — grouped ternary GEMM with the weights as the TMEM operand.
+//
+//   D^T[c, t] = sum_k W[e][c, k] * X[t, k]     (c: output channel, t: token row)
+//
+// The ternary weights are the A operand and live in tensor memory: four unpack
+// warps read the 2-bit split-plane words of a 128-channel x 64-K block (TMA'd
+// into a 2 KB staging buffer), expand them in registers to 16-bit +-1/0 and
+// write them straight into TMEM with tcgen05.st (lane = channel, two K values
+// per 32-bit column).  Shared memory carries only the 128-token x 64-K
+// activation tile (TMA, 128-byte swizzle, no multicast) that is the B operand,
+// so the unpack no longer competes with the MMA for shared-memory bandwidth.
+//
+//   tcgen05.mma.cta_group::1.kind::f16 [D], [A_tmem], B_smem_desc, idesc
+//   M = 128 channels, N = 128 tokens, K = 16 per instruction, fp32 in TMEM.
+//
+// GATEUP tiles interleave channels: A rows 0-63 are gate channels c0..c0+63,
+// rows 64-127 the up channels c0..c0+63, so one accumulator holds both and the
+// epilogue pairs them through shared memory.  TMEM: two accumulators of 128
+// columns (the epilogue of one tile overlaps the next tile's MMAs) plus
+// TS_STAGES A stages of 32 columns.
+//
+// Roles (384 threads): warp 0 TMA producer, warp 1 MMA issuer, warp 2 TMEM
+// allocator, warps 4..7 epilogue, warps 8..11 unpack (warp w owns TMEM lanes
+// 32*(w%4)..+31 in both roles).
+#pragma once
+
+#include "sm100.cuh"
+#include "ternary_gemm.cuh"
+
+namespace sb {
+
+constexpr int TS_THREADS = 384;
+constexpr int TS_STAGES = 6;
+constexpr int TS_N = 128;                          // tokens per tile
+constexpr int TS_X_BYTES = TS_N * 64 * 2;          // 16 KB activation tile
+constexpr int TS_P_BYTES = 128 * 16;               // 2 KB packed weights
+constexpr int TS_STAGE_BYTES = TS_X_BYTES + TS_P_BYTES;  // 18 KB (1024-multiple)
+constexpr int TS_U_BYTES = TS_N * 64 * 4;          // up-projection exchange (GATEUP)
+constexpr int TS_BAR_BYTES = (3 * TS_STAGES + 6) * 8 + 16;
+constexpr int TS_SMEM_BYTES = TS_STAGES * TS_STAGE_BYTES + TS_U_BYTES + TS_BAR_BYTES + 1024;
+constexpr uint32_t TS_TMEM_COLS = 512;
+constexpr uint32_t TS_D_COLS = 2 * TS_N;           // accumulators at columns [0, 256)
+static_assert(TS_STAGE_BYTES % 1024 == 0, "stage alignment");
+static_assert(TS_D_COLS + 32 * TS_STAGES <= TS_TMEM_COLS, "TMEM budget");
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+// D[tmem] (+)= A[tmem] * B[smem]^T, kind::f16.
+__device__ __forceinline__ void umma_ts_f16(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                            uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+template <int MODE, int FMT>
+__global__ void __launch_bounds__(TS_THREADS, 1)
+    ternary_ts_kernel(const __grid_constant__ CUtensorMap tmX,
+                      const __grid_constant__ CUtensorMap tmW0,
+                      const __grid_constant__ CUtensorMap tmW1, TernGemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  float* ubuf = reinterpret_cast<float*>(smem + TS_STAGES * TS_STAGE_BYTES);  // [TS_N][64]
+  uint64_t* full_tma = reinterpret_cast<uint64_t*>(smem + TS_STAGES * TS_STAGE_BYTES + TS_U_BYTES);
+  uint64_t* full_a = full_tma + TS_STAGES;
+  uint64_t* empty = full_a + TS_STAGES;
+  uint64_t* tfull = empty + TS_STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* u_full = tempty + 2;   // GATEUP: up values of a tile are in ubuf
+  uint64_t* u_empty = u_full + 1;  // GATEUP: gate warps are done reading ubuf
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(u_empty + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_mt = *p.num_mtiles;
+  const int num_tiles = n_mt * p.n_ntiles;
+  const int kblocks = (p.K + 63) / 64;
+  // channels per tile of one matrix: GATEUP holds 64 gate + 64 up channels
+  constexpr int CH = (MODE == TG_GATEUP) ? 64 : 128;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TS_STAGES; ++s) {
+      mbar_init(&full_tma[s], 1);
+      mbar_init(&full_a[s], 4);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&tfull[i], 1);
+      mbar_init(&tempty[i], 4);
+    }
+    mbar_init(u_full, 2);
+    mbar_init(u_empty, 2);
+    fence_barrier_init();
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, TS_TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      tma_prefetch_desc(&tmX);
+      tma_prefetch_desc(&tmW0);
+      if (MODE == TG_GATEUP) tma_prefetch_desc(&tmW1);
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+        const MTile mt = p.mtiles[tile / p.n_ntiles];
+        const int c0 = (tile % p.n_ntiles) * CH;
+        const int wrow = mt.expert * p.b_rows + c0;
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, ST_TIMEOUT_PRODUCER)) goto done;
+          uint8_t* st = smem + stage * TS_STAGE_BYTES;
+          mbar_arrive_expect_tx(&full_tma[stage], TS_X_BYTES + TS_P_BYTES);
+          tma_load_2d(st, &tmX, &full_tma[stage], kb * 64, mt.row0);
+          if (MODE == TG_GATEUP) {
+            tma_load_2d(st + TS_X_BYTES, &tmW0, &full_tma[stage], kb * 4, wrow);
+            tma_load_2d(st + TS_X_BYTES + TS_P_BYTES / 2, &tmW1, &full_tma[stage], kb * 4, wrow);
+          } else {
+            tma_load_2d(st + TS_X_BYTES, &tmW0, &full_tma[stage], kb * 4, wrow);
+          }
+          if (++stage == TS_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(FMT, 128, TS_N);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (uint32_t)(local >> 1) & 1u;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, ST_TIMEOUT_MMA)) goto done;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * TS_N);
+        for (int kb = 0; kb < kblocks; ++kb) {
+          if (!mbar_wait(&full_tma[stage], phase, ST_TIMEOUT_MMA)) goto done;
+          if (!mbar_wait(&full_a[stage], phase, ST_TIMEOUT_MMA)) goto done;
+          tc_fence_after();
+          const uint64_t bdesc = sdesc_sw128(smem_u32(smem + stage * TS_STAGE_BYTES));
+          const uint32_t a_tmem = tmem_base + TS_D_COLS + (uint32_t)(stage * 32);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            umma_ts_f16(d_tmem, a_tmem + 8u * k, bdesc + 2u * k, idesc, (kb | k) != 0);
+          umma_commit(&empty[stage]);
+          if (++stage == TS_STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        umma_commit(&tfull[acc]);
+      }
+    }
+  } else if (warp >= 8) {
+    // ------------------------------------------------------------ unpack warps
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // A row = TMEM lane
+    const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16) + TS_D_COLS;
+    int stage = 0;
+    uint32_t phase = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      for (int kb = 0; kb < kblocks; ++kb) {
+        if (!mbar_wait_warp_t(&full_tma[stage], phase, ST_TIMEOUT_UNPACK)) goto done;
+        const uint8_t* bp = smem + stage * TS_STAGE_BYTES + TS_X_BYTES;
+        const uint4 wv = *reinterpret_cast<const uint4*>(bp + r * 16);
+        const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+        uint32_t a[32];
+#pragma unroll
+        for (int w = 0; w < 4; ++w)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) a[8 * w + j] = tern_pair<FMT>(words[w], j);
+        tmem_st_32x32b_x32(lane_base + (uint32_t)(stage * 32), a);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full_a[stage]);
+        if (++stage == TS_STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // accumulator row (channel slot)
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (uint32_t)(local >> 1) & 1u;
+      const MTile mt = p.mtiles[tile / p.n_ntiles];
+      const int c0 = (tile % p.n_ntiles) * CH;
+      if (!mbar_wait_warp_t(&tfull[acc], acc_phase, ST_TIMEOUT_EPILOGUE)) goto done;
+      tc_fence_after();
+      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * TS_N);
+      if (MODE == TG_GATEUP) {
+        // rows 64..127 (up) hand s_u * u to rows 0..63 (gate) through shared
+        // memory; the hand-over uses bounded mbarrier waits (u_full / u_empty)
+        const uint32_t uphase = (uint32_t)local & 1u;
+        const int ch = (r & 63);
+        const int col = c0 + ch;
+        const bool col_ok = col < p.N;
+        const float* sv = (r < 64 ? p.s0 : p.s1) + (int64_t)mt.expert * p.N;
+        const float scale = col_ok ? __ldg(sv + col) : 0.f;
+        if (r >= 64) {
+          if (!mbar_wait_warp_t(u_empty, uphase ^ 1u, ST_TIMEOUT_EPILOGUE)) goto done;
+#pragma unroll 1
+          for (int c = 0; c < TS_N / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tbase + c * 32, v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) ubuf[(c * 32 + j) * 64 + ch] = __uint_as_float(v[j]) * scale;
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(u_full);
+        } else {
+          __half* out = static_cast<__half*>(p.out);
+#pragma unroll 1
+          for (int c = 0; c < TS_N / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tbase + c * 32, v);
+            tmem_ld_wait();
+            if (c == 0 && !mbar_wait_warp_t(u_full, uphase, ST_TIMEOUT_EPILOGUE)) goto done;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              const int t = c * 32 + j;
+              if (t < mt.rows && col_ok) {
+                const float g = __uint_as_float(v[j]) * scale;
+                const float hv = silu_f(g) * ubuf[t * 64 + ch];
+                out[(int64_t)(mt.row0 + t) * p.ldo + col] = __float2half_rn(hv);
+              }
+            }
+          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(u_empty);
+        }
+      } else {
+        const int col = c0 + r;
+        const bool col_ok = col < p.N;
+        const float* sc = (MODE == TG_DOWN) ? p.s0 + (int64_t)mt.expert * p.N : p.s0;
+        const float scale = col_ok ? __ldg(sc + col) : 0.f;
+        const float bias = (MODE == TG_LINEAR && p.bias && col_ok) ? __ldg(p.bias + col) : 0.f;
+        float* out = static_cast<float*>(p.out);
+#pragma unroll 1
+        for (int c = 0; c < TS_N / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int t = c * 32 + j;
+            if (t < mt.rows && col_ok) {
+              float y = __uint_as_float(v[j]) * scale;
+              if (MODE == TG_DOWN) y *= __ldg(p.row_w + mt.row0 + t);
+              if (MODE == TG_LINEAR) y += bias;
+              out[(int64_t)(mt.row0 + t) * p.ldo + col] = y;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+done:
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TS_TMEM_COLS);
+  }
+}
+
+}  // namespace sb
