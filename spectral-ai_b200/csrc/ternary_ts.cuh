@@ -19,9 +19,10 @@
 // columns (the epilogue of one tile overlaps the next tile's MMAs) plus
 // TS_STAGES A stages of 32 columns.
 //
-// Roles (384 threads): warp 0 TMA producer, warp 1 MMA issuer, warp 2 TMEM
-// allocator, warps 4..7 epilogue, warps 8..11 unpack (warp w owns TMEM lanes
-// 32*(w%4)..+31 in both roles).
+// Roles (512 threads): warp 0 TMA producer, warp 1 MMA issuer, warp 2 TMEM
+// allocator, warps 4..7 epilogue, warps 8..15 unpack in two groups of four
+// that take alternate K-blocks, so one group's tcgen05.st completes while the
+// other expands the next block (warp w owns TMEM lanes 32*(w%4)..+31).
 #pragma once
 
 #include "sm100.cuh"
@@ -29,7 +30,8 @@
 
 namespace sb {
 
-constexpr int TS_THREADS = 384;
+constexpr int TS_UNPACK_GROUPS = 2;                 // groups of 4 unpack warps, alternating K-blocks
+constexpr int TS_THREADS = 256 + 128 * TS_UNPACK_GROUPS;
 constexpr int TS_STAGES = 6;
 constexpr int TS_N = 128;                          // tokens per tile
 constexpr int TS_X_BYTES = TS_N * 64 * 2;          // 16 KB activation tile
@@ -42,6 +44,7 @@ constexpr uint32_t TS_TMEM_COLS = 512;
 constexpr uint32_t TS_D_COLS = 2 * TS_N;           // accumulators at columns [0, 256)
 static_assert(TS_STAGE_BYTES % 1024 == 0, "stage alignment");
 static_assert(TS_D_COLS + 32 * TS_STAGES <= TS_TMEM_COLS, "TMEM budget");
+static_assert(TS_STAGES % TS_UNPACK_GROUPS == 0, "groups must own whole stages");
 
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
@@ -182,12 +185,15 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
   } else if (warp >= 8) {
     // ------------------------------------------------------------ unpack warps
     const int q = warp & 3;
+    const int grp = (warp - 8) >> 2;
     const int r = q * 32 + lane;  // A row = TMEM lane
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16) + TS_D_COLS;
-    int stage = 0;
-    uint32_t phase = 0;
+    int it = 0;  // K-block counter over this CTA's whole tile sequence
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      for (int kb = 0; kb < kblocks; ++kb) {
+      for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        if (it % TS_UNPACK_GROUPS != grp) continue;
+        const int stage = it % TS_STAGES;
+        const uint32_t phase = (uint32_t)(it / TS_STAGES) & 1u;
         if (!mbar_wait_warp_t(&full_tma[stage], phase, ST_TIMEOUT_UNPACK)) goto done;
         const uint8_t* bp = smem + stage * TS_STAGE_BYTES + TS_X_BYTES;
         const uint4 wv = *reinterpret_cast<const uint4*>(bp + r * 16);
@@ -202,10 +208,6 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&full_a[stage]);
-        if (++stage == TS_STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
       }
     }
   } else if (warp >= 4) {
