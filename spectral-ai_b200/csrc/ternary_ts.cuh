@@ -19,6 +19,12 @@
 // columns (the epilogue of one tile overlaps the next tile's MMAs) plus
 // TS_STAGES A stages of 32 columns.
 //
+// Epilogue: the four epilogue warps copy the scaled accumulator (one channel
+// per thread) into a token-major shared tile with a padded row (conflict-free
+// both ways), release the TMEM buffer, then each thread owns one token and
+// writes its row with 16-byte stores (GATEUP: h = silu(g) * u, fp16; DOWN:
+// times the routing weight, fp32).
+//
 // Roles (512 threads): warp 0 TMA producer, warp 1 MMA issuer, warp 2 TMEM
 // allocator, warps 4..7 epilogue, warps 8..15 unpack in two groups of four
 // that take alternate K-blocks, so one group's tcgen05.st completes while the
@@ -37,9 +43,10 @@ constexpr int TS_N = 128;                          // tokens per tile
 constexpr int TS_X_BYTES = TS_N * 64 * 2;          // 16 KB activation tile
 constexpr int TS_P_BYTES = 128 * 16;               // 2 KB packed weights
 constexpr int TS_STAGE_BYTES = TS_X_BYTES + TS_P_BYTES;  // 18 KB (1024-multiple)
-constexpr int TS_U_BYTES = TS_N * 64 * 4;          // up-projection exchange (GATEUP)
+constexpr int TS_E_LD = 129;                       // epilogue staging row (128 channels + pad)
+constexpr int TS_E_BYTES = TS_N * TS_E_LD * 4;     // scaled tile, token-major
 constexpr int TS_BAR_BYTES = (3 * TS_STAGES + 6) * 8 + 16;
-constexpr int TS_SMEM_BYTES = TS_STAGES * TS_STAGE_BYTES + TS_U_BYTES + TS_BAR_BYTES + 1024;
+constexpr int TS_SMEM_BYTES = TS_STAGES * TS_STAGE_BYTES + TS_E_BYTES + TS_BAR_BYTES + 1024;
 constexpr uint32_t TS_TMEM_COLS = 512;
 constexpr uint32_t TS_D_COLS = 2 * TS_N;           // accumulators at columns [0, 256)
 static_assert(TS_STAGE_BYTES % 1024 == 0, "stage alignment");
@@ -81,15 +88,15 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-  float* ubuf = reinterpret_cast<float*>(smem + TS_STAGES * TS_STAGE_BYTES);  // [TS_N][64]
-  uint64_t* full_tma = reinterpret_cast<uint64_t*>(smem + TS_STAGES * TS_STAGE_BYTES + TS_U_BYTES);
+  float* ebuf = reinterpret_cast<float*>(smem + TS_STAGES * TS_STAGE_BYTES);  // [TS_N][TS_E_LD]
+  uint64_t* full_tma = reinterpret_cast<uint64_t*>(smem + TS_STAGES * TS_STAGE_BYTES + TS_E_BYTES);
   uint64_t* full_a = full_tma + TS_STAGES;
   uint64_t* empty = full_a + TS_STAGES;
   uint64_t* tfull = empty + TS_STAGES;
   uint64_t* tempty = tfull + 2;
-  uint64_t* u_full = tempty + 2;   // GATEUP: up values of a tile are in ubuf
-  uint64_t* u_empty = u_full + 1;  // GATEUP: gate warps are done reading ubuf
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(u_empty + 1);
+  uint64_t* e_full = tempty + 2;   // the scaled tile is in ebuf
+  uint64_t* e_empty = e_full + 1;  // every epilogue warp is done with ebuf
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(e_empty + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_mt = *p.num_mtiles;
@@ -108,8 +115,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
       mbar_init(&tfull[i], 1);
       mbar_init(&tempty[i], 4);
     }
-    mbar_init(u_full, 2);
-    mbar_init(u_empty, 2);
+    mbar_init(e_full, 4);
+    mbar_init(e_empty, 4);
     fence_barrier_init();
   }
   if (warp == 2) {
@@ -223,75 +230,84 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
       if (!mbar_wait_warp_t(&tfull[acc], acc_phase, ST_TIMEOUT_EPILOGUE)) goto done;
       tc_fence_after();
       const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * TS_N);
-      if (MODE == TG_GATEUP) {
-        // rows 64..127 (up) hand s_u * u to rows 0..63 (gate) through shared
-        // memory; the hand-over uses bounded mbarrier waits (u_full / u_empty)
-        const uint32_t uphase = (uint32_t)local & 1u;
-        const int ch = (r & 63);
-        const int col = c0 + ch;
-        const bool col_ok = col < p.N;
-        const float* sv = (r < 64 ? p.s0 : p.s1) + (int64_t)mt.expert * p.N;
-        const float scale = col_ok ? __ldg(sv + col) : 0.f;
-        if (r >= 64) {
-          if (!mbar_wait_warp_t(u_empty, uphase ^ 1u, ST_TIMEOUT_EPILOGUE)) goto done;
-#pragma unroll 1
-          for (int c = 0; c < TS_N / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(tbase + c * 32, v);
-            tmem_ld_wait();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) ubuf[(c * 32 + j) * 64 + ch] = __uint_as_float(v[j]) * scale;
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(u_full);
+      const uint32_t ephase = (uint32_t)local & 1u;
+      // ---- phase A: accumulator row r (a channel) -> ebuf[token][r], scaled
+      {
+        int col;
+        const float* sv;
+        if (MODE == TG_GATEUP) {
+          col = c0 + (r & 63);
+          sv = (r < 64 ? p.s0 : p.s1) + (int64_t)mt.expert * p.N;
         } else {
-          __half* out = static_cast<__half*>(p.out);
-#pragma unroll 1
-          for (int c = 0; c < TS_N / 32; ++c) {
-            uint32_t v[32];
-            tmem_ld_32x32b_x32(tbase + c * 32, v);
-            tmem_ld_wait();
-            if (c == 0 && !mbar_wait_warp_t(u_full, uphase, ST_TIMEOUT_EPILOGUE)) goto done;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int t = c * 32 + j;
-              if (t < mt.rows && col_ok) {
-                const float g = __uint_as_float(v[j]) * scale;
-                const float hv = silu_f(g) * ubuf[t * 64 + ch];
-                out[(int64_t)(mt.row0 + t) * p.ldo + col] = __float2half_rn(hv);
-              }
-            }
-          }
-          __syncwarp();
-          if (lane == 0) mbar_arrive(u_empty);
+          col = c0 + r;
+          sv = (MODE == TG_DOWN) ? p.s0 + (int64_t)mt.expert * p.N : p.s0;
         }
-      } else {
-        const int col = c0 + r;
         const bool col_ok = col < p.N;
-        const float* sc = (MODE == TG_DOWN) ? p.s0 + (int64_t)mt.expert * p.N : p.s0;
-        const float scale = col_ok ? __ldg(sc + col) : 0.f;
+        const float scale = col_ok ? __ldg(sv + col) : 0.f;
         const float bias = (MODE == TG_LINEAR && p.bias && col_ok) ? __ldg(p.bias + col) : 0.f;
-        float* out = static_cast<float*>(p.out);
+        if (!mbar_wait_warp_t(e_empty, ephase ^ 1u, ST_TIMEOUT_EPILOGUE)) goto done;
 #pragma unroll 1
         for (int c = 0; c < TS_N / 32; ++c) {
           uint32_t v[32];
           tmem_ld_32x32b_x32(tbase + c * 32, v);
           tmem_ld_wait();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            const int t = c * 32 + j;
-            if (t < mt.rows && col_ok) {
-              float y = __uint_as_float(v[j]) * scale;
-              if (MODE == TG_DOWN) y *= __ldg(p.row_w + mt.row0 + t);
-              if (MODE == TG_LINEAR) y += bias;
-              out[(int64_t)(mt.row0 + t) * p.ldo + col] = y;
+          for (int j = 0; j < 32; ++j)
+            ebuf[(c * 32 + j) * TS_E_LD + r] = fmaf(__uint_as_float(v[j]), scale, bias);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&tempty[acc]);  // TMEM buffer free for the tile after next
+          mbar_arrive(e_full);
+        }
+      }
+      // ---- phase B: thread r owns token r of the tile and writes its row
+      if (!mbar_wait_warp_t(e_full, ephase, ST_TIMEOUT_EPILOGUE)) goto done;
+      {
+        const int t = r;
+        const float* er = ebuf + t * TS_E_LD;
+        if (t < mt.rows) {
+          const int64_t orow = (int64_t)(mt.row0 + t) * p.ldo;
+          if (MODE == TG_GATEUP) {
+            __half* out = static_cast<__half*>(p.out) + orow;
+#pragma unroll 1
+            for (int c8 = 0; c8 < 64; c8 += 8) {
+              const int col = c0 + c8;
+              if (col >= p.N) break;
+              float hv[8];
+#pragma unroll
+              for (int u = 0; u < 8; ++u) hv[u] = silu_f(er[c8 + u]) * er[64 + c8 + u];
+              if (col + 8 <= p.N && (p.ldo & 7) == 0) {
+                __half2 h0 = __floats2half2_rn(hv[0], hv[1]), h1 = __floats2half2_rn(hv[2], hv[3]);
+                __half2 h2 = __floats2half2_rn(hv[4], hv[5]), h3 = __floats2half2_rn(hv[6], hv[7]);
+                *reinterpret_cast<uint4*>(out + col) =
+                    make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
+                               *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
+              } else {
+                for (int u = 0; u < 8 && col + u < p.N; ++u) out[col + u] = __float2half_rn(hv[u]);
+              }
+            }
+          } else {
+            float* out = static_cast<float*>(p.out) + orow;
+            const float rw = (MODE == TG_DOWN) ? __ldg(p.row_w + mt.row0 + t) : 1.0f;
+#pragma unroll 1
+            for (int c4 = 0; c4 < 128; c4 += 4) {
+              const int col = c0 + c4;
+              if (col >= p.N) break;
+              const float y0 = er[c4] * rw, y1 = er[c4 + 1] * rw, y2 = er[c4 + 2] * rw, y3 = er[c4 + 3] * rw;
+              if (col + 4 <= p.N && (p.ldo & 3) == 0) {
+                *reinterpret_cast<float4*>(out + col) = make_float4(y0, y1, y2, y3);
+              } else {
+                const float yv[4] = {y0, y1, y2, y3};
+                for (int u = 0; u < 4 && col + u < p.N; ++u) out[col + u] = yv[u];
+              }
             }
           }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(e_empty);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[acc]);
     }
   }
 done:
