@@ -409,7 +409,7 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   CUtensorMap tmx, tmg, tmu, tmh, tmd;
   const CUtensorMapDataType adt = fmt_gu ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const int64_t KWh = ternary_row_words(H), KWi = ternary_row_words(I);
-  const uint32_t gu_box = ts ? 64 : 128, d_box = ts ? 128 : 256;
+  const uint32_t gu_box = 128, d_box = 256;
   if ((rc = make_tmap_2d(&tmx, xp, adt, 2, L.R, H, L.ldx, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) ||
       (rc = make_tmap_2d(&tmg, gate, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, 4, gu_box,
                          CU_TENSOR_MAP_SWIZZLE_NONE)) ||
@@ -424,7 +424,7 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   TernGemmParams pg{};
   pg.mtiles = mtiles;
   pg.num_mtiles = nmt;
-  pg.n_ntiles = ts ? (int)((I + 63) / 64) : (int)((I + 127) / 128);
+  pg.n_ntiles = (int)((I + 127) / 128);
   pg.N = (int)I;
   pg.K = (int)H;
   pg.b_rows = (int)I;
@@ -443,7 +443,7 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   TernGemmParams pd{};
   pd.mtiles = mtiles;
   pd.num_mtiles = nmt;
-  pd.n_ntiles = ts ? (int)((H + 127) / 128) : (int)((H + 255) / 256);
+  pd.n_ntiles = (int)((H + 255) / 256);
   pd.N = (int)H;
   pd.K = (int)I;
   pd.b_rows = (int)H;
@@ -574,13 +574,13 @@ extern "C" int sb_ternary_linear(const void* x, int x_dtype, int64_t M, int64_t 
   const int64_t KW = ternary_row_words(K);
   if ((rc = make_tmap_2d(&tmx, xp, fmt ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, M,
                          K, L.ldx, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) ||
-      (rc = make_tmap_2d(&tmw, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)N, KW, KW, 4,
-                         use_ts_engine() ? 128 : 256, CU_TENSOR_MAP_SWIZZLE_NONE)))
+      (rc = make_tmap_2d(&tmw, w, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)N, KW, KW, 4, 256,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
   TernGemmParams pl{};
   pl.mtiles = mtiles;
   pl.num_mtiles = nmt;
-  pl.n_ntiles = use_ts_engine() ? (int)((N + 127) / 128) : (int)((N + 255) / 256);
+  pl.n_ntiles = (int)((N + 255) / 256);
   pl.N = (int)N;
   pl.K = (int)K;
   pl.b_rows = (int)N;

@@ -2,33 +2,30 @@
 //
 //   D^T[c, t] = sum_k W[e][c, k] * X[t, k]     (c: output channel, t: token row)
 //
-// The ternary weights are the A operand and live in tensor memory: four unpack
-// warps read the 2-bit split-plane words of a 128-channel x 64-K block (TMA'd
-// into a 2 KB staging buffer), expand them in registers to 16-bit +-1/0 and
-// write them straight into TMEM with tcgen05.st (lane = channel, two K values
-// per 32-bit column).  Shared memory carries only the 128-token x 64-K
-// activation tile (TMA, 128-byte swizzle, no multicast) that is the B operand,
-// so the unpack no longer competes with the MMA for shared-memory bandwidth.
+// The ternary weights are the A operand and live in tensor memory: unpack
+// warps read the 2-bit split-plane words of the tile's channels for one 64-K
+// block (TMA'd into a 4 KB staging buffer), expand them in registers to 16-bit
+// +-1/0 and write them straight into TMEM with tcgen05.st (lane = channel, two
+// K values per 32-bit column).  Shared memory carries only the 128-token x
+// 64-K activation tile (TMA, 128-byte swizzle, no multicast) that is the B
+// operand, so the unpack does not compete with the MMA for shared memory.
+//
+// A tile covers 256 output channels with two accumulators that share every
+// activation tile (8 MMAs of M=128, N=128, K=16 per 64-K block): GATEUP puts
+// gate channels c0..c0+127 in accumulator 0 and the up channels c0..c0+127 in
+// accumulator 1, so lane r holds the gate and up value of channel c0+r and
+// the SwiGLU needs no exchange; DOWN/LINEAR cover channels c0..c0+255.
 //
 //   tcgen05.mma.cta_group::1.kind::f16 [D], [A_tmem], B_smem_desc, idesc
-//   M = 128 channels, N = 128 tokens, K = 16 per instruction, fp32 in TMEM.
 //
-// GATEUP tiles interleave channels: A rows 0-63 are gate channels c0..c0+63,
-// rows 64-127 the up channels c0..c0+63, so one accumulator holds both and the
-// epilogue pairs them through shared memory.  TMEM: two accumulators of 128
-// columns (the epilogue of one tile overlaps the next tile's MMAs) plus
-// TS_STAGES A stages of 32 columns.
-//
-// Epilogue: the four epilogue warps copy the scaled accumulator (one channel
-// per thread) into a token-major shared tile with a padded row (conflict-free
-// both ways), release the TMEM buffer, then each thread owns one token and
-// writes its row with 16-byte stores (GATEUP: h = silu(g) * u, fp16; DOWN:
-// times the routing weight, fp32).
+// TMEM (512 columns): accumulators at [0,128) and [128,256), then TS_STAGES A
+// stages of 64 columns (two 128x64 weight blocks).  The accumulators are
+// single-buffered: the epilogue copies them to shared memory first and
+// releases TMEM before doing the arithmetic and the stores.
 //
 // Roles (512 threads): warp 0 TMA producer, warp 1 MMA issuer, warp 2 TMEM
 // allocator, warps 4..7 epilogue, warps 8..15 unpack in two groups of four
-// that take alternate K-blocks, so one group's tcgen05.st completes while the
-// other expands the next block (warp w owns TMEM lanes 32*(w%4)..+31).
+// that take alternate K-blocks (warp w owns TMEM lanes 32*(w%4)..+31).
 #pragma once
 
 #include "sm100.cuh"
@@ -36,22 +33,25 @@
 
 namespace sb {
 
-constexpr int TS_UNPACK_GROUPS = 2;                 // groups of 4 unpack warps, alternating K-blocks
+constexpr int TS_UNPACK_GROUPS = 2;
 constexpr int TS_THREADS = 256 + 128 * TS_UNPACK_GROUPS;
-constexpr int TS_STAGES = 6;
+constexpr int TS_STAGES = 4;
 constexpr int TS_N = 128;                          // tokens per tile
+constexpr int TS_CH = 256;                         // channels per tile (two accumulators)
 constexpr int TS_X_BYTES = TS_N * 64 * 2;          // 16 KB activation tile
-constexpr int TS_P_BYTES = 128 * 16;               // 2 KB packed weights
-constexpr int TS_STAGE_BYTES = TS_X_BYTES + TS_P_BYTES;  // 18 KB (1024-multiple)
-constexpr int TS_E_LD = 129;                       // epilogue staging row (128 channels + pad)
-constexpr int TS_E_BYTES = TS_N * TS_E_LD * 4;     // scaled tile, token-major
-constexpr int TS_BAR_BYTES = (3 * TS_STAGES + 6) * 8 + 16;
+constexpr int TS_P_BYTES = TS_CH * 16;             // 4 KB packed weights
+constexpr int TS_STAGE_BYTES = TS_X_BYTES + TS_P_BYTES;  // 20 KB (1024-multiple)
+constexpr int TS_E_LD = 129;                       // epilogue staging row (128 values + pad)
+constexpr int TS_E_BYTES = 2 * TS_N * TS_E_LD * 4; // two accumulators, token-major
+constexpr int TS_BAR_BYTES = (3 * TS_STAGES + 4) * 8 + 16;
 constexpr int TS_SMEM_BYTES = TS_STAGES * TS_STAGE_BYTES + TS_E_BYTES + TS_BAR_BYTES + 1024;
 constexpr uint32_t TS_TMEM_COLS = 512;
 constexpr uint32_t TS_D_COLS = 2 * TS_N;           // accumulators at columns [0, 256)
+constexpr uint32_t TS_A_COLS = 64;                 // per stage: two 128 x 64 weight blocks
 static_assert(TS_STAGE_BYTES % 1024 == 0, "stage alignment");
-static_assert(TS_D_COLS + 32 * TS_STAGES <= TS_TMEM_COLS, "TMEM budget");
+static_assert(TS_D_COLS + TS_A_COLS * TS_STAGES <= TS_TMEM_COLS, "TMEM budget");
 static_assert(TS_STAGES % TS_UNPACK_GROUPS == 0, "groups must own whole stages");
+static_assert(TS_SMEM_BYTES <= 227 * 1024, "shared memory budget");
 
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
   asm volatile(
@@ -80,6 +80,18 @@ __device__ __forceinline__ void umma_ts_f16(uint32_t d_tmem, uint32_t a_tmem, ui
       : "memory");
 }
 
+// Expands the four packed words of one row (64 K) into 32 TMEM columns.
+template <int FMT>
+__device__ __forceinline__ void unpack_row_to_tmem(const uint4 wv, uint32_t taddr) {
+  const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
+  uint32_t a[32];
+#pragma unroll
+  for (int w = 0; w < 4; ++w)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) a[8 * w + j] = tern_pair<FMT>(words[w], j);
+  tmem_st_32x32b_x32(taddr, a);
+}
+
 template <int MODE, int FMT>
 __global__ void __launch_bounds__(TS_THREADS, 1)
     ternary_ts_kernel(const __grid_constant__ CUtensorMap tmX,
@@ -88,13 +100,13 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   uint8_t* smem = smem_raw + ((1024u - (raw & 1023u)) & 1023u);
-  float* ebuf = reinterpret_cast<float*>(smem + TS_STAGES * TS_STAGE_BYTES);  // [TS_N][TS_E_LD]
+  float* ebuf = reinterpret_cast<float*>(smem + TS_STAGES * TS_STAGE_BYTES);  // [2][TS_N][TS_E_LD]
   uint64_t* full_tma = reinterpret_cast<uint64_t*>(smem + TS_STAGES * TS_STAGE_BYTES + TS_E_BYTES);
   uint64_t* full_a = full_tma + TS_STAGES;
   uint64_t* empty = full_a + TS_STAGES;
   uint64_t* tfull = empty + TS_STAGES;
-  uint64_t* tempty = tfull + 2;
-  uint64_t* e_full = tempty + 2;   // the scaled tile is in ebuf
+  uint64_t* tempty = tfull + 1;
+  uint64_t* e_full = tempty + 1;   // the scaled tile is in ebuf
   uint64_t* e_empty = e_full + 1;  // every epilogue warp is done with ebuf
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(e_empty + 1);
 
@@ -102,8 +114,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
   const int n_mt = *p.num_mtiles;
   const int num_tiles = n_mt * p.n_ntiles;
   const int kblocks = (p.K + 63) / 64;
-  // channels per tile of one matrix: GATEUP holds 64 gate + 64 up channels
-  constexpr int CH = (MODE == TG_GATEUP) ? 64 : 128;
+  // first channel of accumulator 0 (GATEUP: gate and up channels c0..c0+127)
+  constexpr int CSTEP = (MODE == TG_GATEUP) ? 128 : 256;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < TS_STAGES; ++s) {
@@ -111,10 +123,8 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
       mbar_init(&full_a[s], 4);
       mbar_init(&empty[s], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      mbar_init(&tfull[i], 1);
-      mbar_init(&tempty[i], 4);
-    }
+    mbar_init(tfull, 1);
+    mbar_init(tempty, 4);
     mbar_init(e_full, 4);
     mbar_init(e_empty, 4);
     fence_barrier_init();
@@ -138,7 +148,7 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
       uint32_t phase = 0;
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
         const MTile mt = p.mtiles[tile / p.n_ntiles];
-        const int c0 = (tile % p.n_ntiles) * CH;
+        const int c0 = (tile % p.n_ntiles) * CSTEP;
         const int wrow = mt.expert * p.b_rows + c0;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1u, ST_TIMEOUT_PRODUCER)) goto done;
@@ -166,34 +176,33 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
       uint32_t phase = 0;
       int local = 0;
       for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = (uint32_t)(local >> 1) & 1u;
-        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, ST_TIMEOUT_MMA)) goto done;
+        if (!mbar_wait(tempty, ((uint32_t)local & 1u) ^ 1u, ST_TIMEOUT_MMA)) goto done;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * TS_N);
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&full_tma[stage], phase, ST_TIMEOUT_MMA)) goto done;
           if (!mbar_wait(&full_a[stage], phase, ST_TIMEOUT_MMA)) goto done;
           tc_fence_after();
           const uint64_t bdesc = sdesc_sw128(smem_u32(smem + stage * TS_STAGE_BYTES));
-          const uint32_t a_tmem = tmem_base + TS_D_COLS + (uint32_t)(stage * 32);
+          const uint32_t a_tmem = tmem_base + TS_D_COLS + (uint32_t)(stage * TS_A_COLS);
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            umma_ts_f16(d_tmem, a_tmem + 8u * k, bdesc + 2u * k, idesc, (kb | k) != 0);
+          for (int k = 0; k < 4; ++k) {
+            umma_ts_f16(tmem_base, a_tmem + 8u * k, bdesc + 2u * k, idesc, (kb | k) != 0);
+            umma_ts_f16(tmem_base + TS_N, a_tmem + 32u + 8u * k, bdesc + 2u * k, idesc, (kb | k) != 0);
+          }
           umma_commit(&empty[stage]);
           if (++stage == TS_STAGES) {
             stage = 0;
             phase ^= 1u;
           }
         }
-        umma_commit(&tfull[acc]);
+        umma_commit(tfull);
       }
     }
   } else if (warp >= 8) {
     // ------------------------------------------------------------ unpack warps
     const int q = warp & 3;
     const int grp = (warp - 8) >> 2;
-    const int r = q * 32 + lane;  // A row = TMEM lane
+    const int r = q * 32 + lane;  // TMEM lane; packed rows r and 128 + r
     const uint32_t lane_base = tmem_base + ((uint32_t)(q * 32) << 16) + TS_D_COLS;
     int it = 0;  // K-block counter over this CTA's whole tile sequence
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
@@ -203,14 +212,11 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
         const uint32_t phase = (uint32_t)(it / TS_STAGES) & 1u;
         if (!mbar_wait_warp_t(&full_tma[stage], phase, ST_TIMEOUT_UNPACK)) goto done;
         const uint8_t* bp = smem + stage * TS_STAGE_BYTES + TS_X_BYTES;
-        const uint4 wv = *reinterpret_cast<const uint4*>(bp + r * 16);
-        const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
-        uint32_t a[32];
-#pragma unroll
-        for (int w = 0; w < 4; ++w)
-#pragma unroll
-          for (int j = 0; j < 8; ++j) a[8 * w + j] = tern_pair<FMT>(words[w], j);
-        tmem_st_32x32b_x32(lane_base + (uint32_t)(stage * 32), a);
+        const uint4 w0 = *reinterpret_cast<const uint4*>(bp + r * 16);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(bp + (128 + r) * 16);
+        const uint32_t col = lane_base + (uint32_t)(stage * TS_A_COLS);
+        unpack_row_to_tmem<FMT>(w0, col);
+        unpack_row_to_tmem<FMT>(w1, col + 32u);
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
@@ -220,64 +226,70 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    const int r = q * 32 + lane;  // accumulator row (channel slot)
+    const int r = q * 32 + lane;  // accumulator row
     int local = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
-      const int acc = local & 1;
-      const uint32_t acc_phase = (uint32_t)(local >> 1) & 1u;
+      const uint32_t ph = (uint32_t)local & 1u;
       const MTile mt = p.mtiles[tile / p.n_ntiles];
-      const int c0 = (tile % p.n_ntiles) * CH;
-      if (!mbar_wait_warp_t(&tfull[acc], acc_phase, ST_TIMEOUT_EPILOGUE)) goto done;
-      tc_fence_after();
-      const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * TS_N);
-      const uint32_t ephase = (uint32_t)local & 1u;
-      // ---- phase A: accumulator row r (a channel) -> ebuf[token][r], scaled
+      const int c0 = (tile % p.n_ntiles) * CSTEP;
+      // ---- phase A: TMEM -> ebuf[acc][token][r], scaled; then TMEM is free
       {
-        int col;
-        const float* sv;
-        if (MODE == TG_GATEUP) {
-          col = c0 + (r & 63);
-          sv = (r < 64 ? p.s0 : p.s1) + (int64_t)mt.expert * p.N;
-        } else {
-          col = c0 + r;
-          sv = (MODE == TG_DOWN) ? p.s0 + (int64_t)mt.expert * p.N : p.s0;
-        }
-        const bool col_ok = col < p.N;
-        const float scale = col_ok ? __ldg(sv + col) : 0.f;
-        const float bias = (MODE == TG_LINEAR && p.bias && col_ok) ? __ldg(p.bias + col) : 0.f;
-        if (!mbar_wait_warp_t(e_empty, ephase ^ 1u, ST_TIMEOUT_EPILOGUE)) goto done;
-#pragma unroll 1
-        for (int c = 0; c < TS_N / 32; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(tbase + c * 32, v);
-          tmem_ld_wait();
+        float sc[2], bi[2];
 #pragma unroll
-          for (int j = 0; j < 32; ++j)
-            ebuf[(c * 32 + j) * TS_E_LD + r] = fmaf(__uint_as_float(v[j]), scale, bias);
+        for (int a = 0; a < 2; ++a) {
+          int col;
+          const float* sv;
+          if (MODE == TG_GATEUP) {
+            col = c0 + r;
+            sv = (a == 0 ? p.s0 : p.s1) + (int64_t)mt.expert * p.N;
+          } else {
+            col = c0 + 128 * a + r;
+            sv = (MODE == TG_DOWN) ? p.s0 + (int64_t)mt.expert * p.N : p.s0;
+          }
+          const bool ok = col < p.N;
+          sc[a] = ok ? __ldg(sv + col) : 0.f;
+          bi[a] = (MODE == TG_LINEAR && p.bias && ok) ? __ldg(p.bias + col) : 0.f;
+        }
+        if (!mbar_wait_warp_t(e_empty, ph ^ 1u, ST_TIMEOUT_EPILOGUE)) goto done;
+        if (!mbar_wait_warp_t(tfull, ph, ST_TIMEOUT_EPILOGUE)) goto done;
+        tc_fence_after();
+        const uint32_t tbase = tmem_base + ((uint32_t)(q * 32) << 16);
+#pragma unroll
+        for (int a = 0; a < 2; ++a) {
+          float* eb = ebuf + a * TS_N * TS_E_LD;
+#pragma unroll 1
+          for (int c = 0; c < TS_N / 32; ++c) {
+            uint32_t v[32];
+            tmem_ld_32x32b_x32(tbase + (uint32_t)(a * TS_N + c * 32), v);
+            tmem_ld_wait();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) eb[(c * 32 + j) * TS_E_LD + r] = fmaf(__uint_as_float(v[j]), sc[a], bi[a]);
+          }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&tempty[acc]);  // TMEM buffer free for the tile after next
+          mbar_arrive(tempty);  // accumulators free for the next tile
           mbar_arrive(e_full);
         }
       }
       // ---- phase B: thread r owns token r of the tile and writes its row
-      if (!mbar_wait_warp_t(e_full, ephase, ST_TIMEOUT_EPILOGUE)) goto done;
+      if (!mbar_wait_warp_t(e_full, ph, ST_TIMEOUT_EPILOGUE)) goto done;
       {
         const int t = r;
-        const float* er = ebuf + t * TS_E_LD;
         if (t < mt.rows) {
           const int64_t orow = (int64_t)(mt.row0 + t) * p.ldo;
+          const float* g = ebuf + t * TS_E_LD;
+          const float* u = ebuf + (TS_N + t) * TS_E_LD;
           if (MODE == TG_GATEUP) {
             __half* out = static_cast<__half*>(p.out) + orow;
 #pragma unroll 1
-            for (int c8 = 0; c8 < 64; c8 += 8) {
+            for (int c8 = 0; c8 < 128; c8 += 8) {
               const int col = c0 + c8;
               if (col >= p.N) break;
               float hv[8];
 #pragma unroll
-              for (int u = 0; u < 8; ++u) hv[u] = silu_f(er[c8 + u]) * er[64 + c8 + u];
+              for (int e = 0; e < 8; ++e) hv[e] = silu_f(g[c8 + e]) * u[c8 + e];
               if (col + 8 <= p.N && (p.ldo & 7) == 0) {
                 __half2 h0 = __floats2half2_rn(hv[0], hv[1]), h1 = __floats2half2_rn(hv[2], hv[3]);
                 __half2 h2 = __floats2half2_rn(hv[4], hv[5]), h3 = __floats2half2_rn(hv[6], hv[7]);
@@ -285,22 +297,26 @@ __global__ void __launch_bounds__(TS_THREADS, 1)
                     make_uint4(*reinterpret_cast<uint32_t*>(&h0), *reinterpret_cast<uint32_t*>(&h1),
                                *reinterpret_cast<uint32_t*>(&h2), *reinterpret_cast<uint32_t*>(&h3));
               } else {
-                for (int u = 0; u < 8 && col + u < p.N; ++u) out[col + u] = __float2half_rn(hv[u]);
+                for (int e = 0; e < 8 && col + e < p.N; ++e) out[col + e] = __float2half_rn(hv[e]);
               }
             }
           } else {
             float* out = static_cast<float*>(p.out) + orow;
             const float rw = (MODE == TG_DOWN) ? __ldg(p.row_w + mt.row0 + t) : 1.0f;
 #pragma unroll 1
-            for (int c4 = 0; c4 < 128; c4 += 4) {
-              const int col = c0 + c4;
-              if (col >= p.N) break;
-              const float y0 = er[c4] * rw, y1 = er[c4 + 1] * rw, y2 = er[c4 + 2] * rw, y3 = er[c4 + 3] * rw;
-              if (col + 4 <= p.N && (p.ldo & 3) == 0) {
-                *reinterpret_cast<float4*>(out + col) = make_float4(y0, y1, y2, y3);
-              } else {
-                const float yv[4] = {y0, y1, y2, y3};
-                for (int u = 0; u < 4 && col + u < p.N; ++u) out[col + u] = yv[u];
+            for (int a = 0; a < 2; ++a) {
+              const float* er = ebuf + (a * TS_N + t) * TS_E_LD;
+#pragma unroll 1
+              for (int c4 = 0; c4 < 128; c4 += 4) {
+                const int col = c0 + 128 * a + c4;
+                if (col >= p.N) break;
+                const float y0 = er[c4] * rw, y1 = er[c4 + 1] * rw, y2 = er[c4 + 2] * rw, y3 = er[c4 + 3] * rw;
+                if (col + 4 <= p.N && (p.ldo & 3) == 0) {
+                  *reinterpret_cast<float4*>(out + col) = make_float4(y0, y1, y2, y3);
+                } else {
+                  const float yv[4] = {y0, y1, y2, y3};
+                  for (int e = 0; e < 4 && col + e < p.N; ++e) out[col + e] = yv[e];
+                }
               }
             }
           }
