@@ -14,6 +14,10 @@ Workloads (seeded synthetic inputs with BASELINE.json's shapes; no datasets):
   ep         (N > 1) the same layer expert-parallel: 64/N experts per GPU,
              NCCL all-to-all dispatch of bf16 token rows and combine of fp32
              expert outputs.  Reported inside the line as "ep".
+  stack16    (config 3) 16 MoE layers with residual, 16384 tokens in total
+             split over the GPUs; reported as "stack16".
+  config4    6-level router (4096 experts, hidden 4096) at 8192 tokens per GPU
+             against a dense bf16 gate (cuBLAS GEMM + top-8); "config4".
   router     BVH router forward alone at B = 262144 bf16 tokens (config 1);
              1 GiB of input per GPU > L2, so no flush.  Reported inside the
              moe_layer line as "router".
@@ -275,6 +279,64 @@ def moe_workload(batch: int, device, select: str = "soft"):
     return step, e2e_step, meta
 
 
+def config4_workloads(batch: int, device):
+    """Config 4: 6-level router (4^6 = 4096 experts) at hidden 4096 vs a dense
+    linear gate of the same shape (bf16 4096x4096 GEMM + top-8 + softmax)."""
+    import numpy as np
+    import torch
+    from bvh_router import BVHRouter, RouterConfig
+    from sb200 import synth
+    H4, br = 4096, (4,) * 6
+    w = synth.router_weights(H4, S, br, seed=4)
+    r = BVHRouter(RouterConfig(embed_dim=H4, spectral_dim=S, branching=br))
+    r.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in w.items()})
+    r = r.to(device).eval()
+    eng = r.sync_weights(device)
+    x = synth.hidden_states(batch, H4, seed=4, dtype=torch.bfloat16, device=device)
+    outs = {"topk_ids": torch.empty(batch, TOPK, dtype=torch.int32, device=device),
+            "topk_weights": torch.empty(batch, TOPK, dtype=torch.float32, device=device)}
+    g = torch.Generator(device=device).manual_seed(44)
+    wg = (torch.randn(4096, H4, generator=g, device=device) / H4 ** 0.5).to(torch.bfloat16)
+
+    def router_step():
+        eng.forward(x, precision="fast", select="hard", k=TOPK, outputs=outs)
+
+    def dense_step():
+        logits = x @ wg.t()
+        v, i = torch.topk(logits.float(), TOPK, dim=-1)
+        torch.softmax(v, dim=-1)
+
+    return router_step, dense_step
+
+
+def stack_workload(tokens: int, device, layers: int = 16, select: str = "soft"):
+    """Config 3: a stack of MoE layers (router + 64 ternary experts each, own
+    random weights per layer) with residual h <- h + MoE(h); attention omitted."""
+    import numpy as np
+    import torch
+    from bvh_router import BVHRouter, RouterConfig
+    from sb200 import synth
+    from sb200.moe import BVHMoELayer
+    from sb200.ternary import TernaryExperts
+    stack = []
+    for l in range(layers):
+        w = synth.router_weights(H, S, BRANCHING, seed=100 + l)
+        r = BVHRouter(RouterConfig(embed_dim=H, spectral_dim=S))
+        r.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in w.items()})
+        r = r.to(device).eval()
+        stack.append(BVHMoELayer(r, TernaryExperts.random(E_EXPERTS, H, I_INTER, seed=200 + l, device=device),
+                                 top_k=TOPK, select=select))
+    x = synth.hidden_states(tokens, H, seed=3, dtype=torch.bfloat16, device=device)
+
+    def step():
+        h = x
+        for layer in stack:
+            h = h + layer(h)
+        return h
+
+    return step
+
+
 def ep_workload(batch: int, device, world: int, select: str = "soft"):
     import numpy as np
     import torch
@@ -400,6 +462,35 @@ def run_ours(a):
                      "experts_per_gpu": E_EXPERTS // world,
                      "parallelism": f"ep{world}: NCCL all_to_all_single dispatch (bf16 rows) + combine (fp32)",
                      "kernels": {k: {"launches": n, "avg_ms": round(t / max(n, 1), 4)} for k, (n, t) in eprof.items()}}
+    # ---- config 3: 16-layer MoE stack, 16384 tokens sharded over the ranks
+    if not a.skip_stack:
+        stok = max(1, 16384 // world)
+        sstep = stack_workload(stok, dev)
+        st_steps = min(a.steps, 10)
+        s_ms, sprof = time_steps(sstep, st_steps, 2, world, profile=True)
+        out["stack16"] = {"metric": "16-layer MoE stack tokens/s (config 3)", "unit": "tokens/s",
+                          "value": round(stok * world * st_steps / (s_ms / 1e3), 1),
+                          "ms_per_step": round(s_ms / st_steps, 3), "tokens_total": stok * world,
+                          "tokens_per_gpu": stok, "layers": 16, "steps": st_steps,
+                          "scaling": "strong (16384 tokens in total, split over the GPUs)",
+                          "parallelism": f"token-shard x{world}, experts replicated per layer",
+                          "l2": "weights of 16 layers (1.7 GB) stream every step; no flush"}
+    # ---- config 4: 6-level 4096-expert router at hidden 4096 vs a dense gate
+    if not a.skip_config4:
+        c4tok = 65536 // 8
+        rstep4, dstep4 = config4_workloads(c4tok, dev)
+        c4_steps = min(a.steps, 50)
+        r4_ms, r4prof = time_steps(rstep4, c4_steps, a.warmup, world, profile=True, flush=flush)
+        d4_ms, _ = time_steps(dstep4, c4_steps, a.warmup, world, flush=flush)
+        out["config4"] = {"metric": "tokens/s, 6-level BVH router (4096 experts, hidden 4096) vs dense gate",
+                          "unit": "tokens/s", "tokens_per_gpu": c4tok,
+                          "bvh_router": round(c4tok * world * c4_steps / (r4_ms / 1e3), 1),
+                          "dense_gate_cublas": round(c4tok * world * c4_steps / (d4_ms / 1e3), 1),
+                          "bvh_ms_per_step": round(r4_ms / c4_steps, 4), "dense_ms_per_step": round(d4_ms / c4_steps, 4),
+                          "bvh_kernels": {k: {"launches": n, "avg_ms": round(t / max(n, 1), 4)}
+                                          for k, (n, t) in r4prof.items()},
+                          "dense_gate": "torch bf16 x @ W^T (cuBLAS, 4096 x 4096) + topk(8) + softmax",
+                          "l2": "flushed before every step"}
     # ---- router alone (config 1), same process
     if not a.skip_router:
         rstep, _, rmeta = router_workload(a.router_batch, dev)
@@ -520,6 +611,8 @@ def main():
     ap.add_argument("--router-steps", type=int, default=100)
     ap.add_argument("--skip-router", action="store_true")
     ap.add_argument("--skip-ep", action="store_true")
+    ap.add_argument("--skip-stack", action="store_true")
+    ap.add_argument("--skip-config4", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     a = ap.parse_args()

@@ -40,6 +40,22 @@ def pack_device(T: np.ndarray) -> np.ndarray:
     return np.bitwise_or.reduce(w, axis=2).astype(np.uint32)
 
 
+def pack_device_torch(T: torch.Tensor) -> torch.Tensor:
+    """Same layout as ``pack_device`` with torch ops on any device:
+    int8 [N, K] -> int32 [N, ceil(K/64)*4] (the uint32 words viewed as int32)."""
+    N, K = T.shape
+    KW = row_words(K)
+    pad = torch.zeros(N, KW * 16, dtype=torch.int8, device=T.device)
+    pad[:, :K] = T
+    g = pad.view(N, KW, 8, 2).to(torch.int64)
+    nz = (g != 0).to(torch.int64)
+    sg = (g < 0).to(torch.int64)
+    j = torch.arange(8, device=T.device, dtype=torch.int64).view(1, 1, 8)
+    w = ((nz[..., 0] << j) | (sg[..., 0] << (8 + j)) | (nz[..., 1] << (16 + j)) | (sg[..., 1] << (24 + j)))
+    words = w.sum(dim=2)  # the bit fields of the 8 pairs are disjoint
+    return torch.where(words >= 2 ** 31, words - 2 ** 32, words).to(torch.int32)
+
+
 def _stream(dev) -> C.c_void_p:
     return C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
 
@@ -137,6 +153,38 @@ class TernaryExperts:
         self.up_scale = to(np.stack([np.asarray(get(e, "up_scale"), np.float32) for e in experts]))
         self.down_scale = to(np.stack([np.asarray(get(e, "down_scale"), np.float32) for e in experts]))
         self._ws = None
+
+    @classmethod
+    def random(cls, n_experts: int, hidden: int, inter: int, seed: int, device) -> "TernaryExperts":
+        """Random experts built on the device: T uniform over {-1,0,+1}, one
+        scale c/sqrt(fan_in) per matrix with c ~ U[0.5, 1.5) (the recipe of
+        sb200.synth.ternary_experts, drawn from a device generator)."""
+        self = cls.__new__(cls)
+        self.device = torch.device(device)
+        self.E, self.H, self.I = n_experts, hidden, inter
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        rng = np.random.default_rng(seed)
+
+        def mats(rows, cols):
+            out = []
+            for _ in range(n_experts):
+                t = torch.randint(-1, 2, (rows, cols), generator=g, device=self.device, dtype=torch.int8)
+                out.append(pack_device_torch(t))
+            return torch.cat(out)
+
+        self.gate = mats(inter, hidden)
+        self.up = mats(inter, hidden)
+        self.down = mats(hidden, inter)
+
+        def scales(n, fan_in):
+            c = rng.uniform(0.5, 1.5, size=(n_experts, 1)) / np.sqrt(fan_in)
+            return torch.from_numpy(np.repeat(c, n, axis=1).astype(np.float32)).to(self.device)
+
+        self.gate_scale = scales(inter, hidden)
+        self.up_scale = scales(inter, hidden)
+        self.down_scale = scales(hidden, inter)
+        self._ws = None
+        return self
 
     def memory_bytes(self) -> int:
         return sum(t.numel() * t.element_size() for t in (self.gate, self.up, self.down, self.gate_scale,

@@ -177,3 +177,18 @@ def test_reference_api_surface(cuda_device):
                                  (4, 4, 4), mode="hard")
     bad, _ = compare_paths(ref["route_path"], out2.route_path.cpu().numpy(), ref["level_margins"])
     assert bad == 0
+
+
+@pytest.mark.parametrize("precision,dtype", [("exact", torch.float32), ("fast", torch.bfloat16)])
+def test_six_level_router_4096_experts(cuda_device, precision, dtype):
+    """Config-4 tree (4^6 = 4096 experts, 6 levels) against the L-level oracle
+    restatement (parity beyond 3 levels is not pinned by the reference)."""
+    from sb200 import synth
+    H, S, br = 256, 64, (4, 4, 4, 4, 4, 4)
+    w = synth.router_weights(H, S, br, seed=9, perturb=True)
+    r = make_router(w, H, S, br, cuda_device)
+    x = synth.hidden_states(200, H, seed=10, dtype=dtype)
+    got = r.route(x.to(cuda_device), select="hard", k=8, precision=precision)
+    ref = orouter.router_forward(w, x.float().numpy(), br, mode="hard", k=8)
+    assert got["expert_probs"].shape == (200, 4096) and got["route_path"].shape == (200, 6)
+    check_against(ref, got, "hard", wtol=1e-5 if precision == "exact" else 2e-2)

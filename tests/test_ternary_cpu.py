@@ -67,3 +67,12 @@ def test_device_layout_pair_expansion_formula():
                 else:
                     val = float(np.array([half << 16], np.uint32).view(np.float32)[0])
                 assert val == T[0, 2 * j + e]
+
+
+def test_torch_packer_matches_host_packer():
+    from sb200.ternary import pack_device, pack_device_torch
+    rng = np.random.default_rng(9)
+    for shape in [(5, 70), (128, 2048), (3, 16)]:
+        T = rng.integers(-1, 2, size=shape, dtype=np.int8)
+        a = pack_device_torch(torch.from_numpy(T)).numpy().view(np.uint32)
+        assert np.array_equal(a, pack_device(T))
