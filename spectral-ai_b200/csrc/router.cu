@@ -279,6 +279,10 @@ struct TreeDev {
   float tau;    // clamp(T, 0.01)
   const float* centers;  // [total,3]
   const float* portals;  // [total,12]
+  float bbox[SB_MAX_LEVELS][6];  // per level: min x,y,z then max x,y,z of the centers
+  int S;
+  const float* refb;     // [total]
+  const void* refw;      // [total,S], bf16 (FAST) or fp32 (EXACT)
 };
 
 struct DescentOut {
@@ -291,45 +295,156 @@ struct DescentOut {
   int k;
 };
 
-// HARD: one thread per token.  Only the chosen node of a level carries
-// probability, so the parent mask is log(p_c + 1e-10) inside the chosen
-// parent and log(1e-10) elsewhere, and only n at the chosen node is read.
-// n is node-major: n[node * B + tok].
-__global__ void __launch_bounds__(256) descent_hard_kernel(const float* __restrict__ pos,
-                                                           const float* __restrict__ n, int64_t B,
-                                                           TreeDev t, DescentOut o) {
+// HARD: a group of G lanes per token (G = 8 for large batches, 32 when the
+// batch is too small to fill the GPU otherwise).  Only the chosen node of a
+// level carries probability, so the parent mask is log(p_c + 1e-10) inside the
+// chosen parent and log(1e-10) elsewhere, and only the chosen node's refraction
+// n = sigmoid(Wr[c] . spec + br[c]) is needed: the group computes it from the
+// token's spectral row (bf16 for FAST, fp32 for EXACT), one coalesced row read
+// per level.
+//
+// Exact pruning: after the chosen parent's children are scored, every other
+// node of the level has logit <= -dmin^2/denom + log(1e-10), where dmin is the
+// distance from the position to the bounding box of the level's centers.  When
+// the best in-parent logit beats that bound (with a margin for fp32 rounding),
+// no other node can win and the scan over the rest of the level is skipped.
+// When any group of the warp cannot prove that, every group of the warp scans
+// its whole level (the full scan is always the exact answer), which keeps all
+// shuffles warp-uniform.  Either scan is spread over the group's lanes and
+// reduced with the first-index rule of torch.argmax.
+constexpr int HARD_WARPS = 8;
+
+template <int G>
+__device__ __forceinline__ float group_sum(float v) {
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;  // butterfly: every lane of the group holds the same bits
+}
+template <int G>
+__device__ __forceinline__ void group_argmax(float& v, int& i) {
+#pragma unroll
+  for (int o = G / 2; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, i, o);
+    if (ov > v || (ov == v && oi < i)) {
+      v = ov;
+      i = oi;
+    }
+  }
+  // the group's first lane's pair for all of it: with NaN logits the lanes'
+  // pairs could differ
+  v = __shfl_sync(0xffffffffu, v, 0, G);
+  i = __shfl_sync(0xffffffffu, i, 0, G);
+}
+
+template <int G>
+__device__ __forceinline__ float dot_spec_group(const __nv_bfloat16* sp, const __nv_bfloat16* wp, int S,
+                                                int sub) {
+  float a0 = 0.f, a1 = 0.f;
+  for (int i = sub * 8; i < S; i += 8 * G) {
+    const uint4 u = *reinterpret_cast<const uint4*>(sp + i);
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(wp + i));
+    const __nv_bfloat162* hu = reinterpret_cast<const __nv_bfloat162*>(&u);
+    const __nv_bfloat162* hv = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 x = __bfloat1622float2(hu[e]), y = __bfloat1622float2(hv[e]);
+      a0 = fmaf(x.x, y.x, a0);
+      a1 = fmaf(x.y, y.y, a1);
+    }
+  }
+  return group_sum<G>(a0 + a1);
+}
+template <int G>
+__device__ __forceinline__ float dot_spec_group(const float* sp, const float* wp, int S, int sub) {
+  float a0 = 0.f, a1 = 0.f;
+  for (int i = sub * 4; i < S; i += 4 * G) {
+    const float4 u = *reinterpret_cast<const float4*>(sp + i);
+    const float4 v = __ldg(reinterpret_cast<const float4*>(wp + i));
+    a0 = fmaf(u.x, v.x, fmaf(u.z, v.z, a0));
+    a1 = fmaf(u.y, v.y, fmaf(u.w, v.w, a1));
+  }
+  return group_sum<G>(a0 + a1);
+}
+
+template <typename TS, int G>
+__global__ void __launch_bounds__(HARD_WARPS * 32) descent_hard_kernel(const float* __restrict__ pos,
+                                                                       const TS* __restrict__ spec,
+                                                                       int64_t B, TreeDev t, DescentOut o) {
+  constexpr int TPW = 32 / G;  // tokens per warp
   const float m_out = logf(0.0f + 1e-10f);
-  for (int64_t tok = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; tok < B;
-       tok += (int64_t)gridDim.x * blockDim.x) {
+  const TS* __restrict__ wr = static_cast<const TS*>(t.refw);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int grp = lane / G, sub = lane % G;
+  // the loop runs over whole warps so that every lane takes every shuffle;
+  // a group past the end works on the last token and writes nothing
+  for (int64_t base = ((int64_t)blockIdx.x * HARD_WARPS + warp) * TPW; base < B;
+       base += (int64_t)gridDim.x * HARD_WARPS * TPW) {
+    const bool valid = base + grp < B;
+    const int64_t tok = valid ? base + grp : B - 1;
     const float4 p4 = reinterpret_cast<const float4*>(pos)[tok];
     float cx = p4.x, cy = p4.y, cz = p4.z;
+    const TS* srow = spec + tok * (int64_t)t.S;
     int prev = 0;
     float pc = 1.f;
     int choice = 0;
     for (int l = 0; l < t.L; ++l) {
       const int Nl = t.nodes[l], off = t.offset[l], nb = t.branching[l];
       const float m_in = logf(pc + 1e-10f);
-      const int lo = prev * nb, hi = lo + nb;
+      const int lo = l > 0 ? prev * nb : 0, hi = l > 0 ? lo + nb : Nl;
       const float* cen = t.centers + (size_t)off * 3;
       float best = -INFINITY;
-      int bi = 0;
-      for (int j = 0; j < Nl; ++j) {
-        const float dx = cx - __ldg(cen + 3 * j), dy = cy - __ldg(cen + 3 * j + 1),
-                    dz = cz - __ldg(cen + 3 * j + 2);
-        const float d2 = (dx * dx + dy * dy) + dz * dz;
-        float lg = -d2 / t.denom;
-        if (l > 0) lg = lg + ((j >= lo && j < hi) ? m_in : m_out);
-        if (lg > best) {  // strict: the first maximum wins, like torch.argmax
-          best = lg;
-          bi = j;
+      int bi = 0x7fffffff;
+      // a warp-uniform trip count (groups have the same nb; level 0 is whole)
+      for (int j0 = 0; j0 < hi - lo; j0 += G) {
+        const int j = lo + j0 + sub;
+        if (j < hi) {
+          const float dx = cx - __ldg(cen + 3 * j), dy = cy - __ldg(cen + 3 * j + 1),
+                      dz = cz - __ldg(cen + 3 * j + 2);
+          const float d2 = (dx * dx + dy * dy) + dz * dz;
+          float lg = -d2 / t.denom;
+          if (l > 0) lg = lg + m_in;
+          if (lg > best) {  // strided scan: a lane's first maximum is its lowest index
+            best = lg;
+            bi = j;
+          }
         }
       }
-      choice = bi;
-      const float nv = __ldg(n + (int64_t)(off + choice) * B + tok);
+      group_argmax<G>(best, bi);
+      if (l > 0) {
+        const float* bb = t.bbox[l];
+        const float ex = fmaxf(fmaxf(bb[0] - cx, cx - bb[3]), 0.f);
+        const float ey = fmaxf(fmaxf(bb[1] - cy, cy - bb[4]), 0.f);
+        const float ez = fmaxf(fmaxf(bb[2] - cz, cz - bb[5]), 0.f);
+        const float bound = -((ex * ex + ey * ey) + ez * ez) / t.denom + m_out;
+        const float margin = 1e-4f + 1e-5f * (fabsf(best) + fabsf(bound));
+        if (__any_sync(0xffffffffu, !(best > bound + margin))) {
+          best = -INFINITY;
+          bi = 0x7fffffff;
+          for (int j0 = 0; j0 < Nl; j0 += G) {
+            const int j = j0 + sub;
+            if (j < Nl) {
+              const float dx = cx - __ldg(cen + 3 * j), dy = cy - __ldg(cen + 3 * j + 1),
+                          dz = cz - __ldg(cen + 3 * j + 2);
+              const float d2 = (dx * dx + dy * dy) + dz * dz;
+              const float lg = -d2 / t.denom + ((j >= lo && j < hi) ? m_in : m_out);
+              if (lg > best) {
+                best = lg;
+                bi = j;
+              }
+            }
+          }
+          group_argmax<G>(best, bi);
+        }
+      }
+      // every logit NaN: torch.argmax would report the first NaN, the scan's first index
+      choice = bi == 0x7fffffff ? lo : bi;
+      const int node = off + choice;
+      const float nv = sigmoidf_(dot_spec_group<G>(srow, wr + (size_t)node * t.S, t.S, sub) + __ldg(t.refb + node));
       pc = nv / (nv + 1e-8f);
-      if (o.route_path) o.route_path[tok * t.L + l] = choice;
+      if (o.route_path && valid && sub == 0) o.route_path[tok * t.L + l] = choice;
       if (l < t.L - 1) {
-        const float* a = t.portals + (size_t)(off + choice) * 12;
+        const float* a = t.portals + (size_t)node * 12;
         const float lx = fmaf(__ldg(a + 0), cx, fmaf(__ldg(a + 1), cy, fmaf(__ldg(a + 2), cz, __ldg(a + 3))));
         const float ly = fmaf(__ldg(a + 4), cx, fmaf(__ldg(a + 5), cy, fmaf(__ldg(a + 6), cz, __ldg(a + 7))));
         const float lz = fmaf(__ldg(a + 8), cx, fmaf(__ldg(a + 9), cy, fmaf(__ldg(a + 10), cz, __ldg(a + 11))));
@@ -339,19 +454,22 @@ __global__ void __launch_bounds__(256) descent_hard_kernel(const float* __restri
       }
       prev = choice;
     }
+    if (!valid) continue;
     const int NL = t.nodes[t.L - 1];
     const bool live = pc > 0.f;  // an all-zero row: argmax returns index 0
-    if (o.expert_id) o.expert_id[tok] = live ? choice : 0;
-    if (o.confidence) o.confidence[tok] = live ? pc : 0.f;
-    if (o.expert_probs)
-      for (int j = 0; j < NL; ++j) o.expert_probs[tok * NL + j] = (j == choice) ? pc : 0.f;
+    if (o.expert_id && sub == 0) o.expert_id[tok] = live ? choice : 0;
+    if (o.confidence && sub == 0) o.confidence[tok] = live ? pc : 0.f;
+    if (o.expert_probs) {
+      float* row = o.expert_probs + tok * NL;
+      for (int j = sub; j < NL; j += G) row[j] = (j == choice) ? pc : 0.f;
+    }
     if (o.topk_ids) {
       // top-k of a one-hot row: the chosen expert, then the lowest other ids
       const int k = o.k;
       const float v0 = live ? pc : 0.f;
       const float e0 = 1.f, ez = expf(0.f - v0);
       const float den = live ? e0 + (float)(k - 1) * ez : (float)k;
-      for (int i = 0; i < k; ++i) {
+      for (int i = sub; i < k; i += G) {
         int id;
         float w;
         if (live) {
@@ -528,6 +646,7 @@ struct sb_router {
   float* refb = nullptr;             // [total]
   float* portals = nullptr;          // [total,12]
   CUtensorMap tm_w1{}, tm_w2{}, tm_w3s{}, tm_wr{};
+  float bbox[SB_MAX_LEVELS][6] = {};  // per level: min x,y,z, max x,y,z of the centers
 };
 
 namespace sb {
@@ -675,6 +794,16 @@ extern "C" int sb_router_upload(sb_router* h, const sb_router_weights* w) {
   }
   for (int l = 0; l < L; ++l) {
     const size_t off = h->offset[l], n = h->nodes[l];
+    for (int a = 0; a < 3; ++a) {
+      float mn = INFINITY, mx = -INFINITY;
+      for (size_t j = 0; j < n; ++j) {
+        const float v = w->centers[l][j * 3 + a];
+        mn = v < mn ? v : mn;
+        mx = v > mx ? v : mx;
+      }
+      h->bbox[l][a] = mn;
+      h->bbox[l][3 + a] = mx;
+    }
     if ((rc = upload_f32(h->centers + off * 3, w->centers[l], n * 3, 0.f)) ||
         (rc = upload_f32(h->refw + off * S, w->refract_w[l], n * S, 0.f)) ||
         (rc = upload_f32(h->refb + off, w->refract_b[l], n, 0.f))) {
@@ -821,7 +950,8 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
         return rc;
     }
     EpiSigmoidN e3{h->refb, nbuf, ldn, T, node_major};
-    switch (h->bn_ref) {  // tm_wr's box height matches this tile width (set at create)
+    if (select == SB_SELECT_HARD) rc = SB_OK;  // HARD evaluates the chosen nodes in the descent
+    else switch (h->bn_ref) {  // tm_wr's box height matches this tile width (set at create)
       case 32: rc = launch_gemm_tc<32, 4>("router_refract_tc", ts, h->tm_wr, h->tm_wr, M, T, S, e3, stream); break;
       case 64: rc = launch_gemm_tc<64, 4>("router_refract_tc", ts, h->tm_wr, h->tm_wr, M, T, S, e3, stream); break;
       case 96: rc = launch_gemm_tc<96, 4>("router_refract_tc", ts, h->tm_wr, h->tm_wr, M, T, S, e3, stream); break;
@@ -852,7 +982,7 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
       sgemm_nt_kernel<float, ACT_TANH><<<grid2, 256, 0, stream>>>(G32, h->w2_f32, h->b2, S32, M, S, H, S, 0);
       SB_CUDA_TRY(cudaGetLastError());
     }
-    {
+    if (select == SB_SELECT_SOFT) {
       ProfScope prof3("router_refract_f32", stream);
       sgemm_nt_kernel<float, ACT_SIGMOID><<<grid3, 256, 0, stream>>>(S32, h->refw, h->refb, nbuf, M, T, S,
                                                                      ldn, node_major);
@@ -885,14 +1015,32 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
   t.tau = Tm < 0.01f ? 0.01f : Tm;
   t.centers = h->centers;
   t.portals = h->portals;
+  for (int l = 0; l < L; ++l)
+    for (int a = 0; a < 6; ++a) t.bbox[l][a] = h->bbox[l][a];
+  t.S = S;
+  t.refb = h->refb;
+  t.refw = precision == SB_PREC_FAST ? static_cast<const void*>(h->wr_bf16) : static_cast<const void*>(h->refw);
   DescentOut o{out->topk_ids, out->topk_weights, out->expert_id, out->expert_probs,
                out->route_path, out->confidence, top_k};
   ProfScope prof("router_descent", stream);
   if (select == SB_SELECT_HARD) {
-    int64_t blocks = (batch + 255) / 256;
-    const int64_t cap = (int64_t)num_sms() * 16;
+    // 8 lanes per token once the batch fills every warp slot of the GPU that
+    // way; otherwise a whole warp per token for parallelism
+    const bool wide = batch < (int64_t)num_sms() * 64 * 4;
+    const int tpw = wide ? 1 : 4;
+    int64_t blocks = (batch + (int64_t)HARD_WARPS * tpw - 1) / ((int64_t)HARD_WARPS * tpw);
+    const int64_t cap = (int64_t)num_sms() * 8;
     if (blocks > cap) blocks = cap;
-    descent_hard_kernel<<<(unsigned)blocks, 256, 0, stream>>>(pos, nbuf, batch, t, o);
+    const dim3 grid((unsigned)blocks), block(HARD_WARPS * 32);
+    if (precision == SB_PREC_FAST) {
+      const __nv_bfloat16* sp = static_cast<const __nv_bfloat16*>(spec);
+      if (wide) descent_hard_kernel<__nv_bfloat16, 32><<<grid, block, 0, stream>>>(pos, sp, batch, t, o);
+      else descent_hard_kernel<__nv_bfloat16, 8><<<grid, block, 0, stream>>>(pos, sp, batch, t, o);
+    } else {
+      const float* sp = static_cast<const float*>(spec);
+      if (wide) descent_hard_kernel<float, 32><<<grid, block, 0, stream>>>(pos, sp, batch, t, o);
+      else descent_hard_kernel<float, 8><<<grid, block, 0, stream>>>(pos, sp, batch, t, o);
+    }
   } else {
     if (dsm_soft > 48 * 1024) {
       static bool attr = false;
