@@ -46,19 +46,19 @@ struct GemmCfg {
   static_assert(B_BYTES % 1024 == 0, "B tile must keep 1024-byte alignment");
 };
 
-// Warp-uniform bounded wait: every lane polls, the decision is made together.
+// Warp-uniform bounded wait: every lane polls (sleeping between polls), the
+// decision is made together.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity, unsigned code) {
   const uint32_t a = smem_u32(bar);
+  if (__all_sync(0xffffffffu, mbar_try_wait(a, parity))) return true;
   const uint64_t t0 = globaltimer();
-  for (uint32_t it = 0;; ++it) {
-    const bool ok = mbar_try_wait(a, parity);
+  for (;;) {
+    const bool ok = mbar_try_wait_sleep(a, parity, SB_WAIT_SLEEP_NS);
     if (__all_sync(0xffffffffu, ok)) return true;
-    if ((it & 255u) == 255u) {
-      const bool late = globaltimer() - t0 > SB_WAIT_LIMIT_NS;
-      if (__any_sync(0xffffffffu, late)) {
-        if ((threadIdx.x & 31) == 0) set_status(code);
-        return false;
-      }
+    const bool late = globaltimer() - t0 > SB_WAIT_LIMIT_NS;
+    if (__any_sync(0xffffffffu, late)) {
+      if ((threadIdx.x & 31) == 0) set_status(code);
+      return false;
     }
   }
 }

@@ -87,14 +87,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return ok != 0;
 }
 
+// try_wait that may suspend the thread until the phase completes or `ns`
+// nanoseconds pass: a waiting warp sleeps instead of spinning, which leaves
+// the issue slots of its scheduler to the warps that are working.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar_addr, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 P, [%1], %2, %3;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+constexpr uint32_t SB_WAIT_SLEEP_NS = 1000000;  // one suspension: at most 1 ms
+
 // Bounded wait for the phase with the given parity to complete.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int code) {
   const uint32_t a = smem_u32(bar);
   if (mbar_try_wait(a, parity)) return true;
   const uint64_t t0 = globaltimer();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(a, parity)) return true;
-    if ((it & 255u) == 0u && globaltimer() - t0 > SB_WAIT_LIMIT_NS) {
+  for (;;) {
+    if (mbar_try_wait_sleep(a, parity, SB_WAIT_SLEEP_NS)) return true;
+    if (globaltimer() - t0 > SB_WAIT_LIMIT_NS) {
       set_status(code);
       return false;
     }

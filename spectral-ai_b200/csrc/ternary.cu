@@ -9,13 +9,17 @@
 // Device layout: uint32 [N, KW] with KW = ceil(K/64)*4 words per output row
 // (row n holds K contiguous, padded to a multiple of 64 with zeros).  Word w of
 // row n covers K indices 16w .. 16w+15; element 16w+2j+e (e = 0,1; j = 0..7)
-// has its non-zero flag at bit 16e+j and its sign flag at bit 16e+8+j.  A pair
-// (2j, 2j+1) expands to two packed 16-bit floats with
-//   ((w & (0x00010001 << j)) * (M << (P - j))) | ((w & (0x01000100 << j)) << (7 - j))
-// where M << P is the magnitude pattern of 1.0 (bf16: 0x7F << 7, fp16: 0xF << 10).
+// is stored as the biased code value+1 in {0,1,2} at bits 16e+2j .. 16e+2j+1
+// (padding holds code 1, value 0).  A pair (2j, 2j+1) becomes two packed
+// 16-bit floats with one shift, one and-or and one packed subtraction:
+//   ((w >> 2j) & 0x00030003) | B  is the pair  (b + code_2j, b + code_2j+1)
+// with B the 16-bit float b = 128 (bf16 0x4300) or b = 1024 (fp16 0x6400),
+// whose unit in the last place is 1; subtracting b + 1 leaves code - 1 =
+// value exactly.
 #include "common.cuh"
 #include "ternary_gemm.cuh"
 #include "ternary_ts.cuh"
+#include "ternary_pair.cuh"
 
 #include <cstdlib>
 #include <cstring>
@@ -39,7 +43,7 @@ __global__ void ternary_repack_kernel(const uint32_t* __restrict__ ref, int64_t 
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t n = i / KW, w = i % KW;
-    uint32_t out = 0;
+    uint32_t out = 0x55555555u;  // every element code 1 (value 0)
     if (w < P) {
       const uint32_t codes = ref[w * N + n];  // 16 codes of K rows 16w..16w+15, column n
 #pragma unroll
@@ -47,10 +51,9 @@ __global__ void ternary_repack_kernel(const uint32_t* __restrict__ ref, int64_t 
         const int64_t k = w * 16 + t;
         if (k >= K) break;
         const int s = ternary_code_to_sign((codes >> (2 * t)) & 3u);
-        if (s == 0) continue;
         const int e = t & 1, j = t >> 1;
-        out |= 1u << (16 * e + j);
-        if (s < 0) out |= 1u << (16 * e + 8 + j);
+        const int sh = 16 * e + 2 * j;
+        out = (out & ~(3u << sh)) | ((uint32_t)(s + 1) << sh);
       }
     }
     dst[i] = out;
@@ -116,24 +119,28 @@ __global__ void moe_hist_kernel(const int32_t* __restrict__ ids, int64_t R, int 
 }
 
 // expert offsets (exclusive scan), scatter cursors and the m-tile table
+// Expert segments start on 32-row boundaries (segment = count rounded up to
+// 32); m-tiles of `tile_rows` rows cover them, `rows` valid and `pad` rows up
+// to the segment end (a multiple of 32).
 __global__ void moe_scan_kernel(const int* __restrict__ counts, int E, int* __restrict__ offsets,
                                 int* __restrict__ cursor, MTile* __restrict__ mtiles,
-                                int* __restrict__ num_mtiles, int max_mtiles) {
+                                int* __restrict__ num_mtiles, int max_mtiles, int tile_rows) {
   if (threadIdx.x != 0 || blockIdx.x != 0) return;
   int off = 0, nt = 0;
   for (int e = 0; e < E; ++e) {
     const int c = counts[e];
+    const int cp = (c + 31) & ~31;
     offsets[e] = off;
     cursor[e] = 0;
-    for (int r = 0; r < c && nt < max_mtiles; r += 128) {
+    for (int r = 0; r < cp && nt < max_mtiles; r += tile_rows) {
       MTile t;
       t.expert = e;
       t.row0 = off + r;
-      t.rows = (c - r) < 128 ? (c - r) : 128;
-      t.pad = 0;
+      t.rows = (c - r) < tile_rows ? (c - r) : tile_rows;
+      t.pad = (cp - r) < tile_rows ? (cp - r) : tile_rows;
       mtiles[nt++] = t;
     }
-    off += c;
+    off += cp;
   }
   *num_mtiles = nt;
 }
@@ -269,7 +276,7 @@ namespace {
 inline int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
 struct MoeLayout {
-  int64_t R, ldx, ldh, max_mt;
+  int64_t R, Rp, ldx, ldh, max_mt;  // Rp: rows with every expert segment padded to 32
   size_t off_counts, off_offsets, off_cursor, off_nmt, off_mtiles, off_roww, off_inv, off_ids, off_xp,
       off_hp, off_yp, total;
 };
@@ -277,9 +284,10 @@ struct MoeLayout {
 MoeLayout moe_layout(int64_t B, int64_t H, int64_t I, int32_t E, int32_t k) {
   MoeLayout L{};
   L.R = B * k;
+  L.Rp = L.R + 32 * (int64_t)E;
   L.ldx = round_up(H, 64);
   L.ldh = round_up(I, 64);
-  L.max_mt = L.R / 128 + E + 1;
+  L.max_mt = L.Rp / 128 + E + 1;
   size_t o = 0;
   auto take = [&](size_t bytes) {
     size_t at = o;
@@ -291,12 +299,12 @@ MoeLayout moe_layout(int64_t B, int64_t H, int64_t I, int32_t E, int32_t k) {
   L.off_cursor = take(sizeof(int) * E);
   L.off_nmt = take(sizeof(int));
   L.off_mtiles = take(sizeof(MTile) * L.max_mt);
-  L.off_roww = take(sizeof(float) * L.R);
+  L.off_roww = take(sizeof(float) * L.Rp);
   L.off_inv = take(sizeof(int) * L.R);
   L.off_ids = take(sizeof(int) * L.R);
-  L.off_xp = take((size_t)L.R * L.ldx * 2);
-  L.off_hp = take((size_t)L.R * L.ldh * 2);
-  L.off_yp = take((size_t)L.R * H * 4);
+  L.off_xp = take((size_t)L.Rp * L.ldx * 2);
+  L.off_hp = take((size_t)L.Rp * L.ldh * 2);
+  L.off_yp = take((size_t)L.Rp * H * 4);
   L.total = o;
   return L;
 }
@@ -335,11 +343,50 @@ int launch_ts(const char* name, const CUtensorMap& tx, const CUtensorMap& tw0, c
   return SB_OK;
 }
 
-// Which grouped ternary GEMM runs: "ts" (weights in TMEM, the default) or
-// "ss" (weights unpacked into shared memory), from SB_TERNARY_ENGINE.
-bool use_ts_engine() {
+// Which grouped ternary GEMM runs, from SB_TERNARY_ENGINE: "pair" (CTA pairs,
+// cta_group::2; the default), "ts" (one CTA per tile, weights in TMEM) or
+// "ss" (one CTA per tile, weights unpacked into shared memory).
+enum { ENGINE_PAIR = 0, ENGINE_TS = 1, ENGINE_SS = 2 };
+int ternary_engine() {
   const char* e = getenv("SB_TERNARY_ENGINE");
-  return !(e && strcmp(e, "ss") == 0);
+  if (e && strcmp(e, "ss") == 0) return ENGINE_SS;
+  if (e && strcmp(e, "ts") == 0) return ENGINE_TS;
+  return ENGINE_PAIR;
+}
+bool use_ts_engine() { return ternary_engine() != ENGINE_SS; }
+
+// CTA pairs (clusters of two) as many as fit at once, one persistent pair per two SMs.
+template <int MODE, int FMT>
+int launch_pair(const char* name, const CUtensorMap& tx, const CUtensorMap& tw0, const CUtensorMap& tw1,
+                const CUtensorMap& tout, const TernGemmParams& p, cudaStream_t stream) {
+  auto kern = ternary_pair_kernel<MODE, FMT>;
+  static int pairs[64] = {};
+  int dev = 0;
+  SB_CUDA_TRY(cudaGetDevice(&dev));
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(TP_THREADS);
+  cfg.dynamicSmemBytes = TP_SMEM_BYTES;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (dev >= 64) return fail(SB_ERR_CUDA, "device ordinal %d out of range", dev);
+  if (!pairs[dev]) {
+    SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TP_SMEM_BYTES));
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    int n = 0;
+    SB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    if (n < 1) return fail(SB_ERR_CUDA, "no CTA pair of the ternary kernel fits on this GPU");
+    pairs[dev] = n;
+  }
+  cfg.gridDim = dim3(2 * pairs[dev]);
+  ProfScope prof(name, stream);
+  SB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tx, tw0, tw1, tout, p));
+  return SB_OK;
 }
 
 int check_ternary_shapes(int64_t H, int64_t I) {
@@ -381,6 +428,9 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   __half* hp = reinterpret_cast<__half*>(ws + L.off_hp);
   float* yp = reinterpret_cast<float*>(ws + L.off_yp);
   const int fmt_gu = (x_dtype == SB_BF16) ? 1 : 0;  // bf16 inputs stay bf16; fp32 inputs go to fp16
+  // the pair engine stores y rows with TMA: its row pitch (H floats) must be a 16-byte multiple
+  int engine = ternary_engine();
+  if (engine == ENGINE_PAIR && (H % 4) != 0) engine = ENGINE_TS;
 
   {
     ProfScope prof("moe_dispatch", stream);
@@ -389,7 +439,8 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
     int64_t blocks = (R + 255) / 256;
     if (blocks > 4096) blocks = 4096;
     moe_hist_kernel<<<(unsigned)blocks, 256, 0, stream>>>(ids, R, E, counts);
-    moe_scan_kernel<<<1, 32, 0, stream>>>(counts, E, offsets, cursor, mtiles, nmt, (int)L.max_mt);
+    moe_scan_kernel<<<1, 32, 0, stream>>>(counts, E, offsets, cursor, mtiles, nmt, (int)L.max_mt,
+                                          engine == ENGINE_PAIR ? TP_TILE_ROWS : 128);
     int64_t wblocks = (R * 32 + 255) / 256;
     if (wblocks > (int64_t)num_sms() * 16) wblocks = (int64_t)num_sms() * 16;
     const bool x16 = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
@@ -405,20 +456,28 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   }
 
   // tensor maps: activations (SW128, 64 x 128 box) and packed weights (16 B x rows box)
-  const bool ts = use_ts_engine();
   CUtensorMap tmx, tmg, tmu, tmh, tmd;
   const CUtensorMapDataType adt = fmt_gu ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const int64_t KWh = ternary_row_words(H), KWi = ternary_row_words(I);
-  const uint32_t gu_box = 128, d_box = 256;
-  if ((rc = make_tmap_2d(&tmx, xp, adt, 2, L.R, H, L.ldx, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) ||
-      (rc = make_tmap_2d(&tmg, gate, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, 4, gu_box,
+  const bool pair = engine == ENGINE_PAIR;
+  const uint32_t gu_box = pair ? 64 : 128, d_box = pair ? 128 : 256;
+  const uint32_t p_words = pair ? TP_KB / 16 : 4;  // packed words per row in one weight box
+  const uint32_t x_rows = pair ? TP_HALF_ROWS : 128;  // token rows per activation box
+  if ((rc = make_tmap_2d(&tmx, xp, adt, 2, L.Rp, H, L.ldx, 64, x_rows, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&tmg, gate, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, p_words, gu_box,
                          CU_TENSOR_MAP_SWIZZLE_NONE)) ||
-      (rc = make_tmap_2d(&tmu, up, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, 4, gu_box,
+      (rc = make_tmap_2d(&tmu, up, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, p_words, gu_box,
                          CU_TENSOR_MAP_SWIZZLE_NONE)) ||
-      (rc = make_tmap_2d(&tmh, hp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.R, I, L.ldh, 64, 128,
+      (rc = make_tmap_2d(&tmh, hp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.Rp, I, L.ldh, 64, x_rows,
                          CU_TENSOR_MAP_SWIZZLE_128B)) ||
-      (rc = make_tmap_2d(&tmd, down, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * H, KWi, KWi, 4, d_box,
+      (rc = make_tmap_2d(&tmd, down, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * H, KWi, KWi, p_words, d_box,
                          CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  CUtensorMap tmh_out{}, tmy_out{};
+  if (pair && ((rc = make_tmap_2d(&tmh_out, hp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.Rp, I, L.ldh, 16, 32,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+               (rc = make_tmap_2d(&tmy_out, yp, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, L.Rp, H, H, 32, 32,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE))))
     return rc;
 
   TernGemmParams pg{};
@@ -432,7 +491,10 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   pg.s1 = us;
   pg.out = hp;
   pg.ldo = L.ldh;
-  if (ts)
+  if (engine == ENGINE_PAIR)
+    rc = fmt_gu ? launch_pair<TG_GATEUP, 1>("ternary_gateup_tc", tmx, tmg, tmu, tmh_out, pg, stream)
+                : launch_pair<TG_GATEUP, 0>("ternary_gateup_tc", tmx, tmg, tmu, tmh_out, pg, stream);
+  else if (engine == ENGINE_TS)
     rc = fmt_gu ? launch_ts<TG_GATEUP, 1>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream)
                 : launch_ts<TG_GATEUP, 0>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream);
   else
@@ -451,7 +513,9 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   pd.row_w = row_w;
   pd.out = yp;
   pd.ldo = H;
-  if (ts)
+  if (engine == ENGINE_PAIR)
+    rc = launch_pair<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, tmy_out, pd, stream);
+  else if (engine == ENGINE_TS)
     rc = launch_ts<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, pd, stream);
   else
     rc = launch_tgemm<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, pd, stream);
@@ -557,7 +621,7 @@ extern "C" int sb_ternary_linear(const void* x, int x_dtype, int64_t M, int64_t 
   fill_i32_kernel<<<(unsigned)blocks, 256, 0, st>>>(ids, M, 0);
   SB_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int), st));
   moe_hist_kernel<<<(unsigned)blocks, 256, 0, st>>>(ids, M, 1, counts);
-  moe_scan_kernel<<<1, 32, 0, st>>>(counts, 1, offsets, cursor, mtiles, nmt, (int)L.max_mt);
+  moe_scan_kernel<<<1, 32, 0, st>>>(counts, 1, offsets, cursor, mtiles, nmt, (int)L.max_mt, 128);
   {
     int64_t cb = (M * K + 255) / 256;
     if (cb > (int64_t)num_sms() * 32) cb = (int64_t)num_sms() * 32;

@@ -60,27 +60,32 @@ constexpr uint32_t TG_TMEM_COLS = 512;
 static_assert(TG_STAGE_BYTES % 1024 == 0, "stage alignment");
 
 // Two ternary weights (elements 2j, 2j+1 of a word) as two 16-bit floats.
-//   FMT 1: bf16 (+1 = 0x3F80), FMT 0: fp16 (+1 = 0x3C00); sign in bit 15.
+//   FMT 1: bf16, FMT 0: fp16.  The biased codes c in {0,1,2} are placed in the
+//   mantissa of b = 128 (bf16) / 1024 (fp16), whose last place is 1, and b + 1
+//   is subtracted: (b + c) - (b + 1) = c - 1, exact in both formats.
 template <int FMT>
 __device__ __forceinline__ uint32_t tern_pair(uint32_t w, int j) {
-  const uint32_t nz = w & (0x00010001u << j);
-  const uint32_t sg = w & (0x01000100u << j);
-  const uint32_t mag = FMT ? nz * (0x7Fu << (7 - j)) : nz * (0xFu << (10 - j));
-  return mag | (sg << (7 - j));
+  const uint32_t t = ((w >> (2 * j)) & 0x00030003u) | (FMT ? 0x43004300u : 0x64006400u);
+  uint32_t r;
+  if (FMT)
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(t), "r"(0x43014301u));
+  else
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(t), "r"(0x64016401u));
+  return r;
 }
 
+// Bounded wait by a whole warp (the lanes leave together); sleeps while waiting.
 __device__ __forceinline__ bool mbar_wait_warp_t(uint64_t* bar, uint32_t parity, unsigned code) {
   const uint32_t a = smem_u32(bar);
+  if (__all_sync(0xffffffffu, mbar_try_wait(a, parity))) return true;
   const uint64_t t0 = globaltimer();
-  for (uint32_t it = 0;; ++it) {
-    const bool ok = mbar_try_wait(a, parity);
+  for (;;) {
+    const bool ok = mbar_try_wait_sleep(a, parity, SB_WAIT_SLEEP_NS);
     if (__all_sync(0xffffffffu, ok)) return true;
-    if ((it & 255u) == 255u) {
-      const bool late = globaltimer() - t0 > SB_WAIT_LIMIT_NS;
-      if (__any_sync(0xffffffffu, late)) {
-        if ((threadIdx.x & 31) == 0) set_status(code);
-        return false;
-      }
+    const bool late = globaltimer() - t0 > SB_WAIT_LIMIT_NS;
+    if (__any_sync(0xffffffffu, late)) {
+      if ((threadIdx.x & 31) == 0) set_status(code);
+      return false;
     }
   }
 }

@@ -1,9 +1,9 @@
 """Torch-facing wrappers of the ternary C-ABI entry points.
 
 Weights live on the device in the B200 layout: uint32 [N, KW], KW =
-ceil(K/64)*4, one word per 16 consecutive K of an output row; element 2j of a
-word has its non-zero flag at bit j and its sign at bit 8+j, element 2j+1 at
-bits 16+j and 24+j.  ``pack_device`` builds it on the host from int8 ternary
+ceil(K/64)*4, one word per 16 consecutive K of an output row; element 2j+e of
+a word (e = 0, 1) is stored as the biased code value+1 in bits 16e+2j ..
+16e+2j+1, and padding holds code 1 (value 0).  ``pack_device`` builds it on the host from int8 ternary
 matrices in the PyTorch [out, in] layout; ``repack_reference`` converts the
 reference extension's packed layout (int32 [ceil(K/16), N],
 cuda/v5/ternary_torch_ext.cu:197-231) on the device.
@@ -31,12 +31,9 @@ def pack_device(T: np.ndarray) -> np.ndarray:
     KW = row_words(K)
     pad = np.zeros((N, KW * 16), np.int8)
     pad[:, :K] = T
-    g = pad.reshape(N, KW, 8, 2)          # [n, word, pair j, element e]
-    nz = (g != 0).astype(np.uint32)
-    sg = (g < 0).astype(np.uint32)
+    code = (pad.reshape(N, KW, 8, 2).astype(np.int64) + 1).astype(np.uint32)  # [n, word, j, e]
     j = np.arange(8, dtype=np.uint32)[None, None, :]
-    w = ((nz[..., 0] << j) | (sg[..., 0] << (8 + j)) |
-         (nz[..., 1] << (16 + j)) | (sg[..., 1] << (24 + j)))
+    w = (code[..., 0] << (2 * j)) | (code[..., 1] << (16 + 2 * j))
     return np.bitwise_or.reduce(w, axis=2).astype(np.uint32)
 
 
@@ -47,11 +44,9 @@ def pack_device_torch(T: torch.Tensor) -> torch.Tensor:
     KW = row_words(K)
     pad = torch.zeros(N, KW * 16, dtype=torch.int8, device=T.device)
     pad[:, :K] = T
-    g = pad.view(N, KW, 8, 2).to(torch.int64)
-    nz = (g != 0).to(torch.int64)
-    sg = (g < 0).to(torch.int64)
+    code = pad.view(N, KW, 8, 2).to(torch.int64) + 1
     j = torch.arange(8, device=T.device, dtype=torch.int64).view(1, 1, 8)
-    w = ((nz[..., 0] << j) | (sg[..., 0] << (8 + j)) | (nz[..., 1] << (16 + j)) | (sg[..., 1] << (24 + j)))
+    w = (code[..., 0] << (2 * j)) | (code[..., 1] << (16 + 2 * j))
     words = w.sum(dim=2)  # the bit fields of the 8 pairs are disjoint
     return torch.where(words >= 2 ** 31, words - 2 ** 32, words).to(torch.int32)
 

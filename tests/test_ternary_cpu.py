@@ -10,15 +10,16 @@ from conftest import load_golden
 
 
 def decode_device(words: np.ndarray, K: int) -> np.ndarray:
-    """Inverse of the split-plane device layout (test-side restatement)."""
+    """Inverse of the biased-code device layout (test-side restatement):
+    element 2j+e of a word is code value+1 at bits 16e+2j .. 16e+2j+1."""
     w = np.asarray(words).view(np.uint32)
     N, KW = w.shape
     j = np.arange(8, dtype=np.uint32)
     out = np.zeros((N, KW, 8, 2), np.int8)
     for e in range(2):
-        nz = (w[:, :, None] >> (16 * e + j)) & 1
-        sg = (w[:, :, None] >> (16 * e + 8 + j)) & 1
-        out[..., e] = (nz.astype(np.int8) * (1 - 2 * sg.astype(np.int8)))
+        code = (w[:, :, None] >> (16 * e + 2 * j)) & 3
+        assert (code <= 2).all(), "code 3 is not used"
+        out[..., e] = code.astype(np.int8) - 1
     return out.reshape(N, KW * 16)[:, :K]
 
 
@@ -49,24 +50,31 @@ def test_device_layout_round_trip(shape):
 
 
 def test_device_layout_pair_expansion_formula():
-    """Two elements per word expand to 16-bit +-1/0 with and/mul/shift (bf16 and fp16)."""
+    """Two elements per word become 16-bit +-1/0 with shift, and-or and one packed
+    subtraction of b+1 (b = 128 in bf16, 1024 in fp16): (b + code) - (b + 1)."""
     from sb200.ternary import pack_device
     rng = np.random.default_rng(5)
     T = rng.integers(-1, 2, size=(1, 16), dtype=np.int8)
     w = int(pack_device(T)[0, 0])
-    for fmt, (mul, top) in {"bf16": (0x7F, 7), "f16": (0xF, 10)}.items():
+    for fmt, (bias, bias1) in {"bf16": (0x4300, 0x4301), "f16": (0x6400, 0x6401)}.items():
+        def to_f(h):
+            if fmt == "f16":
+                return float(np.array([h], np.uint16).view(np.float16)[0])
+            return float(np.array([h << 16], np.uint32).view(np.float32)[0])
         for j in range(8):
-            nz = w & (0x00010001 << j)
-            sg = w & (0x01000100 << j)
-            v = ((nz * (mul << (top - j))) | (sg << (7 - j))) & 0xFFFFFFFF
+            t = ((w >> (2 * j)) & 0x00030003) | (bias | (bias << 16))
             for e in range(2):
-                half = (v >> (16 * e)) & 0xFFFF
-                dt = np.float16 if fmt == "f16" else None
-                if fmt == "f16":
-                    val = float(np.array([half], np.uint16).view(np.float16)[0])
-                else:
-                    val = float(np.array([half << 16], np.uint32).view(np.float32)[0])
-                assert val == T[0, 2 * j + e]
+                half = (t >> (16 * e)) & 0xFFFF
+                # the subtraction is exact: both operands and the result are representable
+                assert to_f(half) - to_f(bias1) == T[0, 2 * j + e]
+
+
+def test_padding_decodes_to_zero():
+    from sb200.ternary import pack_device
+    T = np.ones((2, 5), np.int8)
+    w = pack_device(T)
+    d = decode_device(w, w.shape[1] * 16)
+    assert (d[:, :5] == 1).all() and (d[:, 5:] == 0).all()
 
 
 def test_torch_packer_matches_host_packer():

@@ -20,6 +20,16 @@ pytestmark = pytest.mark.gpu
 NORM_TOL = 1e-3
 ELEM_TOL = 5e-3
 
+# the grouped GEMM engines (SB_TERNARY_ENGINE): CTA pairs (default), one CTA
+# with the weights in TMEM, one CTA with the weights in shared memory
+ENGINES = ["pair", "ts", "ss"]
+
+
+@pytest.fixture
+def engine(request, monkeypatch):
+    monkeypatch.setenv("SB_TERNARY_ENGINE", request.param)
+    return request.param
+
 
 def experts_from_golden(g, prefix, n):
     keys = ("gate_ternary", "up_ternary", "down_ternary", "gate_scale", "up_scale", "down_scale")
@@ -43,8 +53,9 @@ def test_repack_matches_host_layout(cuda_device):
         assert np.array_equal(dev, pack_device(T))
 
 
+@pytest.mark.parametrize("engine", ENGINES, indirect=True)
 @pytest.mark.parametrize("xdtype", [torch.float32, torch.bfloat16])
-def test_gated_mlp_matches_reference_golden(cuda_device, xdtype):
+def test_gated_mlp_matches_reference_golden(cuda_device, xdtype, engine):
     """Reference API ternary_gated_mlp on the golden expert (H=72, I=40: ragged K and N)."""
     import ternary_expert_ext as ext
     g = load_golden("ternary_small")
@@ -93,7 +104,8 @@ def test_ternary_linear(cuda_device):
         assert_close(y.cpu().numpy(), ref, f"linear {K}x{N}")
 
 
-def test_moe_combine_golden(cuda_device):
+@pytest.mark.parametrize("engine", ENGINES, indirect=True)
+def test_moe_combine_golden(cuda_device, engine):
     """Grouped MoE SwiGLU against the reference OLMoE forward_topk golden (6 experts, top-3)."""
     from sb200.ternary import TernaryExperts
     g = load_golden("ternary_small")
@@ -108,7 +120,8 @@ def test_moe_combine_golden(cuda_device):
     assert_close(y.cpu().numpy(), ref, "moe golden vs oracle")
 
 
-def test_moe_config2_sampled(cuda_device):
+@pytest.mark.parametrize("engine", ENGINES, indirect=True)
+def test_moe_config2_sampled(cuda_device, engine):
     """Config 2: 64 experts, 2048->1024->2048, 4096 tokens x top-8 with Zipf(1.1) loads."""
     from sb200 import synth
     from sb200.ternary import TernaryExperts
@@ -130,7 +143,8 @@ def test_moe_config2_sampled(cuda_device):
     torch.testing.assert_close(yb.float(), y, rtol=8e-3, atol=1e-5)
 
 
-def test_moe_edge_cases(cuda_device):
+@pytest.mark.parametrize("engine", ENGINES, indirect=True)
+def test_moe_edge_cases(cuda_device, engine):
     """Experts with no tokens, one token, duplicate ids in a row, B not a tile multiple."""
     from sb200 import synth
     from sb200.ternary import TernaryExperts
