@@ -646,6 +646,8 @@ struct sb_router {
   float* refb = nullptr;             // [total]
   float* portals = nullptr;          // [total,12]
   CUtensorMap tm_w1{}, tm_w2{}, tm_w3s{}, tm_wr{};
+  // narrower boxes for small batches, where the wide tiles leave SMs idle
+  CUtensorMap tm_w1_128{}, tm_w2_64{}, tm_wr_32{};
   float bbox[SB_MAX_LEVELS][6] = {};  // per level: min x,y,z, max x,y,z of the centers
 };
 
@@ -832,7 +834,13 @@ extern "C" int sb_router_upload(sb_router* h, const sb_router_weights* w) {
       (rc = make_tmap_2d(&h->tm_w3s, h->w3s_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 16, H, H,
                          GEMM_BK, TAIL_N, CU_TENSOR_MAP_SWIZZLE_128B)) ||
       (rc = make_tmap_2d(&h->tm_wr, h->wr_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, S, S,
-                         GEMM_BK, (uint32_t)h->bn_ref, CU_TENSOR_MAP_SWIZZLE_128B))) {
+                         GEMM_BK, (uint32_t)h->bn_ref, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&h->tm_w1_128, h->w1_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, H, H,
+                         GEMM_BK, 128, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&h->tm_w2_64, h->w2_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, S, H, H,
+                         GEMM_BK, 64, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&h->tm_wr_32, h->wr_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, S, S,
+                         GEMM_BK, 32, CU_TENSOR_MAP_SWIZZLE_128B))) {
     free_router_buffers(h);
     return rc;
   }
@@ -937,12 +945,24 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
         (rc = make_tmap_2d(&ts, spec, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, S, S, GEMM_BK, GEMM_BM,
                            CU_TENSOR_MAP_SWIZZLE_128B)))
       return rc;
+    // Tile widths: the widest tile that still gives every SM work.  A batch of
+    // a few thousand tokens has only ceil(M/128) row blocks, so the output
+    // columns are split finer there.
+    const int64_t mblocks = (M + GEMM_BM - 1) / GEMM_BM;
+    const int64_t sms = num_sms();
     EpiGeluBf16 e1{h->b1, static_cast<__nv_bfloat16*>(G), H, H, h->b3d, pos};
-    if ((rc = launch_gemm_tc<256, 4, EpiGeluBf16, true>("router_enc1_gelu_tc", ta, h->tm_w1, h->tm_w3s, M, H,
-                                                         H, e1, stream)))
-      return rc;
+    if (mblocks * ((H + 255) / 256 + 1) >= 2 * sms)
+      rc = launch_gemm_tc<256, 4, EpiGeluBf16, true>("router_enc1_gelu_tc", ta, h->tm_w1, h->tm_w3s, M, H, H,
+                                                      e1, stream);
+    else
+      rc = launch_gemm_tc<128, 4, EpiGeluBf16, true>("router_enc1_gelu_tc", ta, h->tm_w1_128, h->tm_w3s, M, H,
+                                                      H, e1, stream);
+    if (rc) return rc;
     EpiTanhBf16 e2{h->b2, static_cast<__nv_bfloat16*>(spec), S, S};
-    if (S <= 128) {  // tm_w2's box height matches this tile width (set at upload)
+    if (S > 64 && mblocks * ((S + 127) / 128) < sms) {
+      if ((rc = launch_gemm_tc<64, 4>("router_enc2_tanh_tc", tg, h->tm_w2_64, h->tm_w2_64, M, S, H, e2, stream)))
+        return rc;
+    } else if (S <= 128) {  // tm_w2's box height matches this tile width (set at upload)
       if ((rc = launch_gemm_tc<128, 4>("router_enc2_tanh_tc", tg, h->tm_w2, h->tm_w2, M, S, H, e2, stream)))
         return rc;
     } else {
@@ -951,6 +971,8 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
     }
     EpiSigmoidN e3{h->refb, nbuf, ldn, T, node_major};
     if (select == SB_SELECT_HARD) rc = SB_OK;  // HARD evaluates the chosen nodes in the descent
+    else if (h->bn_ref > 32 && mblocks * ((T + h->bn_ref - 1) / h->bn_ref) < sms)
+      rc = launch_gemm_tc<32, 4>("router_refract_tc", ts, h->tm_wr_32, h->tm_wr_32, M, T, S, e3, stream);
     else switch (h->bn_ref) {  // tm_wr's box height matches this tile width (set at create)
       case 32: rc = launch_gemm_tc<32, 4>("router_refract_tc", ts, h->tm_wr, h->tm_wr, M, T, S, e3, stream); break;
       case 64: rc = launch_gemm_tc<64, 4>("router_refract_tc", ts, h->tm_wr, h->tm_wr, M, T, S, e3, stream); break;

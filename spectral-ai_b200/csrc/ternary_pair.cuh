@@ -39,13 +39,15 @@
 // packed words); the token halves of both CTAs complete on the rank-0 CTA's
 // full_x barrier; the packed words on the local full_p.  The MMA commits
 // arrive on the same barrier offset in both CTAs.  Unpack and epilogue warps of
-// both CTAs arrive on the rank-0 CTA's full_a / tempty barriers.
+// both CTAs arrive on the rank-0 CTA's full_a / tempty barriers; the rank-0
+// unpack warps arrive only after full_x, so full_a alone gates an MMA K-block.
 //
-// Roles (640 threads per CTA): warp 0 TMA producer, warp 1 MMA issuer (rank 0
-// only), warp 2 TMEM allocator, warps 4..11 epilogue (TMEM -> registers ->
-// shared tile -> TMA store; two warps per lane quarter take alternate 32-token
-// chunks), warps 12..19 unpack in two groups of four; group g expands K
-// 64g..64g+63 of every K-block.  Warp w may only touch TMEM lanes 32*(w%4)..+31.
+// Roles (384 threads per CTA): warp 0 TMA producer, warp 1 MMA issuer (rank 0
+// only), warp 2 TMEM allocator, warps 4..7 epilogue (TMEM -> registers ->
+// shared tile -> TMA store), warps 8..11 unpack.  Warp w may only touch TMEM
+// lanes 32*(w%4)..+31.  The MMA issuer's scheduler is shared with one epilogue
+// and one unpack warp only: the tensor pipe queues one or two MMAs, so every
+// instruction the issuing thread waits for is idle tensor time.
 #pragma once
 
 #include "sm100_pair.cuh"
@@ -53,9 +55,10 @@
 
 namespace sb {
 
-constexpr int TP_THREADS = 640;
-constexpr int TP_EPI_WARPS = 8;
+constexpr int TP_EPI_WARPS = 4;
+constexpr int TP_EPI_SETS = TP_EPI_WARPS / 4;        // epilogue warps per TMEM lane quarter
 constexpr int TP_UNPACK_WARP0 = 4 + TP_EPI_WARPS;
+constexpr int TP_THREADS = 32 * (TP_UNPACK_WARP0 + 4);
 constexpr int TP_STAGES = 4;
 constexpr int TP_A_STAGES = 2;
 constexpr int TP_KB = 128;                           // K per block
@@ -107,7 +110,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
   uint64_t* full_x = reinterpret_cast<uint64_t*>(epi + TP_EPI_BYTES);  // rank 0: both token halves landed
   uint64_t* full_p = full_x + TP_STAGES;                               // local packed words landed
   uint64_t* xp_empty = full_p + TP_STAGES;                             // slot's MMAs completed
-  uint64_t* full_a = xp_empty + TP_STAGES;                             // rank 0: 8 unpack warps done
+  uint64_t* full_a = xp_empty + TP_STAGES;                             // rank 0: A stage + token tile ready
   uint64_t* a_empty = full_a + TP_A_STAGES;                            // A stage's MMAs completed
   uint64_t* tfull = a_empty + TP_A_STAGES;                             // [2] accumulator's MMAs completed
   uint64_t* tempty = tfull + 2;                                        // [2] rank 0: epilogue warps done
@@ -129,7 +132,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
       mbar_init(&xp_empty[s], 1);
     }
     for (int s = 0; s < TP_A_STAGES; ++s) {
-      mbar_init(&full_a[s], 16);  // 8 unpack warps x 2 CTAs
+      mbar_init(&full_a[s], 8);  // 4 unpack warps x 2 CTAs
       mbar_init(&a_empty[s], 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -196,8 +199,9 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
         if (!mbar_wait_cluster(&tempty[buf], ((uint32_t)(local >> 1) & 1u) ^ 1u, ST_TIMEOUT_MMA)) goto done;
         tc_fence_after();
         for (int kb = 0; kb < kblocks; ++kb) {
+          // one wait per K-block: full_a completes only after the rank-0 unpack
+          // warps have also seen this slot's token halves land (full_x)
           if (!mbar_wait_cluster(&full_a[astage], aphase, ST_TIMEOUT_MMA)) goto done;
-          if (!mbar_wait_cluster(&full_x[stage], phase, ST_TIMEOUT_MMA)) goto done;
           tc_fence_after();
           const uint64_t bdesc = sdesc_sw128(smem_u32(smem + stage * TP_STAGE_BYTES));
           const uint32_t a_tmem = tmem_base + TP_A_BASE + (uint32_t)(astage * TP_A_COLS);
@@ -224,7 +228,6 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
   } else if (warp >= TP_UNPACK_WARP0) {
     // ------------------------------------------------------------ unpack warps
     const int q = warp & 3;
-    const int grp = (warp - TP_UNPACK_WARP0) >> 2;
     // the packed row this lane expands (TMEM lane 32q + lane)
     int prow;
     if (MODE == TG_GATEUP)
@@ -240,22 +243,33 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
         const int astage = it % TP_A_STAGES;
         const uint32_t aphase = (uint32_t)(it / TP_A_STAGES) & 1u;
         if (!mbar_wait_warp_t(&full_p[stage], phase, ST_TIMEOUT_UNPACK)) goto done;
-        // this group's four words (64 K) of the row
-        const uint4 wv =
-            *reinterpret_cast<const uint4*>(smem + stage * TP_STAGE_BYTES + TP_X_BYTES + prow * 32 + grp * 16);
-        if (!mbar_wait_warp_t(&a_empty[astage], aphase ^ 1u, ST_TIMEOUT_UNPACK)) goto done;
-        tc_fence_after();
+        // expand the row's eight words (128 K) into registers first: only the
+        // stores into TMEM have to wait for the A stage to drain
+        const uint8_t* pw = smem + stage * TP_STAGE_BYTES + TP_X_BYTES + prow * 32;
+        const uint4 w0 = *reinterpret_cast<const uint4*>(pw);
+        const uint4 w1 = *reinterpret_cast<const uint4*>(pw + 16);
+        uint32_t a0[32], a1[32];
         {
-          const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
-          uint32_t a[32];
+          const uint32_t words0[4] = {w0.x, w0.y, w0.z, w0.w};
+          const uint32_t words1[4] = {w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
           for (int w = 0; w < 4; ++w)
 #pragma unroll
-            for (int j = 0; j < 8; ++j) a[8 * w + j] = tern_pair<FMT>(words[w], j);
-          tmem_st_32x32b_x32_p(lane_base + (uint32_t)(astage * TP_A_COLS + 32 * grp), a);
+            for (int j = 0; j < 8; ++j) {
+              a0[8 * w + j] = tern_pair<FMT>(words0[w], j);
+              a1[8 * w + j] = tern_pair<FMT>(words1[w], j);
+            }
         }
+        if (!mbar_wait_warp_t(&a_empty[astage], aphase ^ 1u, ST_TIMEOUT_UNPACK)) goto done;
+        tc_fence_after();
+        const uint32_t col = lane_base + (uint32_t)(astage * TP_A_COLS);
+        tmem_st_32x32b_x32_p(col, a0);
+        tmem_st_32x32b_x32_p(col + 32u, a1);
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
+        // rank 0 also waits for both token halves of this slot, so that the MMA
+        // issuer needs a single barrier per K-block
+        if (rank == 0 && !mbar_wait_warp_t(&full_x[stage], phase, ST_TIMEOUT_UNPACK)) goto done;
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&full_a[astage]), 0));
       }
@@ -263,7 +277,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
   } else if (warp >= 4) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;
-    const int half = (warp - 4) >> 2;  // this warp takes chunks half, half+2, ...
+    const int half = (warp - 4) >> 2;  // this warp takes chunks half, half + TP_EPI_SETS, ...
     const uint32_t tlanes = tmem_base + ((uint32_t)(q * 32) << 16);
     uint8_t* ebuf = epi + (warp - 4) * 2 * TP_EBUF_BYTES;
     int local = 0, nbuf = 0;
@@ -292,14 +306,14 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
       tc_fence_after();
       const uint32_t tbase = tlanes + (uint32_t)(buf * TP_D_COLS);
       // this warp's last chunk (or none): the accumulator is released after its load
-      const int last = (nch - 1 - half) >= 0 ? half + ((nch - 1 - half) & ~1) : -1;
+      const int last = (nch - 1 - half) >= 0 ? half + ((nch - 1 - half) / TP_EPI_SETS) * TP_EPI_SETS : -1;
       if (last < 0) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(tempty_leader);
       }
 #pragma unroll 1
-      for (int c = half; c < nch; c += 2) {
+      for (int c = half; c < nch; c += TP_EPI_SETS) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tbase + (uint32_t)(c * 32), v);
         tmem_ld_wait();
