@@ -550,14 +550,25 @@ def cpu_moe_rate(sample_tokens: int, budget_s: float = 15.0):
     return done / el, done, el
 
 
+# committed ncu summary that holds the DRAM traffic of each dominant kernel
+TRAFFIC_PROFILES = {
+    "router_enc1_gelu_tc": "router_enc1_gelu_tc.json",
+    "ternary_gateup_tc": "ternary_pair_gateup_moe4096.json",
+}
+
+
 def traffic_for(meta):
-    """DRAM bytes per launch of the dominant kernel from the committed ncu summary
-    (profiles/<kernel>.json, bytes per token measured on a smaller case), or None."""
-    p = REPO / "profiles" / f"{meta['dominant']}.json"
-    if not p.exists():
+    """DRAM bytes per launch of the dominant kernel from the committed ncu summary:
+    bytes per token (measured on a smaller case, traffic grows with the tokens) or
+    bytes per launch of this very workload (scaled by tokens when they differ)."""
+    name = TRAFFIC_PROFILES.get(meta["dominant"])
+    p = REPO / "profiles" / name if name else None
+    if p is None or not p.exists():
         return None
     d = json.loads(p.read_text())
-    return int(d["dram_bytes_per_token"] * meta["tokens_per_step"])
+    if "dram_bytes_per_token" in d:
+        return int(d["dram_bytes_per_token"] * meta["tokens_per_step"])
+    return int(d["dram_bytes_per_launch"] * meta["tokens_per_step"] / d["tokens"])
 
 
 def run_reference(a):

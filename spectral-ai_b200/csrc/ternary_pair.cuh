@@ -70,7 +70,7 @@ constexpr int TP_P_BYTES = 128 * 32;                 // 4 KB: 128 channels x 128
 constexpr int TP_STAGE_BYTES = TP_X_BYTES + TP_P_BYTES;  // 28 KB (1024-multiple)
 constexpr int TP_EBUF_BYTES = 4096;                  // one 32-token x 32-channel fp32 tile
 constexpr int TP_EPI_BYTES = TP_EPI_WARPS * 2 * TP_EBUF_BYTES;  // double-buffered per warp
-constexpr int TP_BAR_BYTES = (3 * TP_STAGES + 2 * TP_A_STAGES + 4) * 8 + 16;
+constexpr int TP_BAR_BYTES = (3 * TP_STAGES + TP_A_STAGES + 4) * 8 + 16;
 constexpr int TP_SMEM_BYTES = TP_STAGES * TP_STAGE_BYTES + TP_EPI_BYTES + TP_BAR_BYTES + 1024;
 constexpr uint32_t TP_TMEM_COLS = 512;
 constexpr uint32_t TP_D_COLS = TP_TILE_ROWS;         // one accumulator
@@ -111,8 +111,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
   uint64_t* full_p = full_x + TP_STAGES;                               // local packed words landed
   uint64_t* xp_empty = full_p + TP_STAGES;                             // slot's MMAs completed
   uint64_t* full_a = xp_empty + TP_STAGES;                             // rank 0: A stage + token tile ready
-  uint64_t* a_empty = full_a + TP_A_STAGES;                            // A stage's MMAs completed
-  uint64_t* tfull = a_empty + TP_A_STAGES;                             // [2] accumulator's MMAs completed
+  uint64_t* tfull = full_a + TP_A_STAGES;                              // [2] accumulator's MMAs completed
   uint64_t* tempty = tfull + 2;                                        // [2] rank 0: epilogue warps done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
@@ -131,10 +130,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
       mbar_init(&full_p[s], 1);
       mbar_init(&xp_empty[s], 1);
     }
-    for (int s = 0; s < TP_A_STAGES; ++s) {
-      mbar_init(&full_a[s], 8);  // 4 unpack warps x 2 CTAs
-      mbar_init(&a_empty[s], 1);
-    }
+    for (int s = 0; s < TP_A_STAGES; ++s) mbar_init(&full_a[s], 8);  // 4 unpack warps x 2 CTAs
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 2 * TP_EPI_WARPS);
@@ -198,11 +194,17 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
         const uint32_t d_tmem = tmem_base + (uint32_t)(buf * TP_D_COLS);
         if (!mbar_wait_cluster(&tempty[buf], ((uint32_t)(local >> 1) & 1u) ^ 1u, ST_TIMEOUT_MMA)) goto done;
         tc_fence_after();
+        bool ready = false;  // this K-block's full_a was seen complete by the previous peek
         for (int kb = 0; kb < kblocks; ++kb) {
           // one wait per K-block: full_a completes only after the rank-0 unpack
           // warps have also seen this slot's token halves land (full_x)
-          if (!mbar_wait_cluster(&full_a[astage], aphase, ST_TIMEOUT_MMA)) goto done;
+          if (!ready && !mbar_wait_cluster(&full_a[astage], aphase, ST_TIMEOUT_MMA)) goto done;
           tc_fence_after();
+          // peek at the next K-block's barrier now: the poll's latency overlaps
+          // the MMA issue below, and the result is only used in the next pass
+          const int nastage = astage + 1 == TP_A_STAGES ? 0 : astage + 1;
+          const uint32_t naphase = nastage == 0 ? aphase ^ 1u : aphase;
+          const bool peek = kb + 1 < kblocks && mbar_try_wait(smem_u32(&full_a[nastage]), naphase);
           const uint64_t bdesc = sdesc_sw128(smem_u32(smem + stage * TP_STAGE_BYTES));
           const uint32_t a_tmem = tmem_base + TP_A_BASE + (uint32_t)(astage * TP_A_COLS);
 #pragma unroll
@@ -211,16 +213,16 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
             const uint64_t bk = bdesc + (k < 4 ? 2u * k : (uint32_t)(TP_XATOM_BYTES >> 4) + 2u * (k - 4));
             umma_ts_pair(d_tmem, a_tmem + 8u * k, bk, idesc, (kb | k) != 0);
           }
+          // frees the slot's token tile and packed words, and the A stage this
+          // K-block read (the unpack warps wait on this barrier for both)
           umma_commit_pair(&xp_empty[stage]);
-          umma_commit_pair(&a_empty[astage]);
+          ready = peek;
           if (++stage == TP_STAGES) {
             stage = 0;
             phase ^= 1u;
           }
-          if (++astage == TP_A_STAGES) {
-            astage = 0;
-            aphase ^= 1u;
-          }
+          astage = nastage;
+          aphase = naphase;
         }
         umma_commit_pair(&tfull[buf]);
       }
@@ -241,7 +243,6 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
         const int stage = it % TP_STAGES;
         const uint32_t phase = (uint32_t)(it / TP_STAGES) & 1u;
         const int astage = it % TP_A_STAGES;
-        const uint32_t aphase = (uint32_t)(it / TP_A_STAGES) & 1u;
         if (!mbar_wait_warp_t(&full_p[stage], phase, ST_TIMEOUT_UNPACK)) goto done;
         // expand the row's eight words (128 K) into registers first: only the
         // stores into TMEM have to wait for the A stage to drain
@@ -260,7 +261,16 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
               a1[8 * w + j] = tern_pair<FMT>(words1[w], j);
             }
         }
-        if (!mbar_wait_warp_t(&a_empty[astage], aphase ^ 1u, ST_TIMEOUT_UNPACK)) goto done;
+        // The A stage is free once the MMAs of K-block it - TP_A_STAGES have
+        // completed, which the commit on that block's slot barrier signals.
+        // That barrier is then in the phase of that block or one past it (the
+        // block before it completed before this warp's previous pass, and the
+        // next use of the slot needs this very pass), so the parity is exact.
+        if (it >= TP_A_STAGES) {
+          const int pj = it - TP_A_STAGES;
+          if (!mbar_wait_warp_t(&xp_empty[pj % TP_STAGES], (uint32_t)(pj / TP_STAGES) & 1u, ST_TIMEOUT_UNPACK))
+            goto done;
+        }
         tc_fence_after();
         const uint32_t col = lane_base + (uint32_t)(astage * TP_A_COLS);
         tmem_st_32x32b_x32_p(col, a0);
