@@ -951,7 +951,7 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
     const int64_t mblocks = (M + GEMM_BM - 1) / GEMM_BM;
     const int64_t sms = num_sms();
     EpiGeluBf16 e1{h->b1, static_cast<__nv_bfloat16*>(G), H, H, h->b3d, pos};
-    if (mblocks * ((H + 255) / 256 + 1) >= 2 * sms)
+    if (mblocks * ((H + 255) / 256 + 1) >= sms)
       rc = launch_gemm_tc<256, 4, EpiGeluBf16, true>("router_enc1_gelu_tc", ta, h->tm_w1, h->tm_w3s, M, H, H,
                                                       e1, stream);
     else

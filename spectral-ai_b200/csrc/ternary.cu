@@ -118,31 +118,109 @@ __global__ void moe_hist_kernel(const int32_t* __restrict__ ids, int64_t R, int 
   }
 }
 
-// expert offsets (exclusive scan), scatter cursors and the m-tile table
-// Expert segments start on 32-row boundaries (segment = count rounded up to
-// 32); m-tiles of `tile_rows` rows cover them, `rows` valid and `pad` rows up
-// to the segment end (a multiple of 32).
-__global__ void moe_scan_kernel(const int* __restrict__ counts, int E, int* __restrict__ offsets,
-                                int* __restrict__ cursor, MTile* __restrict__ mtiles,
-                                int* __restrict__ num_mtiles, int max_mtiles, int tile_rows) {
-  if (threadIdx.x != 0 || blockIdx.x != 0) return;
-  int off = 0, nt = 0;
-  for (int e = 0; e < E; ++e) {
-    const int c = counts[e];
+// Expert offsets (exclusive scan), scatter cursors and the m-tile table, in
+// one block of 1024 threads.  Expert segments start on 32-row boundaries
+// (segment = count rounded up to 32); m-tiles of `tile_rows` rows cover them,
+// `rows` valid and `pad` rows up to the segment end (a multiple of 32).  With
+// `hist` set the block also counts the ids itself (shared-memory histogram;
+// small batches), otherwise it reads `counts` from moe_hist_kernel.
+constexpr int PLAN_THREADS = 1024;
+
+__global__ void __launch_bounds__(PLAN_THREADS) moe_plan_kernel(const int32_t* __restrict__ ids, int64_t R, int E,
+                                                               int hist, int* __restrict__ counts,
+                                                               int* __restrict__ offsets, int* __restrict__ cursor,
+                                                               MTile* __restrict__ mtiles, int* __restrict__ num_mtiles,
+                                                               int max_mtiles, int tile_rows) {
+  extern __shared__ int sh_count[];  // [E] when hist
+  __shared__ int warp_rows[32], warp_tiles[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (hist) {
+    for (int e = tid; e < E; e += PLAN_THREADS) sh_count[e] = 0;
+    __syncthreads();
+    for (int64_t i = tid; i < R; i += PLAN_THREADS) {
+      const int e = ids[i];
+      if (e >= 0 && e < E)
+        atomicAdd(&sh_count[e], 1);
+      else
+        set_status(ST_BAD_ARGUMENT);
+    }
+    __syncthreads();
+  }
+  // each thread owns a run of consecutive experts
+  const int per = (E + PLAN_THREADS - 1) / PLAN_THREADS;
+  const int e0 = tid * per < E ? tid * per : E, e1 = e0 + per < E ? e0 + per : E;
+  int my_rows = 0, my_tiles = 0;
+  for (int e = e0; e < e1; ++e) {
+    const int cp = ((hist ? sh_count[e] : counts[e]) + 31) & ~31;
+    my_rows += cp;
+    my_tiles += (cp + tile_rows - 1) / tile_rows;
+  }
+  // block-wide exclusive scan of (rows, tiles)
+  int r_inc = my_rows, t_inc = my_tiles;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int rv = __shfl_up_sync(0xffffffffu, r_inc, o), tv = __shfl_up_sync(0xffffffffu, t_inc, o);
+    if (lane >= o) {
+      r_inc += rv;
+      t_inc += tv;
+    }
+  }
+  if (lane == 31) {
+    warp_rows[warp] = r_inc;
+    warp_tiles[warp] = t_inc;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int rw = warp_rows[lane], tw = warp_tiles[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int rv = __shfl_up_sync(0xffffffffu, rw, o), tv = __shfl_up_sync(0xffffffffu, tw, o);
+      if (lane >= o) {
+        rw += rv;
+        tw += tv;
+      }
+    }
+    warp_rows[lane] = rw;  // inclusive over warps
+    warp_tiles[lane] = tw;
+  }
+  __syncthreads();
+  int off = r_inc - my_rows + (warp > 0 ? warp_rows[warp - 1] : 0);
+  int nt = t_inc - my_tiles + (warp > 0 ? warp_tiles[warp - 1] : 0);
+  for (int e = e0; e < e1; ++e) {
+    const int c = hist ? sh_count[e] : counts[e];
     const int cp = (c + 31) & ~31;
+    if (hist) counts[e] = c;
     offsets[e] = off;
     cursor[e] = 0;
-    for (int r = 0; r < cp && nt < max_mtiles; r += tile_rows) {
+    for (int r = 0; r < cp; r += tile_rows, ++nt) {
+      if (nt >= max_mtiles) continue;
       MTile t;
       t.expert = e;
       t.row0 = off + r;
       t.rows = (c - r) < tile_rows ? (c - r) : tile_rows;
       t.pad = (cp - r) < tile_rows ? (cp - r) : tile_rows;
-      mtiles[nt++] = t;
+      mtiles[nt] = t;
     }
     off += cp;
   }
-  *num_mtiles = nt;
+  if (tid == PLAN_THREADS - 1) *num_mtiles = nt < max_mtiles ? nt : max_mtiles;
+}
+
+// Histogram + plan for one batch: one fused block for small batches, else a
+// grid-wide histogram first.
+int moe_plan(const int32_t* ids, int64_t R, int E, int* counts, int* offsets, int* cursor, MTile* mtiles, int* nmt,
+             int max_mt, int tile_rows, cudaStream_t stream) {
+  const bool fused = R <= (int64_t)1 << 17 && E <= 8192;
+  if (!fused) {
+    SB_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int) * E, stream));
+    int64_t blocks = (R + 255) / 256;
+    if (blocks > 4096) blocks = 4096;
+    moe_hist_kernel<<<(unsigned)blocks, 256, 0, stream>>>(ids, R, E, counts);
+  }
+  moe_plan_kernel<<<1, PLAN_THREADS, fused ? sizeof(int) * E : 0, stream>>>(
+      ids, R, E, fused ? 1 : 0, counts, offsets, cursor, mtiles, nmt, max_mt, tile_rows);
+  SB_CUDA_TRY(cudaGetLastError());
+  return SB_OK;
 }
 
 template <typename TX, typename TA>
@@ -434,13 +512,10 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
 
   {
     ProfScope prof("moe_dispatch", stream);
-    SB_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int) * E, stream));
     const int64_t R = L.R;
-    int64_t blocks = (R + 255) / 256;
-    if (blocks > 4096) blocks = 4096;
-    moe_hist_kernel<<<(unsigned)blocks, 256, 0, stream>>>(ids, R, E, counts);
-    moe_scan_kernel<<<1, 32, 0, stream>>>(counts, E, offsets, cursor, mtiles, nmt, (int)L.max_mt,
-                                          engine == ENGINE_PAIR ? TP_TILE_ROWS : 128);
+    if ((rc = moe_plan(ids, R, E, counts, offsets, cursor, mtiles, nmt, (int)L.max_mt,
+                       engine == ENGINE_PAIR ? TP_TILE_ROWS : 128, stream)))
+      return rc;
     int64_t wblocks = (R * 32 + 255) / 256;
     if (wblocks > (int64_t)num_sms() * 16) wblocks = (int64_t)num_sms() * 16;
     const bool x16 = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
@@ -619,9 +694,8 @@ extern "C" int sb_ternary_linear(const void* x, int x_dtype, int64_t M, int64_t 
   int64_t blocks = (M + 255) / 256;
   if (blocks > 4096) blocks = 4096;
   fill_i32_kernel<<<(unsigned)blocks, 256, 0, st>>>(ids, M, 0);
-  SB_CUDA_TRY(cudaMemsetAsync(counts, 0, sizeof(int), st));
-  moe_hist_kernel<<<(unsigned)blocks, 256, 0, st>>>(ids, M, 1, counts);
-  moe_scan_kernel<<<1, 32, 0, st>>>(counts, 1, offsets, cursor, mtiles, nmt, (int)L.max_mt, 128);
+  int rc;
+  if ((rc = moe_plan(ids, M, 1, counts, offsets, cursor, mtiles, nmt, (int)L.max_mt, 128, st))) return rc;
   {
     int64_t cb = (M * K + 255) / 256;
     if (cb > (int64_t)num_sms() * 32) cb = (int64_t)num_sms() * 32;
@@ -634,7 +708,6 @@ extern "C" int sb_ternary_linear(const void* x, int x_dtype, int64_t M, int64_t 
     SB_CUDA_TRY(cudaGetLastError());
   }
   CUtensorMap tmx, tmw;
-  int rc;
   const int64_t KW = ternary_row_words(K);
   if ((rc = make_tmap_2d(&tmx, xp, fmt ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, M,
                          K, L.ldx, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B)) ||
