@@ -256,14 +256,25 @@ def moe_workload(batch: int, device, select: str = "soft"):
     def step():
         layer.forward(x, out=out)
 
-    x_host = x.cpu().pin_memory()
-    out_host = torch.empty(batch, H, dtype=torch.bfloat16).pin_memory()
+    # end to end: host batches through sb200.moe.HostPipeline (copies in and out
+    # on their own streams, overlapped with the neighbouring batches' compute)
+    from sb200.moe import HostPipeline
+    pipe = HostPipeline(layer, batch, H, dtype=torch.bfloat16, device=device)
+    x_host = [x.cpu().pin_memory() for _ in range(2)]
+    out_host = [torch.empty(batch, H, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+
+    def e2e_run(n):
+        pipe.run([x_host[i & 1] for i in range(n)], [out_host[i & 1] for i in range(n)])
+
     x_dev = torch.empty_like(x)
 
-    def e2e_step():
-        x_dev.copy_(x_host, non_blocking=True)
+    def e2e_sequential():
+        # one batch at a time on one stream: copy in, layer, copy out
+        x_dev.copy_(x_host[0], non_blocking=True)
         y = layer(x_dev)
-        out_host.copy_(y, non_blocking=True)
+        out_host[0].copy_(y, non_blocking=True)
+
+    e2e_step = (e2e_run, e2e_sequential)
 
     pairs = batch * TOPK
     meta = {"tokens_per_step": batch, "h2d": batch * H * 2, "d2h": batch * H * 2,
@@ -406,6 +417,25 @@ def time_steps(step, steps, warmup, world, sampler=None, profile=False, flush=No
     return max_over_ranks(ms, world), prof
 
 
+def time_pipelined(run, steps, warmup, world):
+    """Device time of one pipelined run of `steps` batches (CUDA events on the
+    current stream, which the pipeline makes wait for its last copy out), after
+    `warmup` batches; max over ranks."""
+    import torch
+    s = torch.cuda.current_stream()
+    run(max(warmup, 1))
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    run(steps)
+    e1.record(s)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    barrier(world)
+    return max_over_ranks(ms, world)
+
+
 def roofline_tensor(meta, prof, pk, steps_ms, steps):
     dom = prof.get(meta["dominant"], (0, 0.0))
     if not dom[0]:
@@ -433,7 +463,8 @@ def run_ours(a):
     step, e2e_step, meta = moe_workload(batch, dev)
     total_ms, prof = time_steps(step, a.steps, a.warmup, world, sampler, profile=True, flush=flush)
     clocks = sampler.stop()
-    e2e_ms, _ = time_steps(e2e_step, a.steps, a.warmup, world, flush=flush)
+    e2e_ms = time_pipelined(e2e_step[0], a.steps, a.warmup, world)
+    seq_ms, _ = time_steps(e2e_step[1], a.steps, a.warmup, world, flush=flush)
     tokens = meta["tokens_per_step"] * a.steps * world
     value = tokens / (total_ms / 1e3)
     e2e_value = tokens / (e2e_ms / 1e3)
@@ -446,7 +477,14 @@ def run_ours(a):
            "config": dict(meta["config"], parallelism=f"token-shard x{world}, experts replicated, no collective"),
            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                    "h2d_bytes_per_step": meta["h2d"], "d2h_bytes_per_step": meta["d2h"],
-                   "api": "sb200.moe.BVHMoELayer.__call__ (BVHRouter.forward_topk + TernaryExperts)"},
+                   "api": "sb200.moe.HostPipeline.run over sb200.moe.BVHMoELayer (BVHRouter.forward_topk "
+                          "+ TernaryExperts): pinned host batches, copies in/out on their own streams "
+                          "overlapped with the neighbouring batches' compute",
+                   "l2": "no flush between batches; each batch streams > 400 MB through the layer "
+                         "(dispatch rows 134 MB, per-slot outputs 277 MB) against a 126 MB L2",
+                   "sequential_value": round(tokens / (seq_ms / 1e3), 1),
+                   "sequential": "BVHMoELayer.__call__ one batch at a time on one stream (copy in, "
+                                 "layer, copy out; L2 flushed between batches)"},
            "gpu_launches": launches,
            "kernels": {k: {"launches": n, "avg_ms": round(t / max(n, 1), 4),
                            "share": round(t / max(sum(v[1] for v in prof.values()), 1e-9), 4)}

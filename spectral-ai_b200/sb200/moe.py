@@ -41,3 +41,59 @@ class BVHMoELayer:
                      topk_ids: torch.Tensor) -> torch.Tensor:
         """Same signature as OLMoELayer.forward_topk (olmoe_extract.py:126-157)."""
         return self.experts.forward(hidden_states, topk_ids, topk_probs, out_dtype=hidden_states.dtype)
+
+
+class HostPipeline:
+    """Runs a stream of host-resident batches through a layer with the copies
+    overlapped: while the layer computes batch i on the compute stream, batch
+    i+1 is copied in on one copy stream and batch i-1's result copied out on
+    another (two device buffers each way).  Every batch still makes its full
+    host->device and device->host trip; only their timing overlaps.
+
+    ``layer`` is any callable ``layer(x_dev, out=y_dev)`` on the device, such as
+    ``BVHMoELayer``.  Host tensors should be pinned for the copies to be
+    asynchronous.
+    """
+
+    def __init__(self, layer, batch: int, hidden: int, dtype=torch.bfloat16,
+                 device: Optional[torch.device] = None, out_dtype=None):
+        self.layer = layer
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.xin = [torch.empty(batch, hidden, dtype=dtype, device=self.device) for _ in range(2)]
+        self.yout = [torch.empty(batch, hidden, dtype=out_dtype or dtype, device=self.device) for _ in range(2)]
+        self.h2d = torch.cuda.Stream(self.device)
+        self.d2h = torch.cuda.Stream(self.device)
+        ev = lambda: [torch.cuda.Event() for _ in range(2)]
+        self.in_ready, self.in_free, self.out_ready, self.out_free = ev(), ev(), ev(), ev()
+
+    def run(self, inputs: Sequence[torch.Tensor], outputs: Sequence[torch.Tensor]) -> None:
+        """outputs[i] <- layer(inputs[i]) for every i; returns when all copies are queued
+        (synchronise the current stream, or wait on ``done_event``, to read them)."""
+        compute = torch.cuda.current_stream(self.device)
+        start = torch.cuda.Event()
+        start.record(compute)
+        self.h2d.wait_event(start)
+        self.d2h.wait_event(start)
+        for i, (xh, yh) in enumerate(zip(inputs, outputs)):
+            b = i & 1
+            with torch.cuda.stream(self.h2d):
+                if i >= 2:
+                    self.h2d.wait_event(self.in_free[b])   # compute of batch i-2 has read xin[b]
+                self.xin[b].copy_(xh, non_blocking=True)
+                self.in_ready[b].record(self.h2d)
+            compute.wait_event(self.in_ready[b])
+            if i >= 2:
+                compute.wait_event(self.out_free[b])       # batch i-2's result has left yout[b]
+            self.layer(self.xin[b], out=self.yout[b])
+            self.in_free[b].record(compute)
+            self.out_ready[b].record(compute)
+            with torch.cuda.stream(self.d2h):
+                self.d2h.wait_event(self.out_ready[b])
+                yh.copy_(self.yout[b], non_blocking=True)
+                self.out_free[b].record(self.d2h)
+        # the caller's stream is done when the last copy out is
+        last = (len(inputs) - 1) & 1 if len(inputs) else 0
+        if len(inputs):
+            compute.wait_event(self.out_free[last])
+            if len(inputs) > 1:
+                compute.wait_event(self.out_free[last ^ 1])
