@@ -225,6 +225,78 @@ int sb_ternary_moe_swiglu(const void* x, int x_dtype, int64_t B, int64_t H, int6
 size_t sb_ternary_moe_workspace_bytes(int64_t B, int64_t H, int64_t I,
                                       int32_t n_experts, int32_t top_k);
 
+/* ------------------------------------------------------------------------ */
+/* Enhanced BVH router (the OLMoE production router) and its top-k gate       */
+/* ------------------------------------------------------------------------ */
+
+/* EnhancedBVHRouter eval forward (python/olmoe_bvh_distill.py:422-632,
+ * spectral_mode off, n_rays = 1) plus the BVHGateWrapper weight conventions
+ * "softmax" and "topk_softmax" (python/olmoe_e2e_eval.py:316-971).  Replaces
+ * the reference's pure-PyTorch module; the reference has no kernel for it.
+ * Fixed shapes of the reference: input_proj hidden -> 512 -> 256 + LayerNorm,
+ * expert head (feature + n1 + n2 + n3) -> 256 -> n1*n2*n3. */
+typedef struct sb_enh sb_enh;
+
+typedef struct {
+  int hidden;        /* input_dim: multiple of 8 */
+  int feature;       /* feature_dim: 32, 64 or 128 */
+  int branching[3];  /* n_level1, n_level2, n_level3: each 1..32, sum <= 160 - feature,
+                        product <= 256 */
+} sb_enh_desc;
+
+typedef struct {
+  const float* centers;  /* [K,3] */
+  const float* to3d_w;   /* [3,in] */
+  const float* to3d_b;   /* [3] */
+  const float* feat0_w;  /* [F,in]  feature_net.0 */
+  const float* feat0_b;  /* [F] */
+  const float* feat2_w;  /* [F,F]   feature_net.2 */
+  const float* feat2_b;  /* [F] */
+  const float* head_w;   /* [K,F+3] route_head */
+  const float* head_b;   /* [K] */
+} sb_enh_level;
+
+/* Host fp32 pointers, nn.Linear layout ([out, in]); state_dict names in comments. */
+typedef struct {
+  const float* in0_w;   /* input_proj.0.weight [512,H] */
+  const float* in0_b;   /* input_proj.0.bias   [512] */
+  const float* in2_w;   /* input_proj.2.weight [256,512] */
+  const float* in2_b;   /* input_proj.2.bias   [256] */
+  const float* ln_w;    /* input_proj.3.weight [256] */
+  const float* ln_b;    /* input_proj.3.bias   [256] */
+  sb_enh_level level[3];
+  const float* eh0_w;   /* expert_head.0.weight [256, F+n1+n2+n3] */
+  const float* eh0_b;   /* [256] */
+  const float* eh2_w;   /* expert_head.2.weight [E,256] */
+  const float* eh2_b;   /* [E] */
+  float temperature;    /* the module's temperature buffer */
+} sb_enh_weights;
+
+enum sb_gate_mode { SB_GATE_SOFTMAX = 0, SB_GATE_TOPK_SOFTMAX = 1 };
+
+/* Device outputs; any pointer may be NULL (not produced). */
+typedef struct {
+  float* logits;        /* [B,E] the router's raw logits (_last_logits) */
+  float* expert_probs;  /* [B,E] softmax(logits / max(T, 0.1)) */
+  int64_t* expert_ids;  /* [B]   argmax, first index on ties */
+  float* geo_dist;      /* [B,E] d1[i] + d2[j] + d3[k] (_last_geometric_distances) */
+  float* branch_bonus;  /* [B,E] 1 + 0.2 same domain + 0.1 same subdomain (_last_branch_bonus) */
+  float* router_probs;  /* [B,E] gate router_probs */
+  float* topk_weights;  /* [B,k] gate top-k weights (fp32, before the cast to the hidden dtype) */
+  int32_t* topk_ids;    /* [B,k] gate top-k ids, value order, lower index first on ties */
+} sb_enh_outputs;
+
+int sb_enh_create(const sb_enh_desc* desc, int device, sb_enh** out);
+int sb_enh_upload(sb_enh* h, const sb_enh_weights* w);
+size_t sb_enh_workspace_bytes(const sb_enh* h, int64_t batch, int precision);
+/* x: device [B,H], SB_F32 or SB_BF16 (SB_PREC_FAST needs SB_BF16).  The gate
+ * rounds the logits to round_dtype (the hidden-state dtype, SB_F32 or SB_BF16)
+ * before its softmax / top-k, as the reference wrapper's logits.to(dtype). */
+int sb_enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t batch, int precision,
+                   int gate_mode, int norm_topk_prob, int round_dtype, int top_k,
+                   const sb_enh_outputs* out, void* workspace, size_t workspace_bytes, void* stream);
+int sb_enh_destroy(sb_enh* h);
+
 #ifdef __cplusplus
 }
 #endif

@@ -4,3 +4,4 @@
 #include "common.cu"
 #include "router.cu"
 #include "ternary.cu"
+#include "enhanced.cu"

@@ -74,6 +74,30 @@ struct EpiGeluBf16 {
 };
 
 // spec = tanh(acc + b2) as bf16 (the A operand of the refraction GEMM).
+// C = acc + bias, fp32, row-major [M, ldo].
+struct EpiBiasF32 {
+  const float* bias;
+  float* out;
+  int64_t ldo;
+  int N;
+  __device__ __forceinline__ void apply(int64_t row, int col0, const uint32_t (&r)[32]) const {
+    float* dst = out + row * ldo + col0;
+    if (col0 + 32 <= N && (ldo & 3) == 0) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4)
+        *reinterpret_cast<float4*>(dst + j) =
+            make_float4(__uint_as_float(r[j]) + __ldg(bias + col0 + j), __uint_as_float(r[j + 1]) + __ldg(bias + col0 + j + 1),
+                        __uint_as_float(r[j + 2]) + __ldg(bias + col0 + j + 2),
+                        __uint_as_float(r[j + 3]) + __ldg(bias + col0 + j + 3));
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < N) dst[j] = __uint_as_float(r[j]) + __ldg(bias + col0 + j);
+    }
+  }
+  __device__ __forceinline__ void tail(int64_t, const uint32_t (&)[32]) const {}
+};
+
 struct EpiTanhBf16 {
   const float* bias;
   __nv_bfloat16* out;
@@ -130,7 +154,7 @@ struct EpiSigmoidN {
 // EXACT engine: fp32 FFMA GEMM, C = act(A B^T + bias), A [M,K] fp32|bf16, B [N,K] fp32.
 // 128x128 tile, K-step 8, 256 threads, 8x8 outputs per thread.
 // ---------------------------------------------------------------------------
-enum { ACT_GELU = 0, ACT_TANH = 1, ACT_SIGMOID = 2 };
+enum { ACT_GELU = 0, ACT_TANH = 1, ACT_SIGMOID = 2, ACT_NONE = 3 };
 
 template <typename TA>
 __device__ __forceinline__ float to_f32(TA v);
@@ -193,7 +217,10 @@ __global__ void __launch_bounds__(256) sgemm_nt_kernel(const TA* __restrict__ A,
       const int n = n0 + tc * 8 + j;
       if (n >= N) continue;
       const float v = acc[i][j] + bias[n];
-      const float y = ACT == ACT_GELU ? gelu_erf(v) : (ACT == ACT_TANH ? tanhf(v) : sigmoidf_(v));
+      const float y = ACT == ACT_GELU   ? gelu_erf(v)
+                      : ACT == ACT_TANH ? tanhf(v)
+                      : ACT == ACT_NONE ? v
+                                        : sigmoidf_(v);
       if (transposed)
         C[(int64_t)n * ldc + m] = y;
       else

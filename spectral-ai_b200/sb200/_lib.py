@@ -50,6 +50,29 @@ class RouterOutputs(C.Structure):
                 ("route_path", C.c_void_p), ("confidence", C.c_void_p)]
 
 
+class EnhDesc(C.Structure):
+    _fields_ = [("hidden", C.c_int32), ("feature", C.c_int32), ("branching", C.c_int32 * 3)]
+
+
+class EnhLevel(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("centers", "to3d_w", "to3d_b", "feat0_w", "feat0_b",
+                                          "feat2_w", "feat2_b", "head_w", "head_b")]
+
+
+class EnhWeights(C.Structure):
+    _fields_ = ([(n, C.c_void_p) for n in ("in0_w", "in0_b", "in2_w", "in2_b", "ln_w", "ln_b")]
+                + [("level", EnhLevel * 3)]
+                + [(n, C.c_void_p) for n in ("eh0_w", "eh0_b", "eh2_w", "eh2_b")]
+                + [("temperature", C.c_float)])
+
+
+class EnhOutputs(C.Structure):
+    _fields_ = [(n, C.c_void_p) for n in ("logits", "expert_probs", "expert_ids", "geo_dist", "branch_bonus",
+                                          "router_probs", "topk_weights", "topk_ids")]
+
+
+SB_GATE_SOFTMAX, SB_GATE_TOPK_SOFTMAX = 0, 1
+
 # (name, restype, argtypes) of every symbol the header declares
 SIGNATURES = [
     ("sb_abi_version", C.c_int, []),
@@ -88,6 +111,13 @@ SIGNATURES = [
       C.c_void_p, C.c_size_t, C.c_void_p]),
     ("sb_ternary_moe_workspace_bytes", C.c_size_t,
      [C.c_int64, C.c_int64, C.c_int64, C.c_int32, C.c_int32]),
+    ("sb_enh_create", C.c_int, [C.POINTER(EnhDesc), C.c_int, C.POINTER(C.c_void_p)]),
+    ("sb_enh_upload", C.c_int, [C.c_void_p, C.POINTER(EnhWeights)]),
+    ("sb_enh_workspace_bytes", C.c_size_t, [C.c_void_p, C.c_int64, C.c_int]),
+    ("sb_enh_forward", C.c_int,
+     [C.c_void_p, C.c_void_p, C.c_int, C.c_int64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+      C.POINTER(EnhOutputs), C.c_void_p, C.c_size_t, C.c_void_p]),
+    ("sb_enh_destroy", C.c_int, [C.c_void_p]),
 ]
 
 _lib = None

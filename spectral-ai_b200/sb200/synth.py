@@ -100,6 +100,47 @@ def router_weights(hidden: int, spectral: int, branching: Sequence[int] = (4, 4,
     return w
 
 
+def enhanced_router_weights(hidden: int = 2048, branching: Sequence[int] = (4, 4, 4), feature_dim: int = 128,
+                            seed: int = 0, perturb: bool = True,
+                            temperature: float = 1.0) -> Dict[str, np.ndarray]:
+    """fp32 parameters keyed by ``EnhancedBVHRouter`` state_dict names
+    (python/olmoe_bvh_distill.py:422-516, spectral_mode off): Linear weights
+    N(0, 1/in), centers N(0, 0.3^2); with ``perturb`` the biases, the LayerNorm
+    affine and log-radii move off their initial values too."""
+    g = torch.Generator().manual_seed(WEIGHT_STREAM + 0x1000 + seed)
+    n1, n2, n3 = branching
+    F = feature_dim
+    w: Dict[str, np.ndarray] = {}
+
+    def randn(*shape, std):
+        return (torch.randn(*shape, generator=g) * std).numpy().astype(np.float32)
+
+    def linear(name, n_in, n_out):
+        w[name + ".weight"] = randn(n_out, n_in, std=1.0 / math.sqrt(n_in))
+        w[name + ".bias"] = randn(n_out, std=0.1) if perturb else np.zeros(n_out, np.float32)
+
+    w["temperature"] = np.array(temperature, np.float32)
+    w["expert_counts"] = np.zeros(n1 * n2 * n3, np.float32)
+    linear("input_proj.0", hidden, 512)
+    linear("input_proj.2", 512, 256)
+    if perturb:
+        w["input_proj.3.weight"] = (1.0 + randn(256, std=0.1)).astype(np.float32)
+        w["input_proj.3.bias"] = randn(256, std=0.1)
+    else:
+        w["input_proj.3.weight"] = np.ones(256, np.float32)
+        w["input_proj.3.bias"] = np.zeros(256, np.float32)
+    for l, (n_in, k) in enumerate(((256, n1), (F, n2), (F, n3)), start=1):
+        w[f"level{l}.centers"] = randn(k, 3, std=0.3)
+        w[f"level{l}.log_radii"] = randn(k, std=0.1) if perturb else np.zeros(k, np.float32)
+        linear(f"level{l}.to_3d", n_in, 3)
+        linear(f"level{l}.feature_net.0", n_in, F)
+        linear(f"level{l}.feature_net.2", F, F)
+        linear(f"level{l}.route_head", F + 3, k)
+    linear("expert_head.0", F + n1 + n2 + n3, 256)
+    linear("expert_head.2", 256, n1 * n2 * n3)
+    return w
+
+
 def unit_rms_rows(x: torch.Tensor) -> torch.Tensor:
     """Divide each row by its root-mean-square (fp32)."""
     rms = x.float().pow(2).mean(dim=-1, keepdim=True).sqrt()

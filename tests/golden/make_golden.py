@@ -186,6 +186,48 @@ def ternary_cases(ref_python: Path):
     print("wrote ternary_small.npz")
 
 
+def enhanced_case(ref_python: Path, name, H, seed, batch, x_seed, temperature=1.0, perturb=True,
+                  head_gain=1.0):
+    """EnhancedBVHRouter eval forward (olmoe_bvh_distill.py:422-625) and the
+    BVHGateWrapper top-k conventions (olmoe_e2e_eval.py:226-971) on seeded
+    inputs; weights regenerate from sb200.synth.enhanced_router_weights, so
+    only their checksums are stored."""
+    sys.path.insert(0, str(ref_python))
+    import olmoe_bvh_distill
+    import olmoe_e2e_eval
+    w = synth.enhanced_router_weights(H, seed=seed, perturb=perturb, temperature=temperature)
+    # head_gain > 1 spreads the 64 logits (random init leaves them within ~0.1)
+    w["expert_head.2.weight"] = (w["expert_head.2.weight"] * head_gain).astype(np.float32)
+    r = olmoe_bvh_distill.EnhancedBVHRouter(input_dim=H, feature_dim=128)
+    r.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in w.items()}, strict=True)
+    r.eval()
+    x = synth.hidden_states(batch, H, seed=x_seed)
+    out = {"H": H, "seed": seed, "batch": batch, "x_seed": x_seed, "temperature": temperature,
+           "perturb": int(perturb), "head_gain": head_gain, "x_checksum": checksum(x.numpy())}
+    for key, val in w.items():
+        out["wsum/" + key] = checksum(val)
+    with torch.no_grad():
+        probs, ids = r(x)
+        out["expert_probs"] = probs.numpy()
+        out["expert_ids"] = ids.numpy()
+        out["logits"] = r._last_logits.numpy()
+        out["geo_dist"] = r._last_geometric_distances.numpy()
+        out["branch_bonus"] = r._last_branch_bonus.numpy()
+        out["h"] = r.input_proj(x).numpy()
+        variants = {"softmax": dict(weight_mode="softmax"),
+                    "topk_softmax": dict(weight_mode="topk_softmax"),
+                    "softmax_norm": dict(weight_mode="softmax", norm_topk_prob=True)}
+        for vname, kw in variants.items():
+            for dt_name, dt in (("f32", torch.float32), ("bf16", torch.bfloat16)):
+                gw = olmoe_e2e_eval.BVHGateWrapper(r, top_k=8, **kw)
+                rp, tw, ti = gw(x.to(dt))
+                out[f"gate/{vname}/{dt_name}/router_probs"] = rp.float().numpy()
+                out[f"gate/{vname}/{dt_name}/topk_weights"] = tw.float().numpy()
+                out[f"gate/{vname}/{dt_name}/topk_ids"] = ti.numpy()
+    np.savez_compressed(OUT / f"{name}.npz", **out)
+    print(f"wrote {name}.npz")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -204,6 +246,11 @@ def main():
     router_case(bvh, "router_cfg0_perturbed", 2048, 256, (4, 4, 4), seed=5, perturb=True,
                 batch=256, x_seed=6, store_full=False)
     ternary_cases(ref_python)
+    # EnhancedBVHRouter (the OLMoE production router) and its gate wrapper
+    enhanced_case(ref_python, "enhanced_h256", 256, seed=1, batch=96, x_seed=11)
+    enhanced_case(ref_python, "enhanced_h256_t05", 256, seed=2, batch=96, x_seed=12, temperature=0.5)
+    enhanced_case(ref_python, "enhanced_h256_sharp", 256, seed=3, batch=96, x_seed=13, head_gain=20.0)
+    enhanced_case(ref_python, "enhanced_cfg0", 2048, seed=0, batch=256, x_seed=0)
 
 
 if __name__ == "__main__":
