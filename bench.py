@@ -18,6 +18,8 @@ Workloads (seeded synthetic inputs with BASELINE.json's shapes; no datasets):
              split over the GPUs; reported as "stack16".
   config4    6-level router (4096 experts, hidden 4096) at 8192 tokens per GPU
              against a dense bf16 gate (cuBLAS GEMM + top-8); "config4".
+  enhanced   EnhancedBVHRouter (the OLMoE production router) + BVHGateWrapper
+             softmax top-8 at 65,536 bf16 tokens per GPU; "enhanced_router".
   router     BVH router forward alone at B = 262144 bf16 tokens (config 1);
              1 GiB of input per GPU > L2, so no flush.  Reported inside the
              moe_layer line as "router".
@@ -290,6 +292,47 @@ def moe_workload(batch: int, device, select: str = "soft"):
     return step, e2e_step, meta
 
 
+def enhanced_workload(batch: int, device):
+    """EnhancedBVHRouter (the OLMoE production router, python/olmoe_bvh_distill.py:422-632)
+    + BVHGateWrapper softmax top-8 (python/olmoe_e2e_eval.py:928-938) on bf16 tokens."""
+    import torch
+    from sb200 import synth
+    from sb200.enhanced import EnhancedEngine
+    w = synth.enhanced_router_weights(H, seed=0)
+    eng = EnhancedEngine(H, 128, BRANCHING, device)
+    eng.upload(w)
+    x = synth.hidden_states(batch, H, seed=1, dtype=torch.bfloat16, device=device)
+    outs = {"router_probs": torch.empty(batch, 64, dtype=torch.float32, device=device),
+            "topk_weights": torch.empty(batch, TOPK, dtype=torch.float32, device=device),
+            "topk_ids": torch.empty(batch, TOPK, dtype=torch.int32, device=device)}
+
+    def step():
+        eng.forward(x, precision="fast", want=(), gate="softmax", k=TOPK, outputs=outs)
+
+    # 2 (H*512 + 512*256) + tail (levels + head) MAC per token, times 2 FLOP
+    flop = 2.0 * (H * 512 + 512 * 256 + 256 * 131 + 256 * 128 + 128 * 128 + 2 * (128 * 131 + 2 * 128 * 128)
+                  + 140 * 256 + 256 * 64)
+    return step, flop
+
+
+def cpu_enhanced_rate(sample_tokens: int, budget_s: float = 8.0):
+    """Oracle port of the enhanced router + gate on the host cores (tokens/s)."""
+    from oracle import enhanced as oe
+    from sb200 import synth
+    w = synth.enhanced_router_weights(H, seed=0)
+    x = synth.hidden_states(sample_tokens, H, seed=1).numpy()
+    for _ in range(2):
+        oe.gate_topk(oe.router_forward(w, x)[2], TOPK)
+    done, t0 = 0, time.perf_counter()
+    while True:
+        oe.gate_topk(oe.router_forward(w, x)[2], TOPK)
+        done += sample_tokens
+        el = time.perf_counter() - t0
+        if el >= budget_s or done >= 16 * sample_tokens:
+            break
+    return done / el, done, el
+
+
 def config4_workloads(batch: int, device):
     """Config 4: 6-level router (4^6 = 4096 experts) at hidden 4096 vs a dense
     linear gate of the same shape (bf16 4096x4096 GEMM + top-8 + softmax)."""
@@ -529,6 +572,28 @@ def run_ours(a):
                                           for k, (n, t) in r4prof.items()},
                           "dense_gate": "torch bf16 x @ W^T (cuBLAS, 4096 x 4096) + topk(8) + softmax",
                           "l2": "flushed before every step"}
+    # ---- enhanced router (the OLMoE production router) + softmax top-8 gate
+    if not a.skip_enhanced:
+        etok = 65536
+        estep, eflop = enhanced_workload(etok, dev)
+        e_steps = min(a.steps, 50)
+        e_ms, eprof = time_steps(estep, e_steps, a.warmup, world, profile=True, flush=flush)
+        dom = eprof.get("enh_proj0_gelu_tc", (0, 0.0))
+        out["enhanced_router"] = {
+            "metric": "EnhancedBVHRouter + BVHGateWrapper top-8, Mq/s", "unit": "Mq/s",
+            "value": round(etok * world * e_steps / (e_ms / 1e3) / 1e6, 3), "tokens_per_gpu": etok,
+            "ms_per_step": round(e_ms / e_steps, 4), "flop_per_token": eflop,
+            "tensor_frac_of_step": round(etok * eflop / (e_ms / e_steps / 1e3) / 1e12 / pk["bf16_tflops"], 4),
+            "kernels": {k: {"launches": n, "avg_ms": round(t / max(n, 1), 4)} for k, (n, t) in eprof.items()},
+            "proj0_tflops": round(etok * 2.0 * H * 512 / (dom[1] / max(dom[0], 1) / 1e3) / 1e12, 1) if dom[0] else None,
+            "precision": "bf16 tcgen05 input projection, fp32 levels/head/gate",
+            "l2": "flushed before every step"}
+        if rank == 0 and world == 1 and not a.no_cpu_baseline:
+            rate, done, el = cpu_enhanced_rate(2048)
+            out["enhanced_router"]["cpu_baseline"] = {
+                "value": round(rate / 1e6, 6), "unit": "Mq/s", "cores": blas_threads(), "kind": "port",
+                "sample": f"{done} tokens through the numpy port of EnhancedBVHRouter + the gate (fp32) "
+                          f"in {el:.1f} s"}
     # ---- router alone (config 1), same process
     if not a.skip_router:
         rstep, _, rmeta = router_workload(a.router_batch, dev)
@@ -662,6 +727,7 @@ def main():
     ap.add_argument("--skip-ep", action="store_true")
     ap.add_argument("--skip-stack", action="store_true")
     ap.add_argument("--skip-config4", action="store_true")
+    ap.add_argument("--skip-enhanced", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=256)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     a = ap.parse_args()

@@ -101,6 +101,7 @@ __device__ __forceinline__ void enh_dense(const float* in, int ldi, int I, const
 #pragma unroll
   for (int j = 0; j < TPG; ++j) acc[j] = 0.f;
   int i = 0;
+#pragma unroll 4
   for (; i + 4 <= I; i += 4) {
     const float w0 = __ldg(Wt + (int64_t)(i + 0) * O + o), w1 = __ldg(Wt + (int64_t)(i + 1) * O + o);
     const float w2 = __ldg(Wt + (int64_t)(i + 2) * O + o), w3 = __ldg(Wt + (int64_t)(i + 3) * O + o);
