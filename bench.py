@@ -292,22 +292,29 @@ def moe_workload(batch: int, device, select: str = "soft"):
     return step, e2e_step, meta
 
 
-def enhanced_workload(batch: int, device):
+def enhanced_workload(batch: int, device, hybrid: bool = False):
     """EnhancedBVHRouter (the OLMoE production router, python/olmoe_bvh_distill.py:422-632)
-    + BVHGateWrapper softmax top-8 (python/olmoe_e2e_eval.py:928-938) on bf16 tokens."""
+    + BVHGateWrapper softmax top-8 (python/olmoe_e2e_eval.py:928-938) on bf16 tokens;
+    ``hybrid``: the hybrid pre-filter gate instead (BVH top-48 candidates, the
+    layer's dense 64-expert gate, olmoe_e2e_eval.py:1264-1296)."""
     import torch
     from sb200 import synth
     from sb200.enhanced import EnhancedEngine
     w = synth.enhanced_router_weights(H, seed=0)
     eng = EnhancedEngine(H, 128, BRANCHING, device)
     eng.upload(w)
+    if hybrid:
+        eng.set_dense_gate(torch.from_numpy(synth.dense_gate_weight(64, H, seed=0)).to(torch.bfloat16))
     x = synth.hidden_states(batch, H, seed=1, dtype=torch.bfloat16, device=device)
     outs = {"router_probs": torch.empty(batch, 64, dtype=torch.float32, device=device),
             "topk_weights": torch.empty(batch, TOPK, dtype=torch.float32, device=device),
             "topk_ids": torch.empty(batch, TOPK, dtype=torch.int32, device=device)}
 
     def step():
-        eng.forward(x, precision="fast", want=(), gate="softmax", k=TOPK, outputs=outs)
+        if hybrid:
+            eng.forward(x, precision="fast", want=(), gate="hybrid", k=TOPK, n_candidates=48, outputs=outs)
+        else:
+            eng.forward(x, precision="fast", want=(), gate="softmax", k=TOPK, outputs=outs)
 
     # 2 (H*512 + 512*256) + tail (levels + head) MAC per token, times 2 FLOP
     flop = 2.0 * (H * 512 + 512 * 256 + 256 * 131 + 256 * 128 + 128 * 128 + 2 * (128 * 131 + 2 * 128 * 128)
@@ -588,6 +595,13 @@ def run_ours(a):
             "proj0_tflops": round(etok * 2.0 * H * 512 / (dom[1] / max(dom[0], 1) / 1e3) / 1e12, 1) if dom[0] else None,
             "precision": "bf16 tcgen05 input projection, fp32 levels/head/gate",
             "l2": "flushed before every step"}
+        hstep, _ = enhanced_workload(etok, dev, hybrid=True)
+        h_ms, hprof = time_steps(hstep, e_steps, a.warmup, world, profile=True, flush=flush)
+        out["enhanced_router"]["hybrid_gate"] = {
+            "what": "hybrid pre-filter: BVH top-48 candidates + dense 64-expert gate (bf16 GEMM) softmax, top-8",
+            "value": round(etok * world * e_steps / (h_ms / 1e3) / 1e6, 3), "unit": "Mq/s",
+            "ms_per_step": round(h_ms / e_steps, 4),
+            "kernels": {k: {"launches": n, "avg_ms": round(t / max(n, 1), 4)} for k, (n, t) in hprof.items()}}
         if rank == 0 and world == 1 and not a.no_cpu_baseline:
             rate, done, el = cpu_enhanced_rate(2048)
             out["enhanced_router"]["cpu_baseline"] = {
@@ -597,7 +611,18 @@ def run_ours(a):
     # ---- router alone (config 1), same process
     if not a.skip_router:
         rstep, _, rmeta = router_workload(a.router_batch, dev)
+        rsampler = ClockSampler(local)
+        rsampler.start()
         r_ms, rprof = time_steps(rstep, a.router_steps, a.warmup, world, profile=True)
+        rclocks = rsampler.stop()
+        # the same-shape plain GEMM through cuBLAS (no bias, GELU or position
+        # tail), timed the same way right after: the like-for-like yardstick
+        # for encoder GEMM 1 under the clocks this loop runs at
+        gx = torch.randn(a.router_batch, H, device=dev).to(torch.bfloat16)
+        gw = (torch.randn(H, H, device=dev) / H ** 0.5).to(torch.bfloat16)
+        gout = torch.empty(a.router_batch, H, device=dev, dtype=torch.bfloat16)
+        c_ms, _ = time_steps(lambda: torch.mm(gx, gw.t(), out=gout), a.router_steps, a.warmup, world)
+        del gx, gw, gout
         rtok = rmeta["tokens_per_step"] * a.router_steps * world
         out["router"] = {"metric": "router Mq/s", "value": round(rtok / (r_ms / 1e3) / 1e6, 3),
                          "unit": "Mq/s", "batch_per_gpu": a.router_batch,
@@ -609,7 +634,13 @@ def run_ours(a):
                                                       pk["bf16_tflops"], 4),
                          "kernels": {k: {"launches": n, "avg_ms": round(t / max(n, 1), 4)}
                                      for k, (n, t) in rprof.items()},
-                         "roofline": roofline_tensor(rmeta, rprof, pk, r_ms, a.router_steps)}
+                         "roofline": roofline_tensor(rmeta, rprof, pk, r_ms, a.router_steps),
+                         "clocks": rclocks,
+                         "cublas_same_gemm": {
+                             "what": f"torch.mm bf16 [{a.router_batch},{H}] x [{H},{H}]^T (cuBLAS), "
+                                     "same loop length",
+                             "avg_ms": round(c_ms / a.router_steps, 4),
+                             "tflops": round(2.0 * a.router_batch * H * H / (c_ms / a.router_steps / 1e3) / 1e12, 1)}}
         if rank == 0 and world == 1 and not a.no_cpu_baseline:
             rate, done, el = cpu_router_rate(4096)
             out["router"]["cpu_baseline"] = {

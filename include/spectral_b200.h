@@ -272,7 +272,7 @@ typedef struct {
   float temperature;    /* the module's temperature buffer */
 } sb_enh_weights;
 
-enum sb_gate_mode { SB_GATE_SOFTMAX = 0, SB_GATE_TOPK_SOFTMAX = 1 };
+enum sb_gate_mode { SB_GATE_SOFTMAX = 0, SB_GATE_TOPK_SOFTMAX = 1, SB_GATE_HYBRID = 2 };
 
 /* Device outputs; any pointer may be NULL (not produced). */
 typedef struct {
@@ -295,6 +295,26 @@ size_t sb_enh_workspace_bytes(const sb_enh* h, int64_t batch, int precision);
 int sb_enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t batch, int precision,
                    int gate_mode, int norm_topk_prob, int round_dtype, int top_k,
                    const sb_enh_outputs* out, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Hybrid pre-filter gate (python/olmoe_e2e_eval.py:1264-1296, the
+ * _hybrid_forward that replace_gate_with_bvh(hybrid=True) installs): the BVH
+ * router's expert_probs pick n_candidates experts (top-n, lower index first on
+ * ties); the layer's own dense gate gives full_logits = x W_gate^T in the
+ * hidden dtype and router_probs = softmax(full_logits) over all E experts in
+ * fp32; the top_k of router_probs among the candidates are the outputs
+ * (renormalised when norm_topk_prob).
+ *
+ * sb_enh_set_dense_gate copies W_gate [E, hidden] (nn.Linear layout, SB_F32 or
+ * SB_BF16; host or device memory) into the handle. */
+int sb_enh_set_dense_gate(sb_enh* h, const void* w_gate, int w_dtype, int rows, int cols);
+/* x as for sb_enh_forward; round_dtype = the hidden dtype, applied to the dense
+ * logits (the BVH probabilities are computed in fp32 as the reference does on
+ * x.float()).  out->router_probs receives the full dense softmax; the other
+ * router outputs (logits, expert_probs, ...) are produced as by sb_enh_forward. */
+int sb_enh_forward_hybrid(sb_enh* h, const void* x, int x_dtype, int64_t batch, int precision,
+                          int n_candidates, int norm_topk_prob, int round_dtype, int top_k,
+                          const sb_enh_outputs* out, void* workspace, size_t workspace_bytes,
+                          void* stream);
 int sb_enh_destroy(sb_enh* h);
 
 #ifdef __cplusplus

@@ -25,6 +25,10 @@ It restates, in numpy fp32, op by op (spectral_mode off, n_rays = 1):
         top-k of it, renormalised when norm_topk_prob;
       "topk_softmax" (:521-529): top-k of the logits, softmax over those k,
         router_probs = those k weights scattered into zeros.
+  * the hybrid pre-filter gate of ``replace_gate_with_bvh(hybrid=True)``
+                                                   python/olmoe_e2e_eval.py:1264-1296
+      BVH top-n candidates, the dense gate's full fp32 softmax, top-k of it
+      restricted to the candidates.
 
 Parity: pinned against the reference's own outputs through the committed
 fixtures tests/golden/enhanced_*.npz (tests/golden/make_golden.py imports the
@@ -140,3 +144,31 @@ def gate_topk(logits: np.ndarray, k: int = 8, mode: str = "softmax", norm_topk_p
         np.put_along_axis(probs, ids, wts, axis=1)
         return probs, wts, ids
     raise ValueError(f"weight mode {mode!r} is not restated")
+
+
+def dense_gate_logits(x: np.ndarray, w_gate: np.ndarray, dtype: str = "f32") -> np.ndarray:
+    """full_logits = F.linear(h2d, W_gate) in the hidden dtype
+    (python/olmoe_e2e_eval.py:1278): fp32 products accumulated in float64 here,
+    then rounded to the hidden dtype (bf16: round-to-nearest-even)."""
+    acc = (np.asarray(x, np.float64) @ np.asarray(w_gate, np.float64).T).astype(F32)
+    return round_to(acc, dtype)
+
+
+def hybrid_gate(bvh_probs: np.ndarray, full_logits: np.ndarray, n_candidates: int, k: int = 8,
+                norm_topk_prob: bool = False):
+    """The hybrid pre-filter of replace_gate_with_bvh(hybrid=True),
+    python/olmoe_e2e_eval.py:1264-1296:
+      candidate_ids = topk(bvh_probs, n_candidates)
+      full_probs    = softmax(full_logits, fp32) over all experts
+      top-k of full_probs gathered at the candidates, mapped back to expert
+      ids, renormalised when norm_topk_prob.
+    Returns (full_probs [B,E], top-k weights [B,k] f32 before the cast to the
+    hidden dtype, top-k ids [B,k])."""
+    _, cand = topk_desc(np.asarray(bvh_probs, F32), n_candidates)
+    full = softmax(np.asarray(full_logits, F32))
+    cprob = np.take_along_axis(full, cand, axis=1)
+    vals, local = topk_desc(cprob, k)
+    ids = np.take_along_axis(cand, local, axis=1)
+    if norm_topk_prob:
+        vals = (vals / vals.sum(axis=1, keepdims=True)).astype(F32)
+    return full, vals, ids

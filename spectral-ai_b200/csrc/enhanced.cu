@@ -62,6 +62,10 @@ struct EnhOut {
   int mode;        // SB_GATE_*
   int norm;        // norm_topk_prob
   int round_bf16;  // logits.to(bfloat16) before the gate
+  // SB_GATE_HYBRID: the dense gate's raw logits [B,E] (fp32 accumulate) and
+  // the number of BVH candidates
+  const float* dense;
+  int n_cand;
 };
 
 __device__ __forceinline__ float enh_warp_sum(float v) {
@@ -229,6 +233,101 @@ __device__ void enh_gate_token(const float* lg, int E, const EnhOut& o, int64_t 
   }
 }
 
+// Hybrid pre-filter gate of one token (one warp), olmoe_e2e_eval.py:1264-1296:
+//   candidates   = topk(expert_probs, n_cand)            (BVH, fp32)
+//   router_probs = softmax(round(x W_gate^T), fp32)      (all E experts)
+//   top-k of router_probs over the candidates, renormalised when norm.
+// expert_probs are recomputed here with the same operations and order as the
+// values the tail writes to o.probs, so the candidate set follows those bits.
+__device__ void enh_gate_hybrid(const float* lg, int E, float tau, const EnhOut& o, int64_t tok, int lane) {
+  constexpr int PER = 8;  // E <= 256
+  float pb[PER];
+  float m = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    const int e = lane + 32 * u;
+    pb[u] = e < E ? lg[e] / tau : -INFINITY;
+    m = fmaxf(m, pb[u]);
+  }
+  m = enh_warp_max(m);
+  float sum = 0.f;
+#pragma unroll
+  for (int u = 0; u < PER; ++u) sum += lane + 32 * u < E ? expf(pb[u] - m) : 0.f;
+  sum = enh_warp_sum(sum);
+#pragma unroll
+  for (int u = 0; u < PER; ++u) pb[u] = lane + 32 * u < E ? expf(pb[u] - m) / sum : -INFINITY;
+  // rank of each expert by BVH probability: larger first, lower index first on ties
+  int rank[PER];
+#pragma unroll
+  for (int u = 0; u < PER; ++u) rank[u] = 0;
+#pragma unroll
+  for (int u2 = 0; u2 < PER; ++u2) {
+    if (32 * u2 >= E) break;
+    for (int s2 = 0; s2 < 32; ++s2) {
+      const float pj = __shfl_sync(0xffffffffu, pb[u2], s2);
+      const int j = 32 * u2 + s2;
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int e = lane + 32 * u;
+        rank[u] += (pj > pb[u] || (pj == pb[u] && j < e)) ? 1 : 0;
+      }
+    }
+  }
+  // the dense gate's softmax over all experts
+  float d[PER];
+  float m2 = -INFINITY;
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    const int e = lane + 32 * u;
+    d[u] = e < E ? enh_round(o.dense[tok * E + e], o.round_bf16) : -INFINITY;
+    m2 = fmaxf(m2, d[u]);
+  }
+  m2 = enh_warp_max(m2);
+  float s2 = 0.f;
+#pragma unroll
+  for (int u = 0; u < PER; ++u) s2 += lane + 32 * u < E ? expf(d[u] - m2) : 0.f;
+  s2 = enh_warp_sum(s2);
+  float v[PER];
+#pragma unroll
+  for (int u = 0; u < PER; ++u) {
+    const int e = lane + 32 * u;
+    if (e < E) {
+      d[u] = expf(d[u] - m2) / s2;
+      if (o.rprobs) o.rprobs[tok * E + e] = d[u];
+    }
+    v[u] = (e < E && rank[u] < o.n_cand) ? d[u] : -INFINITY;
+  }
+  // top-k over the candidates by repeated warp argmax
+  float sel_v = 0.f;
+  int sel_i = 0;
+  for (int r = 0; r < o.k; ++r) {
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int u = 0; u < PER; ++u) {
+      const int e = lane + 32 * u;
+      if (e < E && (v[u] > bv || (v[u] == bv && e < bi))) {
+        bv = v[u];
+        bi = e;
+      }
+    }
+    enh_warp_argmax(bv, bi);
+    if (lane == r) {
+      sel_v = bv;
+      sel_i = bi;
+    }
+#pragma unroll
+    for (int u = 0; u < PER; ++u)
+      if (lane + 32 * u == bi) v[u] = -INFINITY;
+  }
+  float w = sel_v;
+  if (o.norm) w = sel_v / enh_warp_sum(lane < o.k ? sel_v : 0.f);
+  if (lane < o.k) {
+    o.topi[tok * o.k + lane] = sel_i;
+    if (o.topw) o.topw[tok * o.k + lane] = w;
+  }
+}
+
 // Shared memory of the tail kernel, floats.
 constexpr int ENH_SMEM_FLOATS = 2 * ENH_TOK * ENH_LD       // X, Z
                                 + ENH_TOK * ENH_LDF         // Fb: features | pos | level probs
@@ -371,7 +470,12 @@ __global__ void __launch_bounds__(ENH_THREADS) enh_tail_kernel(const float* __re
           if (o.bonus) o.bonus[tok * E + e] = (1.0f + 0.2f * (float)(i == a1)) + 0.1f * (float)(j == a2);
         }
       }
-      if (o.topi) enh_gate_token(lg, E, o, tok, lane);
+      if (o.topi) {
+        if (o.mode == SB_GATE_HYBRID)
+          enh_gate_hybrid(lg, E, t.tau_soft, o, tok, lane);
+        else
+          enh_gate_token(lg, E, o, tok, lane);
+      }
     }
     __syncthreads();
   }
@@ -399,13 +503,18 @@ struct sb_enh {
   size_t tail_floats = 0;
   sb::EnhTail t{};
   CUtensorMap tm_w0{}, tm_w2{};
+  // the layer's dense gate for the hybrid pre-filter (sb_enh_set_dense_gate)
+  __nv_bfloat16* wg_bf16 = nullptr;  // [E,H]
+  float* wg_f32 = nullptr;           // [E,H]
+  float* zero_e = nullptr;           // [E] zero bias of the dense gate GEMM
+  CUtensorMap tm_wg{};
 };
 
 namespace sb {
 namespace {
 
 struct EnhWs {
-  size_t g, p, total;
+  size_t g, p, d, total;
 };
 
 EnhWs enh_ws(const sb_enh* h, int64_t B, int precision) {
@@ -418,8 +527,8 @@ EnhWs enh_ws(const sb_enh* h, int64_t B, int precision) {
   };
   w.g = take((size_t)B * 512 * (precision == SB_PREC_FAST ? 2 : 4));
   w.p = take((size_t)B * 256 * 4);
+  w.d = take((size_t)B * h->E * 4);  // dense gate logits (hybrid gate only)
   w.total = o;
-  (void)h;
   return w;
 }
 
@@ -433,6 +542,22 @@ void enh_free(sb_enh* h) {
   cudaFree(h->tail);
   h->w0_bf16 = h->w2_bf16 = nullptr;
   h->w0_f32 = h->w2_f32 = h->b0 = h->b2 = h->tail = nullptr;
+}
+
+void enh_free_gate(sb_enh* h) {
+  cudaFree(h->wg_bf16);
+  cudaFree(h->wg_f32);
+  cudaFree(h->zero_e);
+  h->wg_bf16 = nullptr;
+  h->wg_f32 = h->zero_e = nullptr;
+}
+
+__global__ void enh_gate_convert_kernel(const void* in, int bf16_in, float* f32, __nv_bfloat16* bf, int64_t n) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = bf16_in ? __bfloat162float(static_cast<const __nv_bfloat16*>(in)[i]) : static_cast<const float*>(in)[i];
+    f32[i] = v;
+    bf[i] = __float2bfloat16_rn(v);
+  }
 }
 
 __global__ void enh_f32_to_bf16_kernel(const float* in, __nv_bfloat16* out, int64_t n) {
@@ -583,10 +708,12 @@ extern "C" size_t sb_enh_workspace_bytes(const sb_enh* h, int64_t batch, int pre
   return sb::enh_ws(h, batch, precision).total;
 }
 
-extern "C" int sb_enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t batch, int precision, int gate_mode,
-                              int norm_topk_prob, int round_dtype, int top_k, const sb_enh_outputs* out,
-                              void* workspace, size_t workspace_bytes, void* stream_) {
-  using namespace sb;
+namespace sb {
+namespace {
+
+int enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t batch, int precision, int gate_mode, int n_cand,
+                int norm_topk_prob, int round_dtype, int top_k, const sb_enh_outputs* out, void* workspace,
+                size_t workspace_bytes, void* stream_) {
   SB_REQUIRE(h && out, "sb_enh_forward: null argument");
   SB_REQUIRE(h->uploaded, "sb_enh_forward: weights were not uploaded");
   SB_REQUIRE(batch >= 0, "batch=%lld must be >= 0", (long long)batch);
@@ -594,8 +721,15 @@ extern "C" int sb_enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t bat
   SB_REQUIRE(precision == SB_PREC_FAST || precision == SB_PREC_EXACT, "unknown precision %d", precision);
   SB_REQUIRE(precision != SB_PREC_FAST || x_dtype == SB_BF16,
              "FAST precision needs bf16 input (use EXACT for fp32 input)");
-  SB_REQUIRE(gate_mode == SB_GATE_SOFTMAX || gate_mode == SB_GATE_TOPK_SOFTMAX, "unknown gate mode %d",
-             gate_mode);
+  SB_REQUIRE(gate_mode == SB_GATE_SOFTMAX || gate_mode == SB_GATE_TOPK_SOFTMAX || gate_mode == SB_GATE_HYBRID,
+             "unknown gate mode %d", gate_mode);
+  if (gate_mode == SB_GATE_HYBRID) {
+    SB_REQUIRE(h->wg_f32 != nullptr, "the hybrid gate needs the dense gate weight (sb_enh_set_dense_gate)");
+    SB_REQUIRE(out->topk_ids, "the hybrid gate needs topk_ids");
+    SB_REQUIRE(top_k >= 1 && top_k <= 32 && top_k <= h->E, "top_k=%d must be in [1, min(32, %d)]", top_k, h->E);
+    SB_REQUIRE(n_cand >= top_k && n_cand <= h->E, "n_candidates=%d must be in [top_k=%d, %d]", n_cand, top_k,
+               h->E);
+  }
   SB_REQUIRE(round_dtype == SB_F32 || round_dtype == SB_BF16, "round dtype %d must be SB_F32 or SB_BF16",
              round_dtype);
   if (out->topk_ids || out->topk_weights || out->router_probs) {
@@ -615,7 +749,9 @@ extern "C" int sb_enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t bat
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   void* G = ws + W.g;
   float* P = reinterpret_cast<float*>(ws + W.p);
-  const int H = h->H, M = (int)batch;
+  float* D = reinterpret_cast<float*>(ws + W.d);
+  const int H = h->H, M = (int)batch, E = h->E;
+  const bool hybrid = gate_mode == SB_GATE_HYBRID;
   int rc;
   if (precision == SB_PREC_FAST) {
     CUtensorMap ta, tg;
@@ -632,6 +768,12 @@ extern "C" int sb_enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t bat
     if ((rc = launch_gemm_tc<256, 4, EpiBiasF32, false>("enh_proj2_tc", tg, h->tm_w2, h->tm_w2, M, 256, 512, e2,
                                                          stream)))
       return rc;
+    if (hybrid) {  // full_logits = x W_gate^T (fp32 accumulate; rounded to the hidden dtype in the tail)
+      EpiBiasF32 ed{h->zero_e, D, E, E};
+      if ((rc = launch_gemm_tc<64, 4, EpiBiasF32, false>("enh_dense_gate_tc", ta, h->tm_wg, h->tm_wg, M, E, H, ed,
+                                                          stream)))
+        return rc;
+    }
   } else {
     float* G32 = static_cast<float*>(G);
     {
@@ -651,10 +793,21 @@ extern "C" int sb_enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t bat
       sgemm_nt_kernel<float, ACT_NONE><<<grid, 256, 0, stream>>>(G32, h->w2_f32, h->b2, P, M, 256, 512, 256, 0);
       SB_CUDA_TRY(cudaGetLastError());
     }
+    if (hybrid) {
+      ProfScope prof("enh_dense_gate_f32", stream);
+      const dim3 grid((E + 127) / 128, (M + 127) / 128);
+      if (x_dtype == SB_BF16)
+        sgemm_nt_kernel<__nv_bfloat16, ACT_NONE><<<grid, 256, 0, stream>>>(
+            static_cast<const __nv_bfloat16*>(x), h->wg_f32, h->zero_e, D, M, E, H, E, 0);
+      else
+        sgemm_nt_kernel<float, ACT_NONE><<<grid, 256, 0, stream>>>(static_cast<const float*>(x), h->wg_f32,
+                                                                   h->zero_e, D, M, E, H, E, 0);
+      SB_CUDA_TRY(cudaGetLastError());
+    }
   }
   EnhOut o{out->logits, out->expert_probs, out->expert_ids, out->geo_dist, out->branch_bonus,
            out->router_probs, out->topk_weights, out->topk_ids, top_k, gate_mode, norm_topk_prob ? 1 : 0,
-           round_dtype == SB_BF16 ? 1 : 0};
+           round_dtype == SB_BF16 ? 1 : 0, hybrid ? D : nullptr, n_cand};
   {
     static bool attr[64] = {};
     if (h->device < 64 && !attr[h->device]) {
@@ -671,11 +824,62 @@ extern "C" int sb_enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t bat
   return SB_OK;
 }
 
+}  // namespace
+}  // namespace sb
+
+extern "C" int sb_enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t batch, int precision, int gate_mode,
+                              int norm_topk_prob, int round_dtype, int top_k, const sb_enh_outputs* out,
+                              void* workspace, size_t workspace_bytes, void* stream) {
+  using namespace sb;
+  SB_REQUIRE(gate_mode != SB_GATE_HYBRID, "the hybrid gate runs through sb_enh_forward_hybrid");
+  return enh_forward(h, x, x_dtype, batch, precision, gate_mode, 0, norm_topk_prob, round_dtype, top_k, out,
+                     workspace, workspace_bytes, stream);
+}
+
+extern "C" int sb_enh_forward_hybrid(sb_enh* h, const void* x, int x_dtype, int64_t batch, int precision,
+                                     int n_candidates, int norm_topk_prob, int round_dtype, int top_k,
+                                     const sb_enh_outputs* out, void* workspace, size_t workspace_bytes,
+                                     void* stream) {
+  return sb::enh_forward(h, x, x_dtype, batch, precision, SB_GATE_HYBRID, n_candidates, norm_topk_prob, round_dtype,
+                         top_k, out, workspace, workspace_bytes, stream);
+}
+
+extern "C" int sb_enh_set_dense_gate(sb_enh* h, const void* w_gate, int w_dtype, int rows, int cols) {
+  using namespace sb;
+  SB_REQUIRE(h && w_gate, "sb_enh_set_dense_gate: null argument");
+  SB_REQUIRE(w_dtype == SB_F32 || w_dtype == SB_BF16, "gate dtype %d must be SB_F32 or SB_BF16", w_dtype);
+  SB_REQUIRE(rows == h->E && cols == h->H, "gate weight [%d,%d] must be [n_experts=%d, hidden=%d]", rows, cols,
+             h->E, h->H);
+  DeviceGuard g(h->device);
+  enh_free_gate(h);
+  const size_t n = (size_t)rows * cols, el = w_dtype == SB_BF16 ? 2 : 4;
+  void* staging = nullptr;
+  SB_CUDA_TRY(cudaMalloc(&staging, n * el));
+  int rc = SB_OK;
+  if (cudaMemcpy(staging, w_gate, n * el, cudaMemcpyDefault) != cudaSuccess ||
+      cudaMalloc(&h->wg_f32, n * 4) != cudaSuccess || cudaMalloc(&h->wg_bf16, n * 2) != cudaSuccess ||
+      cudaMalloc(&h->zero_e, (size_t)rows * 4) != cudaSuccess ||
+      cudaMemset(h->zero_e, 0, (size_t)rows * 4) != cudaSuccess) {
+    rc = fail(SB_ERR_CUDA, "dense gate upload: %s", cudaGetErrorString(cudaGetLastError()));
+  } else {
+    enh_gate_convert_kernel<<<256, 256>>>(staging, w_dtype == SB_BF16, h->wg_f32, h->wg_bf16, (int64_t)n);
+    if (cudaGetLastError() != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess)
+      rc = fail(SB_ERR_CUDA, "dense gate conversion failed");
+  }
+  cudaFree(staging);
+  if (!rc)
+    rc = make_tmap_2d(&h->tm_wg, h->wg_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, rows, cols, cols, GEMM_BK, 64,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) enh_free_gate(h);
+  return rc;
+}
+
 extern "C" int sb_enh_destroy(sb_enh* h) {
   if (!h) return SB_OK;
   {
     sb::DeviceGuard g(h->device);
     sb::enh_free(h);
+    sb::enh_free_gate(h);
   }
   delete h;
   return SB_OK;

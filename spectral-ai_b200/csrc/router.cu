@@ -16,9 +16,12 @@
 //      (python/olmoe_extract.py:105-118).  HARD runs one thread per token,
 //      SOFT one warp per token.
 #include "common.cuh"
+#include "gemm_pair.cuh"
 #include "gemm_tc.cuh"
 
 #include <math.h>
+#include <stdlib.h>
+#include <string.h>
 #include <mutex>
 #include <new>
 #include <vector>
@@ -675,6 +678,8 @@ struct sb_router {
   CUtensorMap tm_w1{}, tm_w2{}, tm_w3s{}, tm_wr{};
   // narrower boxes for small batches, where the wide tiles leave SMs idle
   CUtensorMap tm_w1_128{}, tm_w2_64{}, tm_wr_32{};
+  // the position rows split over a CTA pair: 8 of the 16 rows per CTA
+  CUtensorMap tm_w3s_8{};
   float bbox[SB_MAX_LEVELS][6] = {};  // per level: min x,y,z, max x,y,z of the centers
 };
 
@@ -867,7 +872,9 @@ extern "C" int sb_router_upload(sb_router* h, const sb_router_weights* w) {
       (rc = make_tmap_2d(&h->tm_w2_64, h->w2_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, S, H, H,
                          GEMM_BK, 64, CU_TENSOR_MAP_SWIZZLE_128B)) ||
       (rc = make_tmap_2d(&h->tm_wr_32, h->wr_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, S, S,
-                         GEMM_BK, 32, CU_TENSOR_MAP_SWIZZLE_128B))) {
+                         GEMM_BK, 32, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&h->tm_w3s_8, h->w3s_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 16, H, H,
+                         GEMM_BK, 8, CU_TENSOR_MAP_SWIZZLE_128B))) {
     free_router_buffers(h);
     return rc;
   }
@@ -913,6 +920,52 @@ int launch_gemm_tc(const char* name, const CUtensorMap& ta, const CUtensorMap& t
                                                       idesc_f16(1, GEMM_BM, TAIL_N), epi);
   SB_CUDA_TRY(cudaGetLastError());
   return SB_OK;
+}
+
+// The CTA-pair GEMM (256 x 256 tiles) as a persistent grid of one pair per
+// two SMs (as many as fit: one CTA per SM).
+template <class Epi, bool TAIL>
+int launch_gemm_pair(const char* name, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2,
+                     int M, int N, int K, Epi epi, cudaStream_t stream) {
+  auto kern = gemm_pair_kernel<Epi, TAIL>;
+  static int pairs[64] = {};
+  int dev = 0;
+  SB_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev >= 64) return fail(SB_ERR_CUDA, "device ordinal %d out of range", dev);
+  cudaLaunchConfig_t cfg{};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.blockDim = dim3(GP_THREADS);
+  cfg.dynamicSmemBytes = GP_SMEM_BYTES;
+  cfg.stream = stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (!pairs[dev]) {
+    SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GP_SMEM_BYTES));
+    cfg.gridDim = dim3(2 * (num_sms() / 2));
+    int n = 0;
+    SB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+    if (n < 1) return fail(SB_ERR_CUDA, "no CTA pair of the GEMM fits on this GPU");
+    pairs[dev] = n;
+  }
+  const int tiles = ((M + GP_BM - 1) / GP_BM) * ((N + GP_BN - 1) / GP_BN + (TAIL ? 1 : 0));
+  cfg.gridDim = dim3(2 * (tiles < pairs[dev] ? tiles : pairs[dev]));
+  ProfScope prof(name, stream);
+  SB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, tb2, M, N, K, idesc_f16(1, GP_BM, GP_BN),
+                                 idesc_f16(1, GP_BM, TAIL_N), epi));
+  return SB_OK;
+}
+
+// SB_ROUTER_GEMM=single keeps the single-CTA GEMM for the wide encoder layer.
+bool router_pair_gemm_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("SB_ROUTER_GEMM");
+    return !(e && strcmp(e, "single") == 0);
+  }();
+  return on;
 }
 
 }  // namespace
@@ -978,7 +1031,12 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
     const int64_t mblocks = (M + GEMM_BM - 1) / GEMM_BM;
     const int64_t sms = num_sms();
     EpiGeluBf16 e1{h->b1, static_cast<__nv_bfloat16*>(G), H, H, h->b3d, pos};
-    if (mblocks * ((H + 255) / 256 + 1) >= sms)
+    const int64_t pair_tiles = ((M + GP_BM - 1) / GP_BM) * ((H + GP_BN - 1) / GP_BN + 1);
+    if (router_pair_gemm_enabled() && pair_tiles >= 2 * (sms / 2))
+      // enough 256 x 256 tiles for two rounds over the pairs: the pair GEMM
+      rc = launch_gemm_pair<EpiGeluBf16, true>("router_enc1_gelu_tc", ta, h->tm_w1_128, h->tm_w3s_8, M, H, H,
+                                               e1, stream);
+    else if (mblocks * ((H + 255) / 256 + 1) >= sms)
       rc = launch_gemm_tc<256, 4, EpiGeluBf16, true>("router_enc1_gelu_tc", ta, h->tm_w1, h->tm_w3s, M, H, H,
                                                       e1, stream);
     else

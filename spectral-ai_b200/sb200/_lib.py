@@ -71,7 +71,7 @@ class EnhOutputs(C.Structure):
                                           "router_probs", "topk_weights", "topk_ids")]
 
 
-SB_GATE_SOFTMAX, SB_GATE_TOPK_SOFTMAX = 0, 1
+SB_GATE_SOFTMAX, SB_GATE_TOPK_SOFTMAX, SB_GATE_HYBRID = 0, 1, 2
 
 # (name, restype, argtypes) of every symbol the header declares
 SIGNATURES = [
@@ -115,6 +115,10 @@ SIGNATURES = [
     ("sb_enh_upload", C.c_int, [C.c_void_p, C.POINTER(EnhWeights)]),
     ("sb_enh_workspace_bytes", C.c_size_t, [C.c_void_p, C.c_int64, C.c_int]),
     ("sb_enh_forward", C.c_int,
+     [C.c_void_p, C.c_void_p, C.c_int, C.c_int64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+      C.POINTER(EnhOutputs), C.c_void_p, C.c_size_t, C.c_void_p]),
+    ("sb_enh_set_dense_gate", C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int]),
+    ("sb_enh_forward_hybrid", C.c_int,
      [C.c_void_p, C.c_void_p, C.c_int, C.c_int64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
       C.POINTER(EnhOutputs), C.c_void_p, C.c_size_t, C.c_void_p]),
     ("sb_enh_destroy", C.c_int, [C.c_void_p]),

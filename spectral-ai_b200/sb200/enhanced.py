@@ -3,7 +3,9 @@
 ``EnhancedEngine`` owns one ``sb_enh`` handle per device: the
 EnhancedBVHRouter eval forward (python/olmoe_bvh_distill.py:422-632) and the
 BVHGateWrapper "softmax" / "topk_softmax" weights (python/olmoe_e2e_eval.py:316-971)
-in three kernels on the current stream.  Outputs are ``torch.empty`` on the
+in three kernels on the current stream, and the hybrid pre-filter gate of
+replace_gate_with_bvh(hybrid=True) (python/olmoe_e2e_eval.py:1264-1296) with one
+more GEMM for the layer's dense gate.  Outputs are ``torch.empty`` on the
 input's device.
 """
 
@@ -91,6 +93,21 @@ class EnhancedEngine:
         with torch.cuda.device(self.dev_index):
             _lib.check(self.lib.sb_enh_upload(self.handle, C.byref(w)), "sb_enh_upload")
 
+    def set_dense_gate(self, weight: torch.Tensor) -> None:
+        """The layer's dense gate weight [E, hidden] (fp32 or bf16, any device)
+        for the hybrid gate."""
+        w = weight.detach()
+        if w.dtype not in (torch.float32, torch.bfloat16):
+            w = w.float()
+        if tuple(w.shape) != (self.n_experts, self.hidden):
+            raise RuntimeError(f"dense gate weight must be [{self.n_experts}, {self.hidden}], got {tuple(w.shape)}")
+        w = w.to(self.device).contiguous()
+        with torch.cuda.device(self.dev_index):
+            torch.cuda.current_stream(self.device).synchronize()
+            _lib.check(self.lib.sb_enh_set_dense_gate(
+                self.handle, C.c_void_p(w.data_ptr()), _lib.SB_BF16 if w.dtype == torch.bfloat16 else _lib.SB_F32,
+                w.shape[0], w.shape[1]), "sb_enh_set_dense_gate")
+
     def workspace(self, batch: int, precision: int) -> torch.Tensor:
         need = int(self.lib.sb_enh_workspace_bytes(self.handle, batch, precision))
         if self._ws is None or self._ws.numel() < need + 1024:
@@ -99,11 +116,13 @@ class EnhancedEngine:
 
     def forward(self, x: torch.Tensor, precision: str = "auto", want=("logits", "expert_probs", "expert_ids"),
                 gate: Optional[str] = None, k: int = 8, norm_topk_prob: bool = False,
-                round_dtype: Optional[torch.dtype] = None,
+                round_dtype: Optional[torch.dtype] = None, n_candidates: int = 16,
                 outputs: Optional[Dict[str, torch.Tensor]] = None) -> Dict[str, torch.Tensor]:
         """Router outputs named in ``want`` (any of OUTPUTS[:5]); with ``gate``
         set also router_probs, topk_weights (fp32) and topk_ids of that mode,
-        logits rounded to ``round_dtype`` (default: x's dtype) first."""
+        logits rounded to ``round_dtype`` (default: x's dtype) first.
+        ``gate="hybrid"``: top-k of the dense gate's softmax among the
+        ``n_candidates`` experts of largest BVH probability (set_dense_gate)."""
         if not x.is_cuda:
             raise RuntimeError("router input must be a CUDA tensor (there is no CPU path)")
         if x.dim() != 2 or x.shape[1] != self.hidden:
@@ -136,12 +155,19 @@ class EnhancedEngine:
         base = ws.data_ptr()
         aligned = (base + 1023) // 1024 * 1024
         stream = torch.cuda.current_stream(dev).cuda_stream
+        xd = _lib.SB_BF16 if x.dtype == torch.bfloat16 else _lib.SB_F32
+        rdt = _lib.SB_BF16 if rd == torch.bfloat16 else _lib.SB_F32
+        wsb = ws.numel() - (aligned - base)
         with torch.cuda.device(dev):
-            rc = self.lib.sb_enh_forward(
-                self.handle, C.c_void_p(x.data_ptr()),
-                _lib.SB_BF16 if x.dtype == torch.bfloat16 else _lib.SB_F32, B, prec,
-                GATE_MODES[gate or "softmax"], int(bool(norm_topk_prob)),
-                _lib.SB_BF16 if rd == torch.bfloat16 else _lib.SB_F32, int(k), C.byref(o),
-                C.c_void_p(aligned), ws.numel() - (aligned - base), C.c_void_p(stream))
-        _lib.check(rc, "sb_enh_forward")
+            if gate == "hybrid":
+                rc = self.lib.sb_enh_forward_hybrid(
+                    self.handle, C.c_void_p(x.data_ptr()), xd, B, prec, int(n_candidates),
+                    int(bool(norm_topk_prob)), rdt, int(k), C.byref(o), C.c_void_p(aligned), wsb,
+                    C.c_void_p(stream))
+            else:
+                rc = self.lib.sb_enh_forward(
+                    self.handle, C.c_void_p(x.data_ptr()), xd, B, prec, GATE_MODES[gate or "softmax"],
+                    int(bool(norm_topk_prob)), rdt, int(k), C.byref(o), C.c_void_p(aligned), wsb,
+                    C.c_void_p(stream))
+        _lib.check(rc, "sb_enh_forward_hybrid" if gate == "hybrid" else "sb_enh_forward")
         return res

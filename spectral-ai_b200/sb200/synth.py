@@ -141,6 +141,14 @@ def enhanced_router_weights(hidden: int = 2048, branching: Sequence[int] = (4, 4
     return w
 
 
+def dense_gate_weight(n_experts: int, hidden: int, seed: int = 0, gain: float = 2.0) -> np.ndarray:
+    """A layer's dense top-k gate ``nn.Linear(hidden, n_experts, bias=False)``
+    weight for the hybrid pre-filter: N(0, gain^2 / hidden), so unit-RMS
+    tokens get logits of standard deviation ``gain``."""
+    g = torch.Generator().manual_seed(WEIGHT_STREAM + 0x2000 + seed)
+    return (torch.randn(n_experts, hidden, generator=g) * (gain / math.sqrt(hidden))).numpy().astype(np.float32)
+
+
 def unit_rms_rows(x: torch.Tensor) -> torch.Tensor:
     """Divide each row by its root-mean-square (fp32)."""
     rms = x.float().pow(2).mean(dim=-1, keepdim=True).sqrt()

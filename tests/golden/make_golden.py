@@ -228,6 +228,77 @@ def enhanced_case(ref_python: Path, name, H, seed, batch, x_seed, temperature=1.
     print(f"wrote {name}.npz")
 
 
+class _GateHost(torch.nn.Module):
+    """The module path replace_gate_with_bvh walks (find_gate_module,
+    olmoe_e2e_eval.py:1145-1174): model.model.layers[i].mlp.gate, with the
+    OLMoE gate attributes top_k and norm_topk_prob."""
+
+    def __init__(self, gate: torch.nn.Linear):
+        super().__init__()
+        self.model = torch.nn.Module()
+        layer = torch.nn.Module()
+        layer.mlp = torch.nn.Module()
+        layer.mlp.gate = gate
+        self.model.layers = torch.nn.ModuleList([layer])
+
+
+def gate_replacement_case(ref_python: Path, name, H, seed, gate_seed, batch, x_seed, head_gain=20.0):
+    """replace_gate_with_bvh (olmoe_e2e_eval.py:1177-1404) run by the reference
+    on a checkpoint it loads with torch.load: the hybrid pre-filter
+    (:1264-1296) at n_candidates 16 and 48, with and without norm_topk_prob,
+    on fp32 and bf16 hidden states; and the pure replacement with an affine
+    calibration and an expert permutation stored in the checkpoint
+    (:1305-1344)."""
+    import tempfile
+    sys.path.insert(0, str(ref_python))
+    import olmoe_e2e_eval
+    w = synth.enhanced_router_weights(H, seed=seed)
+    w["expert_head.2.weight"] = (w["expert_head.2.weight"] * head_gain).astype(np.float32)
+    wg = synth.dense_gate_weight(64, H, seed=gate_seed)
+    x = synth.hidden_states(batch, H, seed=x_seed)
+    sd = {k: torch.from_numpy(np.array(v)) for k, v in w.items()}
+    cfg = {"input_dim": H, "n_level1": 4, "n_level2": 4, "n_level3": 4, "feature_dim": 128}
+    g = torch.Generator().manual_seed(seed + 77)
+    cal = {"scale": (torch.rand(64, generator=g) + 0.5), "bias": torch.randn(64, generator=g) * 0.1}
+    perm = torch.randperm(64, generator=g)
+    out = {"H": H, "seed": seed, "gate_seed": gate_seed, "batch": batch, "x_seed": x_seed,
+           "head_gain": head_gain, "x_checksum": checksum(x.numpy()), "wg_checksum": checksum(wg),
+           "cal_scale": cal["scale"].numpy(), "cal_bias": cal["bias"].numpy(), "expert_perm": perm.numpy()}
+    with tempfile.TemporaryDirectory() as td:
+        plain = Path(td) / "router.pt"
+        torch.save({"config": cfg, "router_state_dict": sd, "topk_accuracy": 0.0, "top1_accuracy": 0.0}, plain)
+        calib = Path(td) / "router_cal.pt"
+        torch.save({"config": cfg, "router_state_dict": sd, "calibration_mode": "affine",
+                    "calibration_state": cal, "expert_perm": perm.tolist()}, calib)
+        for dt_name, dt in (("f32", torch.float32), ("bf16", torch.bfloat16)):
+            for n_cand in (16, 48):
+                for norm in (False, True):
+                    gate = torch.nn.Linear(H, 64, bias=False)
+                    with torch.no_grad():
+                        gate.weight.copy_(torch.from_numpy(wg))
+                    gate.top_k, gate.norm_topk_prob = 8, norm
+                    model = _GateHost(gate.to(dt))
+                    olmoe_e2e_eval.replace_gate_with_bvh(model, str(plain), layer_idx=0, hybrid=True,
+                                                         n_candidates=n_cand)
+                    with torch.no_grad():
+                        fp, ts, ti = model.model.layers[0].mlp.gate(x.to(dt).reshape(2, batch // 2, H))
+                    pre = f"hybrid/{n_cand}/{int(norm)}/{dt_name}/"
+                    out[pre + "router_probs"] = fp.float().numpy()
+                    out[pre + "topk_weights"] = ts.float().numpy()
+                    out[pre + "topk_ids"] = ti.numpy()
+            gate = torch.nn.Linear(H, 64, bias=False)
+            gate.top_k, gate.norm_topk_prob = 8, False
+            model = _GateHost(gate.to(dt))
+            olmoe_e2e_eval.replace_gate_with_bvh(model, str(calib), layer_idx=0, hybrid=False)
+            with torch.no_grad():
+                rp, tw, ti = model.model.layers[0].mlp.gate(x.to(dt))
+            out[f"pure_cal/{dt_name}/router_probs"] = rp.float().numpy()
+            out[f"pure_cal/{dt_name}/topk_weights"] = tw.float().numpy()
+            out[f"pure_cal/{dt_name}/topk_ids"] = ti.numpy()
+    np.savez_compressed(OUT / f"{name}.npz", **out)
+    print(f"wrote {name}.npz")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -251,6 +322,9 @@ def main():
     enhanced_case(ref_python, "enhanced_h256_t05", 256, seed=2, batch=96, x_seed=12, temperature=0.5)
     enhanced_case(ref_python, "enhanced_h256_sharp", 256, seed=3, batch=96, x_seed=13, head_gain=20.0)
     enhanced_case(ref_python, "enhanced_cfg0", 2048, seed=0, batch=256, x_seed=0)
+    # replace_gate_with_bvh: hybrid pre-filter and the checkpoint loader
+    gate_replacement_case(ref_python, "gate_replace_h256", 256, seed=4, gate_seed=1, batch=96, x_seed=14)
+    gate_replacement_case(ref_python, "gate_replace_h2048", 2048, seed=5, gate_seed=2, batch=128, x_seed=15)
 
 
 if __name__ == "__main__":

@@ -67,3 +67,18 @@ def ternary_errors(got, ref):
     rms = rn / np.sqrt(ref.shape[1])
     elem = np.abs(diff) / (np.abs(ref) + rms[:, None])
     return float(norm.max()), float(elem.max())
+
+
+def hybrid_ids_mismatch(bvh_probs: np.ndarray, full_probs: np.ndarray, n_cand: int, ref_ids: np.ndarray,
+                        got_ids: np.ndarray, tie_bvh: float, tie_full: float) -> int:
+    """Hybrid pre-filter ids: rows whose n-th and (n+1)-th BVH probabilities lie
+    within ``tie_bvh`` (relative) have an ambiguous candidate set and are
+    excused; elsewhere the top-k ids agree position by position up to ties of
+    the dense probabilities within ``tie_full``.  Returns unexcused mismatches."""
+    s = -np.sort(-np.asarray(bvh_probs, np.float64), axis=1)
+    if n_cand < s.shape[1]:
+        amb = (s[:, n_cand - 1] - s[:, n_cand]) <= tie_bvh * np.abs(s[:, n_cand - 1])
+    else:
+        amb = np.zeros(s.shape[0], bool)
+    keep = ~amb
+    return topk_ids_match(full_probs[keep], ref_ids[keep], got_ids[keep], tie_full)

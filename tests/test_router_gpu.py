@@ -96,10 +96,13 @@ def test_fast_engine_soft_mode(cuda_device, name):
     np.testing.assert_allclose(got["topk_weights"].cpu().numpy(), ref["topk_weights"], rtol=2e-2)
 
 
-def test_encoder_gemms_against_torch_fp32(cuda_device):
-    """The tcgen05 GEMM chain (bf16 in, fp32 accumulate) against a torch fp32 reference."""
+@pytest.mark.parametrize("B", [300, 8500])
+def test_encoder_gemms_against_torch_fp32(cuda_device, B):
+    """The tcgen05 GEMM chain (bf16 in, fp32 accumulate) against a torch fp32
+    reference: B=300 runs the single-CTA GEMM, B=8500 (34 row blocks of 256,
+    the last one ragged) the CTA-pair GEMM, both with the 3-D position tail."""
     from sb200 import synth
-    H, S, B = 2048, 256, 300
+    H, S = 2048, 256
     w = synth.router_weights(H, S, seed=11, perturb=True)
     r = make_router(w, H, S, (4, 4, 4), cuda_device)
     x = synth.hidden_states(B, H, seed=12, dtype=torch.bfloat16, device=cuda_device)
@@ -113,6 +116,13 @@ def test_encoder_gemms_against_torch_fp32(cuda_device):
     G_ref = torch.nn.functional.gelu(x.float() @ W1.T + b1)
     err = (G - G_ref).abs() / (G_ref.abs() + 1e-2)
     assert err.max().item() < 1e-2, err.max().item()
+    # the position tail: x @ W3^T + b3 from three bf16 pieces of W3 (fp32-accurate)
+    pos_off = base + (B * H * 2 + 1023) // 1024 * 1024 + (B * S * 2 + 1023) // 1024 * 1024
+    pos = ws[pos_off: pos_off + B * 16].view(torch.float32).view(B, 4)
+    W3 = torch.from_numpy(w["to_3d.weight"]).to(cuda_device).double()
+    b3 = torch.from_numpy(w["to_3d.bias"]).to(cuda_device).double()
+    pos_ref = x.double() @ W3.T + b3
+    torch.testing.assert_close(pos[:, :3].double(), pos_ref, rtol=1e-5, atol=1e-5)
 
 
 @pytest.mark.parametrize("B", [1, 3, 129, 256, 4096, 65536])
