@@ -322,6 +322,58 @@ def enhanced_workload(batch: int, device, hybrid: bool = False):
     return step, flop
 
 
+def pipeline_stage_rates(dev, pk, world, steps, warmup):
+    """The stage kernels of the MoE pipeline (cuda/async_pipeline.cu:79-230)
+    at OLMoE shape, each timed alone with inputs larger than L2:
+    calibrated softmax + top-8 and the scatter over 1,048,576 tokens x 64
+    experts, the weighted combine of 8 fp32 expert outputs of width 2048 for
+    16,384 tokens.  Algorithmic bytes: logits in + ids/weights out; ids in +
+    counts and lists out; outputs + weights in, combined rows out."""
+    import torch
+    from sb200 import pipeline as pp
+    from sb200 import synth
+    Bt, E, k = 1 << 20, 64, TOPK
+    g = torch.Generator(device=dev).manual_seed(9)
+    logits = torch.randn(Bt, E, generator=g, device=dev) * 2.0
+    c = synth.calibration_linear(E, seed=9)
+    cw, cb = torch.from_numpy(c["weight"]).to(dev), torch.from_numpy(c["bias"]).to(dev)
+    ids = torch.empty(Bt, k, dtype=torch.int32, device=dev)
+    wts = torch.empty(Bt, k, dtype=torch.float32, device=dev)
+    lib = pp._lib.load()
+
+    def topk_step():
+        pp._lib.check(lib.sb_softmax_topk(pp._ptr(logits), Bt, E, k, pp._ptr(cw), pp._ptr(cb), 1, None,
+                                          pp._ptr(ids), pp._ptr(wts), pp._stream(dev)), "sb_softmax_topk")
+
+    disp = torch.empty(E, Bt, dtype=torch.int32, device=dev)
+    counts = torch.empty(E, dtype=torch.int32, device=dev)
+
+    def scatter_step():
+        pp._lib.check(lib.sb_scatter_by_expert(pp._ptr(ids), Bt, k, E, Bt, 0, pp._ptr(disp), pp._ptr(counts),
+                                               pp._stream(dev)), "sb_scatter_by_expert")
+
+    Bc, Hc = 16384, H
+    eo = torch.randn(Bc, k, Hc, generator=g, device=dev)
+    cwt = torch.rand(Bc, k, generator=g, device=dev)
+    cout = torch.empty(Bc, Hc, device=dev)
+
+    def combine_step():
+        pp._lib.check(lib.sb_weighted_combine(pp._ptr(eo), pp._ptr(cwt), Bc, Hc, k, pp._ptr(cout),
+                                              pp._stream(dev)), "sb_weighted_combine")
+
+    res = {}
+    for name, step, nbytes in (("cal_softmax_topk", topk_step, Bt * (E * 4 + k * 8)),
+                               ("scatter_by_expert", scatter_step, Bt * k * 4 * 2 + E * 4),
+                               ("weighted_combine", combine_step, Bc * (k * Hc * 4 + k * 4 + Hc * 4))):
+        ms, _ = time_steps(step, steps, warmup, world)
+        gbs = nbytes / (ms / steps / 1e3) / 1e9
+        res[name] = {"avg_ms": round(ms / steps, 4), "algorithmic_bytes": nbytes, "gbs": round(gbs, 1),
+                     "hbm_frac": round(gbs / pk["hbm_gbs"], 4)}
+    res["shapes"] = (f"softmax/scatter: {Bt} tokens x {E} experts, top-{k}, calibration 64x64; "
+                     f"combine: {Bc} tokens x {k} x {Hc} fp32")
+    return res
+
+
 def cpu_enhanced_rate(sample_tokens: int, budget_s: float = 8.0):
     """Oracle port of the enhanced router + gate on the host cores (tokens/s)."""
     from oracle import enhanced as oe
@@ -608,6 +660,9 @@ def run_ours(a):
                 "value": round(rate / 1e6, 6), "unit": "Mq/s", "cores": blas_threads(), "kind": "port",
                 "sample": f"{done} tokens through the numpy port of EnhancedBVHRouter + the gate (fp32) "
                           f"in {el:.1f} s"}
+    # ---- the pipeline's stage kernels around the expert GEMMs (HBM-bound)
+    if not a.skip_enhanced:
+        out["pipeline_stages"] = pipeline_stage_rates(dev, pk, world, min(a.steps, 50), a.warmup)
     # ---- router alone (config 1), same process
     if not a.skip_router:
         rstep, _, rmeta = router_workload(a.router_batch, dev)

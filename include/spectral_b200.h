@@ -317,6 +317,39 @@ int sb_enh_forward_hybrid(sb_enh* h, const void* x, int x_dtype, int64_t batch, 
                           void* stream);
 int sb_enh_destroy(sb_enh* h);
 
+/* ------------------------------------------------------------------------ */
+/* MoE pipeline stage kernels (cuda/async_pipeline.cu:79-230,                */
+/* python/async_pipeline_bridge.py:89-150).  Device pointers, async on       */
+/* `stream`, no handle.                                                       */
+/* ------------------------------------------------------------------------ */
+
+/* Per token: optional calibration c = W raw + b (apply_calibration_kernel,
+ * async_pipeline.cu:150-170; W [E,E] nn.Linear layout, E <= 128), softmax over
+ * the E values when apply_softmax (softmax_topk_kernel, :177-230), then the
+ * top_k values in descending order, the lower expert index first among equal
+ * values.  probs [B,E] (may be NULL) receives the values ranked (calibrated /
+ * softmaxed); topk_weights [B,k] (may be NULL) the chosen values, not
+ * renormalised.  E <= 1024, top_k <= 32. */
+int sb_softmax_topk(const float* logits, int64_t batch, int n_experts, int top_k, const float* cal_w,
+                    const float* cal_b, int apply_softmax, float* probs, uint32_t* topk_ids,
+                    float* topk_weights, void* stream);
+/* out [B,E] = raw [B,E] W^T + b, the calibration step alone. */
+int sb_apply_calibration(const float* raw, int64_t batch, int n_experts, const float* cal_w,
+                         const float* cal_b, float* out, void* stream);
+/* Groups the B*k routing entries by expert (scatter_by_expert_kernel,
+ * async_pipeline.cu:79-101): expert_counts[e] = number of entries with id e
+ * (ids >= n_experts are skipped, as the reference's sentinel); entry slots in
+ * ascending entry order r = t*k + j (deterministic: the reference assigns
+ * slots by atomicAdd); dispatch_indices[e * max + slot] = t (or r when
+ * store_entry) for slot < max_tokens_per_expert, as the reference's limit. */
+int sb_scatter_by_expert(const uint32_t* expert_ids, int64_t batch, int top_k, int n_experts,
+                         int max_tokens_per_expert, int store_entry, int32_t* dispatch_indices,
+                         int32_t* expert_counts, void* stream);
+/* output [B,H] = sum_j weights[t,j] * expert_outputs[t,j,:] in slot order with
+ * one fused multiply-add per term (weighted_combine_kernel, async_pipeline.cu:112-132). */
+int sb_weighted_combine(const float* expert_outputs, const float* weights, int64_t batch, int hidden,
+                        int top_k, float* output, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -5,3 +5,4 @@
 #include "router.cu"
 #include "ternary.cu"
 #include "enhanced.cu"
+#include "pipeline.cu"

@@ -122,6 +122,15 @@ SIGNATURES = [
      [C.c_void_p, C.c_void_p, C.c_int, C.c_int64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
       C.POINTER(EnhOutputs), C.c_void_p, C.c_size_t, C.c_void_p]),
     ("sb_enh_destroy", C.c_int, [C.c_void_p]),
+    ("sb_softmax_topk", C.c_int,
+     [C.c_void_p, C.c_int64, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p,
+      C.c_void_p, C.c_void_p]),
+    ("sb_apply_calibration", C.c_int,
+     [C.c_void_p, C.c_int64, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("sb_scatter_by_expert", C.c_int,
+     [C.c_void_p, C.c_int64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("sb_weighted_combine", C.c_int,
+     [C.c_void_p, C.c_void_p, C.c_int64, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
 ]
 
 _lib = None

@@ -149,6 +149,27 @@ def dense_gate_weight(n_experts: int, hidden: int, seed: int = 0, gain: float = 
     return (torch.randn(n_experts, hidden, generator=g) * (gain / math.sqrt(hidden))).numpy().astype(np.float32)
 
 
+def mlp_experts(n_experts: int, hidden: int, inner: int, seed: int = 0) -> List[Dict[str, np.ndarray]]:
+    """State dicts of small dense experts ``Sequential(Linear(hidden, inner),
+    GELU(), Linear(inner, hidden))`` (keys 0.weight, 0.bias, 2.weight,
+    2.bias; N(0, 1/in) weights, N(0, 0.1^2) biases) for pipeline tests."""
+    g = torch.Generator().manual_seed(WEIGHT_STREAM + 0x3000 + seed)
+    out = []
+    for _ in range(n_experts):
+        out.append({"0.weight": (torch.randn(inner, hidden, generator=g) / math.sqrt(hidden)).numpy(),
+                    "0.bias": (torch.randn(inner, generator=g) * 0.1).numpy(),
+                    "2.weight": (torch.randn(hidden, inner, generator=g) / math.sqrt(inner)).numpy(),
+                    "2.bias": (torch.randn(hidden, generator=g) * 0.1).numpy()})
+    return out
+
+
+def calibration_linear(n_experts: int, seed: int = 0) -> Dict[str, np.ndarray]:
+    """A Linear(E, E) calibration state (weight = I + N(0, 0.05^2), bias N(0, 0.1^2))."""
+    g = torch.Generator().manual_seed(WEIGHT_STREAM + 0x4000 + seed)
+    w = torch.eye(n_experts) + torch.randn(n_experts, n_experts, generator=g) * 0.05
+    return {"weight": w.numpy().astype(np.float32), "bias": (torch.randn(n_experts, generator=g) * 0.1).numpy()}
+
+
 def unit_rms_rows(x: torch.Tensor) -> torch.Tensor:
     """Divide each row by its root-mean-square (fp32)."""
     rms = x.float().pow(2).mean(dim=-1, keepdim=True).sqrt()

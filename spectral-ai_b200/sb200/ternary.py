@@ -150,6 +150,31 @@ class TernaryExperts:
         self._ws = None
 
     @classmethod
+    def from_packed_modules(cls, modules: Sequence, device) -> "TernaryExperts":
+        """Group expert modules that hold the reference packed layout
+        (``CUDATernaryExpertModule``: gate_packed / up_packed / down_packed from
+        ``pack_ternary`` and per-channel gate_s / up_s / down_s,
+        python/ternary_expert_ext_bridge.py:93-129) into one device block,
+        repacked on the device."""
+        self = cls.__new__(cls)
+        self.device = torch.device(device)
+        self.E = len(modules)
+        m0 = modules[0]
+        self.H, self.I = int(m0._in_dim), int(m0._inter_dim)
+        for m in modules:
+            if (int(m._in_dim), int(m._inter_dim), int(m._out_dim)) != (self.H, self.I, self.H):
+                raise RuntimeError("grouped experts need equal shapes with out_dim == in_dim")
+        dev = self.device
+        self.gate = torch.cat([repack_reference(m.gate_packed.to(dev), self.H) for m in modules])
+        self.up = torch.cat([repack_reference(m.up_packed.to(dev), self.H) for m in modules])
+        self.down = torch.cat([repack_reference(m.down_packed.to(dev), self.I) for m in modules])
+        self.gate_scale = torch.stack([m.gate_s.to(dev, torch.float32) for m in modules]).contiguous()
+        self.up_scale = torch.stack([m.up_s.to(dev, torch.float32) for m in modules]).contiguous()
+        self.down_scale = torch.stack([m.down_s.to(dev, torch.float32) for m in modules]).contiguous()
+        self._ws = None
+        return self
+
+    @classmethod
     def random(cls, n_experts: int, hidden: int, inter: int, seed: int, device) -> "TernaryExperts":
         """Random experts built on the device: T uniform over {-1,0,+1}, one
         scale c/sqrt(fan_in) per matrix with c ~ U[0.5, 1.5) (the recipe of

@@ -299,6 +299,54 @@ def gate_replacement_case(ref_python: Path, name, H, seed, gate_seed, batch, x_s
     print(f"wrote {name}.npz")
 
 
+def pipeline_case(ref_python: Path, name, H, seed, batch, x_seed, head_gain=20.0, inner=32):
+    """The reference's AsyncPipelineSimulator (python/async_pipeline_bridge.py:49-255)
+    on the CPU: an EnhancedBVHRouter, 64 small dense experts and, in the
+    calibrated variant, a Linear(64,64) calibration; the route stage's top-k,
+    the scatter stage's per-expert token lists and the expert stage's output
+    of forward_sequential."""
+    sys.path.insert(0, str(ref_python))
+    import async_pipeline_bridge as apb
+    import olmoe_bvh_distill
+    w = synth.enhanced_router_weights(H, seed=seed)
+    w["expert_head.2.weight"] = (w["expert_head.2.weight"] * head_gain).astype(np.float32)
+    r = olmoe_bvh_distill.EnhancedBVHRouter(input_dim=H, feature_dim=128)
+    r.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in w.items()}, strict=True)
+    r.eval()
+    experts = torch.nn.ModuleList()
+    for sd in synth.mlp_experts(64, H, inner, seed=seed):
+        m = torch.nn.Sequential(torch.nn.Linear(H, inner), torch.nn.GELU(), torch.nn.Linear(inner, H))
+        m.load_state_dict({k: torch.from_numpy(v) for k, v in sd.items()})
+        experts.append(m.eval())
+    cal = {k: torch.from_numpy(v) for k, v in synth.calibration_linear(64, seed=seed).items()}
+    x = synth.hidden_states(batch, H, seed=x_seed)
+    out = {"H": H, "seed": seed, "batch": batch, "x_seed": x_seed, "head_gain": head_gain, "inner": inner,
+           "x_checksum": checksum(x.numpy())}
+    for variant, cs in (("plain", None), ("cal", cal)):
+        cfg = apb.PipelineConfig(num_experts=64, top_k=8, hidden_dim=H, use_cuda_streams=False)
+        sim = apb.AsyncPipelineSimulator(cfg, r, experts, calibration_state=cs, device="cpu")
+        slot = apb.PipelineSlot()
+        with torch.no_grad():
+            sim._stage_route(slot, x)
+            sim._stage_scatter(slot)
+            sim._stage_expert(slot)
+            seq = sim.forward_sequential(x)
+        assert torch.equal(seq, slot.output)
+        out[f"{variant}/expert_ids"] = slot.expert_ids.numpy()
+        out[f"{variant}/expert_weights"] = slot.expert_weights.numpy()
+        counts = np.zeros(64, np.int32)
+        lists = []
+        for e in range(64):
+            toks = slot.dispatch_indices.get(e, [])
+            counts[e] = len(toks)
+            lists.extend(toks)
+        out[f"{variant}/counts"] = counts
+        out[f"{variant}/lists"] = np.asarray(lists, np.int32)
+        out[f"{variant}/output"] = slot.output.numpy()
+    np.savez_compressed(OUT / f"{name}.npz", **out)
+    print(f"wrote {name}.npz")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default="/root/reference")
@@ -325,6 +373,8 @@ def main():
     # replace_gate_with_bvh: hybrid pre-filter and the checkpoint loader
     gate_replacement_case(ref_python, "gate_replace_h256", 256, seed=4, gate_seed=1, batch=96, x_seed=14)
     gate_replacement_case(ref_python, "gate_replace_h2048", 2048, seed=5, gate_seed=2, batch=128, x_seed=15)
+    # the tri-core pipeline simulator's stages
+    pipeline_case(ref_python, "pipeline_h256", 256, seed=6, batch=96, x_seed=16)
 
 
 if __name__ == "__main__":
