@@ -374,6 +374,66 @@ def pipeline_stage_rates(dev, pk, world, steps, warmup):
     return res
 
 
+def legacy_tree_rates(dev, pk, world, steps, warmup):
+    """The legacy ray-sphere tree router (cuda/v5/bvh_router_kernel.cu): the
+    device kernel over 1,048,576 rays (outputs: expert, 64 scores, path,
+    confidence; 300 algorithmic bytes per ray), and the reference's ctypes
+    entry point bvh_route_batch at 1024 rays with CUDA-graph replay, host
+    buffers in and out (the call the reference times at ~3 us + copies)."""
+    import ctypes as C
+    import time as _t
+    import numpy as np
+    import torch
+    from sb200 import _lib, synth
+    import bvh_router_ext as ext
+    tree = synth.legacy_tree(0)
+    ext.upload_tree(*[torch.from_numpy(np.ascontiguousarray(tree[k], np.float32))
+                      for k in ("centers", "radii", "portals", "snell_w", "snell_b")])
+    B = 1 << 20
+    o, d = synth.rays(B, 1)
+    to, td = torch.from_numpy(o).to(dev), torch.from_numpy(d).to(dev)
+    spec = torch.empty(B, 64, device=dev)
+    lib = _lib.load()
+    h = ext._tree(dev.index if dev.index is not None else 0)
+    ex = torch.empty(B, dtype=torch.int32, device=dev)
+    sc = torch.empty(B, 64, device=dev)
+    pa = torch.empty(B, 3, dtype=torch.int32, device=dev)
+    cf = torch.empty(B, device=dev)
+    P = lambda t: C.c_void_p(t.data_ptr())
+
+    def step():
+        _lib.check(lib.sb_tree_route(h, P(to), P(td), B, P(ex), P(sc), P(pa), P(cf),
+                                     C.c_void_p(torch.cuda.current_stream(dev).cuda_stream)), "sb_tree_route")
+
+    ms, _ = time_steps(step, steps, warmup, world)
+    per = ms / steps
+    nbytes = B * 300
+    res = {"rays": B, "kernel_ms": round(per, 4), "rays_per_s": round(B / (per / 1e3), 1),
+           "gbs": round(nbytes / (per / 1e3) / 1e9, 1), "hbm_frac": round(nbytes / (per / 1e3) / 1e9 / pk["hbm_gbs"], 4)}
+    # the ctypes API, host buffers, graph replay
+    arrs = [np.ascontiguousarray(tree[k], np.float32) for k in ("centers", "radii", "portals", "snell_w", "snell_b")]
+    Pn = lambda a: a.ctypes.data_as(C.c_void_p)
+    assert lib.bvh_upload_tree(*[Pn(a) for a in arrs]) == 0 and lib.bvh_alloc_buffers(1024) == 0
+    ho, hd = np.ascontiguousarray(o[:1024]), np.ascontiguousarray(d[:1024])
+    hs = np.zeros((1024, 64), np.float32)
+    he, hsc = np.zeros(1024, np.int32), np.zeros((1024, 64), np.float32)
+    hp, hc = np.zeros((1024, 3), np.int32), np.zeros(1024, np.float32)
+    args = [Pn(ho), Pn(hd), Pn(hs), Pn(he), Pn(hsc), Pn(hp), Pn(hc), 1024]
+    for g in (1, 0):
+        for _ in range(20):
+            assert lib.bvh_route_batch(*args, g) == 0
+        n = 500
+        t0 = _t.perf_counter()
+        for _ in range(n):
+            lib.bvh_route_batch(*args, g)
+        res["ctypes_us_per_call_graph" if g else "ctypes_us_per_call_nograph"] = round(
+            (_t.perf_counter() - t0) / n * 1e6, 2)
+    lib.bvh_free_buffers()
+    res["ctypes_what"] = ("bvh_route_batch, 1024 rays, host buffers in/out (12 KB in, 300 KB out), "
+                          "host clock per synchronous call, 500 calls")
+    return res
+
+
 def cpu_enhanced_rate(sample_tokens: int, budget_s: float = 8.0):
     """Oracle port of the enhanced router + gate on the host cores (tokens/s)."""
     from oracle import enhanced as oe
@@ -663,6 +723,7 @@ def run_ours(a):
     # ---- the pipeline's stage kernels around the expert GEMMs (HBM-bound)
     if not a.skip_enhanced:
         out["pipeline_stages"] = pipeline_stage_rates(dev, pk, world, min(a.steps, 50), a.warmup)
+        out["legacy_tree"] = legacy_tree_rates(dev, pk, world, min(a.steps, 50), a.warmup)
     # ---- router alone (config 1), same process
     if not a.skip_router:
         rstep, _, rmeta = router_workload(a.router_batch, dev)

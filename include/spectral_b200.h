@@ -345,6 +345,41 @@ int sb_apply_calibration(const float* raw, int64_t batch, int n_experts, const f
 int sb_scatter_by_expert(const uint32_t* expert_ids, int64_t batch, int top_k, int n_experts,
                          int max_tokens_per_expert, int store_entry, int32_t* dispatch_indices,
                          int32_t* expert_counts, void* stream);
+/* ------------------------------------------------------------------------ */
+/* Legacy ray-sphere tree router (cuda/v5/bvh_router_kernel.cu:244-371, the   */
+/* kernel behind the reference's ctypes library and its bvh_router_ext torch  */
+/* extension, cuda/v5/bvh_torch_ext.cu:270-371).  Fixed tree: 85 nodes (root, */
+/* 4, 16, 64 leaves); per level the child of least |ray - center|^2 - r^2,    */
+/* the child's 3x4 portal applied to the ray; scores exp(-|ray - leaf|^2).    */
+/* ------------------------------------------------------------------------ */
+typedef struct sb_tree sb_tree;
+int sb_tree_create(int device, sb_tree** out);
+/* Host fp32: centers [85,3], radii [85], portals [85,12] (row-major 3x4);
+ * snell_w [85,64] and snell_b [85] are accepted for the reference signature
+ * (the dispersion they drive changes no output) and may be NULL. */
+int sb_tree_upload(sb_tree* h, const float* centers, const float* radii, const float* portals,
+                   const float* snell_w, const float* snell_b);
+/* Device pointers: origins/directions [B,3]; outputs (any may be NULL): expert
+ * [B] (leaf 0..63), scores [B,64], path [B,3] (node ids 1..84), confidence [B]. */
+int sb_tree_route(sb_tree* h, const float* origins, const float* directions, int64_t batch,
+                  int32_t* expert, float* scores, int32_t* path, float* confidence, void* stream);
+int sb_tree_destroy(sb_tree* h);
+
+/* The reference's ctypes ABI (cuda/v5/bvh_router_kernel.cu:378-717), same names
+ * and signatures, process-global: 0 ok, -1 failure.  bvh_route_batch is
+ * synchronous on host buffers; use_graph=1 replays one CUDA graph per batch
+ * size (copies through pinned staging, so any caller buffers are valid). */
+int bvh_upload_tree(const float* centers, const float* radii, const float* portals, const float* snell_w,
+                    const float* snell_b);
+int bvh_alloc_buffers(int batch_size);
+void bvh_free_buffers(void);
+int bvh_route_batch(const float* h_origins, const float* h_directions, const float* h_spectral, int* h_expert,
+                    float* h_scores, int* h_path, float* h_confidence, int batch_size, int use_graph);
+int bvh_get_batch_capacity(void);
+int bvh_get_num_nodes(void);
+int bvh_get_num_experts(void);
+int bvh_get_spec_dim(void);
+
 /* output [B,H] = sum_j weights[t,j] * expert_outputs[t,j,:] in slot order with
  * one fused multiply-add per term (weighted_combine_kernel, async_pipeline.cu:112-132). */
 int sb_weighted_combine(const float* expert_outputs, const float* weights, int64_t batch, int hidden,

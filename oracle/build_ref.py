@@ -1,4 +1,5 @@
-"""Build the reference's own ternary torch extension into oracle/_ref/ (checker only).
+"""Build the reference's own kernels into oracle/_ref/ (checker only): the
+ternary torch extension and the legacy ray-sphere tree router library.
 
 Compiles cuda/v5/ternary_torch_ext.cu from the reference tree, where it lies,
 with torch.utils.cpp_extension for sm_100a.  The resulting module
@@ -39,12 +40,35 @@ def build(reference: Path, verbose: bool = False) -> bool:
     return True
 
 
+def build_tree_kernel(reference: Path, verbose: bool = False) -> bool:
+    """cuda/v5/bvh_router_kernel.cu -> oracle/_ref/libbvh_router_ref.so with the
+    reference's own compile line (its file header), for sm_100a."""
+    import shutil
+    import subprocess
+    src = reference / "cuda" / "v5" / "bvh_router_kernel.cu"
+    if not src.is_file():
+        print(f"[oracle/_ref] reference source not found: {src}")
+        return False
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    OUT.mkdir(exist_ok=True)
+    out = OUT / "libbvh_router_ref.so"
+    cmd = [nvcc, "-O3", "--use_fast_math", "-shared", "-Xcompiler", "-fPIC", "--expt-relaxed-constexpr",
+           "--maxrregcount=64", "-gencode", "arch=compute_100a,code=sm_100a", "-o", str(out), str(src)]
+    r = subprocess.run(cmd, capture_output=not verbose, text=True)
+    if r.returncode != 0:
+        print(f"[oracle/_ref] nvcc failed:\n{r.stderr if not verbose else ''}")
+        return False
+    return True
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("SB_REFERENCE_ROOT", "/root/reference"))
     ap.add_argument("-v", action="store_true")
     a = ap.parse_args()
-    return 0 if build(Path(a.reference), a.v) else 1
+    ok = build(Path(a.reference), a.v)
+    ok = build_tree_kernel(Path(a.reference), a.v) and ok
+    return 0 if ok else 1
 
 
 if __name__ == "__main__":

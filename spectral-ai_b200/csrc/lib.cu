@@ -6,3 +6,4 @@
 #include "ternary.cu"
 #include "enhanced.cu"
 #include "pipeline.cu"
+#include "tree.cu"

@@ -260,6 +260,208 @@ __global__ void __launch_bounds__(PIPE_THREADS) pipe_combine_kernel(const float*
   }
 }
 
+// ---------------------------------------------------------------------------
+// Thread-per-token form for E <= 64 (the reference's shape): a CTA stages 128
+// tokens' rows through shared memory (coalesced), each thread keeps its row in
+// registers, the calibration reads W as shared-memory broadcasts, and the
+// softmax sums in ascending expert order like the reference kernel.
+// ---------------------------------------------------------------------------
+constexpr int PIPE_TOK = 128;
+
+template <int EP>
+__global__ void __launch_bounds__(PIPE_TOK) pipe_topk_thread_kernel(
+    const float* __restrict__ logits, int64_t B, int E, int k, const float* __restrict__ cal_w,
+    const float* __restrict__ cal_b, int apply_softmax, int only_calibrate, float* __restrict__ probs,
+    uint32_t* __restrict__ ids, float* __restrict__ wts) {
+  extern __shared__ __align__(16) float pipe_dsm[];
+  float* wt_s = pipe_dsm;             // [EP][EP] W transposed: wt_s[j*EP + e] = W[e][j]
+  float* b_s = wt_s + EP * EP;        // [EP]
+  float* tile = b_s + EP;             // [PIPE_TOK][EP + 1] token rows, padded against bank conflicts
+  const int tid = threadIdx.x;
+  if (cal_w) {
+    for (int i = tid; i < EP * EP; i += PIPE_TOK) {
+      const int e = i / EP, j = i % EP;
+      wt_s[j * EP + e] = (e < E && j < E) ? __ldg(cal_w + e * E + j) : 0.f;
+    }
+    for (int e = tid; e < EP; e += PIPE_TOK) b_s[e] = (e < E && cal_b) ? __ldg(cal_b + e) : 0.f;
+  }
+  for (int64_t t0 = (int64_t)blockIdx.x * PIPE_TOK; t0 < B; t0 += (int64_t)gridDim.x * PIPE_TOK) {
+    const int ntok = (int)((B - t0) < PIPE_TOK ? (B - t0) : PIPE_TOK);
+    __syncthreads();
+    if (E == EP) {
+      for (int i = tid; i < ntok * EP; i += PIPE_TOK) tile[(i / EP) * (EP + 1) + i % EP] = __ldg(logits + t0 * E + i);
+    } else {
+      for (int i = tid; i < ntok * E; i += PIPE_TOK) tile[(i / E) * (EP + 1) + i % E] = __ldg(logits + t0 * E + i);
+    }
+    __syncthreads();
+    const float* myrow = tile + tid * (EP + 1);
+    float v[EP];
+    if (cal_w) {
+      // c[e] = b[e] + sum_j W[e][j] raw[j], j ascending: raw[j] from this
+      // thread's row, W's row j as float4 broadcasts; the loop stays rolled
+      // (a fully unrolled E x E body overflows the instruction cache)
+#pragma unroll
+      for (int e = 0; e < EP; ++e) v[e] = b_s[e];
+#pragma unroll 2
+      for (int j = 0; j < E; ++j) {
+        const float rj = tid < ntok ? myrow[j] : 0.f;
+        const float4* wr = reinterpret_cast<const float4*>(wt_s + j * EP);
+#pragma unroll
+        for (int q = 0; q < EP / 4; ++q) {
+          const float4 w4 = wr[q];
+          v[4 * q + 0] = fmaf(w4.x, rj, v[4 * q + 0]);
+          v[4 * q + 1] = fmaf(w4.y, rj, v[4 * q + 1]);
+          v[4 * q + 2] = fmaf(w4.z, rj, v[4 * q + 2]);
+          v[4 * q + 3] = fmaf(w4.w, rj, v[4 * q + 3]);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < EP; ++e) v[e] = (e < E && tid < ntok) ? myrow[e] : 0.f;
+    }
+    if (!only_calibrate && apply_softmax) {
+      float m = -INFINITY;
+#pragma unroll
+      for (int e = 0; e < EP; ++e)
+        if (e < E) m = fmaxf(m, v[e]);
+      float s = 0.f;
+#pragma unroll
+      for (int e = 0; e < EP; ++e)
+        if (e < E) {
+          v[e] = expf(v[e] - m);
+          s += v[e];
+        }
+#pragma unroll
+      for (int e = 0; e < EP; ++e) v[e] = v[e] / s;
+    }
+    if (probs) {  // through the tile for coalesced stores
+      __syncthreads();
+#pragma unroll
+      for (int e = 0; e < EP; ++e)
+        if (e < E) tile[tid * (EP + 1) + e] = v[e];
+      __syncthreads();
+      for (int i = tid; i < ntok * E; i += PIPE_TOK) probs[t0 * E + i] = tile[(i / E) * (EP + 1) + i % E];
+    }
+    if (only_calibrate || tid >= ntok) continue;
+    const int64_t t = t0 + tid;
+    unsigned long long taken = 0ull;
+    for (int r = 0; r < k; ++r) {
+      float bv = -INFINITY;
+      int bi = -1;
+#pragma unroll
+      for (int e = 0; e < EP; ++e)
+        if (e < E && !((taken >> e) & 1ull) && (bi < 0 || v[e] > bv)) {
+          bv = v[e];
+          bi = e;
+        }
+      taken |= 1ull << bi;
+      ids[t * k + r] = (uint32_t)bi;
+      if (wts) wts[t * k + r] = bv;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Scatter for E <= 512 over all SMs, three passes:
+//   hist:    CTA b counts the entries of its chunk per expert
+//   offsets: per expert, exclusive sum over the CTAs (and the totals)
+//   place:   CTA b walks its chunk in 1024-entry tiles; an entry's slot is its
+//            CTA offset + the tile's earlier entries of its expert (per-warp
+//            counts with a prefix over warps) + its rank among equal ids in
+//            its warp (__match_any_sync), so slots follow ascending entry order.
+// ---------------------------------------------------------------------------
+constexpr int SC_TILE = 1024;
+constexpr int SC_MAX_E = 512;
+
+__global__ void __launch_bounds__(SC_TILE) pipe_scatter_hist_kernel(const uint32_t* __restrict__ ids, int64_t R,
+                                                                    int64_t chunk, int E, int32_t* __restrict__ hist) {
+  extern __shared__ int h_s[];
+  for (int e = threadIdx.x; e < E; e += SC_TILE) h_s[e] = 0;
+  __syncthreads();
+  const int64_t r0 = (int64_t)blockIdx.x * chunk, r1 = r0 + chunk < R ? r0 + chunk : R;
+  const int lane = threadIdx.x & 31;
+  for (int64_t rb = r0; rb < r1; rb += SC_TILE) {  // warp-uniform trip count
+    const int64_t r = rb + threadIdx.x;
+    const uint32_t id = r < r1 ? __ldg(ids + r) : 0xffffffffu;
+    const bool valid = id < (uint32_t)E;
+    // one shared-memory atomic per distinct id in the warp
+    const unsigned same = __match_any_sync(0xffffffffu, valid ? id : 0xffffffffu);
+    if (valid && (same & ((1u << lane) - 1u)) == 0) atomicAdd(&h_s[id], __popc(same));
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E; e += SC_TILE) hist[(int64_t)blockIdx.x * E + e] = h_s[e];
+}
+
+// One CTA per expert, one thread per histogram row (nb <= SC_TILE): block-wide
+// exclusive scan of the expert's column.
+__global__ void __launch_bounds__(SC_TILE) pipe_scatter_offsets_kernel(int32_t* __restrict__ hist, int nb, int E,
+                                                                       int32_t* __restrict__ counts) {
+  __shared__ int wsum[SC_TILE / 32];
+  const int e = blockIdx.x, b = threadIdx.x, warp = b >> 5, lane = b & 31;
+  const int c = b < nb ? hist[(int64_t)b * E + e] : 0;
+  int incl = c;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) wsum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int v = wsum[lane];
+    int wi = v;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += y;
+    }
+    wsum[lane] = wi - v;
+    if (lane == 31) counts[e] = wi;
+  }
+  __syncthreads();
+  if (b < nb) hist[(int64_t)b * E + e] = wsum[warp] + incl - c;
+}
+
+__global__ void __launch_bounds__(SC_TILE) pipe_scatter_place_kernel(const uint32_t* __restrict__ ids, int64_t R,
+                                                                     int64_t chunk, int k, int E, int max_per,
+                                                                     int store_entry, const int32_t* __restrict__ offs,
+                                                                     int32_t* __restrict__ disp) {
+  extern __shared__ int sm[];
+  int* base = sm;            // [E]
+  int* wc = sm + E;          // [32][E] per-warp counts -> exclusive prefix over warps
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int e = threadIdx.x; e < E; e += SC_TILE) base[e] = offs[(int64_t)blockIdx.x * E + e];
+  const int64_t r0 = (int64_t)blockIdx.x * chunk, r1 = r0 + chunk < R ? r0 + chunk : R;
+  for (int64_t t0 = r0; t0 < r1; t0 += SC_TILE) {
+    for (int i = threadIdx.x; i < 32 * E; i += SC_TILE) wc[i] = 0;
+    __syncthreads();
+    const int64_t r = t0 + threadIdx.x;
+    const uint32_t id = r < r1 ? __ldg(ids + r) : 0xffffffffu;
+    const bool valid = id < (uint32_t)E;
+    const unsigned same = __match_any_sync(0xffffffffu, valid ? id : 0xffffffffu);
+    const int rank = __popc(same & ((1u << lane) - 1u));
+    if (valid && rank == 0) wc[warp * E + id] = __popc(same);
+    __syncthreads();
+    int tot = 0;
+    for (int e = threadIdx.x; e < E; e += SC_TILE) {  // E <= SC_TILE: one expert per thread
+      int run = 0;
+      for (int w = 0; w < 32; ++w) {
+        const int c = wc[w * E + e];
+        wc[w * E + e] = run;
+        run += c;
+      }
+      tot = run;
+    }
+    __syncthreads();
+    if (valid) {
+      const int slot = base[id] + wc[warp * E + id] + rank;
+      if (slot < max_per) disp[(int64_t)id * max_per + slot] = store_entry ? (int32_t)r : (int32_t)(r / k);
+    }
+    __syncthreads();
+    if (threadIdx.x < E) base[threadIdx.x] += tot;
+  }
+}
+
 namespace {
 
 int pipe_launch_softmax_topk(const float* logits, int64_t B, int E, int k, const float* cal_w, const float* cal_b,
@@ -269,6 +471,33 @@ int pipe_launch_softmax_topk(const float* logits, int64_t B, int E, int k, const
   int64_t blocks = (B + PIPE_THREADS / 32 - 1) / (PIPE_THREADS / 32);
   const int64_t cap = (int64_t)num_sms() * (cal_w ? 4 : 16);  // calibration: amortise the matrix load
   if (blocks > cap) blocks = cap;
+  if (E <= 64 && k <= E) {  // thread per token
+    int64_t tb = (B + PIPE_TOK - 1) / PIPE_TOK;
+    const int64_t tcap = (int64_t)num_sms() * 8;
+    if (tb > tcap) tb = tcap;
+    ProfScope prof(name, stream);
+    if (E <= 32) {
+      const size_t sm = (size_t)(32 * 32 + 32 + PIPE_TOK * 33) * sizeof(float);
+      pipe_topk_thread_kernel<32><<<(unsigned)tb, PIPE_TOK, sm, stream>>>(logits, B, E, k, cal_w, cal_b,
+                                                                          apply_softmax, only_calibrate, probs, ids,
+                                                                          wts);
+    } else {
+      const size_t sm = (size_t)(64 * 64 + 64 + PIPE_TOK * 65) * sizeof(float);
+      static bool attr_done[64] = {};
+      int dev = 0;
+      SB_CUDA_TRY(cudaGetDevice(&dev));
+      if (dev < 64 && !attr_done[dev]) {
+        SB_CUDA_TRY(cudaFuncSetAttribute(pipe_topk_thread_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sm));
+        attr_done[dev] = true;
+      }
+      pipe_topk_thread_kernel<64><<<(unsigned)tb, PIPE_TOK, sm, stream>>>(logits, B, E, k, cal_w, cal_b,
+                                                                          apply_softmax, only_calibrate, probs, ids,
+                                                                          wts);
+    }
+    SB_CUDA_TRY(cudaGetLastError());
+    return SB_OK;
+  }
   ProfScope prof(name, stream);
 #define SB_PIPE_LAUNCH(P)                                                                                     \
   do {                                                                                                        \
@@ -337,11 +566,38 @@ extern "C" int sb_scatter_by_expert(const uint32_t* expert_ids, int64_t batch, i
     return SB_OK;
   }
   SB_REQUIRE(expert_ids != nullptr, "expert_ids is null");
+  const int64_t R = batch * top_k;
+  if (n_experts <= SC_MAX_E && R > SC_TILE) {
+    // all SMs: per-CTA histograms in a workspace the library keeps per device
+    int64_t nb = (R + 8 * SC_TILE - 1) / (8 * SC_TILE);
+    const int64_t cap = (int64_t)num_sms() * 4 < SC_TILE ? (int64_t)num_sms() * 4 : SC_TILE;
+    if (nb > cap) nb = cap;
+    int64_t chunk = (R + nb - 1) / nb;
+    chunk = (chunk + SC_TILE - 1) / SC_TILE * SC_TILE;
+    nb = (R + chunk - 1) / chunk;
+    // per-CTA histograms: stream-ordered scratch from the device's memory pool
+    // (concurrent scatters on other streams get their own)
+    int32_t* hist = nullptr;
+    SB_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&hist), (size_t)nb * n_experts * sizeof(int32_t), st));
+    const size_t sm_place = (size_t)(33 * n_experts) * sizeof(int);
+    ProfScope prof("pipe_scatter_by_expert", st);
+    pipe_scatter_hist_kernel<<<(unsigned)nb, SC_TILE, (size_t)n_experts * sizeof(int), st>>>(expert_ids, R, chunk,
+                                                                                           n_experts, hist);
+    pipe_scatter_offsets_kernel<<<n_experts, SC_TILE, 0, st>>>(hist, (int)nb, n_experts, expert_counts);
+    if (sm_place > 48 * 1024)
+      SB_CUDA_TRY(cudaFuncSetAttribute(pipe_scatter_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sm_place));
+    pipe_scatter_place_kernel<<<(unsigned)nb, SC_TILE, sm_place, st>>>(expert_ids, R, chunk, top_k, n_experts,
+                                                                      max_tokens_per_expert, store_entry ? 1 : 0,
+                                                                      hist, dispatch_indices);
+    SB_CUDA_TRY(cudaGetLastError());
+    SB_CUDA_TRY(cudaFreeAsync(hist, st));
+    return SB_OK;
+  }
   const int grid = n_experts < 65535 ? n_experts : 65535;
   ProfScope prof("pipe_scatter_by_expert", st);
-  pipe_scatter_kernel<<<grid, SCATTER_THREADS, 0, st>>>(expert_ids, batch * top_k, top_k, n_experts,
-                                                       max_tokens_per_expert, store_entry ? 1 : 0,
-                                                       dispatch_indices, expert_counts);
+  pipe_scatter_kernel<<<grid, SCATTER_THREADS, 0, st>>>(expert_ids, R, top_k, n_experts, max_tokens_per_expert,
+                                                       store_entry ? 1 : 0, dispatch_indices, expert_counts);
   SB_CUDA_TRY(cudaGetLastError());
   return SB_OK;
 }

@@ -131,6 +131,20 @@ SIGNATURES = [
      [C.c_void_p, C.c_int64, C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p]),
     ("sb_weighted_combine", C.c_int,
      [C.c_void_p, C.c_void_p, C.c_int64, C.c_int, C.c_int, C.c_void_p, C.c_void_p]),
+    ("sb_tree_create", C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
+    ("sb_tree_upload", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("sb_tree_route", C.c_int,
+     [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+      C.c_void_p]),
+    ("sb_tree_destroy", C.c_int, [C.c_void_p]),
+    ("bvh_upload_tree", C.c_int, [C.c_void_p] * 5),
+    ("bvh_alloc_buffers", C.c_int, [C.c_int]),
+    ("bvh_free_buffers", None, []),
+    ("bvh_route_batch", C.c_int, [C.c_void_p] * 7 + [C.c_int, C.c_int]),
+    ("bvh_get_batch_capacity", C.c_int, []),
+    ("bvh_get_num_nodes", C.c_int, []),
+    ("bvh_get_num_experts", C.c_int, []),
+    ("bvh_get_spec_dim", C.c_int, []),
 ]
 
 _lib = None

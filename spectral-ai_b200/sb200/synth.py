@@ -170,6 +170,35 @@ def calibration_linear(n_experts: int, seed: int = 0) -> Dict[str, np.ndarray]:
     return {"weight": w.numpy().astype(np.float32), "bias": (torch.randn(n_experts, generator=g) * 0.1).numpy()}
 
 
+def legacy_tree(seed: int = 0) -> Dict[str, np.ndarray]:
+    """Parameters of the legacy 85-node ray-sphere tree (root, 4, 16, 64 leaves)
+    in the layout bvh_upload_tree takes: centers [85,3] (children scattered
+    around their parent at shrinking scale), radii [85] in [0.2, 0.5), portals
+    [85,12] (3x4 identity plus N(0, 0.05^2) and a small translation),
+    snell_w [85,64] N(0, 1/64), snell_b [85] N(0, 0.1^2)."""
+    g = torch.Generator().manual_seed(WEIGHT_STREAM + 0x5000 + seed)
+    c = np.zeros((85, 3), np.float32)
+    for n in range(1, 85):
+        parent = (n - 1) // 4
+        depth = 1 if n < 5 else (2 if n < 21 else 3)
+        c[n] = c[parent] + (torch.randn(3, generator=g) * (1.2 / depth)).numpy()
+    radii = (0.2 + 0.3 * torch.rand(85, generator=g)).numpy().astype(np.float32)
+    eye = np.concatenate([np.eye(3, dtype=np.float32), np.zeros((3, 1), np.float32)], axis=1)
+    portals = (eye[None] + (torch.randn(85, 3, 4, generator=g) * 0.05).numpy()).astype(np.float32)
+    return {"centers": c, "radii": radii, "portals": portals.reshape(85, 12),
+            "snell_w": (torch.randn(85, 64, generator=g) / 8.0).numpy().astype(np.float32),
+            "snell_b": (torch.randn(85, generator=g) * 0.1).numpy().astype(np.float32)}
+
+
+def rays(batch: int, seed: int):
+    """Ray origins N(0, 0.5^2) and unit directions [B,3], fp32."""
+    g = torch.Generator().manual_seed(seed)
+    o = torch.randn(batch, 3, generator=g) * 0.5
+    d = torch.randn(batch, 3, generator=g)
+    d = d / d.norm(dim=1, keepdim=True)
+    return o.numpy().astype(np.float32), d.numpy().astype(np.float32)
+
+
 def unit_rms_rows(x: torch.Tensor) -> torch.Tensor:
     """Divide each row by its root-mean-square (fp32)."""
     rms = x.float().pow(2).mean(dim=-1, keepdim=True).sqrt()
