@@ -255,13 +255,22 @@ def moe_workload(batch: int, device, select: str = "soft"):
     ids, _ = layer.route(x)
     counts = torch.bincount(ids.long().flatten(), minlength=E_EXPERTS).float()
 
-    def step():
+    def eager_step():
         layer.forward(x, out=out)
+
+    # the timed form: the whole layer (router + dispatch + grouped GEMMs +
+    # combine, eight kernels) replayed from one CUDA graph per buffer pair
+    from sb200.moe import GraphedLayer
+    glayer = GraphedLayer(layer)
+    glayer(x, out)
+
+    def step():
+        glayer(x, out)
 
     # end to end: host batches through sb200.moe.HostPipeline (copies in and out
     # on their own streams, overlapped with the neighbouring batches' compute)
     from sb200.moe import HostPipeline
-    pipe = HostPipeline(layer, batch, H, dtype=torch.bfloat16, device=device)
+    pipe = HostPipeline(glayer, batch, H, dtype=torch.bfloat16, device=device)
     x_host = [x.cpu().pin_memory() for _ in range(2)]
     out_host = [torch.empty(batch, H, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
 
@@ -276,7 +285,7 @@ def moe_workload(batch: int, device, select: str = "soft"):
         y = layer(x_dev)
         out_host[0].copy_(y, non_blocking=True)
 
-    e2e_step = (e2e_run, e2e_sequential)
+    e2e_step = (e2e_run, e2e_sequential, eager_step)
 
     pairs = batch * TOPK
     meta = {"tokens_per_step": batch, "h2d": batch * H * 2, "d2h": batch * H * 2,
@@ -623,14 +632,18 @@ def run_ours(a):
     flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     flush = lambda: flush_buf.fill_(1)
     step, e2e_step, meta = moe_workload(batch, dev)
-    total_ms, prof = time_steps(step, a.steps, a.warmup, world, sampler, profile=True, flush=flush)
+    total_ms, _ = time_steps(step, a.steps, a.warmup, world, sampler, flush=flush)
     clocks = sampler.stop()
+    # the same layer launched kernel by kernel with per-kernel CUDA events: the
+    # kernel breakdown and the roofline of the dominant kernel
+    prof_steps = min(a.steps, 100)
+    eager_ms, prof = time_steps(e2e_step[2], prof_steps, a.warmup, world, profile=True, flush=flush)
     e2e_ms = time_pipelined(e2e_step[0], a.steps, a.warmup, world)
     seq_ms, _ = time_steps(e2e_step[1], a.steps, a.warmup, world, flush=flush)
     tokens = meta["tokens_per_step"] * a.steps * world
     value = tokens / (total_ms / 1e3)
     e2e_value = tokens / (e2e_ms / 1e3)
-    launches = sum(n for n, _ in prof.values())
+    launches = sum(n for n, _ in prof.values()) // prof_steps * a.steps  # kernels per step x timed steps
     out = {"metric": "MoE-layer tokens/s (BVH route + ternary SwiGLU)",
            "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": a.steps,
            "warmup": a.warmup, "ms_per_step": round(total_ms / a.steps, 4),
@@ -648,10 +661,13 @@ def run_ours(a):
                    "sequential": "BVHMoELayer.__call__ one batch at a time on one stream (copy in, "
                                  "layer, copy out; L2 flushed between batches)"},
            "gpu_launches": launches,
+           "launch_mode": (f"timed steps replay one CUDA graph of the layer ({launches // a.steps} kernels "
+                           f"per step); kernel breakdown from {prof_steps} eager steps with per-kernel "
+                           f"events ({round(eager_ms / prof_steps, 4)} ms/step eager)"),
            "kernels": {k: {"launches": n, "avg_ms": round(t / max(n, 1), 4),
                            "share": round(t / max(sum(v[1] for v in prof.values()), 1e-9), 4)}
                        for k, (n, t) in prof.items()},
-           "roofline": roofline_tensor(meta, prof, pk, total_ms, a.steps), "clocks": clocks}
+           "roofline": roofline_tensor(meta, prof, pk, eager_ms, prof_steps), "clocks": clocks}
     # ---- expert-parallel form of the same layer (N > 1): E/N experts per GPU,
     #      NCCL all-to-all dispatch and combine
     if world > 1 and not a.skip_ep:

@@ -59,3 +59,29 @@ def test_host_pipeline_equals_direct_calls(cuda_device):
     torch.cuda.current_stream(cuda_device).synchronize()
     for a, b in zip(direct, hy):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("B", [37, 4096])
+def test_graphed_layer_replays_the_eager_layer(cuda_device, B):
+    """GraphedLayer (the layer captured into one CUDA graph) gives the eager
+    layer's bits, picks up new input data in the same buffer, and feeds the
+    host pipeline."""
+    from sb200 import synth
+    from sb200.moe import GraphedLayer, HostPipeline
+    layer, _ = make_layer(cuda_device)
+    g = GraphedLayer(layer)
+    x = synth.hidden_states(B, 256, seed=B + 1, dtype=torch.bfloat16, device=cuda_device)
+    out = torch.empty(B, 256, dtype=torch.bfloat16, device=cuda_device)
+    g(x, out)
+    assert torch.equal(out, layer(x))
+    x.copy_(synth.hidden_states(B, 256, seed=B + 2, dtype=torch.bfloat16, device=cuda_device))
+    g(x, out)
+    assert torch.equal(out, layer(x))
+    assert len(g._graphs) == 1
+    pipe = HostPipeline(g, B, 256, dtype=torch.bfloat16, device=cuda_device)
+    xs = [synth.hidden_states(B, 256, seed=50 + i, dtype=torch.bfloat16).pin_memory() for i in range(4)]
+    ys = [torch.empty(B, 256, dtype=torch.bfloat16).pin_memory() for _ in range(4)]
+    pipe.run(xs, ys)
+    torch.cuda.synchronize()
+    for xh, yh in zip(xs, ys):
+        assert torch.equal(yh, layer(xh.to(cuda_device)).cpu())
