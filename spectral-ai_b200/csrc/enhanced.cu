@@ -18,6 +18,10 @@
 //      activations sit in shared memory and are read as broadcasts.
 #include "common.cuh"
 
+#include <stdlib.h>
+#include <string.h>
+#include <vector>
+
 namespace sb {
 
 constexpr int ENH_TOK = 32;        // tokens per CTA of the tail kernel
@@ -483,6 +487,8 @@ __global__ void __launch_bounds__(ENH_THREADS) enh_tail_kernel(const float* __re
 
 }  // namespace sb
 
+#include "enhanced_tc.cuh"
+
 // ===========================================================================
 // Host side
 // ===========================================================================
@@ -508,6 +514,11 @@ struct sb_enh {
   float* wg_f32 = nullptr;           // [E,H]
   float* zero_e = nullptr;           // [E] zero bias of the dense gate GEMM
   CUtensorMap tm_wg{};
+  // the tail's dense layers as bf16 [N][Kp] blocks for the tensor-core tail
+  // (feature 128, <= 64 experts, <= 8 children per level)
+  uint16_t* tcw = nullptr;
+  sb::EnhTC tc{};
+  bool tc_ok = false;
 };
 
 namespace sb {
@@ -540,8 +551,71 @@ void enh_free(sb_enh* h) {
   cudaFree(h->b0);
   cudaFree(h->b2);
   cudaFree(h->tail);
+  cudaFree(h->tcw);
   h->w0_bf16 = h->w2_bf16 = nullptr;
   h->w0_f32 = h->w2_f32 = h->b0 = h->b2 = h->tail = nullptr;
+  h->tcw = nullptr;
+  h->tc_ok = false;
+}
+
+uint16_t enh_bf16_bits(float f) {  // round to nearest even
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7f800000u) == 0x7f800000u) return (uint16_t)((u >> 16) | ((u & 0xffffu) ? 0x40u : 0u));
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+// The tensor-core tail's weights: each dense layer as bf16 [N][Kp] (nn.Linear
+// rows, K zero-padded to 64, N to 16), one 1024-byte-aligned block per layer.
+int enh_build_tc(sb_enh* h, const sb_enh_weights* w) {
+  const int F = h->F, E = h->E, nsum = h->n[0] + h->n[1] + h->n[2];
+  h->tc_ok = false;
+  if (F != ETC_F || E > ETC_MAXE || h->n[0] > ETC_MAXN || h->n[1] > ETC_MAXN || h->n[2] > ETC_MAXN ||
+      F + nsum > 192)
+    return SB_OK;  // the FFMA tail serves this shape
+  struct L { const float* src; int N, K; const float* bias; };
+  const L layers[ETC_LAYERS] = {
+      {w->level[0].feat0_w, F, 256, h->t.f0b[0]}, {w->level[0].feat2_w, F, F, h->t.f2b[0]},
+      {w->level[1].feat0_w, F, F, h->t.f0b[1]},   {w->level[1].feat2_w, F, F, h->t.f2b[1]},
+      {w->level[2].feat0_w, F, F, h->t.f0b[2]},   {w->level[2].feat2_w, F, F, h->t.f2b[2]},
+      {w->eh0_w, 256, F + nsum, h->t.e0b},        {w->eh2_w, E, 256, h->t.e2b}};
+  size_t off[ETC_LAYERS], total = 0;
+  int Np[ETC_LAYERS], Kp[ETC_LAYERS];
+  for (int l = 0; l < ETC_LAYERS; ++l) {
+    Np[l] = (layers[l].N + 15) / 16 * 16;
+    Kp[l] = (layers[l].K + 63) / 64 * 64;
+    off[l] = total;
+    total += ((size_t)Np[l] * Kp[l] * 2 + 1023) / 1024 * 1024;
+  }
+  std::vector<uint16_t> blk(total / 2, 0);
+  for (int l = 0; l < ETC_LAYERS; ++l) {
+    if (!layers[l].src) return fail(SB_ERR_INVALID, "sb_enh_upload: a dense tail weight is missing");
+    uint16_t* d = blk.data() + off[l] / 2;
+    for (int n = 0; n < layers[l].N; ++n)
+      for (int k = 0; k < layers[l].K; ++k) d[(size_t)n * Kp[l] + k] = enh_bf16_bits(layers[l].src[(size_t)n * layers[l].K + k]);
+  }
+  SB_CUDA_TRY(cudaMalloc(&h->tcw, total));
+  SB_CUDA_TRY(cudaMemcpy(h->tcw, blk.data(), total, cudaMemcpyHostToDevice));
+  for (int l = 0; l < ETC_LAYERS; ++l) {
+    int rc = make_tmap_2d(&h->tc.tm[l], h->tcw + off[l] / 2, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Np[l], Kp[l], Kp[l],
+                          64, (uint32_t)Np[l], CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    h->tc.N[l] = Np[l];
+    h->tc.Kp[l] = Kp[l];
+    h->tc.bias[l] = layers[l].bias;
+  }
+  h->tc_ok = true;
+  return SB_OK;
+}
+
+// SB_ENH_TAIL=simt keeps the FFMA tail for the FAST engine too.
+bool enh_tc_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("SB_ENH_TAIL");
+    return !(e && strcmp(e, "simt") == 0);
+  }();
+  return on;
 }
 
 void enh_free_gate(sb_enh* h) {
@@ -699,6 +773,10 @@ extern "C" int sb_enh_upload(sb_enh* h, const sb_enh_weights* w) {
     enh_free(h);
     return rc;
   }
+  if ((rc = enh_build_tc(h, w))) {
+    enh_free(h);
+    return rc;
+  }
   h->uploaded = true;
   return SB_OK;
 }
@@ -808,6 +886,25 @@ int enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t batch, int precis
   EnhOut o{out->logits, out->expert_probs, out->expert_ids, out->geo_dist, out->branch_bonus,
            out->router_probs, out->topk_weights, out->topk_ids, top_k, gate_mode, norm_topk_prob ? 1 : 0,
            round_dtype == SB_BF16 ? 1 : 0, hybrid ? D : nullptr, n_cand};
+  if (precision == SB_PREC_FAST && h->tc_ok && enh_tc_enabled()) {
+    static bool attr_tc[64] = {};
+    if (h->device < 64 && !attr_tc[h->device]) {
+      SB_CUDA_TRY(cudaFuncSetAttribute(enh_tail_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       ETC_SMEM_BYTES));
+      SB_CUDA_TRY(cudaFuncSetAttribute(enh_tail_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       ETC_SMEM_BYTES));
+      attr_tc[h->device] = true;
+    }
+    ProfScope prof("enh_tail_tc", stream);
+    int64_t blocks = (batch + ETC_TOK - 1) / ETC_TOK;
+    if (blocks > num_sms()) blocks = num_sms();
+    if (h->E <= 32)
+      enh_tail_tc_kernel<32><<<(unsigned)blocks, ETC_THREADS, ETC_SMEM_BYTES, stream>>>(P, batch, h->t, o, h->tc);
+    else
+      enh_tail_tc_kernel<64><<<(unsigned)blocks, ETC_THREADS, ETC_SMEM_BYTES, stream>>>(P, batch, h->t, o, h->tc);
+    SB_CUDA_TRY(cudaGetLastError());
+    return SB_OK;
+  }
   {
     static bool attr[64] = {};
     if (h->device < 64 && !attr[h->device]) {

@@ -1,0 +1,519 @@
+// enhanced_tc.cuh — the EnhancedBVHRouter tail on tcgen05 tensor cores (FAST engine).
+//
+// Same computation as enh_tail_kernel (enhanced.cu), reorganised for sm_100a:
+// a CTA of 128 threads owns a tile of 128 tokens (one TMEM lane and one thread
+// per token).  The eight dense layers of the tail run as M=128 bf16 MMAs with
+// fp32 accumulators in TMEM:
+//   layer 0  level 1 feature_net.0   X[256]  -> 128, GELU
+//   layer 1  level 1 feature_net.2   Z[128]  -> 128          (f1)
+//   layer 2  level 2 feature_net.0   f1      -> 128, GELU
+//   layer 3  level 2 feature_net.2   Z       -> 128          (f2)
+//   layer 4  level 3 feature_net.0   f2      -> 128, GELU
+//   layer 5  level 3 feature_net.2   Z       -> 128          (f3)
+//   layer 6  expert_head.0   [f3|p1|p2|p3] (K 140 -> 192)  -> 256, GELU
+//   layer 7  expert_head.2   [256]   -> E (<= 64)            (logits)
+// Activations are bf16 in shared memory in the 128-byte-swizzled K-major
+// layout the MMA reads; a layer's input is dead once its MMA completes, so
+// each epilogue writes its output over it (two buffers: XA 64 KB, FA 48 KB).
+// Weights stream per layer by TMA into one 96 KB buffer; the next layer's
+// load is issued as soon as the current MMA completes and overlaps the
+// epilogue.  The narrow parts stay on the CUDA cores in fp32, inside the
+// epilogues that produce their inputs: LayerNorm, every level's to_3d (3
+// outputs), route head (n outputs) and geometry, the softmaxes, argmaxes,
+// leaf distances, branch bonus and the gate.
+#pragma once
+
+#include "sm100.cuh"
+
+namespace sb {
+
+constexpr int ETC_TOK = 128;
+constexpr int ETC_THREADS = 128;
+constexpr int ETC_F = 128;         // feature_dim served by this engine
+constexpr int ETC_MAXN = 8;        // children per level
+constexpr int ETC_MAXE = 64;       // experts
+constexpr int ETC_LAYERS = 8;
+constexpr int ETC_ATOM = ETC_TOK * 128;      // 16 KB: 128 rows x 64 bf16
+constexpr int ETC_XA_BYTES = 4 * ETC_ATOM;   // K up to 256
+constexpr int ETC_FA_BYTES = 3 * ETC_ATOM;   // K up to 192
+constexpr int ETC_WB_BYTES = 96 * 1024;      // N x K bf16 of the largest layer (256 x 192)
+constexpr int ETC_SMEM_BYTES = ETC_XA_BYTES + ETC_FA_BYTES + ETC_WB_BYTES + 64 + 1024;
+static_assert(ETC_SMEM_BYTES <= 227 * 1024, "shared memory budget");
+
+struct EnhTC {
+  CUtensorMap tm[ETC_LAYERS];  // bf16 [N][Kp] weights, box {64, N}
+  int N[ETC_LAYERS];           // MMA N (rows of the weight matrix, multiple of 16)
+  int Kp[ETC_LAYERS];          // K padded to 64
+  const float* bias[ETC_LAYERS];
+};
+
+__device__ __forceinline__ float etc_bf(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+// Writes 8 fp32 values as bf16 to columns [c0, c0+8) of row r of a K-major
+// SW128 activation buffer (c0 a multiple of 8).
+__device__ __forceinline__ void etc_store8(uint8_t* buf, int r, int c0, const float* v) {
+  __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]), h1 = __floats2bfloat162_rn(v[2], v[3]);
+  __nv_bfloat162 h2 = __floats2bfloat162_rn(v[4], v[5]), h3 = __floats2bfloat162_rn(v[6], v[7]);
+  uint4 u;
+  u.x = *reinterpret_cast<uint32_t*>(&h0);
+  u.y = *reinterpret_cast<uint32_t*>(&h1);
+  u.z = *reinterpret_cast<uint32_t*>(&h2);
+  u.w = *reinterpret_cast<uint32_t*>(&h3);
+  uint8_t* atom = buf + (c0 >> 6) * ETC_ATOM;
+  *reinterpret_cast<uint4*>(atom + sw128_offset((uint32_t)r, (uint32_t)((c0 & 63) >> 3))) = u;
+}
+
+// One bf16 at column c of row r of a K-major SW128 activation buffer.
+__device__ __forceinline__ void etc_store1(uint8_t* buf, int r, int c, float v) {
+  uint8_t* atom = buf + (c >> 6) * ETC_ATOM;
+  *reinterpret_cast<__nv_bfloat16*>(atom + sw128_offset((uint32_t)r, (uint32_t)((c & 63) >> 3)) + (c & 7) * 2) =
+      __float2bfloat16_rn(v);
+}
+
+// Bounded wait by every thread of the CTA; false when it gave up (status set).
+__device__ __forceinline__ bool etc_wait(uint64_t* bar, uint32_t parity) {
+  return mbar_wait(bar, parity, ST_TIMEOUT_EPILOGUE);
+}
+
+// One layer's MMAs (thread 0): D[128 x N] = A[128 x Kp] W[N x Kp]^T.
+__device__ __forceinline__ void etc_mma(uint32_t d_tmem, const uint8_t* a, const uint8_t* w, int N, int Kp) {
+  const uint32_t idesc = idesc_f16(1, ETC_TOK, (uint32_t)N);
+  const uint32_t w_atom = (uint32_t)(N * 128);
+  for (int kb = 0; kb < Kp / 64; ++kb) {
+    const uint64_t ad = sdesc_sw128(smem_u32(a + kb * ETC_ATOM));
+    const uint64_t bd = sdesc_sw128(smem_u32(w + kb * w_atom));
+#pragma unroll
+    for (int k = 0; k < 4; ++k) umma_f16(d_tmem, ad + 2u * k, bd + 2u * k, idesc, (kb | k) != 0);
+  }
+}
+
+// The per-token outputs after the expert head (thread = token): logits,
+// expert_probs / expert_ids, leaf distances, branch bonus and the gate.
+// sd: this tile's leaf distances in shared memory, [3 * ETC_MAXN][ETC_TOK].
+template <int EP>
+__device__ __forceinline__ void etc_outputs(float (&lg)[EP], int64_t tok, int tid, const EnhTail& t, const EnhOut& o,
+                                            const float* sd, const int (&amx)[3]) {
+  const int E = t.E, n2 = t.n[1], n3 = t.n[2];
+  if (o.logits) {
+#pragma unroll
+    for (int e = 0; e < EP; e += 4)
+      if (e < E) *reinterpret_cast<float4*>(o.logits + tok * E + e) = make_float4(lg[e], lg[e + 1], lg[e + 2], lg[e + 3]);
+  }
+  // expert_probs = softmax(logits / max(T, 0.1)); ids = first argmax
+  float pr[EP];
+  float m = -INFINITY;
+#pragma unroll
+  for (int e = 0; e < EP; ++e)
+    if (e < E) m = fmaxf(m, lg[e] / t.tau_soft);
+  float sum = 0.f;
+#pragma unroll
+  for (int e = 0; e < EP; ++e) {
+    pr[e] = e < E ? expf(lg[e] / t.tau_soft - m) : 0.f;
+    sum += pr[e];
+  }
+  float bv = -INFINITY;
+  int bi = 0;
+#pragma unroll
+  for (int e = 0; e < EP; ++e) {
+    pr[e] = pr[e] / sum;
+    if (e < E && pr[e] > bv) {
+      bv = pr[e];
+      bi = e;
+    }
+  }
+  if (o.probs) {
+#pragma unroll
+    for (int e = 0; e < EP; e += 4)
+      if (e < E) *reinterpret_cast<float4*>(o.probs + tok * E + e) = make_float4(pr[e], pr[e + 1], pr[e + 2], pr[e + 3]);
+  }
+  if (o.ids) o.ids[tok] = bi;
+  if (o.geo || o.bonus) {
+    for (int e = 0; e < E; ++e) {
+      const int i = e / (n2 * n3), j = (e % (n2 * n3)) / n3, k = e % n3;
+      if (o.geo)
+        o.geo[tok * E + e] = (sd[i * ETC_TOK + tid] + sd[(ETC_MAXN + j) * ETC_TOK + tid]) +
+                             sd[(2 * ETC_MAXN + k) * ETC_TOK + tid];
+      if (o.bonus) o.bonus[tok * E + e] = (1.0f + 0.2f * (float)(i == amx[0])) + 0.1f * (float)(j == amx[1]);
+    }
+  }
+  if (!o.topi) return;
+  const int K = o.k;
+  unsigned long long cand = ~0ull;  // experts the top-k may choose from
+  float v[EP];
+  if (o.mode == SB_GATE_HYBRID) {
+    // BVH candidates: the n_cand first experts in the order (expert_probs
+    // descending, index ascending) — by n_cand passes adding the largest
+    // remaining, or, when fewer passes, by removing the smallest remaining
+    // (the last in that order: the higher index among equal values)
+    const unsigned long long all = E < 64 ? (1ull << E) - 1ull : ~0ull;
+    if (2 * o.n_cand <= E) {
+      cand = 0ull;
+      for (int r = 0; r < o.n_cand; ++r) {
+        float best = -INFINITY;
+        int b = -1;
+#pragma unroll
+        for (int e = 0; e < EP; ++e)
+          if (((all & ~cand) >> e) & 1ull)
+            if (b < 0 || pr[e] > best) {
+              best = pr[e];
+              b = e;
+            }
+        cand |= 1ull << b;
+      }
+    } else {
+      cand = all;
+      for (int r = 0; r < E - o.n_cand; ++r) {
+        float worst = INFINITY;
+        int b = -1;
+#pragma unroll
+        for (int e = 0; e < EP; ++e)
+          if ((cand >> e) & 1ull)
+            if (b < 0 || pr[e] <= worst) {
+              worst = pr[e];
+              b = e;
+            }
+        cand &= ~(1ull << b);
+      }
+    }
+    float m2 = -INFINITY;
+#pragma unroll
+    for (int e = 0; e < EP; ++e) {
+      v[e] = e < E ? (o.round_bf16 ? etc_bf(o.dense[tok * E + e]) : o.dense[tok * E + e]) : -INFINITY;
+      m2 = fmaxf(m2, v[e]);
+    }
+    float s2 = 0.f;
+#pragma unroll
+    for (int e = 0; e < EP; ++e) {
+      v[e] = e < E ? expf(v[e] - m2) : 0.f;
+      s2 += v[e];
+    }
+#pragma unroll
+    for (int e = 0; e < EP; ++e) v[e] = v[e] / s2;
+    if (o.rprobs) {
+#pragma unroll
+      for (int e = 0; e < EP; e += 4)
+        if (e < E) *reinterpret_cast<float4*>(o.rprobs + tok * E + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+    }
+  } else {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int e = 0; e < EP; ++e) {
+      v[e] = e < E ? (o.round_bf16 ? etc_bf(lg[e]) : lg[e]) : -INFINITY;
+      mx = fmaxf(mx, v[e]);
+    }
+    if (o.mode == SB_GATE_SOFTMAX) {
+      float s2 = 0.f;
+#pragma unroll
+      for (int e = 0; e < EP; ++e) {
+        v[e] = e < E ? expf(v[e] - mx) : 0.f;
+        s2 += v[e];
+      }
+#pragma unroll
+      for (int e = 0; e < EP; ++e) v[e] = v[e] / s2;
+      if (o.rprobs) {
+#pragma unroll
+        for (int e = 0; e < EP; e += 4)
+          if (e < E) *reinterpret_cast<float4*>(o.rprobs + tok * E + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+      }
+    } else if (o.rprobs) {
+      for (int e = 0; e < E; ++e) o.rprobs[tok * E + e] = 0.f;
+    }
+  }
+  if (E < 64) cand &= (1ull << E) - 1ull;
+  // top-k by k passes, larger first, lower index first among equal values
+  float sel_v[32];
+  int sel_i[32];
+  unsigned long long taken = 0ull;
+  float tot = 0.f;
+  for (int r = 0; r < K; ++r) {
+    float best = -INFINITY;
+    int b = -1;
+#pragma unroll
+    for (int e = 0; e < EP; ++e) {
+      const bool ok = ((cand & ~taken) >> e) & 1ull;
+      if (ok && (b < 0 || v[e] > best)) {
+        best = v[e];
+        b = e;
+      }
+    }
+    taken |= 1ull << b;
+    sel_v[r & 31] = best;
+    sel_i[r & 31] = b;
+    tot += best;
+  }
+  float wmax = -INFINITY, esum = 0.f;
+  if (o.mode == SB_GATE_TOPK_SOFTMAX) {
+    for (int r = 0; r < K; ++r) wmax = fmaxf(wmax, sel_v[r]);
+    for (int r = 0; r < K; ++r) esum += expf(sel_v[r] - wmax);
+  }
+  for (int r = 0; r < K; ++r) {
+    float w = sel_v[r];
+    if (o.mode == SB_GATE_TOPK_SOFTMAX) w = expf(sel_v[r] - wmax) / esum;
+    else if (o.norm) w = sel_v[r] / tot;
+    o.topi[tok * K + r] = sel_i[r];
+    if (o.topw) o.topw[tok * K + r] = w;
+    if (o.mode == SB_GATE_TOPK_SOFTMAX && o.rprobs) o.rprobs[tok * E + sel_i[r]] = w;
+  }
+}
+
+// Epilogue of a feature_net.2 layer for level lv (thread = token): f = acc + b
+// in bf16 over the layer's input (FA), the route head and next level's to_3d
+// on the fp32 values, then the level's geometry, softmax and argmax.
+template <int LV>
+__device__ __forceinline__ void etc_level_epilogue(uint32_t tl, uint8_t* FA, int tid, const EnhTail& t, const float* b2,
+                                                   float (&pos)[3], float (&prob)[3][ETC_MAXN], float* sd,
+                                                   int (&amx)[3]) {
+  constexpr int F = ETC_F;
+  const int K = t.n[LV];
+  const float* rhw = t.rhw[LV];
+  float rh[ETC_MAXN];
+#pragma unroll
+  for (int k = 0; k < ETC_MAXN; ++k) rh[k] = 0.f;
+  float nx[3] = {0.f, 0.f, 0.f};
+#pragma unroll 1
+  for (int c = 0; c < F / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tl + (uint32_t)(c * 32), r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      float f[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int col = c * 32 + g * 8 + j;
+        f[j] = __uint_as_float(r[g * 8 + j]) + __ldg(b2 + col);
+#pragma unroll
+        for (int k = 0; k < ETC_MAXN; ++k)
+          if (k < K) rh[k] = fmaf(f[j], __ldg(rhw + k * (F + 3) + col), rh[k]);
+        if (LV < 2) {
+#pragma unroll
+          for (int a = 0; a < 3; ++a) nx[a] = fmaf(f[j], __ldg(t.t3w[LV + 1] + a * F + col), nx[a]);
+        }
+      }
+      etc_store8(FA, tid, c * 32 + g * 8, f);
+    }
+  }
+  // route head over [f, pos] + 0.5 * geometric logit; softmax(logits / max(T, 0.1))
+  float lg[ETC_MAXN];
+  float m = -INFINITY;
+#pragma unroll
+  for (int k = 0; k < ETC_MAXN; ++k) {
+    if (k >= K) continue;
+    float v = rh[k];
+    v = fmaf(pos[0], __ldg(rhw + k * (F + 3) + F), v);
+    v = fmaf(pos[1], __ldg(rhw + k * (F + 3) + F + 1), v);
+    v = fmaf(pos[2], __ldg(rhw + k * (F + 3) + F + 2), v);
+    v += __ldg(t.rhb[LV] + k);
+    const float* cc = t.centers[LV] + 3 * k;
+    const float dx = pos[0] - __ldg(cc), dy = pos[1] - __ldg(cc + 1), dz = pos[2] - __ldg(cc + 2);
+    const float d2 = (dx * dx + dy * dy) + dz * dz;
+    lg[k] = (v + 0.5f * (-d2 / t.tau_geo)) / t.tau_soft;
+    sd[(LV * ETC_MAXN + k) * ETC_TOK + tid] = sqrtf(d2 + 1e-8f);
+    m = fmaxf(m, lg[k]);
+  }
+  float sum = 0.f;
+#pragma unroll
+  for (int k = 0; k < ETC_MAXN; ++k) {
+    prob[LV][k] = k < K ? expf(lg[k] - m) : 0.f;
+    sum += prob[LV][k];
+  }
+  float bv = -INFINITY;
+  int bi = 0;
+#pragma unroll
+  for (int k = 0; k < ETC_MAXN; ++k) {
+    prob[LV][k] = prob[LV][k] / sum;
+    if (k < K && prob[LV][k] > bv) {
+      bv = prob[LV][k];
+      bi = k;
+    }
+  }
+  amx[LV] = bi;
+  const int off = ETC_F + (LV > 0 ? t.n[0] : 0) + (LV > 1 ? t.n[1] : 0);
+#pragma unroll
+  for (int k = 0; k < ETC_MAXN; ++k)
+    if (k < K) etc_store1(FA, tid, off + k, prob[LV][k]);
+  if (LV < 2) {
+#pragma unroll
+    for (int a = 0; a < 3; ++a) pos[a] = nx[a] + __ldg(t.t3b[LV + 1] + a);
+  }
+}
+
+// GELU(acc + b) over N columns into an activation buffer.
+__device__ __forceinline__ void etc_gelu_epilogue(uint32_t tl, uint8_t* dst, int tid, const float* b, int N) {
+#pragma unroll 1
+  for (int c = 0; c < N / 32; ++c) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tl + (uint32_t)(c * 32), r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = gelu_erf(__uint_as_float(r[g * 8 + j]) + __ldg(b + c * 32 + g * 8 + j));
+      etc_store8(dst, tid, c * 32 + g * 8, v);
+    }
+  }
+}
+
+template <int EP>
+__global__ void __launch_bounds__(ETC_THREADS, 1)
+    enh_tail_tc_kernel(const float* __restrict__ P, int64_t B, const EnhTail t, const EnhOut o,
+                       const __grid_constant__ EnhTC p) {
+  extern __shared__ uint8_t etc_smem_raw[];
+  const uint32_t raw = smem_u32(etc_smem_raw);
+  uint8_t* XA = etc_smem_raw + ((1024u - (raw & 1023u)) & 1023u);
+  uint8_t* FA = XA + ETC_XA_BYTES;
+  uint8_t* WB = FA + ETC_FA_BYTES;
+  uint64_t* wbar = reinterpret_cast<uint64_t*>(WB + ETC_WB_BYTES);
+  uint64_t* mbar = wbar + 1;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + 1);
+  volatile int* s_abort = reinterpret_cast<volatile int*>(tslot + 1);
+  __shared__ float sd[3 * ETC_MAXN * ETC_TOK];  // leaf distances of this tile
+  const int tid = threadIdx.x, warp = tid >> 5;
+
+  if (tid == 0) {
+    mbar_init(wbar, 1);
+    mbar_init(mbar, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tslot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+  const int64_t tile_stride = (int64_t)gridDim.x * ETC_TOK;
+  uint32_t wcount = 0, mcount = 0;  // completed weight loads / MMA batches (phase parity)
+  bool w_pending = false;           // thread 0: a weight load is in flight
+
+  auto load_w = [&](int l) {
+    const int N = p.N[l], Kp = p.Kp[l];
+    mbar_arrive_expect_tx(wbar, (uint32_t)(Kp / 64) * (uint32_t)N * 128u);
+    for (int kb = 0; kb < Kp / 64; ++kb) tma_load_2d(WB + kb * N * 128, &p.tm[l], wbar, kb * 64, 0);
+    w_pending = true;
+  };
+  if (tid == 0 && (int64_t)blockIdx.x * ETC_TOK < B) {
+    for (int l = 0; l < ETC_LAYERS; ++l) tma_prefetch_desc(&p.tm[l]);
+    load_w(0);
+  }
+
+  for (int64_t t0 = (int64_t)blockIdx.x * ETC_TOK; t0 < B; t0 += tile_stride) {
+    const int64_t tok = t0 + tid;
+    const bool live = tok < B;
+    const bool last_tile = t0 + tile_stride >= B;
+    // ---- LayerNorm(P) -> XA (bf16) and level 1's to_3d on the fp32 values
+    float pos[3] = {0.f, 0.f, 0.f};
+    {
+      const float4* row = reinterpret_cast<const float4*>(P + (live ? tok : 0) * 256);
+      float s1 = 0.f;
+#pragma unroll 8
+      for (int i = 0; i < 64; ++i) {
+        const float4 v = __ldg(row + i);
+        s1 += (v.x + v.y) + (v.z + v.w);
+      }
+      const float mean = s1 / 256.f;
+      float s2 = 0.f;
+#pragma unroll 8
+      for (int i = 0; i < 64; ++i) {
+        const float4 v = __ldg(row + i);
+        s2 = fmaf(v.x - mean, v.x - mean, s2);
+        s2 = fmaf(v.y - mean, v.y - mean, s2);
+        s2 = fmaf(v.z - mean, v.z - mean, s2);
+        s2 = fmaf(v.w - mean, v.w - mean, s2);
+      }
+      const float den = sqrtf(s2 / 256.f + 1e-5f);
+#pragma unroll 1
+      for (int c0 = 0; c0 < 256; c0 += 8) {
+        const float4 a = __ldg(row + c0 / 4), b = __ldg(row + c0 / 4 + 1);
+        float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const int c = c0 + j;
+          x[j] = live ? (x[j] - mean) / den * __ldg(t.ln_w + c) + __ldg(t.ln_b + c) : 0.f;
+#pragma unroll
+          for (int d = 0; d < 3; ++d) pos[d] = fmaf(x[j], __ldg(t.t3w[0] + d * 256 + c), pos[d]);
+        }
+        etc_store8(XA, tid, c0, x);
+      }
+#pragma unroll
+      for (int d = 0; d < 3; ++d) pos[d] += __ldg(t.t3b[0] + d);
+      // expert-head input columns F .. 191 start at zero; each level writes its
+      // probabilities there ([p1 | p2 | p3 | 0...], read only by layer 6)
+      const float z8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int g = 0; g < 8; ++g) etc_store8(FA, tid, ETC_F + g * 8, z8);
+    }
+    float prob[3][ETC_MAXN];
+    int amx[3] = {0, 0, 0};
+    float lg[EP];
+#pragma unroll
+    for (int l = 0; l < ETC_LAYERS; ++l) {
+      // this layer's input (written above by every thread) -> the MMA's async proxy
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncthreads();
+      if (*s_abort) break;
+      if (tid == 0) {
+        const bool ok = etc_wait(wbar, wcount & 1u);
+        ++wcount;
+        if (ok) w_pending = false;
+        if (!ok) {
+          *s_abort = 1;
+        } else {
+          tc_fence_after();
+          etc_mma(tmem, (l == 0 || l == 7) ? XA : FA, WB, p.N[l], p.Kp[l]);
+          umma_commit(mbar);
+        }
+      }
+      __syncthreads();
+      if (*s_abort) break;
+      if (!etc_wait(mbar, mcount & 1u)) *s_abort = 1;
+      ++mcount;
+      tc_fence_after();
+      // the MMA that read WB is complete: fetch the next layer's weights
+      if (tid == 0 && !*s_abort && !(last_tile && l == ETC_LAYERS - 1)) load_w((l + 1) % ETC_LAYERS);
+      if (l == 0 || l == 2 || l == 4) {
+        etc_gelu_epilogue(tl, FA, tid, p.bias[l], ETC_F);
+      } else if (l == 1) {
+        etc_level_epilogue<0>(tl, FA, tid, t, p.bias[l], pos, prob, sd, amx);
+      } else if (l == 3) {
+        etc_level_epilogue<1>(tl, FA, tid, t, p.bias[l], pos, prob, sd, amx);
+      } else if (l == 5) {
+        etc_level_epilogue<2>(tl, FA, tid, t, p.bias[l], pos, prob, sd, amx);
+      } else if (l == 6) {
+        etc_gelu_epilogue(tl, XA, tid, p.bias[l], 256);
+      } else {
+        const int E = t.E;
+#pragma unroll
+        for (int c = 0; c < EP / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tl + (uint32_t)(c * 32), r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int e = c * 32 + j;
+            lg[e] = e < E ? __uint_as_float(r[j]) + __ldg(p.bias[l] + e) : 0.f;
+          }
+        }
+      }
+      tc_fence_before();
+    }
+    if (*s_abort) break;
+    if (live) etc_outputs<EP>(lg, tok, tid, t, o, sd, amx);
+  }
+  // unwind: no TMA may still write this CTA's shared memory, no MMA its TMEM
+  __syncthreads();
+  if (tid == 0 && w_pending) etc_wait(wbar, (wcount - (*s_abort ? 1u : 0u)) & 1u);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+}  // namespace sb

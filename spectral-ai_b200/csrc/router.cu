@@ -678,8 +678,9 @@ struct sb_router {
   CUtensorMap tm_w1{}, tm_w2{}, tm_w3s{}, tm_wr{};
   // narrower boxes for small batches, where the wide tiles leave SMs idle
   CUtensorMap tm_w1_128{}, tm_w2_64{}, tm_wr_32{};
-  // the position rows split over a CTA pair: 8 of the 16 rows per CTA
-  CUtensorMap tm_w3s_8{};
+  // the position rows split over a CTA pair: 8 of the 16 rows per CTA; W2 in
+  // 128-row boxes for the pair GEMM
+  CUtensorMap tm_w3s_8{}, tm_w2_128{};
   float bbox[SB_MAX_LEVELS][6] = {};  // per level: min x,y,z, max x,y,z of the centers
 };
 
@@ -874,7 +875,9 @@ extern "C" int sb_router_upload(sb_router* h, const sb_router_weights* w) {
       (rc = make_tmap_2d(&h->tm_wr_32, h->wr_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, T, S, S,
                          GEMM_BK, 32, CU_TENSOR_MAP_SWIZZLE_128B)) ||
       (rc = make_tmap_2d(&h->tm_w3s_8, h->w3s_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 16, H, H,
-                         GEMM_BK, 8, CU_TENSOR_MAP_SWIZZLE_128B))) {
+                         GEMM_BK, 8, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&h->tm_w2_128, h->w2_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, S, H, H,
+                         GEMM_BK, S < 128 ? S : 128, CU_TENSOR_MAP_SWIZZLE_128B))) {
     free_router_buffers(h);
     return rc;
   }
@@ -1044,7 +1047,13 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
                                                       H, e1, stream);
     if (rc) return rc;
     EpiTanhBf16 e2{h->b2, static_cast<__nv_bfloat16*>(spec), S, S};
-    if (S > 64 && mblocks * ((S + 127) / 128) < sms) {
+    const int64_t pair_tiles2 = ((M + GP_BM - 1) / GP_BM) * ((S + GP_BN - 1) / GP_BN);
+    if (router_pair_gemm_enabled() && S % 256 == 0 && pair_tiles2 >= 2 * (sms / 2)) {
+      // tm_w1_128's twin for W2: a 128-row box per CTA of the pair
+      if ((rc = launch_gemm_pair<EpiTanhBf16, false>("router_enc2_tanh_tc", tg, h->tm_w2_128, h->tm_w2_128, M, S, H,
+                                                     e2, stream)))
+        return rc;
+    } else if (S > 64 && mblocks * ((S + 127) / 128) < sms) {
       if ((rc = launch_gemm_tc<64, 4>("router_enc2_tanh_tc", tg, h->tm_w2_64, h->tm_w2_64, M, S, H, e2, stream)))
         return rc;
     } else if (S <= 128) {  // tm_w2's box height matches this tile width (set at upload)
