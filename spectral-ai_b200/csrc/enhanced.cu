@@ -566,34 +566,49 @@ uint16_t enh_bf16_bits(float f) {  // round to nearest even
   return (uint16_t)(u >> 16);
 }
 
-// The tensor-core tail's weights: each dense layer as bf16 [N][Kp] (nn.Linear
-// rows, K zero-padded to 64, N to 16), one 1024-byte-aligned block per layer.
+// The tensor-core tail's weights: each MMA's matrix as bf16 [N][Kp] (rows =
+// output features in nn.Linear layout, K zero-padded to 64, N to 16), one
+// 1024-byte-aligned block per MMA.  A matrix is a stack of row segments: a
+// wide layer plus the narrow layers reading the same input (to_3d rows, the
+// feature part of a route head), in the order enhanced_tc.cuh documents.
 int enh_build_tc(sb_enh* h, const sb_enh_weights* w) {
-  const int F = h->F, E = h->E, nsum = h->n[0] + h->n[1] + h->n[2];
+  const int F = h->F, E = h->E, n1 = h->n[0], n2 = h->n[1], n3 = h->n[2], nsum = n1 + n2 + n3;
   h->tc_ok = false;
-  if (F != ETC_F || E > ETC_MAXE || h->n[0] > ETC_MAXN || h->n[1] > ETC_MAXN || h->n[2] > ETC_MAXN ||
-      F + nsum > 192)
+  if (F != ETC_F || E > ETC_MAXE || n1 > ETC_MAXN || n2 > ETC_MAXN || n3 > ETC_MAXN || F + nsum > 192)
     return SB_OK;  // the FFMA tail serves this shape
-  struct L { const float* src; int N, K; const float* bias; };
-  const L layers[ETC_LAYERS] = {
-      {w->level[0].feat0_w, F, 256, h->t.f0b[0]}, {w->level[0].feat2_w, F, F, h->t.f2b[0]},
-      {w->level[1].feat0_w, F, F, h->t.f0b[1]},   {w->level[1].feat2_w, F, F, h->t.f2b[1]},
-      {w->level[2].feat0_w, F, F, h->t.f0b[2]},   {w->level[2].feat2_w, F, F, h->t.f2b[2]},
-      {w->eh0_w, 256, F + nsum, h->t.e0b},        {w->eh2_w, E, 256, h->t.e2b}};
+  struct Seg { const float* src; int rows, ld; };  // rows x K taken from src (row stride ld)
+  struct M { Seg seg[3]; int nseg, K; const float* bias; };
+  const sb_enh_level* L = w->level;
+  const M mats[ETC_LAYERS] = {
+      {{{L[0].feat0_w, F, 256}, {L[0].to3d_w, 3, 256}}, 2, 256, h->t.f0b[0]},
+      {{{L[0].feat2_w, F, F}}, 1, F, h->t.f2b[0]},
+      {{{L[1].feat0_w, F, F}, {L[0].head_w, n1, F + 3}, {L[1].to3d_w, 3, F}}, 3, F, h->t.f0b[1]},
+      {{{L[1].feat2_w, F, F}}, 1, F, h->t.f2b[1]},
+      {{{L[2].feat0_w, F, F}, {L[1].head_w, n2, F + 3}, {L[2].to3d_w, 3, F}}, 3, F, h->t.f0b[2]},
+      {{{L[2].feat2_w, F, F}}, 1, F, h->t.f2b[2]},
+      {{{L[2].head_w, n3, F + 3}}, 1, F, h->t.rhb[2]},
+      {{{w->eh0_w, 256, F + nsum}}, 1, F + nsum, h->t.e0b},
+      {{{w->eh2_w, E, 256}}, 1, 256, h->t.e2b}};
   size_t off[ETC_LAYERS], total = 0;
   int Np[ETC_LAYERS], Kp[ETC_LAYERS];
   for (int l = 0; l < ETC_LAYERS; ++l) {
-    Np[l] = (layers[l].N + 15) / 16 * 16;
-    Kp[l] = (layers[l].K + 63) / 64 * 64;
+    int rows = 0;
+    for (int g = 0; g < mats[l].nseg; ++g) rows += mats[l].seg[g].rows;
+    Np[l] = (rows + 15) / 16 * 16;
+    Kp[l] = (mats[l].K + 63) / 64 * 64;
     off[l] = total;
     total += ((size_t)Np[l] * Kp[l] * 2 + 1023) / 1024 * 1024;
   }
   std::vector<uint16_t> blk(total / 2, 0);
   for (int l = 0; l < ETC_LAYERS; ++l) {
-    if (!layers[l].src) return fail(SB_ERR_INVALID, "sb_enh_upload: a dense tail weight is missing");
     uint16_t* d = blk.data() + off[l] / 2;
-    for (int n = 0; n < layers[l].N; ++n)
-      for (int k = 0; k < layers[l].K; ++k) d[(size_t)n * Kp[l] + k] = enh_bf16_bits(layers[l].src[(size_t)n * layers[l].K + k]);
+    int row = 0;
+    for (int g = 0; g < mats[l].nseg; ++g) {
+      const Seg& sg = mats[l].seg[g];
+      if (!sg.src) return fail(SB_ERR_INVALID, "sb_enh_upload: a tail weight is missing");
+      for (int r = 0; r < sg.rows; ++r, ++row)
+        for (int k = 0; k < mats[l].K; ++k) d[(size_t)row * Kp[l] + k] = enh_bf16_bits(sg.src[(size_t)r * sg.ld + k]);
+    }
   }
   SB_CUDA_TRY(cudaMalloc(&h->tcw, total));
   SB_CUDA_TRY(cudaMemcpy(h->tcw, blk.data(), total, cudaMemcpyHostToDevice));
@@ -603,7 +618,7 @@ int enh_build_tc(sb_enh* h, const sb_enh_weights* w) {
     if (rc) return rc;
     h->tc.N[l] = Np[l];
     h->tc.Kp[l] = Kp[l];
-    h->tc.bias[l] = layers[l].bias;
+    h->tc.bias[l] = mats[l].bias;
   }
   h->tc_ok = true;
   return SB_OK;

@@ -2,25 +2,27 @@
 //
 // Same computation as enh_tail_kernel (enhanced.cu), reorganised for sm_100a:
 // a CTA of 128 threads owns a tile of 128 tokens (one TMEM lane and one thread
-// per token).  The eight dense layers of the tail run as M=128 bf16 MMAs with
-// fp32 accumulators in TMEM:
-//   layer 0  level 1 feature_net.0   X[256]  -> 128, GELU
-//   layer 1  level 1 feature_net.2   Z[128]  -> 128          (f1)
-//   layer 2  level 2 feature_net.0   f1      -> 128, GELU
-//   layer 3  level 2 feature_net.2   Z       -> 128          (f2)
-//   layer 4  level 3 feature_net.0   f2      -> 128, GELU
-//   layer 5  level 3 feature_net.2   Z       -> 128          (f3)
-//   layer 6  expert_head.0   [f3|p1|p2|p3] (K 140 -> 192)  -> 256, GELU
-//   layer 7  expert_head.2   [256]   -> E (<= 64)            (logits)
+// per token).  The dense layers run as M=128 bf16 MMAs with fp32 accumulators
+// in TMEM; the narrow layers that read the same input ride along as extra
+// rows of the wide layer's weight matrix (columns 128.. of its accumulator):
+//   MMA 0  level-1 feature_net.0 | level-1 to_3d            X      -> 128 GELU | 3
+//   MMA 1  level-1 feature_net.2                            Z      -> 128      (f1)
+//   MMA 2  level-2 feature_net.0 | level-1 route head (f part) | level-2 to_3d
+//                                                           f1     -> 128 GELU | n1 | 3
+//   MMA 3  level-2 feature_net.2                            Z      -> 128      (f2)
+//   MMA 4  level-3 feature_net.0 | level-2 route head | level-3 to_3d
+//   MMA 5  level-3 feature_net.2                            Z      -> 128      (f3)
+//   MMA 6  level-3 route head (f part)                      f3     -> n3
+//   MMA 7  expert_head.0   [f3 | p1 | p2 | p3] (K 140 -> 192) -> 256 GELU
+//   MMA 8  expert_head.2   [256]                            -> E (<= 64) logits
 // Activations are bf16 in shared memory in the 128-byte-swizzled K-major
 // layout the MMA reads; a layer's input is dead once its MMA completes, so
 // each epilogue writes its output over it (two buffers: XA 64 KB, FA 48 KB).
 // Weights stream per layer by TMA into one 96 KB buffer; the next layer's
 // load is issued as soon as the current MMA completes and overlaps the
-// epilogue.  The narrow parts stay on the CUDA cores in fp32, inside the
-// epilogues that produce their inputs: LayerNorm, every level's to_3d (3
-// outputs), route head (n outputs) and geometry, the softmaxes, argmaxes,
-// leaf distances, branch bonus and the gate.
+// epilogue.  On the CUDA cores, in fp32 and thread per token: LayerNorm, the
+// route heads' position terms, the geometry, softmaxes, argmaxes, leaf
+// distances, branch bonus and the gate.
 #pragma once
 
 #include "sm100.cuh"
@@ -28,11 +30,11 @@
 namespace sb {
 
 constexpr int ETC_TOK = 128;
-constexpr int ETC_THREADS = 128;
+constexpr int ETC_THREADS = 256;  // two warps per 32 tokens: each takes half the columns
 constexpr int ETC_F = 128;         // feature_dim served by this engine
 constexpr int ETC_MAXN = 8;        // children per level
 constexpr int ETC_MAXE = 64;       // experts
-constexpr int ETC_LAYERS = 8;
+constexpr int ETC_LAYERS = 9;
 constexpr int ETC_ATOM = ETC_TOK * 128;      // 16 KB: 128 rows x 64 bf16
 constexpr int ETC_XA_BYTES = 4 * ETC_ATOM;   // K up to 256
 constexpr int ETC_FA_BYTES = 3 * ETC_ATOM;   // K up to 192
@@ -99,34 +101,38 @@ __device__ __forceinline__ void etc_outputs(float (&lg)[EP], int64_t tok, int ti
     for (int e = 0; e < EP; e += 4)
       if (e < E) *reinterpret_cast<float4*>(o.logits + tok * E + e) = make_float4(lg[e], lg[e + 1], lg[e + 2], lg[e + 3]);
   }
-  // expert_probs = softmax(logits / max(T, 0.1)); ids = first argmax
+  // expert_probs = softmax(logits / max(T, 0.1)); ids = first argmax (only
+  // when an output or the hybrid gate's candidate ranking reads them)
   float pr[EP];
+  const bool need_pr = o.probs || o.ids || (o.topi && o.mode == SB_GATE_HYBRID);
   float m = -INFINITY;
+  if (need_pr) {
 #pragma unroll
-  for (int e = 0; e < EP; ++e)
-    if (e < E) m = fmaxf(m, lg[e] / t.tau_soft);
-  float sum = 0.f;
+    for (int e = 0; e < EP; ++e)
+      if (e < E) m = fmaxf(m, lg[e] / t.tau_soft);
+    float sum = 0.f;
 #pragma unroll
-  for (int e = 0; e < EP; ++e) {
-    pr[e] = e < E ? expf(lg[e] / t.tau_soft - m) : 0.f;
-    sum += pr[e];
-  }
-  float bv = -INFINITY;
-  int bi = 0;
-#pragma unroll
-  for (int e = 0; e < EP; ++e) {
-    pr[e] = pr[e] / sum;
-    if (e < E && pr[e] > bv) {
-      bv = pr[e];
-      bi = e;
+    for (int e = 0; e < EP; ++e) {
+      pr[e] = e < E ? expf(lg[e] / t.tau_soft - m) : 0.f;
+      sum += pr[e];
     }
-  }
-  if (o.probs) {
+    float bv = -INFINITY;
+    int bi = 0;
 #pragma unroll
-    for (int e = 0; e < EP; e += 4)
-      if (e < E) *reinterpret_cast<float4*>(o.probs + tok * E + e) = make_float4(pr[e], pr[e + 1], pr[e + 2], pr[e + 3]);
+    for (int e = 0; e < EP; ++e) {
+      pr[e] = pr[e] / sum;
+      if (e < E && pr[e] > bv) {
+        bv = pr[e];
+        bi = e;
+      }
+    }
+    if (o.probs) {
+#pragma unroll
+      for (int e = 0; e < EP; e += 4)
+        if (e < E) *reinterpret_cast<float4*>(o.probs + tok * E + e) = make_float4(pr[e], pr[e + 1], pr[e + 2], pr[e + 3]);
+    }
+    if (o.ids) o.ids[tok] = bi;
   }
-  if (o.ids) o.ids[tok] = bi;
   if (o.geo || o.bonus) {
     for (int e = 0; e < E; ++e) {
       const int i = e / (n2 * n3), j = (e % (n2 * n3)) / n3, k = e % n3;
@@ -256,50 +262,23 @@ __device__ __forceinline__ void etc_outputs(float (&lg)[EP], int64_t tok, int ti
   }
 }
 
-// Epilogue of a feature_net.2 layer for level lv (thread = token): f = acc + b
-// in bf16 over the layer's input (FA), the route head and next level's to_3d
-// on the fp32 values, then the level's geometry, softmax and argmax.
+// Route of level LV (thread = token): logits = rh + W_pos . pos + b + 0.5 *
+// geometric logit, softmax(logits / max(T, 0.1)), first argmax, leaf
+// distances; the probabilities go to the expert-head input columns of FA.
+// rh: the route head's feature part, computed by the tensor cores.
 template <int LV>
-__device__ __forceinline__ void etc_level_epilogue(uint32_t tl, uint8_t* FA, int tid, const EnhTail& t, const float* b2,
-                                                   float (&pos)[3], float (&prob)[3][ETC_MAXN], float* sd,
-                                                   int (&amx)[3]) {
+__device__ __forceinline__ void etc_route(const uint32_t (&rh)[32], int rh0, uint8_t* FA, int tid, const EnhTail& t,
+                                          const float (&pos)[3], float* sd, int (&amx)[3]) {
   constexpr int F = ETC_F;
   const int K = t.n[LV];
   const float* rhw = t.rhw[LV];
-  float rh[ETC_MAXN];
-#pragma unroll
-  for (int k = 0; k < ETC_MAXN; ++k) rh[k] = 0.f;
-  float nx[3] = {0.f, 0.f, 0.f};
-#pragma unroll 1
-  for (int c = 0; c < F / 32; ++c) {
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(tl + (uint32_t)(c * 32), r);
-    tmem_ld_wait();
-#pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      float f[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const int col = c * 32 + g * 8 + j;
-        f[j] = __uint_as_float(r[g * 8 + j]) + __ldg(b2 + col);
-#pragma unroll
-        for (int k = 0; k < ETC_MAXN; ++k)
-          if (k < K) rh[k] = fmaf(f[j], __ldg(rhw + k * (F + 3) + col), rh[k]);
-        if (LV < 2) {
-#pragma unroll
-          for (int a = 0; a < 3; ++a) nx[a] = fmaf(f[j], __ldg(t.t3w[LV + 1] + a * F + col), nx[a]);
-        }
-      }
-      etc_store8(FA, tid, c * 32 + g * 8, f);
-    }
-  }
-  // route head over [f, pos] + 0.5 * geometric logit; softmax(logits / max(T, 0.1))
   float lg[ETC_MAXN];
   float m = -INFINITY;
 #pragma unroll
   for (int k = 0; k < ETC_MAXN; ++k) {
+    lg[k] = -INFINITY;
     if (k >= K) continue;
-    float v = rh[k];
+    float v = __uint_as_float(rh[rh0 + k]);
     v = fmaf(pos[0], __ldg(rhw + k * (F + 3) + F), v);
     v = fmaf(pos[1], __ldg(rhw + k * (F + 3) + F + 1), v);
     v = fmaf(pos[2], __ldg(rhw + k * (F + 3) + F + 2), v);
@@ -311,47 +290,65 @@ __device__ __forceinline__ void etc_level_epilogue(uint32_t tl, uint8_t* FA, int
     sd[(LV * ETC_MAXN + k) * ETC_TOK + tid] = sqrtf(d2 + 1e-8f);
     m = fmaxf(m, lg[k]);
   }
+  float pr[ETC_MAXN];
   float sum = 0.f;
 #pragma unroll
   for (int k = 0; k < ETC_MAXN; ++k) {
-    prob[LV][k] = k < K ? expf(lg[k] - m) : 0.f;
-    sum += prob[LV][k];
+    pr[k] = k < K ? expf(lg[k] - m) : 0.f;
+    sum += pr[k];
   }
   float bv = -INFINITY;
   int bi = 0;
+  const int off = F + (LV > 0 ? t.n[0] : 0) + (LV > 1 ? t.n[1] : 0);
 #pragma unroll
   for (int k = 0; k < ETC_MAXN; ++k) {
-    prob[LV][k] = prob[LV][k] / sum;
-    if (k < K && prob[LV][k] > bv) {
-      bv = prob[LV][k];
+    if (k >= K) continue;
+    pr[k] = pr[k] / sum;
+    if (pr[k] > bv) {
+      bv = pr[k];
       bi = k;
     }
+    etc_store1(FA, tid, off + k, pr[k]);
   }
   amx[LV] = bi;
-  const int off = ETC_F + (LV > 0 ? t.n[0] : 0) + (LV > 1 ? t.n[1] : 0);
-#pragma unroll
-  for (int k = 0; k < ETC_MAXN; ++k)
-    if (k < K) etc_store1(FA, tid, off + k, prob[LV][k]);
-  if (LV < 2) {
-#pragma unroll
-    for (int a = 0; a < 3; ++a) pos[a] = nx[a] + __ldg(t.t3b[LV + 1] + a);
-  }
 }
 
-// GELU(acc + b) over N columns into an activation buffer.
-__device__ __forceinline__ void etc_gelu_epilogue(uint32_t tl, uint8_t* dst, int tid, const float* b, int N) {
+__device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[8]) {
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+}
+
+// act(acc + b) over columns [c0, c1) of this warp's 32 rows into an activation
+// buffer, 8 columns per step (a short loop the whole CTA reuses).
+// GELU in its tanh form (Hendrycks & Gimpel, 2016) on the hardware tanh: it
+// departs from the erf form by about 1e-3 at most, below the bf16 rounding the
+// FAST engine applies to the same activation right after.
+__device__ __forceinline__ float etc_gelu(float x) {
+  const float u = 0.7978845608f * fmaf(0.044715f * x, x * x, x);
+  float th;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(th) : "f"(u));
+  return 0.5f * x * (1.f + th);
+}
+
+template <bool GELU>
+__device__ __noinline__ void etc_act_epilogue(uint32_t tl, uint8_t* dst, int row, const float* __restrict__ b, int c0,
+                                              int c1) {
 #pragma unroll 1
-  for (int c = 0; c < N / 32; ++c) {
-    uint32_t r[32];
-    tmem_ld_32x32b_x32(tl + (uint32_t)(c * 32), r);
+  for (int c = c0; c < c1; c += 8) {
+    uint32_t r[8];
+    tmem_ld_32x32b_x8(tl + (uint32_t)c, r);
+    float bb[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) bb[j] = __ldg(b + c + j);
     tmem_ld_wait();
+    float v[8];
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      float v[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) v[j] = gelu_erf(__uint_as_float(r[g * 8 + j]) + __ldg(b + c * 32 + g * 8 + j));
-      etc_store8(dst, tid, c * 32 + g * 8, v);
+    for (int j = 0; j < 8; ++j) {
+      const float a = __uint_as_float(r[j]) + bb[j];
+      v[j] = GELU ? etc_gelu(a) : a;
     }
+    etc_store8(dst, row, c, v);
   }
 }
 
@@ -370,6 +367,8 @@ __global__ void __launch_bounds__(ETC_THREADS, 1)
   volatile int* s_abort = reinterpret_cast<volatile int*>(tslot + 1);
   __shared__ float sd[3 * ETC_MAXN * ETC_TOK];  // leaf distances of this tile
   const int tid = threadIdx.x, warp = tid >> 5;
+  const int row = tid & (ETC_TOK - 1);  // token of this thread (TMEM lane)
+  const int half = tid >> 7;            // which half of each layer's columns
 
   if (tid == 0) {
     mbar_init(wbar, 1);
@@ -385,7 +384,7 @@ __global__ void __launch_bounds__(ETC_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tslot;
-  const uint32_t tl = tmem + ((uint32_t)(warp * 32) << 16);
+  const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
   const int64_t tile_stride = (int64_t)gridDim.x * ETC_TOK;
   uint32_t wcount = 0, mcount = 0;  // completed weight loads / MMA batches (phase parity)
   bool w_pending = false;           // thread 0: a weight load is in flight
@@ -402,24 +401,24 @@ __global__ void __launch_bounds__(ETC_THREADS, 1)
   }
 
   for (int64_t t0 = (int64_t)blockIdx.x * ETC_TOK; t0 < B; t0 += tile_stride) {
-    const int64_t tok = t0 + tid;
+    const int64_t tok = t0 + row;
     const bool live = tok < B;
     const bool last_tile = t0 + tile_stride >= B;
     // ---- LayerNorm(P) -> XA (bf16) and level 1's to_3d on the fp32 values
     float pos[3] = {0.f, 0.f, 0.f};
     {
-      const float4* row = reinterpret_cast<const float4*>(P + (live ? tok : 0) * 256);
+      const float4* prow = reinterpret_cast<const float4*>(P + (live ? tok : 0) * 256);
       float s1 = 0.f;
 #pragma unroll 8
       for (int i = 0; i < 64; ++i) {
-        const float4 v = __ldg(row + i);
+        const float4 v = __ldg(prow + i);
         s1 += (v.x + v.y) + (v.z + v.w);
       }
       const float mean = s1 / 256.f;
       float s2 = 0.f;
 #pragma unroll 8
       for (int i = 0; i < 64; ++i) {
-        const float4 v = __ldg(row + i);
+        const float4 v = __ldg(prow + i);
         s2 = fmaf(v.x - mean, v.x - mean, s2);
         s2 = fmaf(v.y - mean, v.y - mean, s2);
         s2 = fmaf(v.z - mean, v.z - mean, s2);
@@ -427,27 +426,22 @@ __global__ void __launch_bounds__(ETC_THREADS, 1)
       }
       const float den = sqrtf(s2 / 256.f + 1e-5f);
 #pragma unroll 1
-      for (int c0 = 0; c0 < 256; c0 += 8) {
-        const float4 a = __ldg(row + c0 / 4), b = __ldg(row + c0 / 4 + 1);
+      for (int c0 = half * 128; c0 < half * 128 + 128; c0 += 8) {
+        const float4 a = __ldg(prow + c0 / 4), b = __ldg(prow + c0 / 4 + 1);
         float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
           const int c = c0 + j;
           x[j] = live ? (x[j] - mean) / den * __ldg(t.ln_w + c) + __ldg(t.ln_b + c) : 0.f;
-#pragma unroll
-          for (int d = 0; d < 3; ++d) pos[d] = fmaf(x[j], __ldg(t.t3w[0] + d * 256 + c), pos[d]);
         }
-        etc_store8(XA, tid, c0, x);
+        etc_store8(XA, row, c0, x);
       }
-#pragma unroll
-      for (int d = 0; d < 3; ++d) pos[d] += __ldg(t.t3b[0] + d);
       // expert-head input columns F .. 191 start at zero; each level writes its
       // probabilities there ([p1 | p2 | p3 | 0...], read only by layer 6)
       const float z8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int g = 0; g < 8; ++g) etc_store8(FA, tid, ETC_F + g * 8, z8);
+      for (int g = 0; g < 4; ++g) etc_store8(FA, row, ETC_F + (half * 4 + g) * 8, z8);
     }
-    float prob[3][ETC_MAXN];
     int amx[3] = {0, 0, 0};
     float lg[EP];
 #pragma unroll
@@ -465,7 +459,7 @@ __global__ void __launch_bounds__(ETC_THREADS, 1)
           *s_abort = 1;
         } else {
           tc_fence_after();
-          etc_mma(tmem, (l == 0 || l == 7) ? XA : FA, WB, p.N[l], p.Kp[l]);
+          etc_mma(tmem, (l == 0 || l == 8) ? XA : FA, WB, p.N[l], p.Kp[l]);
           umma_commit(mbar);
         }
       }
@@ -477,16 +471,38 @@ __global__ void __launch_bounds__(ETC_THREADS, 1)
       // the MMA that read WB is complete: fetch the next layer's weights
       if (tid == 0 && !*s_abort && !(last_tile && l == ETC_LAYERS - 1)) load_w((l + 1) % ETC_LAYERS);
       if (l == 0 || l == 2 || l == 4) {
-        etc_gelu_epilogue(tl, FA, tid, p.bias[l], ETC_F);
-      } else if (l == 1) {
-        etc_level_epilogue<0>(tl, FA, tid, t, p.bias[l], pos, prob, sd, amx);
-      } else if (l == 3) {
-        etc_level_epilogue<1>(tl, FA, tid, t, p.bias[l], pos, prob, sd, amx);
-      } else if (l == 5) {
-        etc_level_epilogue<2>(tl, FA, tid, t, p.bias[l], pos, prob, sd, amx);
+        // feature_net.0 (GELU) and the rows riding along: [route head of the
+        // previous level (n) | this level's to_3d (3)]
+        etc_act_epilogue<true>(tl, FA, row, p.bias[l], half * 64, half * 64 + 64);
+        if (half == 0) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tl + (uint32_t)ETC_F, r);
+          tmem_ld_wait();
+          const int lv = l / 2;  // the level this feature_net belongs to
+          const int nprev = lv > 0 ? t.n[lv - 1] : 0;
+          if (l == 2) etc_route<0>(r, 0, FA, row, t, pos, sd, amx);
+          if (l == 4) etc_route<1>(r, 0, FA, row, t, pos, sd, amx);
+#pragma unroll
+          for (int d = 0; d < 3; ++d) {
+            float v = 0.f;
+#pragma unroll
+            for (int q = 0; q < 16; ++q)
+              if (q == nprev + d) v = __uint_as_float(r[q]);
+            pos[d] = v + __ldg(t.t3b[lv] + d);
+          }
+        }
+      } else if (l == 1 || l == 3 || l == 5) {
+        etc_act_epilogue<false>(tl, FA, row, p.bias[l], half * 64, half * 64 + 64);
       } else if (l == 6) {
-        etc_gelu_epilogue(tl, XA, tid, p.bias[l], 256);
-      } else {
+        if (half == 0) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tl, r);
+          tmem_ld_wait();
+          etc_route<2>(r, 0, FA, row, t, pos, sd, amx);
+        }
+      } else if (l == 7) {
+        etc_act_epilogue<true>(tl, XA, row, p.bias[l], half * 128, half * 128 + 128);
+      } else if (half == 0) {
         const int E = t.E;
 #pragma unroll
         for (int c = 0; c < EP / 32; ++c) {
@@ -503,7 +519,7 @@ __global__ void __launch_bounds__(ETC_THREADS, 1)
       tc_fence_before();
     }
     if (*s_abort) break;
-    if (live) etc_outputs<EP>(lg, tok, tid, t, o, sd, amx);
+    if (live && half == 0) etc_outputs<EP>(lg, tok, row, t, o, sd, amx);
   }
   // unwind: no TMA may still write this CTA's shared memory, no MMA its TMEM
   __syncthreads();
