@@ -489,6 +489,84 @@ __global__ void __launch_bounds__(ENH_THREADS) enh_tail_kernel(const float* __re
 
 #include "enhanced_tc.cuh"
 
+namespace sb {
+
+// input_proj.2 + LayerNorm as the GEMM's epilogue (FAST engine with the
+// tensor-core tail): X = LN(acc + b2) * ln_w + ln_b over the 256 columns of a
+// row, in bf16 [M, 256] — three passes over the row's accumulators in TMEM
+// (mean, biased variance, normalise), eps 1e-5 (olmoe_bvh_distill.py:465).
+struct EpiLayerNormBf16 {
+  static constexpr bool kWholeRow = true;
+  const float* bias;
+  const float* ln_w;
+  const float* ln_b;
+  __nv_bfloat16* out;
+  __device__ __forceinline__ void apply_row(uint32_t taddr, int64_t row, bool valid) const {
+    const float4* b4 = reinterpret_cast<const float4*>(bias);
+    float s1 = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 bb = __ldg(b4 + c * 8 + q);
+        s1 += ((__uint_as_float(r[4 * q]) + bb.x) + (__uint_as_float(r[4 * q + 1]) + bb.y)) +
+              ((__uint_as_float(r[4 * q + 2]) + bb.z) + (__uint_as_float(r[4 * q + 3]) + bb.w));
+      }
+    }
+    const float mean = s1 / 256.f;
+    float s2 = 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), r);
+      tmem_ld_wait();
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 bb = __ldg(b4 + c * 8 + q);
+        const float d0 = __uint_as_float(r[4 * q]) + bb.x - mean, d1 = __uint_as_float(r[4 * q + 1]) + bb.y - mean;
+        const float d2 = __uint_as_float(r[4 * q + 2]) + bb.z - mean, d3 = __uint_as_float(r[4 * q + 3]) + bb.w - mean;
+        s2 = fmaf(d0, d0, s2);
+        s2 = fmaf(d1, d1, s2);
+        s2 = fmaf(d2, d2, s2);
+        s2 = fmaf(d3, d3, s2);
+      }
+    }
+    const float inv = 1.f / sqrtf(s2 / 256.f + 1e-5f);
+    const float4* w4 = reinterpret_cast<const float4*>(ln_w);
+    const float4* l4 = reinterpret_cast<const float4*>(ln_b);
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + (uint32_t)(c * 32), r);
+      tmem_ld_wait();
+      uint32_t packed[16];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 bb = __ldg(b4 + c * 8 + q), ww = __ldg(w4 + c * 8 + q), ll = __ldg(l4 + c * 8 + q);
+        const float x0 = (__uint_as_float(r[4 * q]) + bb.x - mean) * inv * ww.x + ll.x;
+        const float x1 = (__uint_as_float(r[4 * q + 1]) + bb.y - mean) * inv * ww.y + ll.y;
+        const float x2 = (__uint_as_float(r[4 * q + 2]) + bb.z - mean) * inv * ww.z + ll.z;
+        const float x3 = (__uint_as_float(r[4 * q + 3]) + bb.w - mean) * inv * ww.w + ll.w;
+        __nv_bfloat162 h0 = __floats2bfloat162_rn(x0, x1), h1 = __floats2bfloat162_rn(x2, x3);
+        packed[2 * q] = *reinterpret_cast<uint32_t*>(&h0);
+        packed[2 * q + 1] = *reinterpret_cast<uint32_t*>(&h1);
+      }
+      if (valid) {
+        uint4* d4 = reinterpret_cast<uint4*>(out + row * 256 + c * 32);
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          d4[j] = make_uint4(packed[4 * j], packed[4 * j + 1], packed[4 * j + 2], packed[4 * j + 3]);
+      }
+    }
+  }
+  __device__ __forceinline__ void tail(int64_t, const uint32_t (&)[32]) const {}
+};
+
+}  // namespace sb
+
 // ===========================================================================
 // Host side
 // ===========================================================================
@@ -845,6 +923,7 @@ int enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t batch, int precis
   float* D = reinterpret_cast<float*>(ws + W.d);
   const int H = h->H, M = (int)batch, E = h->E;
   const bool hybrid = gate_mode == SB_GATE_HYBRID;
+  const bool use_tc = precision == SB_PREC_FAST && h->tc_ok && enh_tc_enabled();
   int rc;
   if (precision == SB_PREC_FAST) {
     CUtensorMap ta, tg;
@@ -857,10 +936,17 @@ int enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t batch, int precis
     if ((rc = launch_gemm_tc<256, 4, EpiGeluBf16, false>("enh_proj0_gelu_tc", ta, h->tm_w0, h->tm_w0, M, 512, H,
                                                           e0, stream)))
       return rc;
-    EpiBiasF32 e2{h->b2, P, 256, 256};
-    if ((rc = launch_gemm_tc<256, 4, EpiBiasF32, false>("enh_proj2_tc", tg, h->tm_w2, h->tm_w2, M, 256, 512, e2,
-                                                         stream)))
-      return rc;
+    if (use_tc) {  // input_proj.2 + LayerNorm -> X bf16 (the tensor-core tail's input)
+      EpiLayerNormBf16 e2{h->b2, h->t.ln_w, h->t.ln_b, reinterpret_cast<__nv_bfloat16*>(P)};
+      if ((rc = launch_gemm_tc<256, 4, EpiLayerNormBf16, false>("enh_proj2_ln_tc", tg, h->tm_w2, h->tm_w2, M, 256,
+                                                                512, e2, stream)))
+        return rc;
+    } else {
+      EpiBiasF32 e2{h->b2, P, 256, 256};
+      if ((rc = launch_gemm_tc<256, 4, EpiBiasF32, false>("enh_proj2_tc", tg, h->tm_w2, h->tm_w2, M, 256, 512, e2,
+                                                           stream)))
+        return rc;
+    }
     if (hybrid) {  // full_logits = x W_gate^T (fp32 accumulate; rounded to the hidden dtype in the tail)
       EpiBiasF32 ed{h->zero_e, D, E, E};
       if ((rc = launch_gemm_tc<64, 4, EpiBiasF32, false>("enh_dense_gate_tc", ta, h->tm_wg, h->tm_wg, M, E, H, ed,
@@ -901,7 +987,11 @@ int enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t batch, int precis
   EnhOut o{out->logits, out->expert_probs, out->expert_ids, out->geo_dist, out->branch_bonus,
            out->router_probs, out->topk_weights, out->topk_ids, top_k, gate_mode, norm_topk_prob ? 1 : 0,
            round_dtype == SB_BF16 ? 1 : 0, hybrid ? D : nullptr, n_cand};
-  if (precision == SB_PREC_FAST && h->tc_ok && enh_tc_enabled()) {
+  if (use_tc) {
+    CUtensorMap tmx;
+    if ((rc = make_tmap_2d(&tmx, P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, 256, 256, 64, ETC_TOK,
+                           CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc;
     static bool attr_tc[64] = {};
     if (h->device < 64 && !attr_tc[h->device]) {
       SB_CUDA_TRY(cudaFuncSetAttribute(enh_tail_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -914,9 +1004,9 @@ int enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t batch, int precis
     int64_t blocks = (batch + ETC_TOK - 1) / ETC_TOK;
     if (blocks > num_sms()) blocks = num_sms();
     if (h->E <= 32)
-      enh_tail_tc_kernel<32><<<(unsigned)blocks, ETC_THREADS, ETC_SMEM_BYTES, stream>>>(P, batch, h->t, o, h->tc);
+      enh_tail_tc_kernel<32><<<(unsigned)blocks, ETC_THREADS, ETC_SMEM_BYTES, stream>>>(tmx, batch, h->t, o, h->tc);
     else
-      enh_tail_tc_kernel<64><<<(unsigned)blocks, ETC_THREADS, ETC_SMEM_BYTES, stream>>>(P, batch, h->t, o, h->tc);
+      enh_tail_tc_kernel<64><<<(unsigned)blocks, ETC_THREADS, ETC_SMEM_BYTES, stream>>>(tmx, batch, h->t, o, h->tc);
     SB_CUDA_TRY(cudaGetLastError());
     return SB_OK;
   }

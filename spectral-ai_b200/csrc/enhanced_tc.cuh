@@ -102,36 +102,74 @@ __device__ __forceinline__ void etc_outputs(float (&lg)[EP], int64_t tok, int ti
       if (e < E) *reinterpret_cast<float4*>(o.logits + tok * E + e) = make_float4(lg[e], lg[e + 1], lg[e + 2], lg[e + 3]);
   }
   // expert_probs = softmax(logits / max(T, 0.1)); ids = first argmax (only
-  // when an output or the hybrid gate's candidate ranking reads them)
-  float pr[EP];
-  const bool need_pr = o.probs || o.ids || (o.topi && o.mode == SB_GATE_HYBRID);
-  float m = -INFINITY;
-  if (need_pr) {
+  // when an output or the hybrid gate's candidate ranking reads them).  v
+  // holds them, then the gate's values (two arrays of EP live, not three).
+  float v[EP];
+  const bool hybrid = o.topi && o.mode == SB_GATE_HYBRID;
+  unsigned long long cand = ~0ull;  // experts the top-k may choose from
+  if (o.probs || o.ids || hybrid) {
+    float m = -INFINITY;
 #pragma unroll
     for (int e = 0; e < EP; ++e)
       if (e < E) m = fmaxf(m, lg[e] / t.tau_soft);
     float sum = 0.f;
 #pragma unroll
     for (int e = 0; e < EP; ++e) {
-      pr[e] = e < E ? expf(lg[e] / t.tau_soft - m) : 0.f;
-      sum += pr[e];
+      v[e] = e < E ? expf(lg[e] / t.tau_soft - m) : 0.f;
+      sum += v[e];
     }
     float bv = -INFINITY;
     int bi = 0;
 #pragma unroll
     for (int e = 0; e < EP; ++e) {
-      pr[e] = pr[e] / sum;
-      if (e < E && pr[e] > bv) {
-        bv = pr[e];
+      v[e] = v[e] / sum;
+      if (e < E && v[e] > bv) {
+        bv = v[e];
         bi = e;
       }
     }
     if (o.probs) {
 #pragma unroll
       for (int e = 0; e < EP; e += 4)
-        if (e < E) *reinterpret_cast<float4*>(o.probs + tok * E + e) = make_float4(pr[e], pr[e + 1], pr[e + 2], pr[e + 3]);
+        if (e < E) *reinterpret_cast<float4*>(o.probs + tok * E + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
     }
     if (o.ids) o.ids[tok] = bi;
+    if (hybrid) {
+      // BVH candidates: the n_cand first experts in the order (expert_probs
+      // descending, index ascending) — by n_cand passes adding the largest
+      // remaining, or, when fewer passes, by removing the smallest remaining
+      // (the last in that order: the higher index among equal values)
+      const unsigned long long all = E < 64 ? (1ull << E) - 1ull : ~0ull;
+      if (2 * o.n_cand <= E) {
+        cand = 0ull;
+        for (int r = 0; r < o.n_cand; ++r) {
+          float best = -INFINITY;
+          int b = -1;
+#pragma unroll
+          for (int e = 0; e < EP; ++e)
+            if (((all & ~cand) >> e) & 1ull)
+              if (b < 0 || v[e] > best) {
+                best = v[e];
+                b = e;
+              }
+          cand |= 1ull << b;
+        }
+      } else {
+        cand = all;
+        for (int r = 0; r < E - o.n_cand; ++r) {
+          float worst = INFINITY;
+          int b = -1;
+#pragma unroll
+          for (int e = 0; e < EP; ++e)
+            if ((cand >> e) & 1ull)
+              if (b < 0 || v[e] <= worst) {
+                worst = v[e];
+                b = e;
+              }
+          cand &= ~(1ull << b);
+        }
+      }
+    }
   }
   if (o.geo || o.bonus) {
     for (int e = 0; e < E; ++e) {
@@ -144,43 +182,7 @@ __device__ __forceinline__ void etc_outputs(float (&lg)[EP], int64_t tok, int ti
   }
   if (!o.topi) return;
   const int K = o.k;
-  unsigned long long cand = ~0ull;  // experts the top-k may choose from
-  float v[EP];
-  if (o.mode == SB_GATE_HYBRID) {
-    // BVH candidates: the n_cand first experts in the order (expert_probs
-    // descending, index ascending) — by n_cand passes adding the largest
-    // remaining, or, when fewer passes, by removing the smallest remaining
-    // (the last in that order: the higher index among equal values)
-    const unsigned long long all = E < 64 ? (1ull << E) - 1ull : ~0ull;
-    if (2 * o.n_cand <= E) {
-      cand = 0ull;
-      for (int r = 0; r < o.n_cand; ++r) {
-        float best = -INFINITY;
-        int b = -1;
-#pragma unroll
-        for (int e = 0; e < EP; ++e)
-          if (((all & ~cand) >> e) & 1ull)
-            if (b < 0 || pr[e] > best) {
-              best = pr[e];
-              b = e;
-            }
-        cand |= 1ull << b;
-      }
-    } else {
-      cand = all;
-      for (int r = 0; r < E - o.n_cand; ++r) {
-        float worst = INFINITY;
-        int b = -1;
-#pragma unroll
-        for (int e = 0; e < EP; ++e)
-          if ((cand >> e) & 1ull)
-            if (b < 0 || pr[e] <= worst) {
-              worst = pr[e];
-              b = e;
-            }
-        cand &= ~(1ull << b);
-      }
-    }
+  if (hybrid) {
     float m2 = -INFINITY;
 #pragma unroll
     for (int e = 0; e < EP; ++e) {
@@ -338,9 +340,8 @@ __device__ __noinline__ void etc_act_epilogue(uint32_t tl, uint8_t* dst, int row
   for (int c = c0; c < c1; c += 8) {
     uint32_t r[8];
     tmem_ld_32x32b_x8(tl + (uint32_t)c, r);
-    float bb[8];
-#pragma unroll
-    for (int j = 0; j < 8; ++j) bb[j] = __ldg(b + c + j);
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(b + c)), b1 = __ldg(reinterpret_cast<const float4*>(b + c + 4));
+    const float bb[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
     tmem_ld_wait();
     float v[8];
 #pragma unroll
@@ -354,7 +355,7 @@ __device__ __noinline__ void etc_act_epilogue(uint32_t tl, uint8_t* dst, int row
 
 template <int EP>
 __global__ void __launch_bounds__(ETC_THREADS, 1)
-    enh_tail_tc_kernel(const float* __restrict__ P, int64_t B, const EnhTail t, const EnhOut o,
+    enh_tail_tc_kernel(const __grid_constant__ CUtensorMap tmx, int64_t B, const EnhTail t, const EnhOut o,
                        const __grid_constant__ EnhTC p) {
   extern __shared__ uint8_t etc_smem_raw[];
   const uint32_t raw = smem_u32(etc_smem_raw);
@@ -363,7 +364,8 @@ __global__ void __launch_bounds__(ETC_THREADS, 1)
   uint8_t* WB = FA + ETC_FA_BYTES;
   uint64_t* wbar = reinterpret_cast<uint64_t*>(WB + ETC_WB_BYTES);
   uint64_t* mbar = wbar + 1;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(mbar + 1);
+  uint64_t* xbar = mbar + 1;  // the tile's LayerNorm output X arrived in XA
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(xbar + 1);
   volatile int* s_abort = reinterpret_cast<volatile int*>(tslot + 1);
   __shared__ float sd[3 * ETC_MAXN * ETC_TOK];  // leaf distances of this tile
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -373,6 +375,7 @@ __global__ void __launch_bounds__(ETC_THREADS, 1)
   if (tid == 0) {
     mbar_init(wbar, 1);
     mbar_init(mbar, 1);
+    mbar_init(xbar, 1);
     *s_abort = 0;
     fence_barrier_init();
   }
@@ -386,8 +389,8 @@ __global__ void __launch_bounds__(ETC_THREADS, 1)
   const uint32_t tmem = *tslot;
   const uint32_t tl = tmem + ((uint32_t)((warp & 3) * 32) << 16);
   const int64_t tile_stride = (int64_t)gridDim.x * ETC_TOK;
-  uint32_t wcount = 0, mcount = 0;  // completed weight loads / MMA batches (phase parity)
-  bool w_pending = false;           // thread 0: a weight load is in flight
+  uint32_t wcount = 0, mcount = 0, xcount = 0;  // completed weight loads / MMA batches / X tiles
+  bool w_pending = false, x_pending = false;     // thread 0: a load is in flight
 
   auto load_w = [&](int l) {
     const int N = p.N[l], Kp = p.Kp[l];
@@ -395,8 +398,17 @@ __global__ void __launch_bounds__(ETC_THREADS, 1)
     for (int kb = 0; kb < Kp / 64; ++kb) tma_load_2d(WB + kb * N * 128, &p.tm[l], wbar, kb * 64, 0);
     w_pending = true;
   };
+  // X rows t0 .. t0+127 (bf16, 4 boxes of 64 columns) into XA; rows past the
+  // batch arrive as zeros
+  auto load_x = [&](int64_t t0) {
+    mbar_arrive_expect_tx(xbar, 4u * ETC_ATOM);
+    for (int kb = 0; kb < 4; ++kb) tma_load_2d(XA + kb * ETC_ATOM, &tmx, xbar, kb * 64, (int32_t)t0);
+    x_pending = true;
+  };
   if (tid == 0 && (int64_t)blockIdx.x * ETC_TOK < B) {
     for (int l = 0; l < ETC_LAYERS; ++l) tma_prefetch_desc(&p.tm[l]);
+    tma_prefetch_desc(&tmx);
+    load_x((int64_t)blockIdx.x * ETC_TOK);
     load_w(0);
   }
 
@@ -404,40 +416,10 @@ __global__ void __launch_bounds__(ETC_THREADS, 1)
     const int64_t tok = t0 + row;
     const bool live = tok < B;
     const bool last_tile = t0 + tile_stride >= B;
-    // ---- LayerNorm(P) -> XA (bf16) and level 1's to_3d on the fp32 values
     float pos[3] = {0.f, 0.f, 0.f};
     {
-      const float4* prow = reinterpret_cast<const float4*>(P + (live ? tok : 0) * 256);
-      float s1 = 0.f;
-#pragma unroll 8
-      for (int i = 0; i < 64; ++i) {
-        const float4 v = __ldg(prow + i);
-        s1 += (v.x + v.y) + (v.z + v.w);
-      }
-      const float mean = s1 / 256.f;
-      float s2 = 0.f;
-#pragma unroll 8
-      for (int i = 0; i < 64; ++i) {
-        const float4 v = __ldg(prow + i);
-        s2 = fmaf(v.x - mean, v.x - mean, s2);
-        s2 = fmaf(v.y - mean, v.y - mean, s2);
-        s2 = fmaf(v.z - mean, v.z - mean, s2);
-        s2 = fmaf(v.w - mean, v.w - mean, s2);
-      }
-      const float den = sqrtf(s2 / 256.f + 1e-5f);
-#pragma unroll 1
-      for (int c0 = half * 128; c0 < half * 128 + 128; c0 += 8) {
-        const float4 a = __ldg(prow + c0 / 4), b = __ldg(prow + c0 / 4 + 1);
-        float x[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const int c = c0 + j;
-          x[j] = live ? (x[j] - mean) / den * __ldg(t.ln_w + c) + __ldg(t.ln_b + c) : 0.f;
-        }
-        etc_store8(XA, row, c0, x);
-      }
       // expert-head input columns F .. 191 start at zero; each level writes its
-      // probabilities there ([p1 | p2 | p3 | 0...], read only by layer 6)
+      // probabilities there ([p1 | p2 | p3 | 0...], read only by MMA 7)
       const float z8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int g = 0; g < 4; ++g) etc_store8(FA, row, ETC_F + (half * 4 + g) * 8, z8);
@@ -452,9 +434,14 @@ __global__ void __launch_bounds__(ETC_THREADS, 1)
       __syncthreads();
       if (*s_abort) break;
       if (tid == 0) {
-        const bool ok = etc_wait(wbar, wcount & 1u);
+        bool ok = etc_wait(wbar, wcount & 1u);
         ++wcount;
         if (ok) w_pending = false;
+        if (ok && l == 0) {
+          ok = etc_wait(xbar, xcount & 1u);
+          ++xcount;
+          if (ok) x_pending = false;
+        }
         if (!ok) {
           *s_abort = 1;
         } else {
@@ -470,6 +457,8 @@ __global__ void __launch_bounds__(ETC_THREADS, 1)
       tc_fence_after();
       // the MMA that read WB is complete: fetch the next layer's weights
       if (tid == 0 && !*s_abort && !(last_tile && l == ETC_LAYERS - 1)) load_w((l + 1) % ETC_LAYERS);
+      // MMA 8 has read XA: the next tile's X may land there now
+      if (tid == 0 && !*s_abort && !last_tile && l == ETC_LAYERS - 1) load_x(t0 + tile_stride);
       if (l == 0 || l == 2 || l == 4) {
         // feature_net.0 (GELU) and the rows riding along: [route head of the
         // previous level (n) | this level's to_3d (3)]
@@ -524,6 +513,7 @@ __global__ void __launch_bounds__(ETC_THREADS, 1)
   // unwind: no TMA may still write this CTA's shared memory, no MMA its TMEM
   __syncthreads();
   if (tid == 0 && w_pending) etc_wait(wbar, (wcount - (*s_abort ? 1u : 0u)) & 1u);
+  if (tid == 0 && x_pending) etc_wait(xbar, (xcount - (*s_abort ? 1u : 0u)) & 1u);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {

@@ -14,7 +14,22 @@
 
 #include "sm100.cuh"
 
+#include <type_traits>
+
 namespace sb {
+
+// An epilogue that needs whole rows (one n-tile covers N) declares
+// `static constexpr bool kWholeRow = true` and `apply_row(taddr, row, valid)`,
+// which reads the row's BN accumulator columns from TMEM itself (every lane of
+// the warp calls it; `valid` says whether the row exists).
+template <class E, class = void>
+struct EpiWholeRow {
+  static constexpr bool value = false;
+};
+template <class E>
+struct EpiWholeRow<E, std::void_t<decltype(E::kWholeRow)>> {
+  static constexpr bool value = E::kWholeRow;
+};
 
 constexpr int GEMM_BM = 128;
 constexpr int GEMM_BK = 64;  // 64 x 16-bit = one 128-byte swizzle row
@@ -180,6 +195,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN), r);
         tmem_ld_wait();
         if (row < M) epi.tail(row, r);
+      } else if constexpr (EpiWholeRow<Epi>::value) {
+        epi.apply_row(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN), row, row < M);
       } else {
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
