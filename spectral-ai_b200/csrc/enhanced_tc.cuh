@@ -89,6 +89,23 @@ __device__ __forceinline__ void etc_mma(uint32_t d_tmem, const uint8_t* a, const
   }
 }
 
+// One token's E values to a row-major [B, E] output: float4 stores when every
+// row starts on a 16-byte boundary (E a multiple of 4, aligned base), scalar
+// stores otherwise.
+template <int EP>
+__device__ __forceinline__ void etc_store_row(float* out, int64_t tok, int E, const float (&v)[EP]) {
+  float* row = out + tok * E;
+  if ((E & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15u) == 0) {
+#pragma unroll
+    for (int e = 0; e < EP; e += 4)
+      if (e < E) *reinterpret_cast<float4*>(row + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < EP; ++e)
+      if (e < E) row[e] = v[e];
+  }
+}
+
 // The per-token outputs after the expert head (thread = token): logits,
 // expert_probs / expert_ids, leaf distances, branch bonus and the gate.
 // sd: this tile's leaf distances in shared memory, [3 * ETC_MAXN][ETC_TOK].
@@ -96,11 +113,7 @@ template <int EP>
 __device__ __forceinline__ void etc_outputs(float (&lg)[EP], int64_t tok, int tid, const EnhTail& t, const EnhOut& o,
                                             const float* sd, const int (&amx)[3]) {
   const int E = t.E, n2 = t.n[1], n3 = t.n[2];
-  if (o.logits) {
-#pragma unroll
-    for (int e = 0; e < EP; e += 4)
-      if (e < E) *reinterpret_cast<float4*>(o.logits + tok * E + e) = make_float4(lg[e], lg[e + 1], lg[e + 2], lg[e + 3]);
-  }
+  if (o.logits) etc_store_row<EP>(o.logits, tok, E, lg);
   // expert_probs = softmax(logits / max(T, 0.1)); ids = first argmax (only
   // when an output or the hybrid gate's candidate ranking reads them).  v
   // holds them, then the gate's values (two arrays of EP live, not three).
@@ -128,11 +141,7 @@ __device__ __forceinline__ void etc_outputs(float (&lg)[EP], int64_t tok, int ti
         bi = e;
       }
     }
-    if (o.probs) {
-#pragma unroll
-      for (int e = 0; e < EP; e += 4)
-        if (e < E) *reinterpret_cast<float4*>(o.probs + tok * E + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-    }
+    if (o.probs) etc_store_row<EP>(o.probs, tok, E, v);
     if (o.ids) o.ids[tok] = bi;
     if (hybrid) {
       // BVH candidates: the n_cand first experts in the order (expert_probs
@@ -197,11 +206,7 @@ __device__ __forceinline__ void etc_outputs(float (&lg)[EP], int64_t tok, int ti
     }
 #pragma unroll
     for (int e = 0; e < EP; ++e) v[e] = v[e] / s2;
-    if (o.rprobs) {
-#pragma unroll
-      for (int e = 0; e < EP; e += 4)
-        if (e < E) *reinterpret_cast<float4*>(o.rprobs + tok * E + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-    }
+    if (o.rprobs) etc_store_row<EP>(o.rprobs, tok, E, v);
   } else {
     float mx = -INFINITY;
 #pragma unroll
@@ -218,11 +223,7 @@ __device__ __forceinline__ void etc_outputs(float (&lg)[EP], int64_t tok, int ti
       }
 #pragma unroll
       for (int e = 0; e < EP; ++e) v[e] = v[e] / s2;
-      if (o.rprobs) {
-#pragma unroll
-        for (int e = 0; e < EP; e += 4)
-          if (e < E) *reinterpret_cast<float4*>(o.rprobs + tok * E + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-      }
+      if (o.rprobs) etc_store_row<EP>(o.rprobs, tok, E, v);
     } else if (o.rprobs) {
       for (int e = 0; e < E; ++e) o.rprobs[tok * E + e] = 0.f;
     }

@@ -151,3 +151,48 @@ def test_dropin_modules(cuda_device):
         r.expert_head[2].bias.add_(1.0)
     r(x.to(cuda_device))  # softmax is shift-invariant: the logits show the update
     np.testing.assert_allclose(r._last_logits.cpu().numpy(), ologits + 1.0, rtol=1e-5, atol=3e-6)
+
+
+@pytest.mark.parametrize("branching", [(4, 4, 2), (3, 5, 2), (8, 2, 4), (2, 2, 2)])
+@pytest.mark.parametrize("gate", ["softmax", "topk_softmax", "hybrid"])
+def test_fast_engine_other_tree_shapes(cuda_device, branching, gate):
+    """The tensor-core tail at other trees (32, 30, 64 and 8 experts; up to 8
+    children per level) against the oracle, on bf16 hidden states."""
+    from sb200 import synth
+    from sb200.enhanced import EnhancedEngine
+    H = 256
+    E = int(np.prod(branching))
+    w = synth.enhanced_router_weights(H, branching=branching, seed=sum(branching))
+    w["expert_head.2.weight"] = (w["expert_head.2.weight"] * 10.0).astype(np.float32)
+    eng = EnhancedEngine(H, 128, branching, cuda_device)
+    eng.upload(w)
+    k = min(4, E)
+    xb = synth.hidden_states(300, H, seed=E, dtype=torch.bfloat16)
+    kw = {}
+    if gate == "hybrid":
+        wg = synth.dense_gate_weight(E, H, seed=E)
+        eng.set_dense_gate(torch.from_numpy(wg))
+        kw["n_candidates"] = max(k, E // 2)
+    out = eng.forward(xb.to(cuda_device), precision="fast", want=("logits", "expert_probs", "expert_ids"),
+                      gate=gate, k=k, **kw)
+    probs, ids, logits, _ = oe.router_forward(w, xb.float().numpy())
+    scale = max(1.0, float(np.abs(logits).max()) / 2.0)
+    lg = out["logits"].cpu().numpy()
+    assert np.abs(lg - logits).max() / max(1.0, np.abs(logits).max()) < 2e-2
+    assert topk_ids_match(probs, ids[:, None], out["expert_ids"].cpu().numpy()[:, None], 5e-2 * scale) == 0
+    tw = out["topk_weights"].cpu().numpy()
+    ti = out["topk_ids"].cpu().numpy()
+    assert ((ti >= 0) & (ti < E)).all()
+    assert (np.sort(ti, axis=1)[:, 1:] != np.sort(ti, axis=1)[:, :-1]).all()
+    if gate == "softmax":
+        rp, rw, ri = oe.gate_topk(logits, k, "softmax", False, "bf16")
+        assert topk_ids_match(gate_key(logits, "softmax", "bf16"), ri, ti, 2e-2 * scale) == 0
+        np.testing.assert_allclose(np.sort(tw, axis=1), np.sort(rw, axis=1), rtol=2e-2 * scale, atol=1e-6)
+    elif gate == "topk_softmax":
+        np.testing.assert_allclose(tw.sum(axis=1), 1.0, rtol=1e-5)
+    else:
+        full = out["router_probs"].cpu().numpy()
+        np.testing.assert_allclose(full.sum(axis=1), 1.0, rtol=1e-5)
+        # every chosen expert is among the BVH candidates of the kernel's own probabilities
+        cand = np.argsort(-out["expert_probs"].cpu().numpy(), axis=1, kind="stable")[:, :kw["n_candidates"]]
+        assert all(set(r) <= set(c) for r, c in zip(ti, cand))
