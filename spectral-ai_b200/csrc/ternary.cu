@@ -433,11 +433,22 @@ int ternary_engine() {
 }
 bool use_ts_engine() { return ternary_engine() != ENGINE_SS; }
 
+// MMA streams per pair tile.  One issuing thread is the default: two streams
+// (SB_PAIR_STREAMS=2) measured 3 % slower on the OLMoE layer (gate/up 0.263 vs
+// 0.255 ms), so the issuer's per-block stall is not hidden by a second issuer.
+int pair_streams() {
+  static const int n = [] {
+    const char* e = getenv("SB_PAIR_STREAMS");
+    return (e && strcmp(e, "2") == 0) ? 2 : 1;
+  }();
+  return n;
+}
+
 // CTA pairs (clusters of two) as many as fit at once, one persistent pair per two SMs.
-template <int MODE, int FMT>
-int launch_pair(const char* name, const CUtensorMap& tx, const CUtensorMap& tw0, const CUtensorMap& tw1,
-                const CUtensorMap& tout, const TernGemmParams& p, cudaStream_t stream) {
-  auto kern = ternary_pair_kernel<MODE, FMT>;
+template <int MODE, int FMT, int STREAMS>
+int launch_pair_s(const char* name, const CUtensorMap& tx, const CUtensorMap& tw0, const CUtensorMap& tw1,
+                  const CUtensorMap& tout, const TernGemmParams& p, cudaStream_t stream) {
+  auto kern = ternary_pair_kernel<MODE, FMT, STREAMS>;
   static int pairs[64] = {};
   int dev = 0;
   SB_CUDA_TRY(cudaGetDevice(&dev));
@@ -465,6 +476,13 @@ int launch_pair(const char* name, const CUtensorMap& tx, const CUtensorMap& tw0,
   ProfScope prof(name, stream);
   SB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tx, tw0, tw1, tout, p));
   return SB_OK;
+}
+
+template <int MODE, int FMT>
+int launch_pair(const char* name, const CUtensorMap& tx, const CUtensorMap& tw0, const CUtensorMap& tw1,
+                const CUtensorMap& tout, const TernGemmParams& p, cudaStream_t stream) {
+  return pair_streams() == 2 ? launch_pair_s<MODE, FMT, 2>(name, tx, tw0, tw1, tout, p, stream)
+                             : launch_pair_s<MODE, FMT, 1>(name, tx, tw0, tw1, tout, p, stream);
 }
 
 int check_ternary_shapes(int64_t H, int64_t I) {
@@ -537,7 +555,8 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   const bool pair = engine == ENGINE_PAIR;
   const uint32_t gu_box = pair ? 64 : 128, d_box = pair ? 128 : 256;
   const uint32_t p_words = pair ? TP_KB / 16 : 4;  // packed words per row in one weight box
-  const uint32_t x_rows = pair ? TP_HALF_ROWS : 128;  // token rows per activation box
+  // token rows per activation box: two 48-row boxes per CTA with two MMA streams
+  const uint32_t x_rows = pair ? (pair_streams() == 2 ? TP_QROWS : TP_HALF_ROWS) : 128;
   if ((rc = make_tmap_2d(&tmx, xp, adt, 2, L.Rp, H, L.ldx, 64, x_rows, CU_TENSOR_MAP_SWIZZLE_128B)) ||
       (rc = make_tmap_2d(&tmg, gate, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, p_words, gu_box,
                          CU_TENSOR_MAP_SWIZZLE_NONE)) ||

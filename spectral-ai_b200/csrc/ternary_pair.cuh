@@ -64,6 +64,7 @@ constexpr int TP_A_STAGES = 2;
 constexpr int TP_KB = 128;                           // K per block
 constexpr int TP_TILE_ROWS = 192;                    // tokens per tile (both CTAs)
 constexpr int TP_HALF_ROWS = TP_TILE_ROWS / 2;       // token rows loaded by each CTA
+constexpr int TP_QROWS = TP_HALF_ROWS / 2;           // rows per activation box (two boxes per CTA)
 constexpr int TP_XATOM_BYTES = TP_HALF_ROWS * 128;   // 12 KB: 96 token rows x 64 K
 constexpr int TP_X_BYTES = 2 * TP_XATOM_BYTES;       // 24 KB: 96 token rows x 128 K
 constexpr int TP_P_BYTES = 128 * 32;                 // 4 KB: 128 channels x 128 K at 2 bits
@@ -97,7 +98,14 @@ __device__ __forceinline__ void tmem_st_32x32b_x32_p(uint32_t taddr, const uint3
       : "memory");
 }
 
-template <int MODE, int FMT>
+// STREAMS = 2: a tile of P tokens, P a multiple of 64, is computed by two MMA
+// streams of N = P/2, each issued by its own thread (warps 1 and 3 of the even CTA) into
+// its half of the accumulator.  Each CTA holds stream 0's quarter of the
+// tokens in shared-memory rows 0.. and stream 1's in rows TP_QROWS.., so each
+// stream's B operand is a contiguous run of rows and the accumulator columns
+// stay in token order.  While one issuer waits on a barrier (a few hundred
+// cycles once its MMAs are queued), the other keeps the tensor pipe fed.
+template <int MODE, int FMT, int STREAMS>
 __global__ void __launch_bounds__(TP_THREADS, 1)
     ternary_pair_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW0,
                         const __grid_constant__ CUtensorMap tmW1, const __grid_constant__ CUtensorMap tmOut,
@@ -128,11 +136,11 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
     for (int s = 0; s < TP_STAGES; ++s) {
       mbar_init(&full_x[s], 1);
       mbar_init(&full_p[s], 1);
-      mbar_init(&xp_empty[s], 1);
+      mbar_init(&xp_empty[s], STREAMS);  // one commit per MMA stream
     }
     for (int s = 0; s < TP_A_STAGES; ++s) mbar_init(&full_a[s], 8);  // 4 unpack warps x 2 CTAs
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&tfull[b], 1);
+      mbar_init(&tfull[b], STREAMS);
       mbar_init(&tempty[b], 2 * TP_EPI_WARPS);
     }
     fence_barrier_init();
@@ -159,7 +167,12 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
         const MTile mt = p.mtiles[tile / p.n_ntiles];
         const int c0 = (tile % p.n_ntiles) * CPAIR + (int)rank * CCTA;
         const int wrow = mt.expert * p.b_rows + c0;
-        const int xrow = mt.row0 + (int)rank * (mt.pad >> 1);  // this CTA's half of the tokens
+        // this CTA's tokens: stream 0's quarter (rows 0..) and stream 1's
+        // (rows TP_QROWS..); one stream per CTA half when the tile is small
+        const bool two = STREAMS == 2 && (mt.pad & 63) == 0;  // stream N = pad/2, a multiple of 32
+        const int q = two ? mt.pad >> 2 : mt.pad >> 1;
+        const int xrow0 = mt.row0 + (int)rank * q;
+        const int xrow1 = mt.row0 + (mt.pad >> 1) + (int)rank * q;
         for (int kb = 0; kb < kblocks; ++kb) {
           if (!mbar_wait(&xp_empty[stage], phase ^ 1u, ST_TIMEOUT_PRODUCER)) goto done;
           uint8_t* st = smem + stage * TP_STAGE_BYTES;
@@ -172,8 +185,17 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
           }
           if (rank == 0) mbar_arrive_expect_tx(&full_x[stage], 2 * TP_X_BYTES);
           const uint32_t fx = mapa_shared(smem_u32(&full_x[stage]), 0);
-          tma_load_2d_pair(st, &tmX, fx, kb * TP_KB, xrow);
-          tma_load_2d_pair(st + TP_XATOM_BYTES, &tmX, fx, kb * TP_KB + 64, xrow);
+          if (STREAMS == 2) {
+            // 48-row boxes: rows 0..47 and 48..95 of each 64-K atom
+            const int h = TP_QROWS * 128;
+            tma_load_2d_pair(st, &tmX, fx, kb * TP_KB, xrow0);
+            tma_load_2d_pair(st + h, &tmX, fx, kb * TP_KB, two ? xrow1 : xrow0 + TP_QROWS);
+            tma_load_2d_pair(st + TP_XATOM_BYTES, &tmX, fx, kb * TP_KB + 64, xrow0);
+            tma_load_2d_pair(st + TP_XATOM_BYTES + h, &tmX, fx, kb * TP_KB + 64, two ? xrow1 : xrow0 + TP_QROWS);
+          } else {
+            tma_load_2d_pair(st, &tmX, fx, kb * TP_KB, xrow0);
+            tma_load_2d_pair(st + TP_XATOM_BYTES, &tmX, fx, kb * TP_KB + 64, xrow0);
+          }
           if (++stage == TP_STAGES) {
             stage = 0;
             phase ^= 1u;
@@ -181,17 +203,22 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
         }
       }
     }
-  } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer (rank 0)
+  } else if (warp == 1 || (STREAMS == 2 && warp == 3)) {
+    // ------------------------------------------------------------ MMA issuers (rank 0)
+    const int sid = warp == 1 ? 0 : 1;  // this thread's MMA stream
     if (lane == 0 && rank == 0) {
       int stage = 0, astage = 0;
       uint32_t phase = 0, aphase = 0;
       int local = 0;
       for (int tile = pair; tile < num_tiles; tile += npairs, ++local) {
         const MTile mt = p.mtiles[tile / p.n_ntiles];
-        const uint32_t idesc = idesc_f16(FMT, 256, mt.pad);
+        const bool two = STREAMS == 2 && (mt.pad & 63) == 0;  // stream N = pad/2, a multiple of 32
+        const int n = two ? mt.pad >> 1 : mt.pad;  // this stream's tokens
+        const bool active = two || sid == 0;       // stream 1 idles on small tiles (commits only)
+        const uint32_t idesc = idesc_f16(FMT, 256, (uint32_t)n);
         const int buf = local & 1;
-        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * TP_D_COLS);
+        const uint32_t d_tmem = tmem_base + (uint32_t)(buf * TP_D_COLS) + (uint32_t)(sid * n);
+        const uint32_t b_off = (uint32_t)(sid * TP_QROWS * 128) >> 4;  // stream's rows in the slot
         if (!mbar_wait_cluster(&tempty[buf], ((uint32_t)(local >> 1) & 1u) ^ 1u, ST_TIMEOUT_MMA)) goto done;
         tc_fence_after();
         bool ready = false;  // this K-block's full_a was seen complete by the previous peek
@@ -207,11 +234,14 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
           const bool peek = kb + 1 < kblocks && mbar_try_wait(smem_u32(&full_a[nastage]), naphase);
           const uint64_t bdesc = sdesc_sw128(smem_u32(smem + stage * TP_STAGE_BYTES));
           const uint32_t a_tmem = tmem_base + TP_A_BASE + (uint32_t)(astage * TP_A_COLS);
+          if (active) {
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            // K 16k..16k+15: A columns 8k..; B in the first or second 64-K atom
-            const uint64_t bk = bdesc + (k < 4 ? 2u * k : (uint32_t)(TP_XATOM_BYTES >> 4) + 2u * (k - 4));
-            umma_ts_pair(d_tmem, a_tmem + 8u * k, bk, idesc, (kb | k) != 0);
+            for (int k = 0; k < 8; ++k) {
+              // K 16k..16k+15: A columns 8k..; B in the first or second 64-K atom
+              const uint64_t bk =
+                  bdesc + b_off + (k < 4 ? 2u * k : (uint32_t)(TP_XATOM_BYTES >> 4) + 2u * (k - 4));
+              umma_ts_pair(d_tmem, a_tmem + 8u * k, bk, idesc, (kb | k) != 0);
+            }
           }
           // frees the slot's token tile and packed words, and the A stage this
           // K-block read (the unpack warps wait on this barrier for both)
