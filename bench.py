@@ -443,6 +443,31 @@ def legacy_tree_rates(dev, pk, world, steps, warmup):
     return res
 
 
+def optix_route_rates(dev, world, steps, warmup):
+    """The OptiX router's route / route_topk served by CUDA (optix_training_ext
+    drop-in): 65,536 queries against 64 expert octahedra, one ray and the
+    8-ray fan, queries/s."""
+    import numpy as np
+    import torch
+    import optix_training_ext as ext
+    g = np.random.default_rng(0)
+    centers = torch.from_numpy((g.standard_normal((64, 3)) * 3.0).astype(np.float32))
+    radii = torch.from_numpy((0.4 + 0.6 * g.random(64)).astype(np.float32))
+    B = 65536
+    pos = torch.from_numpy((g.standard_normal((B, 3)) * 2.0).astype(np.float32)).to(dev)
+    d = g.standard_normal((B, 3))
+    dirs = torch.from_numpy((d / np.linalg.norm(d, axis=1, keepdims=True)).astype(np.float32)).to(dev)
+    ext.initialize("", "")
+    ext.build_gas(centers, radii, use_triangles=True)
+    res = {"queries": B, "experts": 64, "geometry": "octahedra (use_triangles=True)"}
+    for name, fn in (("route", lambda: ext.route_async(pos, dirs)),
+                     ("route_topk8", lambda: ext._route(pos, dirs, 8, False))):
+        ms, _ = time_steps(fn, steps, warmup, world)
+        res[name] = {"ms": round(ms / steps, 4), "queries_per_s": round(B / (ms / steps / 1e3), 1)}
+    ext.shutdown()
+    return res
+
+
 def cpu_enhanced_rate(sample_tokens: int, budget_s: float = 8.0):
     """Oracle port of the enhanced router + gate on the host cores (tokens/s)."""
     from oracle import enhanced as oe
@@ -740,6 +765,7 @@ def run_ours(a):
     if not a.skip_enhanced:
         out["pipeline_stages"] = pipeline_stage_rates(dev, pk, world, min(a.steps, 50), a.warmup)
         out["legacy_tree"] = legacy_tree_rates(dev, pk, world, min(a.steps, 50), a.warmup)
+        out["optix_route"] = optix_route_rates(dev, world, min(a.steps, 50), a.warmup)
     # ---- router alone (config 1), same process
     if not a.skip_router:
         rstep, _, rmeta = router_workload(a.router_batch, dev)

@@ -380,6 +380,24 @@ int bvh_get_num_nodes(void);
 int bvh_get_num_experts(void);
 int bvh_get_spec_dim(void);
 
+/* ------------------------------------------------------------------------ */
+/* The OptiX router's route / route_topk served by CUDA                       */
+/* (cuda/v5/optix_training_ext.cu:182-263; programs cuda/optix_router_raygen.cu, */
+/* cuda/optix_router_hitgroup.cu; geometry cuda/optix_router_host.cpp:372-600). */
+/* Experts are spheres (center, radius) drawn as octahedra (use_triangles) or  */
+/* boxes; a ray's closest hit in t in [0.001, 1000] gives (expert, t), a miss  */
+/* (-1, 1e30).  top_k > 1 traces the reference's fan of k rays.               */
+/* ------------------------------------------------------------------------ */
+typedef struct sb_gas sb_gas;
+int sb_gas_create(int device, sb_gas** out);
+/* Host fp32 centers [n,3], radii [n]; n <= 4096. */
+int sb_gas_build(sb_gas* h, const float* centers, const float* radii, int n_experts, int use_triangles);
+/* Device fp32 positions/directions [B,3]; expert_ids/distances [B] (first ray
+ * of the fan when top_k > 1); topk_ids/topk_dists [B,k] may be NULL. */
+int sb_gas_route(sb_gas* h, const float* positions, const float* directions, int64_t batch, int top_k,
+                 int32_t* expert_ids, float* distances, int32_t* topk_ids, float* topk_dists, void* stream);
+int sb_gas_destroy(sb_gas* h);
+
 /* output [B,H] = sum_j weights[t,j] * expert_outputs[t,j,:] in slot order with
  * one fused multiply-add per term (weighted_combine_kernel, async_pipeline.cu:112-132). */
 int sb_weighted_combine(const float* expert_outputs, const float* weights, int64_t batch, int hidden,

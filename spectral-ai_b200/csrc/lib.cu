@@ -7,3 +7,4 @@
 #include "enhanced.cu"
 #include "pipeline.cu"
 #include "tree.cu"
+#include "gas.cu"

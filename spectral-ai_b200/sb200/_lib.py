@@ -145,6 +145,12 @@ SIGNATURES = [
     ("bvh_get_num_nodes", C.c_int, []),
     ("bvh_get_num_experts", C.c_int, []),
     ("bvh_get_spec_dim", C.c_int, []),
+    ("sb_gas_create", C.c_int, [C.c_int, C.POINTER(C.c_void_p)]),
+    ("sb_gas_build", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
+    ("sb_gas_route", C.c_int,
+     [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+      C.c_void_p]),
+    ("sb_gas_destroy", C.c_int, [C.c_void_p]),
 ]
 
 _lib = None
