@@ -867,20 +867,31 @@ def run_reference(a):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    sample = a.cpu_sample
     from oracle import router as orouter
     from oracle import ternary as otern
     from sb200 import synth
     cores = blas_threads()
     w = synth.router_weights(H, S, BRANCHING, seed=0)
     experts = synth.ternary_experts(E_EXPERTS, H, I_INTER, seed=2)
-    x = synth.hidden_states(sample, H, seed=2).numpy()
+    xall = synth.hidden_states(max(a.cpu_sample, 64), H, seed=2).numpy()
+
+    def run(xs):
+        o = orouter.router_forward(w, xs, BRANCHING, mode="soft", k=TOPK)
+        otern.moe_combine(xs, o["topk_ids"], o["topk_weights"], experts, fp32=True)
+
+    # a bounded sample per step: sized from one 64-token probe so that the
+    # requested W + K steps take about two minutes (16 .. cpu_sample tokens)
+    t0 = time.perf_counter()
+    run(xall[:64])
+    per_tok = (time.perf_counter() - t0) / 64
+    budget = 120.0 / max(a.steps + a.warmup, 1)
+    sample = int(max(16, min(a.cpu_sample, budget / max(per_tok, 1e-9))))
+    x = xall[:sample]
 
     def one():
-        o = orouter.router_forward(w, x, BRANCHING, mode="soft", k=TOPK)
-        otern.moe_combine(x, o["topk_ids"], o["topk_weights"], experts, fp32=True)
+        run(x)
 
-    for _ in range(max(a.warmup, 1)):
+    for _ in range(a.warmup):
         one()
     t0 = time.perf_counter()
     for _ in range(a.steps):
@@ -922,8 +933,6 @@ def main():
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3) if a.impl == "ours" else a.warmup
     if a.impl == "reference":
-        a.steps = min(a.steps, 8)
-        a.warmup = min(a.warmup, 1)
         run_reference(a)
     else:
         run_ours(a)
