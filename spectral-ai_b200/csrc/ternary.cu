@@ -23,6 +23,7 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <type_traits>
 
 namespace sb {
 
@@ -137,13 +138,38 @@ __global__ void __launch_bounds__(PLAN_THREADS) moe_plan_kernel(const int32_t* _
   if (hist) {
     for (int e = tid; e < E; e += PLAN_THREADS) sh_count[e] = 0;
     __syncthreads();
-    for (int64_t i = tid; i < R; i += PLAN_THREADS) {
-      const int e = ids[i];
+    auto count = [&](int e) {
       if (e >= 0 && e < E)
         atomicAdd(&sh_count[e], 1);
       else
         set_status(ST_BAD_ARGUMENT);
+    };
+    int64_t i0 = 0;
+    if ((reinterpret_cast<uintptr_t>(ids) & 15u) == 0) {
+      // 16-byte words, eight a thread loaded before any is counted: one
+      // memory round trip per 32 Ki ids instead of one per 1 Ki
+      const int4* ids4 = reinterpret_cast<const int4*>(ids);
+      const int64_t R4 = R >> 2;
+      for (int64_t b = 0; b < R4; b += 8 * PLAN_THREADS) {
+        int4 w[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          const int64_t j = b + u * PLAN_THREADS + tid;
+          if (j < R4) w[u] = __ldg(ids4 + j);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (b + u * PLAN_THREADS + tid < R4) {
+            count(w[u].x);
+            count(w[u].y);
+            count(w[u].z);
+            count(w[u].w);
+          }
+        }
+      }
+      i0 = R4 << 2;
     }
+    for (int64_t i = i0 + tid; i < R; i += PLAN_THREADS) count(ids[i]);
     __syncthreads();
   }
   // each thread owns a run of consecutive experts
@@ -230,6 +256,8 @@ template <> __device__ __forceinline__ __half cvt_act<float, __half>(float v) { 
 template <> __device__ __forceinline__ __nv_bfloat16 cvt_act<__nv_bfloat16, __nv_bfloat16>(__nv_bfloat16 v) { return v; }
 template <> __device__ __forceinline__ __half cvt_act<__nv_bfloat16, __half>(__nv_bfloat16 v) { return __float2half_rn(__bfloat162float(v)); }
 
+constexpr int SCATTER_REG_ROW = 8 * 32 * 8;  // bf16 row width held in a warp's registers
+
 // One warp per (token, slot) pair: claim a row of the expert's segment, record
 // the routing weight and the inverse map, and copy the token's activations.
 // 16-byte vector row copies (bf16 -> bf16: 8 values per lane step; fp32 -> fp16: 4)
@@ -259,6 +287,30 @@ __global__ void moe_scatter_kernel(const TX* __restrict__ x, const int32_t* __re
   for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < R;
        i += ((int64_t)gridDim.x * blockDim.x) >> 5) {
     const int e = ids[i];
+    if constexpr (std::is_same<TX, __nv_bfloat16>::value && std::is_same<TA, __nv_bfloat16>::value) {
+      if (vec && H <= SCATTER_REG_ROW) {
+        // The whole row (up to 2048 bf16: eight 16-byte words a lane) is
+        // loaded into registers before the slot is claimed, so its loads are
+        // in flight during the claim's atomic round trip.
+        const uint4* s4 = reinterpret_cast<const uint4*>(x + (i / k) * (int64_t)H);
+        const int n = H >> 3;
+        uint4 v[8];
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (lane + 32 * u < n) v[u] = __ldg(s4 + lane + 32 * u);
+        int pos = -1;
+        if (lane == 0 && e >= 0 && e < E) pos = offsets[e] + atomicAdd(&cursor[e], 1);
+        pos = __shfl_sync(0xffffffffu, pos, 0);
+        if (lane == 0) inv[i] = pos;
+        if (pos < 0) continue;
+        if (lane == 0) row_w[pos] = wts ? wts[i] : 1.0f;
+        uint4* d4 = reinterpret_cast<uint4*>(xp + (int64_t)pos * ldx);
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (lane + 32 * u < n) d4[lane + 32 * u] = v[u];
+        continue;
+      }
+    }
     int pos = -1;
     if (lane == 0 && e >= 0 && e < E) pos = offsets[e] + atomicAdd(&cursor[e], 1);
     pos = __shfl_sync(0xffffffffu, pos, 0);
@@ -293,7 +345,9 @@ __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* p, float4 v
 
 // out[t] = sum_j y[inv[t*k+j]] in slot order (fixed, so results are reproducible).
 // Vector path: one thread per 4 columns (needs H % 4 == 0).
-template <typename TO>
+// KC > 0: k == KC known at compile time; the k row indices, then the k
+// float4 loads, go out before the sums (same slot order, same results).
+template <typename TO, int KC>
 __global__ void moe_combine_kernel(const float* __restrict__ y, const int* __restrict__ inv, int64_t B,
                                    int k, int H, TO* __restrict__ out) {
   if ((H & 3) == 0) {
@@ -304,6 +358,25 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int* __res
       const int64_t t = i / H4;
       const int c = (int)(i % H4) * 4;
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      if constexpr (KC > 0) {
+        int pos[KC];
+        float4 v[KC];
+#pragma unroll
+        for (int j = 0; j < KC; ++j) pos[j] = __ldg(inv + t * KC + j);
+#pragma unroll
+        for (int j = 0; j < KC; ++j)
+          if (pos[j] >= 0) v[j] = __ldg(reinterpret_cast<const float4*>(y + (int64_t)pos[j] * H + c));
+#pragma unroll
+        for (int j = 0; j < KC; ++j)
+          if (pos[j] >= 0) {
+            acc.x += v[j].x;
+            acc.y += v[j].y;
+            acc.z += v[j].z;
+            acc.w += v[j].w;
+          }
+        store4<TO>(out + t * H + c, acc);
+        continue;
+      }
       for (int j = 0; j < k; ++j) {
         const int pos = __ldg(inv + t * k + j);
         if (pos >= 0) {
@@ -527,16 +600,19 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   // the pair engine stores y rows with TMA: its row pitch (H floats) must be a 16-byte multiple
   int engine = ternary_engine();
   if (engine == ENGINE_PAIR && (H % 4) != 0) engine = ENGINE_TS;
+  const bool x16 = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
 
   {
-    ProfScope prof("moe_dispatch", stream);
     const int64_t R = L.R;
-    if ((rc = moe_plan(ids, R, E, counts, offsets, cursor, mtiles, nmt, (int)L.max_mt,
-                       engine == ENGINE_PAIR ? TP_TILE_ROWS : 128, stream)))
-      return rc;
+    {
+      ProfScope prof_plan("moe_plan", stream);
+      if ((rc = moe_plan(ids, R, E, counts, offsets, cursor, mtiles, nmt, (int)L.max_mt,
+                         engine == ENGINE_PAIR ? TP_TILE_ROWS : 128, stream)))
+        return rc;
+    }
+    ProfScope prof("moe_dispatch", stream);
     int64_t wblocks = (R * 32 + 255) / 256;
     if (wblocks > (int64_t)num_sms() * 16) wblocks = (int64_t)num_sms() * 16;
-    const bool x16 = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
     if (x_dtype == SB_BF16)
       moe_scatter_kernel<__nv_bfloat16, __nv_bfloat16><<<(unsigned)wblocks, 256, 0, stream>>>(
           static_cast<const __nv_bfloat16*>(x), ids, weights, B, k, (int)H, E, offsets, cursor,
@@ -619,11 +695,21 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
     ProfScope prof("moe_combine", stream);
     int64_t blocks = (B * H + 255) / 256;
     if (blocks > (int64_t)num_sms() * 32) blocks = (int64_t)num_sms() * 32;
-    if (out_dtype == SB_F32)
-      moe_combine_kernel<float><<<(unsigned)blocks, 256, 0, stream>>>(yp, inv, B, k, (int)H, static_cast<float*>(out));
-    else
-      moe_combine_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, stream>>>(yp, inv, B, k, (int)H,
-                                                                               static_cast<__nv_bfloat16*>(out));
+    if (out_dtype == SB_F32) {
+      if (k == 8)
+        moe_combine_kernel<float, 8><<<(unsigned)blocks, 256, 0, stream>>>(yp, inv, B, k, (int)H,
+                                                                          static_cast<float*>(out));
+      else
+        moe_combine_kernel<float, 0><<<(unsigned)blocks, 256, 0, stream>>>(yp, inv, B, k, (int)H,
+                                                                          static_cast<float*>(out));
+    } else {
+      if (k == 8)
+        moe_combine_kernel<__nv_bfloat16, 8><<<(unsigned)blocks, 256, 0, stream>>>(
+            yp, inv, B, k, (int)H, static_cast<__nv_bfloat16*>(out));
+      else
+        moe_combine_kernel<__nv_bfloat16, 0><<<(unsigned)blocks, 256, 0, stream>>>(
+            yp, inv, B, k, (int)H, static_cast<__nv_bfloat16*>(out));
+    }
     SB_CUDA_TRY(cudaGetLastError());
   }
   return SB_OK;
