@@ -87,6 +87,20 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
   return ok != 0;
 }
 
+// Non-blocking poll (test_wait): never suspends the thread, unlike try_wait,
+// which may hold it until the phase completes or a system time limit passes.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar_addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(bar_addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
 // try_wait that may suspend the thread until the phase completes or `ns`
 // nanoseconds pass: a waiting warp sleeps instead of spinning, which leaves
 // the issue slots of its scheduler to the warps that are working.

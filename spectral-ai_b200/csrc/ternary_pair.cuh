@@ -231,7 +231,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
           // the MMA issue below, and the result is only used in the next pass
           const int nastage = astage + 1 == TP_A_STAGES ? 0 : astage + 1;
           const uint32_t naphase = nastage == 0 ? aphase ^ 1u : aphase;
-          const bool peek = kb + 1 < kblocks && mbar_try_wait(smem_u32(&full_a[nastage]), naphase);
+          const bool peek = kb + 1 < kblocks && mbar_test_wait(smem_u32(&full_a[nastage]), naphase);
           const uint64_t bdesc = sdesc_sw128(smem_u32(smem + stage * TP_STAGE_BYTES));
           const uint32_t a_tmem = tmem_base + TP_A_BASE + (uint32_t)(astage * TP_A_COLS);
           if (active) {
