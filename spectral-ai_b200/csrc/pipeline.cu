@@ -268,15 +268,34 @@ __global__ void __launch_bounds__(PIPE_THREADS) pipe_combine_kernel(const float*
 // ---------------------------------------------------------------------------
 constexpr int PIPE_TOK = 128;
 
+// Two fp32 lanes in a 64-bit register; d = a * b + c per lane, each rounded
+// once like fmaf.
+__device__ __forceinline__ uint64_t pipe_pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void pipe_unpack2(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t pipe_ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+
 template <int EP>
-__global__ void __launch_bounds__(PIPE_TOK) pipe_topk_thread_kernel(
+__global__ void __launch_bounds__(PIPE_TOK, 3) pipe_topk_thread_kernel(
     const float* __restrict__ logits, int64_t B, int E, int k, const float* __restrict__ cal_w,
     const float* __restrict__ cal_b, int apply_softmax, int only_calibrate, float* __restrict__ probs,
     uint32_t* __restrict__ ids, float* __restrict__ wts) {
+  // tile rows of EP + 4 floats: 16-byte aligned, and a quarter-warp's float4
+  // reads of eight consecutive rows fall in distinct banks
+  constexpr int LD = EP + 4;
   extern __shared__ __align__(16) float pipe_dsm[];
   float* wt_s = pipe_dsm;             // [EP][EP] W transposed: wt_s[j*EP + e] = W[e][j]
   float* b_s = wt_s + EP * EP;        // [EP]
-  float* tile = b_s + EP;             // [PIPE_TOK][EP + 1] token rows, padded against bank conflicts
+  float* tile = b_s + EP;             // [PIPE_TOK][LD] token rows, zero past E
   const int tid = threadIdx.x;
   if (cal_w) {
     for (int i = tid; i < EP * EP; i += PIPE_TOK) {
@@ -285,36 +304,62 @@ __global__ void __launch_bounds__(PIPE_TOK) pipe_topk_thread_kernel(
     }
     for (int e = tid; e < EP; e += PIPE_TOK) b_s[e] = (e < E && cal_b) ? __ldg(cal_b + e) : 0.f;
   }
+  const bool vec = E == EP && (reinterpret_cast<uintptr_t>(logits) & 15u) == 0;
+  const int E4 = (E + 3) >> 2;  // row length in float4 (zero padded)
   for (int64_t t0 = (int64_t)blockIdx.x * PIPE_TOK; t0 < B; t0 += (int64_t)gridDim.x * PIPE_TOK) {
     const int ntok = (int)((B - t0) < PIPE_TOK ? (B - t0) : PIPE_TOK);
     __syncthreads();
-    if (E == EP) {
-      for (int i = tid; i < ntok * EP; i += PIPE_TOK) tile[(i / EP) * (EP + 1) + i % EP] = __ldg(logits + t0 * E + i);
+    if (vec) {
+      // the tile's rows as float4, all of a thread's loads in flight before
+      // the first store to shared memory
+      constexpr int Q = EP / 4;  // float4 per row; PIPE_TOK rows, so Q per thread
+      const float4* src = reinterpret_cast<const float4*>(logits + t0 * EP);
+      float4 r4[Q];
+#pragma unroll
+      for (int u = 0; u < Q; ++u) {
+        const int i = tid + u * PIPE_TOK;
+        if (i < ntok * Q) r4[u] = __ldg(src + i);
+      }
+#pragma unroll
+      for (int u = 0; u < Q; ++u) {
+        const int i = tid + u * PIPE_TOK;
+        if (i < ntok * Q) *reinterpret_cast<float4*>(tile + (i / Q) * LD + (i % Q) * 4) = r4[u];
+      }
     } else {
-      for (int i = tid; i < ntok * E; i += PIPE_TOK) tile[(i / E) * (EP + 1) + i % E] = __ldg(logits + t0 * E + i);
+      for (int i = tid; i < ntok * E4 * 4; i += PIPE_TOK) {
+        const int r = i / (E4 * 4), c = i % (E4 * 4);
+        tile[r * LD + c] = c < E ? __ldg(logits + (t0 + r) * E + c) : 0.f;
+      }
     }
     __syncthreads();
-    const float* myrow = tile + tid * (EP + 1);
+    const float* myrow = tile + tid * LD;
     float v[EP];
     if (cal_w) {
-      // c[e] = b[e] + sum_j W[e][j] raw[j], j ascending: raw[j] from this
-      // thread's row, W's row j as float4 broadcasts; the loop stays rolled
-      // (a fully unrolled E x E body overflows the instruction cache)
+      // c[e] = b[e] + sum_j W[e][j] raw[j], j ascending: raw[j..j+3] as one
+      // float4 of this thread's row, W's row j as float4 broadcasts; the loop
+      // stays rolled (a fully unrolled E x E body overflows the instruction cache)
+      // two experts per instruction (fma.rn.f32x2: each lane one fmaf)
+      uint64_t vp[EP / 2];
 #pragma unroll
-      for (int e = 0; e < EP; ++e) v[e] = b_s[e];
-#pragma unroll 2
-      for (int j = 0; j < E; ++j) {
-        const float rj = tid < ntok ? myrow[j] : 0.f;
-        const float4* wr = reinterpret_cast<const float4*>(wt_s + j * EP);
+      for (int q = 0; q < EP / 2; ++q) vp[q] = *reinterpret_cast<const uint64_t*>(b_s + 2 * q);
+#pragma unroll 1
+      for (int j4 = 0; j4 < E4; ++j4) {
+        const float4 r4 = tid < ntok ? *reinterpret_cast<const float4*>(myrow + 4 * j4) : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float rr[4] = {r4.x, r4.y, r4.z, r4.w};
 #pragma unroll
-        for (int q = 0; q < EP / 4; ++q) {
-          const float4 w4 = wr[q];
-          v[4 * q + 0] = fmaf(w4.x, rj, v[4 * q + 0]);
-          v[4 * q + 1] = fmaf(w4.y, rj, v[4 * q + 1]);
-          v[4 * q + 2] = fmaf(w4.z, rj, v[4 * q + 2]);
-          v[4 * q + 3] = fmaf(w4.w, rj, v[4 * q + 3]);
+        for (int jj = 0; jj < 4; ++jj) {
+          const uint64_t r2 = pipe_pack2(rr[jj], rr[jj]);
+          const ulonglong2* wr = reinterpret_cast<const ulonglong2*>(wt_s + (4 * j4 + jj) * EP);
+#pragma unroll
+          for (int q = 0; q < EP / 4; ++q) {
+            const ulonglong2 w4 = wr[q];
+            vp[2 * q + 0] = pipe_ffma2(w4.x, r2, vp[2 * q + 0]);
+            vp[2 * q + 1] = pipe_ffma2(w4.y, r2, vp[2 * q + 1]);
+          }
         }
       }
+#pragma unroll
+      for (int q = 0; q < EP / 2; ++q) pipe_unpack2(vp[q], v[2 * q], v[2 * q + 1]);
     } else {
 #pragma unroll
       for (int e = 0; e < EP; ++e) v[e] = (e < E && tid < ntok) ? myrow[e] : 0.f;
@@ -338,9 +383,9 @@ __global__ void __launch_bounds__(PIPE_TOK) pipe_topk_thread_kernel(
       __syncthreads();
 #pragma unroll
       for (int e = 0; e < EP; ++e)
-        if (e < E) tile[tid * (EP + 1) + e] = v[e];
+        if (e < E) tile[tid * LD + e] = v[e];
       __syncthreads();
-      for (int i = tid; i < ntok * E; i += PIPE_TOK) probs[t0 * E + i] = tile[(i / E) * (EP + 1) + i % E];
+      for (int i = tid; i < ntok * E; i += PIPE_TOK) probs[t0 * E + i] = tile[(i / E) * LD + i % E];
     }
     if (only_calibrate || tid >= ntok) continue;
     const int64_t t = t0 + tid;
@@ -477,12 +522,12 @@ int pipe_launch_softmax_topk(const float* logits, int64_t B, int E, int k, const
     if (tb > tcap) tb = tcap;
     ProfScope prof(name, stream);
     if (E <= 32) {
-      const size_t sm = (size_t)(32 * 32 + 32 + PIPE_TOK * 33) * sizeof(float);
+      const size_t sm = (size_t)(32 * 32 + 32 + PIPE_TOK * 36) * sizeof(float);
       pipe_topk_thread_kernel<32><<<(unsigned)tb, PIPE_TOK, sm, stream>>>(logits, B, E, k, cal_w, cal_b,
                                                                           apply_softmax, only_calibrate, probs, ids,
                                                                           wts);
     } else {
-      const size_t sm = (size_t)(64 * 64 + 64 + PIPE_TOK * 65) * sizeof(float);
+      const size_t sm = (size_t)(64 * 64 + 64 + PIPE_TOK * 68) * sizeof(float);
       static bool attr_done[64] = {};
       int dev = 0;
       SB_CUDA_TRY(cudaGetDevice(&dev));
