@@ -412,8 +412,9 @@ __global__ void __launch_bounds__(PIPE_TOK, 3) pipe_topk_thread_kernel(
 //   offsets: per expert, exclusive sum over the CTAs (and the totals)
 //   place:   CTA b walks its chunk in 1024-entry tiles; an entry's slot is its
 //            CTA offset + the tile's earlier entries of its expert (per-warp
-//            counts with a prefix over warps) + its rank among equal ids in
-//            its warp (__match_any_sync), so slots follow ascending entry order.
+//            counts, scanned over the warps by warp shuffles) + its rank among
+//            equal ids in its warp (the equal-id lanes from one ballot per id
+//            bit), so slots follow ascending entry order.
 // ---------------------------------------------------------------------------
 constexpr int SC_TILE = 1024;
 constexpr int SC_MAX_E = 512;
@@ -424,14 +425,19 @@ __global__ void __launch_bounds__(SC_TILE) pipe_scatter_hist_kernel(const uint32
   for (int e = threadIdx.x; e < E; e += SC_TILE) h_s[e] = 0;
   __syncthreads();
   const int64_t r0 = (int64_t)blockIdx.x * chunk, r1 = r0 + chunk < R ? r0 + chunk : R;
-  const int lane = threadIdx.x & 31;
-  for (int64_t rb = r0; rb < r1; rb += SC_TILE) {  // warp-uniform trip count
+  int64_t rb = r0;
+  for (; rb + 4 * SC_TILE <= r1; rb += 4 * SC_TILE) {  // four ids a thread in flight
+    uint32_t v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = __ldg(ids + rb + u * SC_TILE + threadIdx.x);
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (v[u] < (uint32_t)E) atomicAdd(&h_s[v[u]], 1);
+  }
+  for (; rb < r1; rb += SC_TILE) {
     const int64_t r = rb + threadIdx.x;
     const uint32_t id = r < r1 ? __ldg(ids + r) : 0xffffffffu;
-    const bool valid = id < (uint32_t)E;
-    // one shared-memory atomic per distinct id in the warp
-    const unsigned same = __match_any_sync(0xffffffffu, valid ? id : 0xffffffffu);
-    if (valid && (same & ((1u << lane) - 1u)) == 0) atomicAdd(&h_s[id], __popc(same));
+    if (id < (uint32_t)E) atomicAdd(&h_s[id], 1);
   }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += SC_TILE) hist[(int64_t)blockIdx.x * E + e] = h_s[e];
@@ -467,43 +473,61 @@ __global__ void __launch_bounds__(SC_TILE) pipe_scatter_offsets_kernel(int32_t* 
   if (b < nb) hist[(int64_t)b * E + e] = wsum[warp] + incl - c;
 }
 
+// Lanes of this warp whose key equals this lane's: one ballot per key bit
+// (keys below 2^nbits).
+__device__ __forceinline__ unsigned pipe_same_key(uint32_t key, int nbits) {
+  unsigned same = 0xffffffffu;
+  for (int b = 0; b < nbits; ++b) {
+    const bool bit = (key >> b) & 1u;
+    const unsigned bal = __ballot_sync(0xffffffffu, bit);
+    same &= bit ? bal : ~bal;
+  }
+  return same;
+}
+
 __global__ void __launch_bounds__(SC_TILE) pipe_scatter_place_kernel(const uint32_t* __restrict__ ids, int64_t R,
                                                                      int64_t chunk, int k, int E, int max_per,
                                                                      int store_entry, const int32_t* __restrict__ offs,
                                                                      int32_t* __restrict__ disp) {
   extern __shared__ int sm[];
-  int* base = sm;            // [E]
-  int* wc = sm + E;          // [32][E] per-warp counts -> exclusive prefix over warps
+  int* base = sm;            // [E] next slot of each expert for this CTA
+  int* tot = sm + E;         // [E] the tile's entries per expert
+  int* wc = sm + 2 * E;      // [E][32] per-warp counts -> exclusive prefix over the warps
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nbits = 32 - __clz(E);  // keys 0..E (E: no expert)
   for (int e = threadIdx.x; e < E; e += SC_TILE) base[e] = offs[(int64_t)blockIdx.x * E + e];
   const int64_t r0 = (int64_t)blockIdx.x * chunk, r1 = r0 + chunk < R ? r0 + chunk : R;
+  uint32_t next = r0 + threadIdx.x < r1 ? __ldg(ids + r0 + threadIdx.x) : 0xffffffffu;
   for (int64_t t0 = r0; t0 < r1; t0 += SC_TILE) {
+    const int64_t r = t0 + threadIdx.x;
+    const uint32_t id = next;  // loaded one tile ahead
+    next = r + SC_TILE < r1 ? __ldg(ids + r + SC_TILE) : 0xffffffffu;
     for (int i = threadIdx.x; i < 32 * E; i += SC_TILE) wc[i] = 0;
     __syncthreads();
-    const int64_t r = t0 + threadIdx.x;
-    const uint32_t id = r < r1 ? __ldg(ids + r) : 0xffffffffu;
     const bool valid = id < (uint32_t)E;
-    const unsigned same = __match_any_sync(0xffffffffu, valid ? id : 0xffffffffu);
+    const unsigned same = pipe_same_key(valid ? id : (uint32_t)E, nbits);
     const int rank = __popc(same & ((1u << lane) - 1u));
-    if (valid && rank == 0) wc[warp * E + id] = __popc(same);
+    if (valid && rank == 0) wc[id * 32 + warp] = __popc(same);
     __syncthreads();
-    int tot = 0;
-    for (int e = threadIdx.x; e < E; e += SC_TILE) {  // E <= SC_TILE: one expert per thread
-      int run = 0;
-      for (int w = 0; w < 32; ++w) {
-        const int c = wc[w * E + e];
-        wc[w * E + e] = run;
-        run += c;
+    // warp w scans experts w, w + 32, ...: lane = warp index of the tile
+    for (int e = warp; e < E; e += SC_TILE / 32) {
+      const int c = wc[e * 32 + lane];
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
       }
-      tot = run;
+      wc[e * 32 + lane] = incl - c;
+      if (lane == 31) tot[e] = incl;
     }
     __syncthreads();
     if (valid) {
-      const int slot = base[id] + wc[warp * E + id] + rank;
+      const int slot = base[id] + wc[id * 32 + warp] + rank;
       if (slot < max_per) disp[(int64_t)id * max_per + slot] = store_entry ? (int32_t)r : (int32_t)(r / k);
     }
     __syncthreads();
-    if (threadIdx.x < E) base[threadIdx.x] += tot;
+    for (int e = threadIdx.x; e < E; e += SC_TILE) base[e] += tot[e];
   }
 }
 
@@ -624,7 +648,7 @@ extern "C" int sb_scatter_by_expert(const uint32_t* expert_ids, int64_t batch, i
     // (concurrent scatters on other streams get their own)
     int32_t* hist = nullptr;
     SB_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&hist), (size_t)nb * n_experts * sizeof(int32_t), st));
-    const size_t sm_place = (size_t)(33 * n_experts) * sizeof(int);
+    const size_t sm_place = (size_t)(34 * n_experts) * sizeof(int);
     ProfScope prof("pipe_scatter_by_expert", st);
     pipe_scatter_hist_kernel<<<(unsigned)nb, SC_TILE, (size_t)n_experts * sizeof(int), st>>>(expert_ids, R, chunk,
                                                                                            n_experts, hist);
