@@ -492,7 +492,9 @@ __global__ void __launch_bounds__(SC_TILE) pipe_scatter_place_kernel(const uint3
   extern __shared__ int sm[];
   int* base = sm;            // [E] next slot of each expert for this CTA
   int* tot = sm + E;         // [E] the tile's entries per expert
-  int* wc = sm + 2 * E;      // [E][32] per-warp counts -> exclusive prefix over the warps
+  int* wc = sm + 2 * E;      // [E][33] per-warp counts -> exclusive prefix over the warps
+                             // (rows of 33: lanes with distinct ids, and a scan's 32
+                             // lanes, fall in distinct banks)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nbits = 32 - __clz(E);  // keys 0..E (E: no expert)
   for (int e = threadIdx.x; e < E; e += SC_TILE) base[e] = offs[(int64_t)blockIdx.x * E + e];
@@ -502,28 +504,28 @@ __global__ void __launch_bounds__(SC_TILE) pipe_scatter_place_kernel(const uint3
     const int64_t r = t0 + threadIdx.x;
     const uint32_t id = next;  // loaded one tile ahead
     next = r + SC_TILE < r1 ? __ldg(ids + r + SC_TILE) : 0xffffffffu;
-    for (int i = threadIdx.x; i < 32 * E; i += SC_TILE) wc[i] = 0;
+    for (int i = threadIdx.x; i < 33 * E; i += SC_TILE) wc[i] = 0;
     __syncthreads();
     const bool valid = id < (uint32_t)E;
     const unsigned same = pipe_same_key(valid ? id : (uint32_t)E, nbits);
     const int rank = __popc(same & ((1u << lane) - 1u));
-    if (valid && rank == 0) wc[id * 32 + warp] = __popc(same);
+    if (valid && rank == 0) wc[id * 33 + warp] = __popc(same);
     __syncthreads();
     // warp w scans experts w, w + 32, ...: lane = warp index of the tile
     for (int e = warp; e < E; e += SC_TILE / 32) {
-      const int c = wc[e * 32 + lane];
+      const int c = wc[e * 33 + lane];
       int incl = c;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const int y = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += y;
       }
-      wc[e * 32 + lane] = incl - c;
+      wc[e * 33 + lane] = incl - c;
       if (lane == 31) tot[e] = incl;
     }
     __syncthreads();
     if (valid) {
-      const int slot = base[id] + wc[id * 32 + warp] + rank;
+      const int slot = base[id] + wc[id * 33 + warp] + rank;
       if (slot < max_per) disp[(int64_t)id * max_per + slot] = store_entry ? (int32_t)r : (int32_t)(r / k);
     }
     __syncthreads();
@@ -648,7 +650,7 @@ extern "C" int sb_scatter_by_expert(const uint32_t* expert_ids, int64_t batch, i
     // (concurrent scatters on other streams get their own)
     int32_t* hist = nullptr;
     SB_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&hist), (size_t)nb * n_experts * sizeof(int32_t), st));
-    const size_t sm_place = (size_t)(34 * n_experts) * sizeof(int);
+    const size_t sm_place = (size_t)(35 * n_experts) * sizeof(int);
     ProfScope prof("pipe_scatter_by_expert", st);
     pipe_scatter_hist_kernel<<<(unsigned)nb, SC_TILE, (size_t)n_experts * sizeof(int), st>>>(expert_ids, R, chunk,
                                                                                            n_experts, hist);
