@@ -389,17 +389,20 @@ __global__ void __launch_bounds__(PIPE_TOK, 3) pipe_topk_thread_kernel(
     }
     if (only_calibrate || tid >= ntok) continue;
     const int64_t t = t0 + tid;
-    unsigned long long taken = 0ull;
+    // experts still to choose from (k <= E, so never empty)
+    unsigned long long avail = E >= 64 ? ~0ull : (1ull << E) - 1ull;
     for (int r = 0; r < k; ++r) {
+      // the first largest remaining value (NaN ranks as -inf)
       float bv = -INFINITY;
       int bi = -1;
 #pragma unroll
       for (int e = 0; e < EP; ++e)
-        if (e < E && !((taken >> e) & 1ull) && (bi < 0 || v[e] > bv)) {
+        if (((avail >> e) & 1ull) && v[e] > bv) {
           bv = v[e];
           bi = e;
         }
-      taken |= 1ull << bi;
+      if (bi < 0) bi = __ffsll((long long)avail) - 1;  // only -inf left: the lowest remaining expert
+      avail &= ~(1ull << bi);
       ids[t * k + r] = (uint32_t)bi;
       if (wts) wts[t * k + r] = bv;
     }
