@@ -48,6 +48,27 @@ def test_softmax_topk_kernel(cuda_device, E, B, cal):
         assert torch.equal(qw[0].cpu(), torch.tensor([0.3, 0.3, 0.2, 0.1]))
 
 
+@pytest.mark.parametrize("E", [16, 64, 100])
+def test_topk_with_minus_inf_scores(cuda_device, E):
+    """Scores of -inf are ranked last and, when fewer than k finite scores are
+    left, taken in expert order with weight -inf — the oracle's stable order
+    (thread-per-token kernel for E <= 64, warp per token above)."""
+    from sb200 import pipeline as pp
+    k = 8
+    rng = np.random.default_rng(E)
+    v = rng.standard_normal((64, E)).astype(np.float32)
+    for t in range(64):
+        n_inf = (t * 7) % (E + 1)  # 0 .. E scores of -inf per row
+        v[t, rng.permutation(E)[:n_inf]] = -np.inf
+    v[5, :] = -np.inf
+    v[6, 3] = 1.0
+    v[6, 9] = 1.0  # an exact tie among the finite scores
+    ids, w, _ = pp.softmax_topk(torch.from_numpy(v).to(cuda_device), k, apply_softmax=False)
+    rw, rids = op.topk_first_max(v, k)
+    assert np.array_equal(ids.cpu().numpy(), rids)
+    assert np.array_equal(w.cpu().numpy(), rw)
+
+
 def test_apply_calibration_kernel(cuda_device):
     from sb200 import pipeline as pp
     from sb200 import synth
