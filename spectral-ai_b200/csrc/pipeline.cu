@@ -410,50 +410,60 @@ __global__ void __launch_bounds__(PIPE_TOK, 3) pipe_topk_thread_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Scatter for E <= 512 over all SMs, three passes:
-//   hist:    CTA b counts the entries of its chunk per expert
-//   offsets: per expert, exclusive sum over the CTAs (and the totals)
-//   place:   CTA b walks its chunk in 1024-entry tiles; an entry's slot is its
-//            CTA offset + the tile's earlier entries of its expert (per-warp
-//            counts, scanned over the warps by warp shuffles) + its rank among
-//            equal ids in its warp (the equal-id lanes from one ballot per id
-//            bit), so slots follow ascending entry order.
+// Scatter for E <= 512 over all SMs, three passes.  Every warp owns one
+// contiguous segment of the entries (CTA b, warp w: segment 32 b + w), so the
+// segments in row order are the entries in ascending order:
+//   hist:    each warp counts its segment per expert (shared-memory atomics
+//            into its own row) -> hist[e][segment]
+//   offsets: per expert, exclusive sum over the segments (and the totals)
+//   place:   each warp walks its segment 32 entries at a time; an entry's slot
+//            is its segment's next slot for the expert + its rank among equal
+//            ids in the 32 (the equal-id lanes from one ballot per id bit),
+//            so slots follow ascending entry order.  No block-wide barrier.
 // ---------------------------------------------------------------------------
 constexpr int SC_TILE = 1024;
+constexpr int SC_WARPS = SC_TILE / 32;
 constexpr int SC_MAX_E = 512;
 
 __global__ void __launch_bounds__(SC_TILE) pipe_scatter_hist_kernel(const uint32_t* __restrict__ ids, int64_t R,
-                                                                    int64_t chunk, int E, int32_t* __restrict__ hist) {
-  extern __shared__ int h_s[];
-  for (int e = threadIdx.x; e < E; e += SC_TILE) h_s[e] = 0;
-  __syncthreads();
-  const int64_t r0 = (int64_t)blockIdx.x * chunk, r1 = r0 + chunk < R ? r0 + chunk : R;
-  int64_t rb = r0;
-  for (; rb + 4 * SC_TILE <= r1; rb += 4 * SC_TILE) {  // four ids a thread in flight
-    uint32_t v[4];
+                                                                    int64_t seg, int E, int nseg,
+                                                                    int32_t* __restrict__ hist) {
+  extern __shared__ int h_s[];  // [SC_WARPS][E]
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* h = h_s + warp * E;
+  for (int e = lane; e < E; e += 32) h[e] = 0;
+  __syncwarp();
+  const int s = blockIdx.x * SC_WARPS + warp;
+  const int64_t r0 = (int64_t)s * seg, r1 = r0 + seg < R ? r0 + seg : R;
+  for (int64_t rb = r0; rb < r1; rb += 8 * 32) {  // eight ids a lane in flight
+    uint32_t v[8];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) v[u] = __ldg(ids + rb + u * SC_TILE + threadIdx.x);
+    for (int u = 0; u < 8; ++u) {
+      const int64_t r = rb + u * 32 + lane;
+      v[u] = r < r1 ? __ldg(ids + r) : 0xffffffffu;
+    }
 #pragma unroll
-    for (int u = 0; u < 4; ++u)
-      if (v[u] < (uint32_t)E) atomicAdd(&h_s[v[u]], 1);
+    for (int u = 0; u < 8; ++u)
+      if (v[u] < (uint32_t)E) atomicAdd(&h[v[u]], 1);
   }
-  for (; rb < r1; rb += SC_TILE) {
-    const int64_t r = rb + threadIdx.x;
-    const uint32_t id = r < r1 ? __ldg(ids + r) : 0xffffffffu;
-    if (id < (uint32_t)E) atomicAdd(&h_s[id], 1);
-  }
-  __syncthreads();
-  for (int e = threadIdx.x; e < E; e += SC_TILE) hist[(int64_t)blockIdx.x * E + e] = h_s[e];
+  __syncwarp();
+  for (int e = lane; e < E; e += 32) hist[(int64_t)e * nseg + s] = h[e];
 }
 
-// One CTA per expert, one thread per histogram row (nb <= SC_TILE): block-wide
-// exclusive scan of the expert's column.
-__global__ void __launch_bounds__(SC_TILE) pipe_scatter_offsets_kernel(int32_t* __restrict__ hist, int nb, int E,
+// One CTA per expert: exclusive scan of the expert's row of segment counts,
+// in place: each thread sums a run of consecutive segments, one block-wide
+// scan of the run sums, then each thread writes its run's prefixes;
+// counts[e] = the total.
+__global__ void __launch_bounds__(SC_TILE) pipe_scatter_offsets_kernel(int32_t* __restrict__ hist, int nseg, int E,
                                                                        int32_t* __restrict__ counts) {
-  __shared__ int wsum[SC_TILE / 32];
-  const int e = blockIdx.x, b = threadIdx.x, warp = b >> 5, lane = b & 31;
-  const int c = b < nb ? hist[(int64_t)b * E + e] : 0;
-  int incl = c;
+  __shared__ int wsum[SC_WARPS];
+  const int e = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int32_t* row = hist + (int64_t)e * nseg;
+  const int per = (nseg + SC_TILE - 1) / SC_TILE;
+  const int i0 = threadIdx.x * per, i1 = i0 + per < nseg ? i0 + per : nseg;
+  int sum = 0;
+  for (int i = i0; i < i1; ++i) sum += row[i];
+  int incl = sum;
 #pragma unroll
   for (int o = 1; o < 32; o <<= 1) {
     const int y = __shfl_up_sync(0xffffffffu, incl, o);
@@ -473,7 +483,12 @@ __global__ void __launch_bounds__(SC_TILE) pipe_scatter_offsets_kernel(int32_t* 
     if (lane == 31) counts[e] = wi;
   }
   __syncthreads();
-  if (b < nb) hist[(int64_t)b * E + e] = wsum[warp] + incl - c;
+  int run = wsum[warp] + incl - sum;
+  for (int i = i0; i < i1; ++i) {
+    const int c = row[i];
+    row[i] = run;
+    run += c;
+  }
 }
 
 // Lanes of this warp whose key equals this lane's: one ballot per key bit
@@ -489,50 +504,39 @@ __device__ __forceinline__ unsigned pipe_same_key(uint32_t key, int nbits) {
 }
 
 __global__ void __launch_bounds__(SC_TILE) pipe_scatter_place_kernel(const uint32_t* __restrict__ ids, int64_t R,
-                                                                     int64_t chunk, int k, int E, int max_per,
+                                                                     int64_t seg, int k, int E, int nseg, int max_per,
                                                                      int store_entry, const int32_t* __restrict__ offs,
                                                                      int32_t* __restrict__ disp) {
-  extern __shared__ int sm[];
-  int* base = sm;            // [E] next slot of each expert for this CTA
-  int* tot = sm + E;         // [E] the tile's entries per expert
-  int* wc = sm + 2 * E;      // [E][33] per-warp counts -> exclusive prefix over the warps
-                             // (rows of 33: lanes with distinct ids, and a scan's 32
-                             // lanes, fall in distinct banks)
+  extern __shared__ int sm[];  // [SC_WARPS][E] next slot of each expert for each warp's segment
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* base = sm + warp * E;
   const int nbits = 32 - __clz(E);  // keys 0..E (E: no expert)
-  for (int e = threadIdx.x; e < E; e += SC_TILE) base[e] = offs[(int64_t)blockIdx.x * E + e];
-  const int64_t r0 = (int64_t)blockIdx.x * chunk, r1 = r0 + chunk < R ? r0 + chunk : R;
-  uint32_t next = r0 + threadIdx.x < r1 ? __ldg(ids + r0 + threadIdx.x) : 0xffffffffu;
-  for (int64_t t0 = r0; t0 < r1; t0 += SC_TILE) {
-    const int64_t r = t0 + threadIdx.x;
-    const uint32_t id = next;  // loaded one tile ahead
-    next = r + SC_TILE < r1 ? __ldg(ids + r + SC_TILE) : 0xffffffffu;
-    for (int i = threadIdx.x; i < 33 * E; i += SC_TILE) wc[i] = 0;
-    __syncthreads();
-    const bool valid = id < (uint32_t)E;
-    const unsigned same = pipe_same_key(valid ? id : (uint32_t)E, nbits);
-    const int rank = __popc(same & ((1u << lane) - 1u));
-    if (valid && rank == 0) wc[id * 33 + warp] = __popc(same);
-    __syncthreads();
-    // warp w scans experts w, w + 32, ...: lane = warp index of the tile
-    for (int e = warp; e < E; e += SC_TILE / 32) {
-      const int c = wc[e * 33 + lane];
-      int incl = c;
+  const int s = blockIdx.x * SC_WARPS + warp;
+  for (int e = lane; e < E; e += 32) base[e] = offs[(int64_t)e * nseg + s];
+  __syncwarp();
+  const int64_t r0 = (int64_t)s * seg, r1 = r0 + seg < R ? r0 + seg : R;
+  for (int64_t t0 = r0; t0 < r1; t0 += 8 * 32) {  // warp-uniform trip count
+    uint32_t v[8];  // eight steps of ids in flight before the first is placed
 #pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += y;
+    for (int u = 0; u < 8; ++u) {
+      const int64_t r = t0 + 32 * u + lane;
+      v[u] = r < r1 ? __ldg(ids + r) : 0xffffffffu;
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int64_t r = t0 + 32 * u + lane;
+      const uint32_t id = v[u];
+      const bool valid = id < (uint32_t)E;
+      const unsigned same = pipe_same_key(valid ? id : (uint32_t)E, nbits);
+      const int rank = __popc(same & ((1u << lane) - 1u));
+      if (valid) {
+        const int slot = base[id] + rank;
+        if (slot < max_per) disp[(int64_t)id * max_per + slot] = store_entry ? (int32_t)r : (int32_t)(r / k);
       }
-      wc[e * 33 + lane] = incl - c;
-      if (lane == 31) tot[e] = incl;
+      __syncwarp();
+      if (valid && rank == 0) base[id] += __popc(same);
+      __syncwarp();
     }
-    __syncthreads();
-    if (valid) {
-      const int slot = base[id] + wc[id * 33 + warp] + rank;
-      if (slot < max_per) disp[(int64_t)id * max_per + slot] = store_entry ? (int32_t)r : (int32_t)(r / k);
-    }
-    __syncthreads();
-    for (int e = threadIdx.x; e < E; e += SC_TILE) base[e] += tot[e];
   }
 }
 
@@ -642,28 +646,32 @@ extern "C" int sb_scatter_by_expert(const uint32_t* expert_ids, int64_t batch, i
   SB_REQUIRE(expert_ids != nullptr, "expert_ids is null");
   const int64_t R = batch * top_k;
   if (n_experts <= SC_MAX_E && R > SC_TILE) {
-    // all SMs: per-CTA histograms in a workspace the library keeps per device
+    // all SMs: one histogram row per warp segment in stream-ordered scratch
+    // from the device's memory pool (concurrent scatters on other streams get
+    // their own)
     int64_t nb = (R + 8 * SC_TILE - 1) / (8 * SC_TILE);
-    const int64_t cap = (int64_t)num_sms() * 4 < SC_TILE ? (int64_t)num_sms() * 4 : SC_TILE;
+    const int64_t cap = (int64_t)num_sms() * 4;
     if (nb > cap) nb = cap;
     int64_t chunk = (R + nb - 1) / nb;
-    chunk = (chunk + SC_TILE - 1) / SC_TILE * SC_TILE;
+    chunk = (chunk + SC_TILE - 1) / SC_TILE * SC_TILE;  // whole 32-entry steps per warp
     nb = (R + chunk - 1) / chunk;
-    // per-CTA histograms: stream-ordered scratch from the device's memory pool
-    // (concurrent scatters on other streams get their own)
+    const int64_t seg = chunk / SC_WARPS;
+    const int nseg = (int)(nb * SC_WARPS);
     int32_t* hist = nullptr;
-    SB_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&hist), (size_t)nb * n_experts * sizeof(int32_t), st));
-    const size_t sm_place = (size_t)(35 * n_experts) * sizeof(int);
-    ProfScope prof("pipe_scatter_by_expert", st);
-    pipe_scatter_hist_kernel<<<(unsigned)nb, SC_TILE, (size_t)n_experts * sizeof(int), st>>>(expert_ids, R, chunk,
-                                                                                           n_experts, hist);
-    pipe_scatter_offsets_kernel<<<n_experts, SC_TILE, 0, st>>>(hist, (int)nb, n_experts, expert_counts);
-    if (sm_place > 48 * 1024)
+    SB_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&hist), (size_t)nseg * n_experts * sizeof(int32_t), st));
+    const size_t sm_rows = (size_t)SC_WARPS * n_experts * sizeof(int);
+    if (sm_rows > 48 * 1024) {
+      SB_CUDA_TRY(cudaFuncSetAttribute(pipe_scatter_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sm_rows));
       SB_CUDA_TRY(cudaFuncSetAttribute(pipe_scatter_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)sm_place));
-    pipe_scatter_place_kernel<<<(unsigned)nb, SC_TILE, sm_place, st>>>(expert_ids, R, chunk, top_k, n_experts,
-                                                                      max_tokens_per_expert, store_entry ? 1 : 0,
-                                                                      hist, dispatch_indices);
+                                       (int)sm_rows));
+    }
+    ProfScope prof("pipe_scatter_by_expert", st);
+    pipe_scatter_hist_kernel<<<(unsigned)nb, SC_TILE, sm_rows, st>>>(expert_ids, R, seg, n_experts, nseg, hist);
+    pipe_scatter_offsets_kernel<<<n_experts, SC_TILE, 0, st>>>(hist, nseg, n_experts, expert_counts);
+    pipe_scatter_place_kernel<<<(unsigned)nb, SC_TILE, sm_rows, st>>>(expert_ids, R, seg, top_k, n_experts, nseg,
+                                                                     max_tokens_per_expert, store_entry ? 1 : 0,
+                                                                     hist, dispatch_indices);
     SB_CUDA_TRY(cudaGetLastError());
     SB_CUDA_TRY(cudaFreeAsync(hist, st));
     return SB_OK;
