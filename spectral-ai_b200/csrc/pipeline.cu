@@ -11,9 +11,11 @@
 //     one thread per token for the softmax and the top-k scan); values stay in
 //     registers, reductions are warp shuffles; the calibration matrix sits
 //     transposed in shared memory, loaded once per CTA of a grid-stride loop.
-//   * scatter: a stable stream compaction per expert (one CTA per expert, 4096
-//     entries per pass, block-wide exclusive scan) instead of atomicAdd slots,
-//     so each expert's list is in token order and the result is deterministic.
+//   * scatter: stable lists instead of atomicAdd slots, so each expert's list
+//     is in entry order and the result is deterministic.  Up to 512 experts,
+//     every warp owns a contiguous segment of the entries (a histogram row per
+//     segment, a scan over the segments, then each warp places its segment);
+//     above that, a stream compaction per expert (one CTA per expert).
 //   * combine: float4 over the hidden dimension, fused multiply-add over the k
 //     slots in slot order (the reference kernel's order).
 #include "common.cuh"
