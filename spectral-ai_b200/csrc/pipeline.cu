@@ -453,14 +453,19 @@ __global__ void __launch_bounds__(SC_TILE) pipe_scatter_hist_kernel(const uint32
 }
 
 // One CTA per expert: exclusive scan of the expert's row of segment counts,
-// in place: each thread sums a run of consecutive segments, one block-wide
-// scan of the run sums, then each thread writes its run's prefixes;
+// in place.  The row is staged in shared memory (coalesced), each thread sums
+// a run of consecutive segments there, one block-wide scan of the run sums,
+// each thread writes its run's prefixes, and the row goes back (coalesced);
 // counts[e] = the total.
 __global__ void __launch_bounds__(SC_TILE) pipe_scatter_offsets_kernel(int32_t* __restrict__ hist, int nseg, int E,
                                                                        int32_t* __restrict__ counts) {
   __shared__ int wsum[SC_WARPS];
+  extern __shared__ int row_s[];  // [nseg]
   const int e = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int32_t* row = hist + (int64_t)e * nseg;
+  int32_t* grow = hist + (int64_t)e * nseg;
+  for (int i = threadIdx.x; i < nseg; i += SC_TILE) row_s[i] = grow[i];
+  __syncthreads();
+  int* row = row_s;
   const int per = (nseg + SC_TILE - 1) / SC_TILE;
   const int i0 = threadIdx.x * per, i1 = i0 + per < nseg ? i0 + per : nseg;
   int sum = 0;
@@ -491,6 +496,8 @@ __global__ void __launch_bounds__(SC_TILE) pipe_scatter_offsets_kernel(int32_t* 
     row[i] = run;
     run += c;
   }
+  __syncthreads();
+  for (int i = threadIdx.x; i < nseg; i += SC_TILE) grow[i] = row_s[i];
 }
 
 // Lanes of this warp whose key equals this lane's: one ballot per key bit
@@ -659,18 +666,23 @@ extern "C" int sb_scatter_by_expert(const uint32_t* expert_ids, int64_t batch, i
     nb = (R + chunk - 1) / chunk;
     const int64_t seg = chunk / SC_WARPS;
     const int nseg = (int)(nb * SC_WARPS);
-    int32_t* hist = nullptr;
-    SB_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&hist), (size_t)nseg * n_experts * sizeof(int32_t), st));
     const size_t sm_rows = (size_t)SC_WARPS * n_experts * sizeof(int);
+    const size_t sm_seg = (size_t)nseg * sizeof(int);  // one expert's row of segment counts
+    SB_REQUIRE(sm_seg <= 200 * 1024, "too many scatter segments (%d) for one CTA's shared memory", nseg);
+    if (sm_seg > 48 * 1024)
+      SB_CUDA_TRY(cudaFuncSetAttribute(pipe_scatter_offsets_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)sm_seg));
     if (sm_rows > 48 * 1024) {
       SB_CUDA_TRY(cudaFuncSetAttribute(pipe_scatter_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)sm_rows));
       SB_CUDA_TRY(cudaFuncSetAttribute(pipe_scatter_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)sm_rows));
     }
+    int32_t* hist = nullptr;
+    SB_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&hist), (size_t)nseg * n_experts * sizeof(int32_t), st));
     ProfScope prof("pipe_scatter_by_expert", st);
     pipe_scatter_hist_kernel<<<(unsigned)nb, SC_TILE, sm_rows, st>>>(expert_ids, R, seg, n_experts, nseg, hist);
-    pipe_scatter_offsets_kernel<<<n_experts, SC_TILE, 0, st>>>(hist, nseg, n_experts, expert_counts);
+    pipe_scatter_offsets_kernel<<<n_experts, SC_TILE, sm_seg, st>>>(hist, nseg, n_experts, expert_counts);
     pipe_scatter_place_kernel<<<(unsigned)nb, SC_TILE, sm_rows, st>>>(expert_ids, R, seg, top_k, n_experts, nseg,
                                                                      max_tokens_per_expert, store_entry ? 1 : 0,
                                                                      hist, dispatch_indices);
