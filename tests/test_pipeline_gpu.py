@@ -81,7 +81,8 @@ def test_apply_calibration_kernel(cuda_device):
 
 
 @pytest.mark.parametrize("B,k,E,mx", [(1, 1, 1, 1), (96, 8, 64, 96), (5000, 8, 64, 700), (70000, 8, 64, 70000),
-                                      (300, 2, 4096, 300), (0, 8, 64, 10)])
+                                      (20000, 8, 300, 20000), (40000, 4, 512, 500), (300, 2, 4096, 300),
+                                      (0, 8, 64, 10)])
 def test_scatter_kernel_exact(cuda_device, B, k, E, mx):
     from sb200 import pipeline as pp
     g = torch.Generator().manual_seed(B + E)
