@@ -669,14 +669,22 @@ extern "C" int sb_scatter_by_expert(const uint32_t* expert_ids, int64_t batch, i
     const size_t sm_rows = (size_t)SC_WARPS * n_experts * sizeof(int);
     const size_t sm_seg = (size_t)nseg * sizeof(int);  // one expert's row of segment counts
     SB_REQUIRE(sm_seg <= 200 * 1024, "too many scatter segments (%d) for one CTA's shared memory", nseg);
-    if (sm_seg > 48 * 1024)
+    // opt-in shared memory, set once per device for the largest size asked so far
+    static size_t sm_seg_set[64] = {}, sm_rows_set[64] = {};
+    int dev = 0;
+    SB_CUDA_TRY(cudaGetDevice(&dev));
+    SB_REQUIRE(dev < 64, "device ordinal %d out of range", dev);
+    if (sm_seg > 48 * 1024 && sm_seg > sm_seg_set[dev]) {
       SB_CUDA_TRY(cudaFuncSetAttribute(pipe_scatter_offsets_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)sm_seg));
-    if (sm_rows > 48 * 1024) {
+      sm_seg_set[dev] = sm_seg;
+    }
+    if (sm_rows > 48 * 1024 && sm_rows > sm_rows_set[dev]) {
       SB_CUDA_TRY(cudaFuncSetAttribute(pipe_scatter_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)sm_rows));
       SB_CUDA_TRY(cudaFuncSetAttribute(pipe_scatter_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)sm_rows));
+      sm_rows_set[dev] = sm_rows;
     }
     int32_t* hist = nullptr;
     SB_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&hist), (size_t)nseg * n_experts * sizeof(int32_t), st));
