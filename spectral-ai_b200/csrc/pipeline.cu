@@ -586,11 +586,18 @@ int pipe_launch_softmax_topk(const float* logits, int64_t B, int E, int k, const
     return SB_OK;
   }
   ProfScope prof(name, stream);
+  int dev = 0;
+  SB_CUDA_TRY(cudaGetDevice(&dev));
+  SB_REQUIRE(dev < 64, "device ordinal %d out of range", dev);
+  // opt-in shared memory (a calibration of up to PIPE_CAL_MAX experts), once per device and kernel
 #define SB_PIPE_LAUNCH(P)                                                                                     \
   do {                                                                                                        \
-    if (smem > 48 * 1024)                                                                                     \
-      SB_CUDA_TRY(cudaFuncSetAttribute(pipe_softmax_topk_kernel<P>,                                           \
-                                       cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));              \
+    static bool attr_p[64] = {};                                                                              \
+    if (smem > 48 * 1024 && !attr_p[dev]) {                                                                   \
+      SB_CUDA_TRY(cudaFuncSetAttribute(pipe_softmax_topk_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                       PIPE_CAL_MAX * PIPE_CAL_MAX * (int)sizeof(float)));                   \
+      attr_p[dev] = true;                                                                                     \
+    }                                                                                                         \
     pipe_softmax_topk_kernel<P><<<(unsigned)blocks, PIPE_THREADS, smem, stream>>>(                           \
         logits, B, E, k, cal_w, cal_b, apply_softmax, only_calibrate, probs, ids, wts);                      \
   } while (0)

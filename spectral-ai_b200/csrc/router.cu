@@ -1159,11 +1159,15 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
     }
   } else {
     if (dsm_soft > 48 * 1024) {
-      static bool attr = false;
-      if (!attr) {
+      // the opt-in limit is per device: set it once on each
+      static bool attr[64] = {};
+      int dev = 0;
+      SB_CUDA_TRY(cudaGetDevice(&dev));
+      SB_REQUIRE(dev < 64, "device ordinal %d out of range", dev);
+      if (!attr[dev]) {
         SB_CUDA_TRY(cudaFuncSetAttribute(descent_soft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          227 * 1024));
-        attr = true;
+        attr[dev] = true;
       }
     }
     int64_t blocks = (batch + SOFT_WARPS - 1) / SOFT_WARPS;
