@@ -327,7 +327,7 @@ int sb_enh_destroy(sb_enh* h);
  * async_pipeline.cu:150-170; W [E,E] nn.Linear layout, E <= 128), softmax over
  * the E values when apply_softmax (softmax_topk_kernel, :177-230), then the
  * top_k values in descending order, the lower expert index first among equal
- * values.  probs [B,E] (may be NULL) receives the values ranked (calibrated /
+ * values (-inf ranks last; NaN ranks as -inf and is reported as -inf).  probs [B,E] (may be NULL) receives the values ranked (calibrated /
  * softmaxed); topk_weights [B,k] (may be NULL) the chosen values, not
  * renormalised.  E <= 1024, top_k <= 32. */
 int sb_softmax_topk(const float* logits, int64_t batch, int n_experts, int top_k, const float* cal_w,

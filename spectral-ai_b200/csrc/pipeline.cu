@@ -126,7 +126,11 @@ __global__ void __launch_bounds__(PIPE_THREADS) pipe_softmax_topk_kernel(
         if (lane + 32 * u < E) probs[t * E + lane + 32 * u] = v[u];
     }
     // top-k by repeated warp argmax; a chosen entry drops out (by a mask, so
-    // -inf inputs are still picked once each)
+    // -inf inputs are still picked once each); NaN ranks as -inf, as in the
+    // thread-per-token kernel, so every chosen id is a valid expert
+#pragma unroll
+    for (int u = 0; u < PER; ++u)
+      if (v[u] != v[u]) v[u] = -INFINITY;
     float sel_v = 0.f;
     uint32_t sel_i = 0;
     unsigned taken = 0;

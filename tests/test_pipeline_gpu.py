@@ -67,6 +67,17 @@ def test_topk_with_minus_inf_scores(cuda_device, E):
     rw, rids = op.topk_first_max(v, k)
     assert np.array_equal(ids.cpu().numpy(), rids)
     assert np.array_equal(w.cpu().numpy(), rw)
+    # NaN scores rank as -inf: the finite scores first, then the lowest remaining
+    # experts with weight -inf; every id valid and distinct
+    vn = v.copy()
+    vn[7, :] = np.nan
+    vn[8, :] = np.nan
+    vn[8, [2, 11]] = [0.5, 0.25]
+    ids, w, _ = pp.softmax_topk(torch.from_numpy(vn).to(cuda_device), k, apply_softmax=False)
+    ids, w = ids.cpu().numpy(), w.cpu().numpy()
+    assert ids[7].tolist() == list(range(k)) and np.all(w[7] == -np.inf)
+    assert ids[8].tolist() == [2, 11] + [e for e in range(E) if e not in (2, 11)][:k - 2]
+    assert w[8, :2].tolist() == [0.5, 0.25] and np.all(w[8, 2:] == -np.inf)
 
 
 def test_apply_calibration_kernel(cuda_device):
