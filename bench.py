@@ -164,7 +164,8 @@ def max_over_ranks(v: float, world: int) -> float:
 
 
 # ---------------------------------------------------------------------------
-# CPU baseline (oracle port of the reference path)
+# CPU baselines: the reference's CPU path (its torch operators, restated in
+# oracle/torch_ref.py) on the host cores
 # ---------------------------------------------------------------------------
 def blas_threads():
     try:
@@ -175,22 +176,32 @@ def blas_threads():
         return os.cpu_count() or 1
 
 
+def cpu_threads():
+    """All host threads for the CPU baselines (torch's intra-op pool)."""
+    import torch
+    n = os.cpu_count() or 1
+    torch.set_num_threads(n)
+    return torch.get_num_threads()
+
+
 def cpu_router_rate(sample_tokens: int, budget_s: float = 12.0):
-    """Tokens/s of the oracle router (numpy fp32) on the host cores."""
-    import numpy as np
-    from oracle import router as orouter
+    """Tokens/s of the reference router's CPU path (BVHRouter.forward eval, fp32,
+    the reference's torch operators as restated in oracle/torch_ref.py)."""
+    import torch
+    from oracle import torch_ref
     from sb200 import synth
-    w = synth.router_weights(H, S, BRANCHING, seed=0)
-    x = synth.hidden_states(sample_tokens, H, seed=1).numpy()
-    for _ in range(2):   # warm the BLAS and thread pools
-        orouter.router_forward(w, x, BRANCHING, mode="hard", k=TOPK)
-    done, t0 = 0, time.perf_counter()
-    while True:
-        orouter.router_forward(w, x, BRANCHING, mode="hard", k=TOPK)
-        done += sample_tokens
-        el = time.perf_counter() - t0
-        if el >= budget_s or done >= 8 * sample_tokens:
-            break
+    cpu_threads()
+    r = torch_ref.TorchRouter(synth.router_weights(H, S, BRANCHING, seed=0), BRANCHING)
+    x = synth.hidden_states(sample_tokens, H, seed=1)
+    with torch.no_grad():
+        r.topk(x, TOPK, soft=False)   # warm the thread pool
+        done, t0 = 0, time.perf_counter()
+        while True:
+            r.topk(x, TOPK, soft=False)
+            done += sample_tokens
+            el = time.perf_counter() - t0
+            if el >= budget_s or done >= 8 * sample_tokens:
+                break
     return done / el, done, el
 
 
@@ -516,9 +527,11 @@ def config4_workloads(batch: int, device):
     return router_step, dense_step
 
 
-def stack_workload(tokens: int, device, layers: int = 16, select: str = "soft"):
+def stack_workload(tokens: int, device, layers: int = 16, select: str = "soft", world: int = 1):
     """Config 3: a stack of MoE layers (router + 64 ternary experts each, own
-    random weights per layer) with residual h <- h + MoE(h); attention omitted."""
+    random weights per layer) with residual h <- h + MoE(h); attention omitted.
+    At N > 1 every layer is expert-parallel (64/N experts per GPU, the
+    peer-memory exchange), the layers sharing one workspace."""
     import numpy as np
     import torch
     from bvh_router import BVHRouter, RouterConfig
@@ -526,13 +539,26 @@ def stack_workload(tokens: int, device, layers: int = 16, select: str = "soft"):
     from sb200.moe import BVHMoELayer
     from sb200.ternary import TernaryExperts
     stack = []
+    rank = 0
+    if world > 1:
+        import torch.distributed as dist
+        from sb200.ep import EPMoELayer, ExpertParallelMoE
+        rank = dist.get_rank()
+    shared = None
     for l in range(layers):
         w = synth.router_weights(H, S, BRANCHING, seed=100 + l)
         r = BVHRouter(RouterConfig(embed_dim=H, spectral_dim=S))
         r.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in w.items()})
         r = r.to(device).eval()
-        stack.append(BVHMoELayer(r, TernaryExperts.random(E_EXPERTS, H, I_INTER, seed=200 + l, device=device),
-                                 top_k=TOPK, select=select))
+        if world > 1:
+            el = E_EXPERTS // world
+            local = TernaryExperts.random(el, H, I_INTER, seed=200 + 64 * l + rank, device=device)
+            ep = ExpertParallelMoE(local, E_EXPERTS, TOPK, tokens, workspace=shared)
+            shared = ep.workspace
+            stack.append(EPMoELayer(r, ep, top_k=TOPK, select=select))
+        else:
+            stack.append(BVHMoELayer(r, TernaryExperts.random(E_EXPERTS, H, I_INTER, seed=200 + l, device=device),
+                                     top_k=TOPK, select=select))
     x = synth.hidden_states(tokens, H, seed=3, dtype=torch.bfloat16, device=device)
 
     def step():
@@ -545,12 +571,18 @@ def stack_workload(tokens: int, device, layers: int = 16, select: str = "soft"):
 
 
 def ep_workload(batch: int, device, world: int, select: str = "soft"):
+    """The headline layer expert-parallel (N > 1): the same router on every
+    rank, 64/N experts per GPU, the tokens exchanged by the layer's own kernels
+    through peer memory (sb200.ep.ExpertParallelMoE); replayed from one CUDA
+    graph like the single-GPU layer.  Returns (step, e2e pieces, meta) as
+    moe_workload does."""
     import numpy as np
     import torch
     import torch.distributed as dist
     from bvh_router import BVHRouter, RouterConfig
     from sb200 import synth
-    from sb200.ep import ExpertParallelMoE
+    from sb200.ep import EPMoELayer, ExpertParallelMoE
+    from sb200.moe import GraphedLayer, HostPipeline
     from sb200.ternary import TernaryExperts
     rank = dist.get_rank()
     w = synth.router_weights(H, S, BRANCHING, seed=0)
@@ -560,15 +592,234 @@ def ep_workload(batch: int, device, world: int, select: str = "soft"):
     e_local = E_EXPERTS // world
     allx = synth.ternary_experts(E_EXPERTS, H, I_INTER, seed=2)
     local = TernaryExperts(allx[rank * e_local:(rank + 1) * e_local], device)
-    layer = ExpertParallelMoE(lambda rows, ids, ww: local.forward(rows, ids, ww, out_dtype=torch.float32),
-                              E_EXPERTS)
+    ep = ExpertParallelMoE(local, E_EXPERTS, TOPK, batch)
+    layer = EPMoELayer(r, ep, top_k=TOPK, select=select)
+    x = synth.hidden_states(batch, H, seed=2 + 1000 * rank, dtype=torch.bfloat16, device=device)
+    out = torch.empty(batch, H, dtype=torch.bfloat16, device=device)
+    ids, _ = layer.route(x)
+    counts = torch.bincount(ids.long().flatten(), minlength=E_EXPERTS).float()
+    dist.all_reduce(counts)                      # the whole job's expert loads
+    per_rank = counts.view(world, e_local).sum(dim=1)
+    dests = torch.zeros(batch, world, dtype=torch.bool, device=device)
+    dests.scatter_(1, (ids.long() // e_local), True)
+    rows_sent = float(dests.sum()) / max(batch, 1)
+
+    def eager_step():
+        layer(x, out=out)
+
+    glayer = GraphedLayer(layer)
+    glayer(x, out)
+
+    def step():
+        glayer(x, out)
+
+    pipe = HostPipeline(glayer, batch, H, dtype=torch.bfloat16, device=device)
+    x_host = [x.cpu().pin_memory() for _ in range(2)]
+    out_host = [torch.empty(batch, H, dtype=torch.bfloat16).pin_memory() for _ in range(2)]
+
+    def e2e_run(n):
+        pipe.run([x_host[i & 1] for i in range(n)], [out_host[i & 1] for i in range(n)])
+
+    x_dev = torch.empty_like(x)
+
+    def e2e_sequential():
+        x_dev.copy_(x_host[0], non_blocking=True)
+        y = layer(x_dev)
+        out_host[0].copy_(y, non_blocking=True)
+
+    mine = float(per_rank[rank])   # (token, expert) entries this rank's experts process
+    meta = {"tokens_per_step": batch, "h2d": batch * H * 2, "d2h": batch * H * 2,
+            "dominant": "ternary_gateup_tc", "dominant_flop": 2.0 * mine * H * 2 * I_INTER,
+            "layer": layer,
+            "config": {"workload": "moe_layer_bvh_route_ternary_swiglu", "hidden": H,
+                       "intermediate": I_INTER, "experts": E_EXPERTS, "top_k": TOPK,
+                       "tokens_per_gpu": batch, "router_select": select,
+                       "experts_per_gpu": e_local,
+                       "entries_per_gpu_max_over_mean": round(float(per_rank.max() / per_rank.mean()), 3),
+                       "expert_load_max_over_mean": round(float(counts.max() / counts.mean()), 3),
+                       "rows_sent_per_token": round(rows_sent, 3),
+                       "precision": "router bf16 tcgen05 + fp32 descent; ternary bf16 x {-1,0,1} "
+                                    "tcgen05, fp16 hidden, fp32 accumulate; fp32 partial sums; bf16 out",
+                       "l2": "flushed (256 MiB write) before every timed step, outside the events"},
+            "parallelism": (f"ep{world}: {e_local} experts per GPU; each token row sent once per GPU "
+                            "holding one of its experts and one fp32 partial sum returned, by the "
+                            "layer's own kernels through peer memory (no host sync, no library collective)")}
+    return step, (e2e_run, e2e_sequential, eager_step), meta
+
+
+def nccl_alltoall_rate(batch: int, device, world: int, steps: int, warmup: int, flush):
+    """The baseline of the fused exchange: the same sharded layer over the library
+    collective (sb200.ep.AllToAllMoE: torch.distributed.all_to_all_single on
+    NCCL, host-synchronised split sizes, one row per slot each way)."""
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    from bvh_router import BVHRouter, RouterConfig
+    from sb200 import synth
+    from sb200.ep import AllToAllMoE
+    from sb200.ternary import TernaryExperts
+    rank = dist.get_rank()
+    w = synth.router_weights(H, S, BRANCHING, seed=0)
+    r = BVHRouter(RouterConfig(embed_dim=H, spectral_dim=S))
+    r.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in w.items()})
+    r = r.to(device).eval()
+    e_local = E_EXPERTS // world
+    allx = synth.ternary_experts(E_EXPERTS, H, I_INTER, seed=2)
+    local = TernaryExperts(allx[rank * e_local:(rank + 1) * e_local], device)
+    layer = AllToAllMoE(lambda rows, ids, ww: local.forward(rows, ids, ww, out_dtype=torch.float32), E_EXPERTS)
     x = synth.hidden_states(batch, H, seed=2 + 1000 * rank, dtype=torch.bfloat16, device=device)
 
     def step():
-        ids, wts = r.forward_topk(x, k=TOPK, select=select)
+        ids, wts = r.forward_topk(x, k=TOPK, select="soft")
         layer(x, ids, wts, out_dtype=torch.bfloat16)
 
-    return step, {}
+    ms, _ = time_steps(step, steps, warmup, world, flush=flush)
+    return {"value": round(batch * world * steps / (ms / 1e3), 1), "unit": "tokens/s",
+            "ms_per_step": round(ms / steps, 4),
+            "what": "sb200.ep.AllToAllMoE: all_to_all_single (NCCL) of counts, bf16 rows (one per slot), "
+                    "ids, weights; fp32 outputs back; host-read split sizes; eager launches"}
+
+
+def router_sweep(dev, pk, world, steps, warmup, flush, cpu: bool):
+    """Config 1: the router (hard top-8, bf16 FAST engine) at B = 1, 256, 4096
+    and 65536 tokens (262,144 is the "router" line).  Inputs below 126 MB sit
+    in L2, so L2 is flushed before every step (outside the events).  With
+    ``cpu`` the reference's CPU router (oracle/torch_ref.py) is timed at the
+    same batch sizes on every host core."""
+    import torch
+    out = {}
+    for B in (1, 256, 4096, 65536):
+        step, _, meta = router_workload(B, dev)
+        n = steps if B <= 4096 else max(10, steps // 4)
+        ms, prof = time_steps(step, n, warmup, world, flush=flush if B <= 4096 else None, profile=True)
+        per = ms / n
+        row = {"batch": B, "us_per_batch": round(per * 1e3, 2),
+               "mq_per_s": round(B * world / (per / 1e3) / 1e6, 4),
+               "tensor_frac": round(B * ROUTER_FLOP_PER_TOKEN / (per / 1e3) / 1e12 / pk["bf16_tflops"], 4),
+               "hbm_frac": round(B * ROUTER_BYTES_PER_TOKEN / (per / 1e3) / 1e9 / pk["hbm_gbs"], 4),
+               "kernels": {k: round(t / max(c, 1), 4) for k, (c, t) in prof.items()},
+               "l2": "flushed before every step" if B <= 4096 else "inputs > L2 (268 MB), no flush"}
+        if cpu:
+            from oracle import torch_ref
+            from sb200 import synth
+            cores = cpu_threads()
+            r = torch_ref.TorchRouter(synth.router_weights(H, S, BRANCHING, seed=0), BRANCHING)
+            x = synth.hidden_states(B, H, seed=1)
+            with torch.no_grad():
+                r.topk(x, TOPK, soft=False)
+                reps = max(1, min(50, int(4096 // B)))
+                t0 = time.perf_counter()
+                for _ in range(reps):
+                    r.topk(x, TOPK, soft=False)
+                el = (time.perf_counter() - t0) / reps
+            row["cpu_reference"] = {"us_per_batch": round(el * 1e6, 1), "mq_per_s": round(B / el / 1e6, 6),
+                                    "cores": cores, "kind": "port",
+                                    "what": "BVHRouter.forward (eval, fp32), the reference's torch operators "
+                                            "(oracle/torch_ref.py)"}
+        out[str(B)] = row
+        del step
+    return out
+
+
+def small_batch_rates(dev, pk, world, steps, warmup, flush):
+    """Small batches, where the expert weights set the cost: the drop-in
+    ternary_gated_mlp (one OLMoE-shaped expert, fp32 input as the reference API
+    takes it) at M = 1, 64, 256 tokens, and the whole MoE layer (router + 64
+    ternary experts) at B = 1, 64, 256 tokens.  hbm_frac counts the 2-bit
+    weights of the experts a step touches plus its activations, against the
+    step's device time."""
+    import numpy as np
+    import torch
+    import ternary_expert_ext as tx
+    from sb200 import synth
+    res = {"gated_mlp": {}, "moe_layer": {}}
+    ex = synth.ternary_experts(1, H, I_INTER, seed=21)[0]
+    packs = [tx.pack_ternary(torch.from_numpy(np.ascontiguousarray(ex[k].T))).to(dev)
+             for k in ("gate_ternary", "up_ternary", "down_ternary")]
+    scales = [torch.from_numpy(ex[k]).to(dev) for k in ("gate_scale", "up_scale", "down_scale")]
+    wbytes = 3 * H * I_INTER // 4
+    for M in (1, 64, 256):
+        x = synth.hidden_states(M, H, seed=22, device=dev)
+        fn = lambda: tx.ternary_gated_mlp(x, *packs, *scales)
+        ms, _ = time_steps(fn, steps, warmup, world, flush=flush)
+        per = ms / steps / 1e3
+        nbytes = wbytes + M * H * 4 * 2
+        res["gated_mlp"][str(M)] = {"us": round(per * 1e6, 2), "tokens_per_s": round(M / per, 1),
+                                    "gbs": round(nbytes / per / 1e9, 1),
+                                    "hbm_frac": round(nbytes / per / 1e9 / pk["hbm_gbs"], 4)}
+    for B in (1, 64, 256):
+        step, _, meta = moe_workload(B, dev)
+        ms, prof = time_steps(step, steps, warmup, world, flush=flush)
+        per = ms / steps / 1e3
+        used = meta["config"]["experts_with_tokens"]
+        nbytes = used * wbytes + B * H * 2 * 2
+        res["moe_layer"][str(B)] = {"us": round(per * 1e6, 2), "tokens_per_s": round(B * world / per, 1),
+                                    "experts_touched": used, "gbs": round(nbytes / per / 1e9, 1),
+                                    "hbm_frac": round(nbytes / per / 1e9 / pk["hbm_gbs"], 4)}
+    res["l2"] = "flushed before every step (outside the events)"
+    return res
+
+
+def reference_gpu_rates(dev, steps, warmup, flush):
+    """Baseline leg: the reference's own CUDA kernels, compiled from its sources
+    into oracle/_ref by oracle/build_ref.py, timed on this GPU beside ours on the
+    same inputs (rank 0, 1 GPU; absent when oracle/_ref was not built):
+    ternary_gated_mlp (cuda/v5/ternary_torch_ext.cu:123-191, one token per CTA)
+    at M = 1, 64, 256, and the legacy tree router's bvh_route_batch
+    (cuda/v5/bvh_router_kernel.cu:558-687, host buffers in and out) at 256 and
+    1024 rays.  The tree kernel computes other math than BVHRouter, so it is
+    timed against our implementation of the same tree router, not against the
+    BVH router."""
+    import ctypes as C
+    import glob
+    import importlib.util
+    import numpy as np
+    import torch
+    from sb200 import _lib, synth
+    out = {}
+    so = glob.glob(str(REPO / "oracle" / "_ref" / "ternary_expert_ext_ref*.so"))
+    if so:
+        spec = importlib.util.spec_from_file_location("ternary_expert_ext_ref", so[0])
+        ref = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(ref)
+        import ternary_expert_ext as tx
+        ex = synth.ternary_experts(1, H, I_INTER, seed=21)[0]
+        packs = [ref.pack_ternary(torch.from_numpy(np.ascontiguousarray(ex[k].T))).to(dev)
+                 for k in ("gate_ternary", "up_ternary", "down_ternary")]
+        scales = [torch.from_numpy(ex[k]).to(dev) for k in ("gate_scale", "up_scale", "down_scale")]
+        rows = {}
+        for M in (1, 64, 256):
+            x = synth.hidden_states(M, H, seed=22, device=dev)
+            r_ms, _ = time_steps(lambda: ref.ternary_gated_mlp(x, *packs, *scales), steps, warmup, 1, flush=flush)
+            o_ms, _ = time_steps(lambda: tx.ternary_gated_mlp(x, *packs, *scales), steps, warmup, 1, flush=flush)
+            rows[str(M)] = {"reference_us": round(r_ms / steps * 1e3, 2), "ours_us": round(o_ms / steps * 1e3, 2),
+                            "speedup": round(r_ms / o_ms, 2)}
+        out["ternary_gated_mlp"] = {"shape": f"{H} -> {I_INTER} -> {H}, fp32 input, one expert", **rows}
+    lib_path = REPO / "oracle" / "_ref" / "libbvh_router_ref.so"
+    if lib_path.is_file():
+        P = lambda a: a.ctypes.data_as(C.c_void_p)
+        tree = synth.legacy_tree(0)
+        arrs = [np.ascontiguousarray(tree[k], np.float32) for k in ("centers", "radii", "portals", "snell_w", "snell_b")]
+        rows = {}
+        for name, lib in (("reference", C.CDLL(str(lib_path))), ("ours", _lib.load())):
+            assert lib.bvh_upload_tree(*[P(a) for a in arrs]) == 0
+            for B in (256, 1024):
+                assert lib.bvh_alloc_buffers(B) == 0
+                o, d = synth.rays(B, 1)
+                spec = np.zeros((B, 64), np.float32)
+                he, hsc = np.zeros(B, np.int32), np.zeros((B, 64), np.float32)
+                hp, hc = np.zeros((B, 3), np.int32), np.zeros(B, np.float32)
+                args = [P(o), P(d), P(spec), P(he), P(hsc), P(hp), P(hc), B, 1]
+                for _ in range(20):
+                    assert lib.bvh_route_batch(*args) == 0
+                t0 = time.perf_counter()
+                for _ in range(300):
+                    lib.bvh_route_batch(*args)
+                rows.setdefault(str(B), {})[f"{name}_us"] = round((time.perf_counter() - t0) / 300 * 1e6, 2)
+            lib.bvh_free_buffers()
+        out["bvh_route_batch"] = {"what": "host buffers in and out, CUDA-graph replay, synchronous call, "
+                                          "host clock over 300 calls", **rows}
+    return out
 
 
 def time_steps(step, steps, warmup, world, sampler=None, profile=False, flush=None):
@@ -656,7 +907,16 @@ def run_ours(a):
     batch = a.batch or 4096
     flush_buf = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
     flush = lambda: flush_buf.fill_(1)
-    step, e2e_step, meta = moe_workload(batch, dev)
+    use_ep = world > 1 and not a.skip_ep
+    if use_ep:
+        step, e2e_step, meta = ep_workload(batch, dev, world)
+        parallelism = meta["parallelism"]
+        api = ("sb200.moe.HostPipeline.run over sb200.ep.EPMoELayer (BVHRouter.forward_topk + "
+               "ExpertParallelMoE)")
+    else:
+        step, e2e_step, meta = moe_workload(batch, dev)
+        parallelism = "single GPU, all 64 experts"
+        api = "sb200.moe.HostPipeline.run over sb200.moe.BVHMoELayer (BVHRouter.forward_topk + TernaryExperts)"
     total_ms, _ = time_steps(step, a.steps, a.warmup, world, sampler, flush=flush)
     clocks = sampler.stop()
     # the same layer launched kernel by kernel with per-kernel CUDA events: the
@@ -674,16 +934,15 @@ def run_ours(a):
            "warmup": a.warmup, "ms_per_step": round(total_ms / a.steps, 4),
            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
            "data": "synthetic (seeded unit-RMS Gaussian tokens, random-init router and ternary experts)",
-           "config": dict(meta["config"], parallelism=f"token-shard x{world}, experts replicated, no collective"),
+           "config": dict(meta["config"], parallelism=parallelism),
            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s",
                    "h2d_bytes_per_step": meta["h2d"], "d2h_bytes_per_step": meta["d2h"],
-                   "api": "sb200.moe.HostPipeline.run over sb200.moe.BVHMoELayer (BVHRouter.forward_topk "
-                          "+ TernaryExperts): pinned host batches, copies in/out on their own streams "
+                   "api": api + ": pinned host batches, copies in/out on their own streams "
                           "overlapped with the neighbouring batches' compute",
                    "l2": "no flush between batches; each batch streams > 400 MB through the layer "
                          "(dispatch rows 134 MB, per-slot outputs 277 MB) against a 126 MB L2",
                    "sequential_value": round(tokens / (seq_ms / 1e3), 1),
-                   "sequential": "BVHMoELayer.__call__ one batch at a time on one stream (copy in, "
+                   "sequential": "the layer's __call__ one batch at a time on one stream (copy in, "
                                  "layer, copy out; L2 flushed between batches)"},
            "gpu_launches": launches,
            "launch_mode": (f"timed steps replay one CUDA graph of the layer ({launches // a.steps} kernels "
@@ -693,20 +952,21 @@ def run_ours(a):
                            "share": round(t / max(sum(v[1] for v in prof.values()), 1e-9), 4)}
                        for k, (n, t) in prof.items()},
            "roofline": roofline_tensor(meta, prof, pk, eager_ms, prof_steps), "clocks": clocks}
-    # ---- expert-parallel form of the same layer (N > 1): E/N experts per GPU,
-    #      NCCL all-to-all dispatch and combine
-    if world > 1 and not a.skip_ep:
-        estep, emeta = ep_workload(batch, dev, world)
-        ep_ms, eprof = time_steps(estep, a.steps, a.warmup, world, profile=True, flush=flush)
-        out["ep"] = {"metric": "MoE-layer tokens/s, expert parallel", "unit": "tokens/s",
-                     "value": round(tokens / (ep_ms / 1e3), 1), "ms_per_step": round(ep_ms / a.steps, 4),
-                     "experts_per_gpu": E_EXPERTS // world,
-                     "parallelism": f"ep{world}: NCCL all_to_all_single dispatch (bf16 rows) + combine (fp32)",
-                     "kernels": {k: {"launches": n, "avg_ms": round(t / max(n, 1), 4)} for k, (n, t) in eprof.items()}}
+    # ---- N > 1: the replicated form (every GPU all 64 experts, its own tokens,
+    #      no exchange) and the library-collective form of the sharded layer
+    if use_ep:
+        rstep, _, rmeta = moe_workload(batch, dev)
+        r_ms, _ = time_steps(rstep, a.steps, a.warmup, world, flush=flush)
+        out["replicated"] = {"metric": "MoE-layer tokens/s, experts replicated", "unit": "tokens/s",
+                             "value": round(tokens / (r_ms / 1e3), 1), "ms_per_step": round(r_ms / a.steps, 4),
+                             "parallelism": f"token-shard x{world}: all 64 experts (100 MB of 2-bit weights) "
+                                            "on every GPU, no exchange"}
+        del rstep
+        out["nccl_all_to_all"] = nccl_alltoall_rate(batch, dev, world, min(a.steps, 20), a.warmup, flush)
     # ---- config 3: 16-layer MoE stack, 16384 tokens sharded over the ranks
     if not a.skip_stack:
         stok = max(1, 16384 // world)
-        sstep = stack_workload(stok, dev)
+        sstep = stack_workload(stok, dev, world=world)
         st_steps = min(a.steps, 10)
         s_ms, sprof = time_steps(sstep, st_steps, 2, world, profile=True)
         out["stack16"] = {"metric": "16-layer MoE stack tokens/s (config 3)", "unit": "tokens/s",
@@ -714,7 +974,8 @@ def run_ours(a):
                           "ms_per_step": round(s_ms / st_steps, 3), "tokens_total": stok * world,
                           "tokens_per_gpu": stok, "layers": 16, "steps": st_steps,
                           "scaling": "strong (16384 tokens in total, split over the GPUs)",
-                          "parallelism": f"token-shard x{world}, experts replicated per layer",
+                          "parallelism": (f"ep{world} per layer ({E_EXPERTS // world} experts per GPU, "
+                                          "peer-memory exchange)" if world > 1 else "single GPU"),
                           "l2": "weights of 16 layers (1.7 GB) stream every step; no flush"}
     # ---- config 4: 6-level 4096-expert router at hidden 4096 vs a dense gate
     if not a.skip_config4:
@@ -802,15 +1063,25 @@ def run_ours(a):
         if rank == 0 and world == 1 and not a.no_cpu_baseline:
             rate, done, el = cpu_router_rate(4096)
             out["router"]["cpu_baseline"] = {
-                "value": round(rate / 1e6, 6), "unit": "Mq/s", "cores": blas_threads(), "kind": "port",
-                "sample": f"{done} tokens through the numpy port of python/bvh_router.py (fp32) in {el:.1f} s"}
+                "value": round(rate / 1e6, 6), "unit": "Mq/s", "cores": cpu_threads(), "kind": "port",
+                "sample": f"{done} tokens through BVHRouter.forward (eval, fp32) as the reference's torch "
+                          f"operators (oracle/torch_ref.py) in {el:.1f} s"}
+    # ---- config-1 sweep and the small-batch regime
+    if not a.skip_sweeps:
+        sw_steps = min(a.steps, 100)
+        out["router_sweep"] = router_sweep(dev, pk, world, sw_steps, a.warmup, flush,
+                                           cpu=(rank == 0 and world == 1 and not a.no_cpu_baseline))
+        out["small_batch"] = small_batch_rates(dev, pk, world, sw_steps, a.warmup, flush)
+        if rank == 0 and world == 1 and not a.no_cpu_baseline:
+            out["reference_gpu"] = reference_gpu_rates(dev, sw_steps, a.warmup, flush)
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
-        rate, done, el = cpu_moe_rate(a.cpu_sample)
-        out["cpu_baseline"] = {"value": round(rate, 2), "unit": "tokens/s", "cores": blas_threads(),
+        rate, done, el = cpu_moe_rate(batch)
+        out["cpu_baseline"] = {"value": round(rate, 2), "unit": "tokens/s", "cores": cpu_threads(),
                                "kind": "port",
-                               "sample": f"{done} tokens of the same workload (router soft top-8 + "
-                                         f"64 ternary experts, fp32 numpy port of the reference CPU "
-                                         f"path) in {el:.1f} s"}
+                               "sample": f"{done} tokens of the same workload ({batch}-token batches: "
+                                         f"BVHRouter soft top-8 + OLMoELayer.forward_topk over 64 "
+                                         f"TernaryExpertModule experts, fp32, the reference's torch "
+                                         f"operators as restated in oracle/torch_ref.py) in {el:.1f} s"}
     if rank == 0:
         print(json.dumps(out), flush=True)
     if world > 1:
@@ -818,26 +1089,31 @@ def run_ours(a):
         dist.destroy_process_group()
 
 
-def cpu_moe_rate(sample_tokens: int, budget_s: float = 15.0):
-    """Tokens/s of the CPU path: oracle router (soft, top-8) + fp32 ternary experts."""
-    from oracle import router as orouter
-    from oracle import ternary as otern
+def cpu_moe_layer(tokens: int):
+    """The reference's CPU MoE layer (oracle/torch_ref.py: BVHRouter soft top-8 +
+    OLMoELayer.forward_topk over TernaryExpertModule experts) and its input: the
+    headline's tokens (seed 2, rounded to bf16 as the GPU arm reads them) in fp32."""
+    import torch
+    from oracle import torch_ref
     from sb200 import synth
-    w = synth.router_weights(H, S, BRANCHING, seed=0)
-    experts = synth.ternary_experts(E_EXPERTS, H, I_INTER, seed=2)
-    x = synth.hidden_states(sample_tokens, H, seed=2).numpy()
+    layer = torch_ref.TorchMoELayer(synth.router_weights(H, S, BRANCHING, seed=0),
+                                    synth.ternary_experts(E_EXPERTS, H, I_INTER, seed=2), BRANCHING, TOPK)
+    x = synth.hidden_states(tokens, H, seed=2, dtype=torch.bfloat16).float()
+    return layer, x
 
-    def one():
-        o = orouter.router_forward(w, x, BRANCHING, mode="soft", k=TOPK)
-        otern.moe_combine(x, o["topk_ids"], o["topk_weights"], experts, fp32=True)
 
-    one()   # warm the BLAS and thread pools
+def cpu_moe_rate(tokens: int, budget_s: float = 20.0):
+    """Tokens/s of the reference's CPU layer on the host cores: whole batches of
+    the headline's token count until the budget is spent (at least one)."""
+    cpu_threads()
+    layer, x = cpu_moe_layer(tokens)
+    layer(x[:64])   # warm the thread pool
     done, t0 = 0, time.perf_counter()
     while True:
-        one()
-        done += sample_tokens
+        layer(x)
+        done += tokens
         el = time.perf_counter() - t0
-        if el >= budget_s or done >= 16 * sample_tokens:
+        if el >= budget_s:
             break
     return done / el, done, el
 
@@ -864,38 +1140,28 @@ def traffic_for(meta):
 
 
 def run_reference(a):
+    """The reference arm: the reference's CPU path (its torch operators, restated
+    op for op in oracle/torch_ref.py and checked there against the reference's
+    own outputs) over the headline's 4096 tokens per step, on every host core.
+    Rank 0 only; a step that would not let W + K steps end within about four
+    minutes is cut to a smaller token sample (reported in the config)."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from oracle import router as orouter
-    from oracle import ternary as otern
-    from sb200 import synth
-    cores = blas_threads()
-    w = synth.router_weights(H, S, BRANCHING, seed=0)
-    experts = synth.ternary_experts(E_EXPERTS, H, I_INTER, seed=2)
-    xall = synth.hidden_states(max(a.cpu_sample, 64), H, seed=2).numpy()
-
-    def run(xs):
-        o = orouter.router_forward(w, xs, BRANCHING, mode="soft", k=TOPK)
-        otern.moe_combine(xs, o["topk_ids"], o["topk_weights"], experts, fp32=True)
-
-    # a bounded sample per step: sized from one 64-token probe so that the
-    # requested W + K steps take about two minutes (16 .. cpu_sample tokens)
+    cores = cpu_threads()
+    tokens = a.batch or 4096
+    layer, x = cpu_moe_layer(tokens)
     t0 = time.perf_counter()
-    run(xall[:64])
-    per_tok = (time.perf_counter() - t0) / 64
-    budget = 120.0 / max(a.steps + a.warmup, 1)
-    sample = int(max(16, min(a.cpu_sample, budget / max(per_tok, 1e-9))))
-    x = xall[:sample]
-
-    def one():
-        run(x)
-
+    layer(x[:256])
+    per_tok = (time.perf_counter() - t0) / 256
+    budget = 240.0 / max(a.steps + a.warmup, 1)
+    sample = int(max(64, min(tokens, budget / max(per_tok, 1e-9))))
+    xs = x[:sample]
     for _ in range(a.warmup):
-        one()
+        layer(xs)
     t0 = time.perf_counter()
     for _ in range(a.steps):
-        one()
+        layer(xs)
     el = time.perf_counter() - t0
     value = sample * a.steps / el
     out = {"impl": "reference", "metric": "MoE-layer tokens/s (BVH route + ternary SwiGLU)",
@@ -905,10 +1171,13 @@ def run_reference(a):
            "data": "synthetic (seeded unit-RMS Gaussian tokens, random-init router and ternary experts)",
            "config": {"workload": "moe_layer_bvh_route_ternary_swiglu", "hidden": H,
                       "intermediate": I_INTER, "experts": E_EXPERTS, "top_k": TOPK,
-                      "tokens_per_step": sample, "router_select": "soft"},
+                      "tokens_per_step": sample, "tokens_per_gpu": tokens, "router_select": "soft",
+                      "parallelism": "host cores"},
            "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": cores, "kind": "port",
-                            "sample": f"{sample} tokens per step through the numpy ports of "
-                                      "python/bvh_router.py and TernaryExpertModule (fp32), host cores"},
+                            "sample": f"{sample} tokens per step: BVHRouter soft top-8 + OLMoELayer.forward_topk "
+                                      "over 64 TernaryExpertModule experts, the reference's torch operators in "
+                                      "its order (oracle/torch_ref.py; equal outputs to the reference modules), "
+                                      f"fp32, torch.set_num_threads({cores})"},
            "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                    "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
@@ -928,7 +1197,7 @@ def main():
     ap.add_argument("--skip-stack", action="store_true")
     ap.add_argument("--skip-config4", action="store_true")
     ap.add_argument("--skip-enhanced", action="store_true")
-    ap.add_argument("--cpu-sample", type=int, default=256)
+    ap.add_argument("--skip-sweeps", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     a = ap.parse_args()
     a.warmup = max(a.warmup, 3) if a.impl == "ours" else a.warmup

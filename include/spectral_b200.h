@@ -207,7 +207,10 @@ int sb_ternary_linear(const void* x, int x_dtype, int64_t M, int64_t K, int64_t 
 size_t sb_ternary_linear_workspace_bytes(int64_t M, int64_t K, int64_t N);
 
 /* Grouped MoE SwiGLU over E experts with top-k routing:
- *   out[t] = sum_j weights[t,j] * expert_{ids[t,j]}(x[t])   (j in fixed order 0..k-1)
+ *   out[t] = sum_j weights[t,j] * expert_{ids[t,j]}(x[t])
+ * The k terms of a token are added along a binary tree over the expert ids
+ * (two partial sums meet where their experts' indices first differ, deepest
+ * bit first), the order the expert-parallel layer below reproduces across GPUs.
  * Replaces the reference's per-(slot, expert) Python loop OLMoELayer.forward_topk
  * (python/olmoe_extract.py:126-157) over CUDATernaryExpertModule experts.
  * x: device [B,H] (SB_F32/SB_BF16); ids int32 [B,k] (each in [0,E)); weights fp32 [B,k];
@@ -224,6 +227,79 @@ int sb_ternary_moe_swiglu(const void* x, int x_dtype, int64_t B, int64_t H, int6
 
 size_t sb_ternary_moe_workspace_bytes(int64_t B, int64_t H, int64_t I,
                                       int32_t n_experts, int32_t top_k);
+
+/* ------------------------------------------------------------------------ */
+/* Expert-parallel MoE layer over the GPUs of one node                       */
+/* ------------------------------------------------------------------------ */
+/* The grouped ternary SwiGLU with the experts spread over W ranks (one
+ * process per GPU, W <= 8): rank r holds experts [r*E/W, (r+1)*E/W).  The
+ * layer's own kernels move each token row once to every rank that holds one of
+ * its experts, and the expert outputs back, through peer memory (NVLink /
+ * NVSwitch; CUDA IPC mappings), with no host synchronisation on the data path.
+ * The output equals sb_ternary_moe_swiglu on one GPU bit for bit when E/W is
+ * a power of two (same kernels per row, same summation tree).
+ * Replaces the reference's per-slot dispatch loop (python/olmoe_extract.py:
+ * 146-155) and its scatter / weighted-combine kernels (cuda/async_pipeline.cu:
+ * 79-133) when the experts do not all live on one GPU; the reference has no
+ * multi-GPU code.
+ *
+ * Set-up (collective over the W ranks):
+ *   sb_ep_create        on each rank, with its GPU current; allocates the
+ *                       peer-visible receive buffers (W * max_tokens rows each
+ *                       way) and a control block;
+ *   sb_ep_connect_nccl  exchanges the buffers' IPC handles over an NCCL
+ *                       communicator of the same W ranks (an ncclComm_t passed
+ *                       as void*, like the streams), or
+ *   sb_ep_export / sb_ep_connect  the same exchange done by the caller: each
+ *                       rank's SB_EP_HANDLE_BYTES bytes, gathered in rank order.
+ * Forward (collective: every rank calls it, equally often, any batch <=
+ * max_tokens including 0): x bf16 [B,H]; ids int32 [B,k] in [0,E); weights
+ * fp32 [B,k]; gate/up/down and scales: this rank's E/W experts in the layout
+ * of sb_ternary_moe_swiglu; out [B,H] SB_F32 or SB_BF16; workspace of
+ * sb_ep_workspace_bytes(h) bytes (1024-byte aligned), owned by the caller.
+ * Every wait for a peer is bounded by timeout_ms; one that runs out is
+ * reported by sb_ep_status (SB_ERR_DEVICE_TIMEOUT), after which the handle
+ * must be destroyed and the layer set up again.
+ * Tear-down: all ranks call sb_ep_destroy after a barrier (a rank's buffers
+ * stay mapped by its peers until they destroy theirs). */
+typedef struct sb_ep sb_ep;
+
+typedef struct {
+  int32_t world;        /* ranks W, 1..8 */
+  int32_t rank;         /* this process's rank */
+  int32_t n_experts;    /* E, a multiple of W, at most 255 per rank */
+  int32_t top_k;        /* k, 1..16 */
+  int64_t max_tokens;   /* tokens per rank per forward, at most */
+  int64_t hidden;       /* H, a multiple of 8 */
+  int64_t intermediate; /* I */
+  int32_t timeout_ms;   /* bound of each wait for a peer; 0 = 2000 */
+} sb_ep_desc;
+
+#define SB_EP_HANDLE_BYTES 128
+
+int sb_ep_create(const sb_ep_desc* desc, sb_ep** out);
+int sb_ep_export(const sb_ep* h, void* handle);
+int sb_ep_connect(sb_ep* h, const void* handles);
+int sb_ep_connect_nccl(sb_ep* h, void* nccl_comm, void* stream);
+size_t sb_ep_workspace_bytes(const sb_ep* h);
+int sb_ep_forward(sb_ep* h, const void* x, int x_dtype, int64_t batch, const int32_t* ids,
+                  const float* weights, const uint32_t* gate, const uint32_t* up, const uint32_t* down,
+                  const float* gate_scale, const float* up_scale, const float* down_scale,
+                  void* out, int out_dtype, void* workspace, size_t workspace_bytes, void* stream);
+/* Reads the handle's error word (synchronous): SB_OK, SB_ERR_DEVICE_TIMEOUT
+ * (a wait for a peer ran out) or SB_ERR_INVALID (an expert id out of range). */
+int sb_ep_status(sb_ep* h);
+/* Failure injection for tests: one bounded wait, on this rank's GPU, for a
+ * flag value no rank ever writes; sb_ep_status then reports the timeout. */
+int sb_ep_inject_stale_wait(sb_ep* h, void* stream);
+int sb_ep_destroy(sb_ep* h);
+
+/* NCCL bootstrap for C callers without a communicator of their own (NCCL is
+ * loaded at run time from libnccl.so.2): a 128-byte unique id made on one
+ * rank and shared by the caller, then one communicator per rank. */
+int sb_nccl_unique_id(void* id);
+int sb_nccl_comm_init(int nranks, int rank, const void* id, void** comm);
+int sb_nccl_comm_destroy(void* comm);
 
 /* ------------------------------------------------------------------------ */
 /* Enhanced BVH router (the OLMoE production router) and its top-k gate       */

@@ -8,7 +8,7 @@ pin for the packing restatement (its ``pack_ternary`` is host code and runs
 without a GPU) and, on a GPU box, as the timed reference-GPU kernel.  Nothing
 in the product loads it.  Sources are never copied into this repository.
 
-Usage: python oracle/build_ref.py [--reference /path/to/reference]
+Usage: python oracle/build_ref.py --reference /path/to/reference   (or SB_REFERENCE_ROOT)
 """
 
 from __future__ import annotations
@@ -63,9 +63,12 @@ def build_tree_kernel(reference: Path, verbose: bool = False) -> bool:
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("SB_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("SB_REFERENCE_ROOT"),
+                    help="root of the reference checkout (default: $SB_REFERENCE_ROOT)")
     ap.add_argument("-v", action="store_true")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("pass --reference or set SB_REFERENCE_ROOT")
     ok = build(Path(a.reference), a.v)
     ok = build_tree_kernel(Path(a.reference), a.v) and ok
     return 0 if ok else 1

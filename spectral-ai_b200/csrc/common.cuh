@@ -8,6 +8,8 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include <atomic>
+#include <mutex>
 #include <string>
 
 #include "../../include/spectral_b200.h"
@@ -40,6 +42,30 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dtype,
                  uint32_t box_cols, uint32_t box_rows, CUtensorMapSwizzle swizzle);
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// One-time set-up per device for one call site (kernel attributes, occupancy
+// queries): the first caller on a device runs `fn` under the object's lock,
+// concurrent first callers wait for it, and later callers only read an
+// atomic flag.  `value[dev]` keeps an int that `fn` may store (it is read
+// after once() returned SB_OK, which orders it after the store).
+struct PerDevice {
+  static constexpr int kMaxDevices = 64;
+  int value[kMaxDevices] = {};
+  template <typename F>
+  int once(int dev, F&& fn) {
+    if (dev < 0 || dev >= kMaxDevices) return fail(SB_ERR_CUDA, "device ordinal %d out of range", dev);
+    if (done_[dev].load(std::memory_order_acquire)) return SB_OK;
+    std::lock_guard<std::mutex> g(mu_);
+    if (done_[dev].load(std::memory_order_relaxed)) return SB_OK;
+    const int rc = fn();
+    if (rc == SB_OK) done_[dev].store(true, std::memory_order_release);
+    return rc;
+  }
+
+ private:
+  std::mutex mu_;
+  std::atomic<bool> done_[kMaxDevices] = {};
+};
 
 // Per-kernel CUDA-event timing (off by default).  A ProfScope records an event
 // pair around one launch on its stream; sb_profile_count()/sb_profile_entry()

@@ -992,14 +992,15 @@ int enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t batch, int precis
     if ((rc = make_tmap_2d(&tmx, P, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, M, 256, 256, 64, ETC_TOK,
                            CU_TENSOR_MAP_SWIZZLE_128B)))
       return rc;
-    static bool attr_tc[64] = {};
-    if (h->device < 64 && !attr_tc[h->device]) {
-      SB_CUDA_TRY(cudaFuncSetAttribute(enh_tail_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       ETC_SMEM_BYTES));
-      SB_CUDA_TRY(cudaFuncSetAttribute(enh_tail_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       ETC_SMEM_BYTES));
-      attr_tc[h->device] = true;
-    }
+    static PerDevice attr_tc;
+    if ((rc = attr_tc.once(h->device, []() -> int {
+           SB_CUDA_TRY(cudaFuncSetAttribute(enh_tail_tc_kernel<32>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            ETC_SMEM_BYTES));
+           SB_CUDA_TRY(cudaFuncSetAttribute(enh_tail_tc_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            ETC_SMEM_BYTES));
+           return SB_OK;
+         })))
+      return rc;
     ProfScope prof("enh_tail_tc", stream);
     int64_t blocks = (batch + ETC_TOK - 1) / ETC_TOK;
     if (blocks > num_sms()) blocks = num_sms();
@@ -1011,11 +1012,13 @@ int enh_forward(sb_enh* h, const void* x, int x_dtype, int64_t batch, int precis
     return SB_OK;
   }
   {
-    static bool attr[64] = {};
-    if (h->device < 64 && !attr[h->device]) {
-      SB_CUDA_TRY(cudaFuncSetAttribute(enh_tail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, ENH_SMEM_BYTES));
-      attr[h->device] = true;
-    }
+    static PerDevice attr;
+    if ((rc = attr.once(h->device, []() -> int {
+           SB_CUDA_TRY(cudaFuncSetAttribute(enh_tail_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            ENH_SMEM_BYTES));
+           return SB_OK;
+         })))
+      return rc;
     ProfScope prof("enh_tail", stream);
     int64_t blocks = (batch + ENH_TOK - 1) / ENH_TOK;
     const int64_t cap = (int64_t)num_sms() * 16;

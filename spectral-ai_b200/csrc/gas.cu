@@ -222,12 +222,14 @@ extern "C" int sb_gas_route(sb_gas* h, const float* positions, const float* dire
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const size_t smem = (size_t)h->n * sizeof(float4);
   cudaError_t e = cudaSuccess;
-  // opt-in shared memory, set once per device for the largest size asked so far
-  static size_t smem_set[64] = {};
-  if (smem > 48 * 1024 && (h->device >= 64 || smem > smem_set[h->device])) {
-    e = cudaFuncSetAttribute(gas_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e == cudaSuccess && h->device < 64) smem_set[h->device] = smem;
-  }
+  // opt-in shared memory: the kernel's cap is raised to 227 KB once per device
+  static PerDevice attr;
+  if (smem > 48 * 1024 &&
+      attr.once(h->device, [&]() -> int {
+        e = cudaFuncSetAttribute(gas_route_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+        return e == cudaSuccess ? SB_OK : SB_ERR_CUDA;
+      }) != SB_OK && e == cudaSuccess)
+    e = cudaErrorInvalidDevice;
   if (e == cudaSuccess) {
     ProfScope prof("gas_route", st);
     gas_route_kernel<<<(unsigned)blocks, GAS_THREADS, smem, st>>>(h->spheres, h->n, h->tris, positions, directions,

@@ -8,3 +8,4 @@
 #include "pipeline.cu"
 #include "tree.cu"
 #include "gas.cu"
+#include "ep.cu"

@@ -574,14 +574,15 @@ int pipe_launch_softmax_topk(const float* logits, int64_t B, int E, int k, const
                                                                           wts);
     } else {
       const size_t sm = (size_t)(64 * 64 + 64 + PIPE_TOK * 68) * sizeof(float);
-      static bool attr_done[64] = {};
-      int dev = 0;
+      static PerDevice attr;
+      int dev = 0, rc;
       SB_CUDA_TRY(cudaGetDevice(&dev));
-      if (dev < 64 && !attr_done[dev]) {
-        SB_CUDA_TRY(cudaFuncSetAttribute(pipe_topk_thread_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)sm));
-        attr_done[dev] = true;
-      }
+      if ((rc = attr.once(dev, [&]() -> int {
+             SB_CUDA_TRY(cudaFuncSetAttribute(pipe_topk_thread_kernel<64>,
+                                              cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm));
+             return SB_OK;
+           })))
+        return rc;
       pipe_topk_thread_kernel<64><<<(unsigned)tb, PIPE_TOK, sm, stream>>>(logits, B, E, k, cal_w, cal_b,
                                                                           apply_softmax, only_calibrate, probs, ids,
                                                                           wts);
@@ -596,11 +597,15 @@ int pipe_launch_softmax_topk(const float* logits, int64_t B, int E, int k, const
   // opt-in shared memory (a calibration of up to PIPE_CAL_MAX experts), once per device and kernel
 #define SB_PIPE_LAUNCH(P)                                                                                     \
   do {                                                                                                        \
-    static bool attr_p[64] = {};                                                                              \
-    if (smem > 48 * 1024 && !attr_p[dev]) {                                                                   \
-      SB_CUDA_TRY(cudaFuncSetAttribute(pipe_softmax_topk_kernel<P>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                       PIPE_CAL_MAX * PIPE_CAL_MAX * (int)sizeof(float)));                   \
-      attr_p[dev] = true;                                                                                     \
+    static PerDevice attr_p;                                                                                  \
+    if (smem > 48 * 1024) {                                                                                   \
+      const int arc = attr_p.once(dev, [&]() -> int {                                                                  \
+        SB_CUDA_TRY(cudaFuncSetAttribute(pipe_softmax_topk_kernel<P>,                                         \
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,                         \
+                                         PIPE_CAL_MAX * PIPE_CAL_MAX * (int)sizeof(float)));                  \
+        return SB_OK;                                                                                         \
+      });                                                                                                     \
+      if (arc) return arc;                                                                                    \
     }                                                                                                         \
     pipe_softmax_topk_kernel<P><<<(unsigned)blocks, PIPE_THREADS, smem, stream>>>(                           \
         logits, B, E, k, cal_w, cal_b, apply_softmax, only_calibrate, probs, ids, wts);                      \
@@ -680,23 +685,21 @@ extern "C" int sb_scatter_by_expert(const uint32_t* expert_ids, int64_t batch, i
     const size_t sm_rows = (size_t)SC_WARPS * n_experts * sizeof(int);
     const size_t sm_seg = (size_t)nseg * sizeof(int);  // one expert's row of segment counts
     SB_REQUIRE(sm_seg <= 200 * 1024, "too many scatter segments (%d) for one CTA's shared memory", nseg);
-    // opt-in shared memory, set once per device for the largest size asked so far
-    static size_t sm_seg_set[64] = {}, sm_rows_set[64] = {};
-    int dev = 0;
+    // opt-in shared memory: the kernels' caps are raised to 200 KB once per device
+    static PerDevice attr;
+    int dev = 0, arc;
     SB_CUDA_TRY(cudaGetDevice(&dev));
-    SB_REQUIRE(dev < 64, "device ordinal %d out of range", dev);
-    if (sm_seg > 48 * 1024 && sm_seg > sm_seg_set[dev]) {
-      SB_CUDA_TRY(cudaFuncSetAttribute(pipe_scatter_offsets_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)sm_seg));
-      sm_seg_set[dev] = sm_seg;
-    }
-    if (sm_rows > 48 * 1024 && sm_rows > sm_rows_set[dev]) {
-      SB_CUDA_TRY(cudaFuncSetAttribute(pipe_scatter_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)sm_rows));
-      SB_CUDA_TRY(cudaFuncSetAttribute(pipe_scatter_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)sm_rows));
-      sm_rows_set[dev] = sm_rows;
-    }
+    if ((sm_seg > 48 * 1024 || sm_rows > 48 * 1024) &&
+        (arc = attr.once(dev, []() -> int {
+           SB_CUDA_TRY(cudaFuncSetAttribute(pipe_scatter_offsets_kernel,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024));
+           SB_CUDA_TRY(cudaFuncSetAttribute(pipe_scatter_hist_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            200 * 1024));
+           SB_CUDA_TRY(cudaFuncSetAttribute(pipe_scatter_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            200 * 1024));
+           return SB_OK;
+         })))
+      return arc;
     int32_t* hist = nullptr;
     SB_CUDA_TRY(cudaMallocAsync(reinterpret_cast<void**>(&hist), (size_t)nseg * n_experts * sizeof(int32_t), st));
     ProfScope prof("pipe_scatter_by_expert", st);

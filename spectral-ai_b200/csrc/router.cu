@@ -909,13 +909,14 @@ int launch_gemm_tc(const char* name, const CUtensorMap& ta, const CUtensorMap& t
                    int M, int N, int K, Epi epi, cudaStream_t stream) {
   using C = GemmCfg<BN, STAGES>;
   auto kern = gemm_tc_kernel<BN, STAGES, Epi, TAIL>;
-  static bool attr_done[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_done[dev]) {
-    SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
-    attr_done[dev] = true;
-  }
+  static PerDevice attr;
+  int dev = 0, rc;
+  SB_CUDA_TRY(cudaGetDevice(&dev));
+  if ((rc = attr.once(dev, [&]() -> int {
+         SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES));
+         return SB_OK;
+       })))
+    return rc;
   const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN + (TAIL ? 1 : 0));
   const int grid = tiles < num_sms() ? tiles : num_sms();
   ProfScope prof(name, stream);
@@ -931,10 +932,9 @@ template <class Epi, bool TAIL>
 int launch_gemm_pair(const char* name, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tb2,
                      int M, int N, int K, Epi epi, cudaStream_t stream) {
   auto kern = gemm_pair_kernel<Epi, TAIL>;
-  static int pairs[64] = {};
-  int dev = 0;
+  static PerDevice pairs;
+  int dev = 0, rc;
   SB_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev >= 64) return fail(SB_ERR_CUDA, "device ordinal %d out of range", dev);
   cudaLaunchConfig_t cfg{};
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -946,16 +946,18 @@ int launch_gemm_pair(const char* name, const CUtensorMap& ta, const CUtensorMap&
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (!pairs[dev]) {
-    SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GP_SMEM_BYTES));
-    cfg.gridDim = dim3(2 * (num_sms() / 2));
-    int n = 0;
-    SB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
-    if (n < 1) return fail(SB_ERR_CUDA, "no CTA pair of the GEMM fits on this GPU");
-    pairs[dev] = n;
-  }
+  if ((rc = pairs.once(dev, [&]() -> int {
+         SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, GP_SMEM_BYTES));
+         cfg.gridDim = dim3(2 * (num_sms() / 2));
+         int n = 0;
+         SB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+         if (n < 1) return fail(SB_ERR_CUDA, "no CTA pair of the GEMM fits on this GPU");
+         pairs.value[dev] = n;
+         return SB_OK;
+       })))
+    return rc;
   const int tiles = ((M + GP_BM - 1) / GP_BM) * ((N + GP_BN - 1) / GP_BN + (TAIL ? 1 : 0));
-  cfg.gridDim = dim3(2 * (tiles < pairs[dev] ? tiles : pairs[dev]));
+  cfg.gridDim = dim3(2 * (tiles < pairs.value[dev] ? tiles : pairs.value[dev]));
   ProfScope prof(name, stream);
   SB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, ta, tb, tb2, M, N, K, idesc_f16(1, GP_BM, GP_BN),
                                  idesc_f16(1, GP_BM, TAIL_N), epi));
@@ -1160,15 +1162,15 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
   } else {
     if (dsm_soft > 48 * 1024) {
       // the opt-in limit is per device: set it once on each
-      static bool attr[64] = {};
-      int dev = 0;
+      static PerDevice attr;
+      int dev = 0, arc;
       SB_CUDA_TRY(cudaGetDevice(&dev));
-      SB_REQUIRE(dev < 64, "device ordinal %d out of range", dev);
-      if (!attr[dev]) {
-        SB_CUDA_TRY(cudaFuncSetAttribute(descent_soft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         227 * 1024));
-        attr[dev] = true;
-      }
+      if ((arc = attr.once(dev, []() -> int {
+             SB_CUDA_TRY(cudaFuncSetAttribute(descent_soft_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                              227 * 1024));
+             return SB_OK;
+           })))
+        return arc;
     }
     int64_t blocks = (batch + SOFT_WARPS - 1) / SOFT_WARPS;
     const int64_t cap = (int64_t)num_sms() * 8;

@@ -20,6 +20,7 @@
 #include "ternary_gemm.cuh"
 #include "ternary_ts.cuh"
 #include "ternary_pair.cuh"
+#include "tree_sum.cuh"
 
 #include <cstdlib>
 #include <cstring>
@@ -119,22 +120,91 @@ __global__ void moe_hist_kernel(const int32_t* __restrict__ ids, int64_t R, int 
   }
 }
 
-// Expert offsets (exclusive scan), scatter cursors and the m-tile table, in
-// one block of 1024 threads.  Expert segments start on 32-row boundaries
-// (segment = count rounded up to 32); m-tiles of `tile_rows` rows cover them,
-// `rows` valid and `pad` rows up to the segment end (a multiple of 32).  With
-// `hist` set the block also counts the ids itself (shared-memory histogram;
-// small batches), otherwise it reads `counts` from moe_hist_kernel.
 constexpr int PLAN_THREADS = 1024;
 
+// Expert offsets (exclusive scan of the counts rounded up to 32), zeroed
+// scatter cursors and the m-tile table, by one block of PLAN_THREADS threads;
+// `count(e)` gives expert e's rows (with `write_counts` they are also stored).
+// Expert segments start on 32-row boundaries (segment = count rounded up to
+// 32); m-tiles of `tile_rows` rows cover them, `rows` valid and `pad` rows up
+// to the segment end (a multiple of 32).
+template <typename CountFn>
+__device__ __forceinline__ void plan_segments(int E, CountFn count, bool write_counts, int* __restrict__ counts,
+                                              int* __restrict__ offsets, int* __restrict__ cursor,
+                                              MTile* __restrict__ mtiles, int* __restrict__ num_mtiles,
+                                              int max_mtiles, int tile_rows) {
+  __shared__ int warp_rows[32], warp_tiles[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // each thread owns a run of consecutive experts
+  const int per = (E + PLAN_THREADS - 1) / PLAN_THREADS;
+  const int e0 = tid * per < E ? tid * per : E, e1 = e0 + per < E ? e0 + per : E;
+  int my_rows = 0, my_tiles = 0;
+  for (int e = e0; e < e1; ++e) {
+    const int cp = (count(e) + 31) & ~31;
+    my_rows += cp;
+    my_tiles += (cp + tile_rows - 1) / tile_rows;
+  }
+  // block-wide exclusive scan of (rows, tiles)
+  int r_inc = my_rows, t_inc = my_tiles;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int rv = __shfl_up_sync(0xffffffffu, r_inc, o), tv = __shfl_up_sync(0xffffffffu, t_inc, o);
+    if (lane >= o) {
+      r_inc += rv;
+      t_inc += tv;
+    }
+  }
+  if (lane == 31) {
+    warp_rows[warp] = r_inc;
+    warp_tiles[warp] = t_inc;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    int rw = warp_rows[lane], tw = warp_tiles[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int rv = __shfl_up_sync(0xffffffffu, rw, o), tv = __shfl_up_sync(0xffffffffu, tw, o);
+      if (lane >= o) {
+        rw += rv;
+        tw += tv;
+      }
+    }
+    warp_rows[lane] = rw;  // inclusive over warps
+    warp_tiles[lane] = tw;
+  }
+  __syncthreads();
+  int off = r_inc - my_rows + (warp > 0 ? warp_rows[warp - 1] : 0);
+  int nt = t_inc - my_tiles + (warp > 0 ? warp_tiles[warp - 1] : 0);
+  for (int e = e0; e < e1; ++e) {
+    const int c = count(e);
+    const int cp = (c + 31) & ~31;
+    if (write_counts) counts[e] = c;
+    offsets[e] = off;
+    cursor[e] = 0;
+    for (int r = 0; r < cp; r += tile_rows, ++nt) {
+      if (nt >= max_mtiles) continue;
+      MTile t;
+      t.expert = e;
+      t.row0 = off + r;
+      t.rows = (c - r) < tile_rows ? (c - r) : tile_rows;
+      t.pad = (cp - r) < tile_rows ? (cp - r) : tile_rows;
+      mtiles[nt] = t;
+    }
+    off += cp;
+  }
+  if (tid == PLAN_THREADS - 1) *num_mtiles = nt < max_mtiles ? nt : max_mtiles;
+}
+
+// The plan of one batch in one block: with `hist` set the block also counts
+// the ids itself (shared-memory histogram; small batches), otherwise it reads
+// `counts` from moe_hist_kernel.
 __global__ void __launch_bounds__(PLAN_THREADS) moe_plan_kernel(const int32_t* __restrict__ ids, int64_t R, int E,
                                                                int hist, int* __restrict__ counts,
                                                                int* __restrict__ offsets, int* __restrict__ cursor,
                                                                MTile* __restrict__ mtiles, int* __restrict__ num_mtiles,
                                                                int max_mtiles, int tile_rows) {
   extern __shared__ int sh_count[];  // [E] when hist
-  __shared__ int warp_rows[32], warp_tiles[32];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int tid = threadIdx.x;
   if (hist) {
     for (int e = tid; e < E; e += PLAN_THREADS) sh_count[e] = 0;
     __syncthreads();
@@ -172,64 +242,8 @@ __global__ void __launch_bounds__(PLAN_THREADS) moe_plan_kernel(const int32_t* _
     for (int64_t i = i0 + tid; i < R; i += PLAN_THREADS) count(ids[i]);
     __syncthreads();
   }
-  // each thread owns a run of consecutive experts
-  const int per = (E + PLAN_THREADS - 1) / PLAN_THREADS;
-  const int e0 = tid * per < E ? tid * per : E, e1 = e0 + per < E ? e0 + per : E;
-  int my_rows = 0, my_tiles = 0;
-  for (int e = e0; e < e1; ++e) {
-    const int cp = ((hist ? sh_count[e] : counts[e]) + 31) & ~31;
-    my_rows += cp;
-    my_tiles += (cp + tile_rows - 1) / tile_rows;
-  }
-  // block-wide exclusive scan of (rows, tiles)
-  int r_inc = my_rows, t_inc = my_tiles;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int rv = __shfl_up_sync(0xffffffffu, r_inc, o), tv = __shfl_up_sync(0xffffffffu, t_inc, o);
-    if (lane >= o) {
-      r_inc += rv;
-      t_inc += tv;
-    }
-  }
-  if (lane == 31) {
-    warp_rows[warp] = r_inc;
-    warp_tiles[warp] = t_inc;
-  }
-  __syncthreads();
-  if (warp == 0) {
-    int rw = warp_rows[lane], tw = warp_tiles[lane];
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int rv = __shfl_up_sync(0xffffffffu, rw, o), tv = __shfl_up_sync(0xffffffffu, tw, o);
-      if (lane >= o) {
-        rw += rv;
-        tw += tv;
-      }
-    }
-    warp_rows[lane] = rw;  // inclusive over warps
-    warp_tiles[lane] = tw;
-  }
-  __syncthreads();
-  int off = r_inc - my_rows + (warp > 0 ? warp_rows[warp - 1] : 0);
-  int nt = t_inc - my_tiles + (warp > 0 ? warp_tiles[warp - 1] : 0);
-  for (int e = e0; e < e1; ++e) {
-    const int c = hist ? sh_count[e] : counts[e];
-    const int cp = (c + 31) & ~31;
-    if (hist) counts[e] = c;
-    offsets[e] = off;
-    cursor[e] = 0;
-    for (int r = 0; r < cp; r += tile_rows, ++nt) {
-      if (nt >= max_mtiles) continue;
-      MTile t;
-      t.expert = e;
-      t.row0 = off + r;
-      t.rows = (c - r) < tile_rows ? (c - r) : tile_rows;
-      t.pad = (cp - r) < tile_rows ? (cp - r) : tile_rows;
-      mtiles[nt] = t;
-    }
-    off += cp;
-  }
-  if (tid == PLAN_THREADS - 1) *num_mtiles = nt < max_mtiles ? nt : max_mtiles;
+  plan_segments(E, [&](int e) { return hist ? sh_count[e] : counts[e]; }, hist != 0, counts, offsets, cursor,
+                mtiles, num_mtiles, max_mtiles, tile_rows);
 }
 
 // Histogram + plan for one batch: one fused block for small batches, else a
@@ -327,7 +341,6 @@ __global__ void moe_scatter_kernel(const TX* __restrict__ x, const int32_t* __re
   }
 }
 
-// out[t] = sum_j y[inv[t*k+j]] in slot order (fixed, so results are reproducible)
 template <typename TO>
 __device__ __forceinline__ TO cvt_out(float v);
 template <> __device__ __forceinline__ float cvt_out<float>(float v) { return v; }
@@ -343,54 +356,64 @@ __device__ __forceinline__ void store4<__nv_bfloat16>(__nv_bfloat16* p, float4 v
   *reinterpret_cast<uint2*>(p) = make_uint2(*reinterpret_cast<uint32_t*>(&a), *reinterpret_cast<uint32_t*>(&b));
 }
 
-// out[t] = sum_j y[inv[t*k+j]] in slot order (fixed, so results are reproducible).
-// Vector path: one thread per 4 columns (needs H % 4 == 0).
-// KC > 0: k == KC known at compile time; the k row indices, then the k
-// float4 loads, go out before the sums (same slot order, same results).
+// out[t] = the tree sum (tree_sum.cuh) of y[inv[t*k + j]] over the token's
+// slots j whose expert is in range, the positions being the expert ids, so the
+// single-GPU layer and the expert-parallel layer add the same values in the
+// same grouping.  One warp per token: the warp ranks the token's entries, then
+// each lane sums its columns (16-byte groups when H % 4 == 0) with the KC
+// values of one column group in registers (KC >= k).
 template <typename TO, int KC>
-__global__ void moe_combine_kernel(const float* __restrict__ y, const int* __restrict__ inv, int64_t B,
-                                   int k, int H, TO* __restrict__ out) {
-  if ((H & 3) == 0) {
-    const int H4 = H >> 2;
-    const int64_t total = B * (int64_t)H4;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-      const int64_t t = i / H4;
-      const int c = (int)(i % H4) * 4;
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      if constexpr (KC > 0) {
-        int pos[KC];
-        float4 v[KC];
+__global__ void moe_combine_kernel(const float* __restrict__ y, const int* __restrict__ inv,
+                                   const int32_t* __restrict__ ids, int64_t B, int k, int H,
+                                   TO* __restrict__ out) {
+  const int lane = threadIdx.x & 31;
+  const bool vec = (H & 3) == 0;
+  const int ncol = vec ? H >> 2 : H;
+  for (int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < B;
+       t += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    int pos = -1, e = 0;
+    if (lane < k) {
+      pos = __ldg(inv + t * k + lane);
+      e = __ldg(ids + t * k + lane);
+    }
+    const unsigned vm = __ballot_sync(0xffffffffu, lane < k && pos >= 0);
+    const int n = __popc(vm);
+    // entry `lane` of the compacted list (lanes < n)
+    int from = 0;
+    if (lane < n) {
+      unsigned m = vm;
+      for (int i = 0; i < lane; ++i) m &= m - 1u;
+      from = __ffs(m) - 1;
+    }
+    const int cp = __shfl_sync(0xffffffffu, e, from), crow = __shfl_sync(0xffffffffu, pos, from);
+    const WarpTree wt = warp_tree(cp, n);
+    int64_t row[KC];
 #pragma unroll
-        for (int j = 0; j < KC; ++j) pos[j] = __ldg(inv + t * KC + j);
+    for (int r = 0; r < KC; ++r) row[r] = (int64_t)__shfl_sync(0xffffffffu, crow, r < n ? tree_order(wt, r) : 0);
+    for (int c = lane; c < ncol; c += 32) {
+      float4 v[KC];
 #pragma unroll
-        for (int j = 0; j < KC; ++j)
-          if (pos[j] >= 0) v[j] = __ldg(reinterpret_cast<const float4*>(y + (int64_t)pos[j] * H + c));
-#pragma unroll
-        for (int j = 0; j < KC; ++j)
-          if (pos[j] >= 0) {
-            acc.x += v[j].x;
-            acc.y += v[j].y;
-            acc.z += v[j].z;
-            acc.w += v[j].w;
-          }
-        store4<TO>(out + t * H + c, acc);
-        continue;
-      }
-      for (int j = 0; j < k; ++j) {
-        const int pos = __ldg(inv + t * k + j);
-        if (pos >= 0) {
-          const float4 v = __ldg(reinterpret_cast<const float4*>(y + (int64_t)pos * H + c));
-          acc.x += v.x;
-          acc.y += v.y;
-          acc.z += v.z;
-          acc.w += v.w;
+      for (int r = 0; r < KC; ++r) {
+        if (r < n) {
+          v[r] = vec ? __ldg(reinterpret_cast<const float4*>(y + row[r] * H) + c)
+                     : make_float4(__ldg(y + row[r] * H + c), 0.f, 0.f, 0.f);
+        } else {
+          v[r] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
       }
-      store4<TO>(out + t * H + c, acc);
+      const float4 acc = tree_apply<KC>(v, wt.sched);
+      if (vec)
+        store4<TO>(out + t * H + 4 * c, acc);
+      else
+        out[t * H + c] = cvt_out<TO>(acc.x);
     }
-    return;
   }
+}
+
+// Slot-order sum for k > TREE_MAX (outside the tree's range).
+template <typename TO>
+__global__ void moe_combine_slots_kernel(const float* __restrict__ y, const int* __restrict__ inv, int64_t B,
+                                         int k, int H, TO* __restrict__ out) {
   const int64_t total = B * (int64_t)H;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
        i += (int64_t)gridDim.x * blockDim.x) {
@@ -464,13 +487,14 @@ template <int MODE, int FMT>
 int launch_tgemm(const char* name, const CUtensorMap& ta, const CUtensorMap& tb0, const CUtensorMap& tb1,
                  const TernGemmParams& p, cudaStream_t stream) {
   auto kern = ternary_gemm_kernel<MODE, FMT>;
-  static bool attr_done[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_done[dev]) {
-    SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TG_SMEM_BYTES));
-    attr_done[dev] = true;
-  }
+  static PerDevice attr;
+  int dev = 0, rc;
+  SB_CUDA_TRY(cudaGetDevice(&dev));
+  if ((rc = attr.once(dev, [&]() -> int {
+         SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TG_SMEM_BYTES));
+         return SB_OK;
+       })))
+    return rc;
   ProfScope prof(name, stream);
   kern<<<num_sms(), TG_THREADS, TG_SMEM_BYTES, stream>>>(ta, tb0, tb1, p);
   SB_CUDA_TRY(cudaGetLastError());
@@ -481,13 +505,14 @@ template <int MODE, int FMT>
 int launch_ts(const char* name, const CUtensorMap& tx, const CUtensorMap& tw0, const CUtensorMap& tw1,
               const TernGemmParams& p, cudaStream_t stream) {
   auto kern = ternary_ts_kernel<MODE, FMT>;
-  static bool attr_done[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 64 && !attr_done[dev]) {
-    SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TS_SMEM_BYTES));
-    attr_done[dev] = true;
-  }
+  static PerDevice attr;
+  int dev = 0, rc;
+  SB_CUDA_TRY(cudaGetDevice(&dev));
+  if ((rc = attr.once(dev, [&]() -> int {
+         SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TS_SMEM_BYTES));
+         return SB_OK;
+       })))
+    return rc;
   ProfScope prof(name, stream);
   kern<<<num_sms(), TS_THREADS, TS_SMEM_BYTES, stream>>>(tx, tw0, tw1, p);
   SB_CUDA_TRY(cudaGetLastError());
@@ -522,8 +547,8 @@ template <int MODE, int FMT, int STREAMS>
 int launch_pair_s(const char* name, const CUtensorMap& tx, const CUtensorMap& tw0, const CUtensorMap& tw1,
                   const CUtensorMap& tout, const TernGemmParams& p, cudaStream_t stream) {
   auto kern = ternary_pair_kernel<MODE, FMT, STREAMS>;
-  static int pairs[64] = {};
-  int dev = 0;
+  static PerDevice pairs;
+  int dev = 0, rc;
   SB_CUDA_TRY(cudaGetDevice(&dev));
   cudaLaunchConfig_t cfg{};
   cudaLaunchAttribute attr[1];
@@ -536,16 +561,17 @@ int launch_pair_s(const char* name, const CUtensorMap& tx, const CUtensorMap& tw
   cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (dev >= 64) return fail(SB_ERR_CUDA, "device ordinal %d out of range", dev);
-  if (!pairs[dev]) {
-    SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TP_SMEM_BYTES));
-    cfg.gridDim = dim3(2 * (num_sms() / 2));
-    int n = 0;
-    SB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
-    if (n < 1) return fail(SB_ERR_CUDA, "no CTA pair of the ternary kernel fits on this GPU");
-    pairs[dev] = n;
-  }
-  cfg.gridDim = dim3(2 * pairs[dev]);
+  if ((rc = pairs.once(dev, [&]() -> int {
+         SB_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, TP_SMEM_BYTES));
+         cfg.gridDim = dim3(2 * (num_sms() / 2));
+         int n = 0;
+         SB_CUDA_TRY(cudaOccupancyMaxActiveClusters(&n, kern, &cfg));
+         if (n < 1) return fail(SB_ERR_CUDA, "no CTA pair of the ternary kernel fits on this GPU");
+         pairs.value[dev] = n;
+         return SB_OK;
+       })))
+    return rc;
+  cfg.gridDim = dim3(2 * pairs.value[dev]);
   ProfScope prof(name, stream);
   SB_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, tx, tw0, tw1, tout, p));
   return SB_OK;
@@ -561,6 +587,133 @@ int launch_pair(const char* name, const CUtensorMap& tx, const CUtensorMap& tw0,
 int check_ternary_shapes(int64_t H, int64_t I) {
   SB_REQUIRE(H > 0 && I > 0, "hidden=%lld and intermediate=%lld must be positive", (long long)H, (long long)I);
   SB_REQUIRE(H <= (1 << 20) && I <= (1 << 20), "dimensions too large");
+  return SB_OK;
+}
+
+template <typename TO>
+int launch_combine(const float* yp, const int* inv, const int32_t* ids, int64_t B, int k, int64_t H, TO* out,
+                   cudaStream_t stream) {
+  if (k > TREE_MAX) {
+    int64_t blocks = (B * H + 255) / 256;
+    if (blocks > (int64_t)num_sms() * 32) blocks = (int64_t)num_sms() * 32;
+    moe_combine_slots_kernel<TO><<<(unsigned)blocks, 256, 0, stream>>>(yp, inv, B, k, (int)H, out);
+  } else {
+    int64_t blocks = (B + 7) / 8;  // 8 tokens (warps) per block
+    if (blocks > (int64_t)num_sms() * 16) blocks = (int64_t)num_sms() * 16;
+    if (k <= 8)
+      moe_combine_kernel<TO, 8><<<(unsigned)blocks, 256, 0, stream>>>(yp, inv, ids, B, k, (int)H, out);
+    else
+      moe_combine_kernel<TO, 16><<<(unsigned)blocks, 256, 0, stream>>>(yp, inv, ids, B, k, (int)H, out);
+  }
+  SB_CUDA_TRY(cudaGetLastError());
+  return SB_OK;
+}
+
+// The k per-slot outputs of each token summed into out (tree order).
+int moe_combine(const float* yp, const int* inv, const int32_t* ids, int64_t B, int k, int64_t H, void* out,
+                int out_dtype, cudaStream_t stream) {
+  ProfScope prof("moe_combine", stream);
+  if (out_dtype == SB_F32) return launch_combine(yp, inv, ids, B, k, H, static_cast<float*>(out), stream);
+  return launch_combine(yp, inv, ids, B, k, H, static_cast<__nv_bfloat16*>(out), stream);
+}
+
+// The two grouped GEMMs of the SwiGLU over rows grouped by expert (the m-tile
+// table in device memory): h = silu(s_g * (x T_g^T)) * (s_u * (x T_u^T)) into
+// hp (fp16), then y = w * s_d * (h T_d^T) into yp (fp32, one row per slot).
+struct GroupedSwiGLU {
+  const void* xp;
+  __half* hp;
+  float* yp;
+  int64_t Rp, ldx, ldh, H, I;
+  int32_t E;
+  const MTile* mtiles;
+  const int* nmt;
+  const float* row_w;
+  const uint32_t *gate, *up, *down;
+  const float *gs, *us, *ds;
+  int fmt_gu;  // 1: bf16 activations, 0: fp16
+  int engine;
+};
+
+int grouped_swiglu(const GroupedSwiGLU& g, cudaStream_t stream) {
+  int rc;
+  const int64_t H = g.H, I = g.I;
+  const int32_t E = g.E;
+  const int engine = g.engine, fmt_gu = g.fmt_gu;
+  const void* xp = g.xp;
+  __half* hp = g.hp;
+  float* yp = g.yp;
+  const uint32_t *gate = g.gate, *up = g.up, *down = g.down;
+  const float *gs = g.gs, *us = g.us, *ds = g.ds;
+  const MTile* mtiles = g.mtiles;
+  const int* nmt = g.nmt;
+  const float* row_w = g.row_w;
+  // tensor maps: activations (SW128, 64 x 128 box) and packed weights (16 B x rows box)
+  CUtensorMap tmx, tmg, tmu, tmh, tmd;
+  const CUtensorMapDataType adt = fmt_gu ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int64_t KWh = ternary_row_words(H), KWi = ternary_row_words(I);
+  const bool pair = engine == ENGINE_PAIR;
+  const uint32_t gu_box = pair ? 64 : 128, d_box = pair ? 128 : 256;
+  const uint32_t p_words = pair ? TP_KB / 16 : 4;  // packed words per row in one weight box
+  // token rows per activation box: two 48-row boxes per CTA with two MMA streams
+  const uint32_t x_rows = pair ? (pair_streams() == 2 ? TP_QROWS : TP_HALF_ROWS) : 128;
+  if ((rc = make_tmap_2d(&tmx, xp, adt, 2, g.Rp, H, g.ldx, 64, x_rows, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&tmg, gate, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, p_words, gu_box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+      (rc = make_tmap_2d(&tmu, up, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, p_words, gu_box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+      (rc = make_tmap_2d(&tmh, hp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.Rp, I, g.ldh, 64, x_rows,
+                         CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&tmd, down, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * H, KWi, KWi, p_words, d_box,
+                         CU_TENSOR_MAP_SWIZZLE_NONE)))
+    return rc;
+  CUtensorMap tmh_out{}, tmy_out{};
+  if (pair && ((rc = make_tmap_2d(&tmh_out, hp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.Rp, I, g.ldh, 16, 32,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+               (rc = make_tmap_2d(&tmy_out, yp, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.Rp, H, H, 32, 32,
+                                  CU_TENSOR_MAP_SWIZZLE_NONE))))
+    return rc;
+
+  TernGemmParams pg{};
+  pg.mtiles = mtiles;
+  pg.num_mtiles = nmt;
+  pg.n_ntiles = (int)((I + 127) / 128);
+  pg.N = (int)I;
+  pg.K = (int)H;
+  pg.b_rows = (int)I;
+  pg.s0 = gs;
+  pg.s1 = us;
+  pg.out = hp;
+  pg.ldo = g.ldh;
+  if (engine == ENGINE_PAIR)
+    rc = fmt_gu ? launch_pair<TG_GATEUP, 1>("ternary_gateup_tc", tmx, tmg, tmu, tmh_out, pg, stream)
+                : launch_pair<TG_GATEUP, 0>("ternary_gateup_tc", tmx, tmg, tmu, tmh_out, pg, stream);
+  else if (engine == ENGINE_TS)
+    rc = fmt_gu ? launch_ts<TG_GATEUP, 1>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream)
+                : launch_ts<TG_GATEUP, 0>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream);
+  else
+    rc = fmt_gu ? launch_tgemm<TG_GATEUP, 1>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream)
+                : launch_tgemm<TG_GATEUP, 0>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream);
+  if (rc) return rc;
+  TernGemmParams pd{};
+  pd.mtiles = mtiles;
+  pd.num_mtiles = nmt;
+  pd.n_ntiles = (int)((H + 255) / 256);
+  pd.N = (int)H;
+  pd.K = (int)I;
+  pd.b_rows = (int)H;
+  pd.s0 = ds;
+  pd.row_w = row_w;
+  pd.out = yp;
+  pd.ldo = H;
+  if (engine == ENGINE_PAIR)
+    rc = launch_pair<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, tmy_out, pd, stream);
+  else if (engine == ENGINE_TS)
+    rc = launch_ts<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, pd, stream);
+  else
+    rc = launch_tgemm<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, pd, stream);
+  if (rc) return rc;
+
   return SB_OK;
 }
 
@@ -624,95 +777,10 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
     SB_CUDA_TRY(cudaGetLastError());
   }
 
-  // tensor maps: activations (SW128, 64 x 128 box) and packed weights (16 B x rows box)
-  CUtensorMap tmx, tmg, tmu, tmh, tmd;
-  const CUtensorMapDataType adt = fmt_gu ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
-  const int64_t KWh = ternary_row_words(H), KWi = ternary_row_words(I);
-  const bool pair = engine == ENGINE_PAIR;
-  const uint32_t gu_box = pair ? 64 : 128, d_box = pair ? 128 : 256;
-  const uint32_t p_words = pair ? TP_KB / 16 : 4;  // packed words per row in one weight box
-  // token rows per activation box: two 48-row boxes per CTA with two MMA streams
-  const uint32_t x_rows = pair ? (pair_streams() == 2 ? TP_QROWS : TP_HALF_ROWS) : 128;
-  if ((rc = make_tmap_2d(&tmx, xp, adt, 2, L.Rp, H, L.ldx, 64, x_rows, CU_TENSOR_MAP_SWIZZLE_128B)) ||
-      (rc = make_tmap_2d(&tmg, gate, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, p_words, gu_box,
-                         CU_TENSOR_MAP_SWIZZLE_NONE)) ||
-      (rc = make_tmap_2d(&tmu, up, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, p_words, gu_box,
-                         CU_TENSOR_MAP_SWIZZLE_NONE)) ||
-      (rc = make_tmap_2d(&tmh, hp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.Rp, I, L.ldh, 64, x_rows,
-                         CU_TENSOR_MAP_SWIZZLE_128B)) ||
-      (rc = make_tmap_2d(&tmd, down, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * H, KWi, KWi, p_words, d_box,
-                         CU_TENSOR_MAP_SWIZZLE_NONE)))
-    return rc;
-  CUtensorMap tmh_out{}, tmy_out{};
-  if (pair && ((rc = make_tmap_2d(&tmh_out, hp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, L.Rp, I, L.ldh, 16, 32,
-                                  CU_TENSOR_MAP_SWIZZLE_NONE)) ||
-               (rc = make_tmap_2d(&tmy_out, yp, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, L.Rp, H, H, 32, 32,
-                                  CU_TENSOR_MAP_SWIZZLE_NONE))))
-    return rc;
-
-  TernGemmParams pg{};
-  pg.mtiles = mtiles;
-  pg.num_mtiles = nmt;
-  pg.n_ntiles = (int)((I + 127) / 128);
-  pg.N = (int)I;
-  pg.K = (int)H;
-  pg.b_rows = (int)I;
-  pg.s0 = gs;
-  pg.s1 = us;
-  pg.out = hp;
-  pg.ldo = L.ldh;
-  if (engine == ENGINE_PAIR)
-    rc = fmt_gu ? launch_pair<TG_GATEUP, 1>("ternary_gateup_tc", tmx, tmg, tmu, tmh_out, pg, stream)
-                : launch_pair<TG_GATEUP, 0>("ternary_gateup_tc", tmx, tmg, tmu, tmh_out, pg, stream);
-  else if (engine == ENGINE_TS)
-    rc = fmt_gu ? launch_ts<TG_GATEUP, 1>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream)
-                : launch_ts<TG_GATEUP, 0>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream);
-  else
-    rc = fmt_gu ? launch_tgemm<TG_GATEUP, 1>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream)
-                : launch_tgemm<TG_GATEUP, 0>("ternary_gateup_tc", tmx, tmg, tmu, pg, stream);
-  if (rc) return rc;
-
-  TernGemmParams pd{};
-  pd.mtiles = mtiles;
-  pd.num_mtiles = nmt;
-  pd.n_ntiles = (int)((H + 255) / 256);
-  pd.N = (int)H;
-  pd.K = (int)I;
-  pd.b_rows = (int)H;
-  pd.s0 = ds;
-  pd.row_w = row_w;
-  pd.out = yp;
-  pd.ldo = H;
-  if (engine == ENGINE_PAIR)
-    rc = launch_pair<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, tmy_out, pd, stream);
-  else if (engine == ENGINE_TS)
-    rc = launch_ts<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, pd, stream);
-  else
-    rc = launch_tgemm<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, pd, stream);
-  if (rc) return rc;
-
-  {
-    ProfScope prof("moe_combine", stream);
-    int64_t blocks = (B * H + 255) / 256;
-    if (blocks > (int64_t)num_sms() * 32) blocks = (int64_t)num_sms() * 32;
-    if (out_dtype == SB_F32) {
-      if (k == 8)
-        moe_combine_kernel<float, 8><<<(unsigned)blocks, 256, 0, stream>>>(yp, inv, B, k, (int)H,
-                                                                          static_cast<float*>(out));
-      else
-        moe_combine_kernel<float, 0><<<(unsigned)blocks, 256, 0, stream>>>(yp, inv, B, k, (int)H,
-                                                                          static_cast<float*>(out));
-    } else {
-      if (k == 8)
-        moe_combine_kernel<__nv_bfloat16, 8><<<(unsigned)blocks, 256, 0, stream>>>(
-            yp, inv, B, k, (int)H, static_cast<__nv_bfloat16*>(out));
-      else
-        moe_combine_kernel<__nv_bfloat16, 0><<<(unsigned)blocks, 256, 0, stream>>>(
-            yp, inv, B, k, (int)H, static_cast<__nv_bfloat16*>(out));
-    }
-    SB_CUDA_TRY(cudaGetLastError());
-  }
-  return SB_OK;
+  GroupedSwiGLU g{xp, hp, yp, L.Rp, L.ldx, L.ldh, H, I, E, mtiles, nmt, row_w,
+                  gate, up, down, gs, us, ds, fmt_gu, engine};
+  if ((rc = grouped_swiglu(g, stream))) return rc;
+  return moe_combine(yp, inv, ids, B, k, H, out, out_dtype, stream);
 }
 
 }  // namespace

@@ -73,6 +73,15 @@ class EnhOutputs(C.Structure):
 
 SB_GATE_SOFTMAX, SB_GATE_TOPK_SOFTMAX, SB_GATE_HYBRID = 0, 1, 2
 
+
+class EpDesc(C.Structure):
+    _fields_ = [("world", C.c_int32), ("rank", C.c_int32), ("n_experts", C.c_int32), ("top_k", C.c_int32),
+                ("max_tokens", C.c_int64), ("hidden", C.c_int64), ("intermediate", C.c_int64),
+                ("timeout_ms", C.c_int32)]
+
+
+SB_EP_HANDLE_BYTES = 128
+
 # (name, restype, argtypes) of every symbol the header declares
 SIGNATURES = [
     ("sb_abi_version", C.c_int, []),
@@ -151,6 +160,20 @@ SIGNATURES = [
      [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int64, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
       C.c_void_p]),
     ("sb_gas_destroy", C.c_int, [C.c_void_p]),
+    ("sb_ep_create", C.c_int, [C.POINTER(EpDesc), C.POINTER(C.c_void_p)]),
+    ("sb_ep_export", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("sb_ep_connect", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("sb_ep_connect_nccl", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
+    ("sb_ep_workspace_bytes", C.c_size_t, [C.c_void_p]),
+    ("sb_ep_forward", C.c_int,
+     [C.c_void_p, C.c_void_p, C.c_int, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+      C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),
+    ("sb_ep_status", C.c_int, [C.c_void_p]),
+    ("sb_ep_inject_stale_wait", C.c_int, [C.c_void_p, C.c_void_p]),
+    ("sb_ep_destroy", C.c_int, [C.c_void_p]),
+    ("sb_nccl_unique_id", C.c_int, [C.c_void_p]),
+    ("sb_nccl_comm_init", C.c_int, [C.c_int, C.c_int, C.c_void_p, C.POINTER(C.c_void_p)]),
+    ("sb_nccl_comm_destroy", C.c_int, [C.c_void_p]),
 ]
 
 _lib = None

@@ -1,37 +1,153 @@
-"""Expert-parallel MoE layer: experts sharded over the ranks of a process group,
-tokens exchanged with all-to-all (NCCL over NVLink on B200; gloo on CPU for tests).
+"""Expert-parallel MoE layer over the GPUs of one node (one process per GPU).
 
-The reference has no multi-GPU code; this is the layer's distributed form.
-With E experts on W ranks, rank r holds experts [r*E/W, (r+1)*E/W).  One
-forward on every rank:
+With E experts on W ranks, rank r holds experts [r*E/W, (r+1)*E/W).  The
+layer's own kernels (``sb_ep_forward``, csrc/ep.cu) move every token row once
+to each rank that holds one of its experts and bring back one partial sum per
+(token, rank), all through peer memory over NVLink: there is no host
+synchronisation and no library collective on the data path.  The output equals
+the single-GPU layer (``TernaryExperts.forward``) bit for bit when E/W is a
+power of two, because both add a token's expert outputs along the same binary
+tree over the expert ids (csrc/tree_sum.cuh).
 
-  1. local routing (ids, weights [B, k]) -> destination rank of every
-     (token, slot) pair = ids // (E/W); pairs are grouped by destination with
-     a stable sort;
-  2. all-to-all of the pair counts, then of the token rows, local expert ids
-     and routing weights (dispatch);
-  3. the local experts run on the received rows (one slot per row, weight
-     applied in the down-projection epilogue);
-  4. all-to-all of the fp32 expert outputs back to the senders (combine), and
-     out[t] = sum_j y[t, j] accumulated in slot order j = 0..k-1.
+The reference has no multi-GPU code; this replaces its per-slot Python
+dispatch loop (python/olmoe_extract.py:146-155) when the experts are spread
+over GPUs.
 
-Because every row's expert output is computed by the same kernel with the
-same arithmetic as in the single-GPU layer, and the final sum runs in the
-same slot order, the sharded output equals the single-GPU output bit for bit.
+``torch.distributed`` is the plumbing of the set-up only: the ranks exchange
+the 128-byte IPC handles of their receive buffers (``exchange_handles``), or
+the C ABI does it over an NCCL communicator (``sb_ep_connect_nccl``).
+
+``AllToAllMoE`` is the same layer over the library collective
+(``torch.distributed.all_to_all_single``, NCCL), kept as the measured baseline
+of the fused exchange.
 """
 
 from __future__ import annotations
 
+import ctypes as C
 from typing import Callable, Optional
 
 import torch
 import torch.distributed as dist
 
+from . import _lib
+
+
+def exchange_handles(mine: bytes, group: Optional[dist.ProcessGroup] = None) -> bytes:
+    """Every rank's handle bytes, concatenated in rank order (a collective).
+    Raises if a rank does not join within the process group's timeout."""
+    world = dist.get_world_size(group)
+    got = [None] * world
+    dist.all_gather_object(got, bytes(mine), group=group)
+    if any(g is None or len(g) != len(mine) for g in got):
+        raise RuntimeError("handle exchange: a rank sent no handle")
+    return b"".join(got)
+
 
 class ExpertParallelMoE:
+    """The grouped ternary SwiGLU with this rank's experts (``TernaryExperts``
+    holding experts [rank*E/W, (rank+1)*E/W)) and the token exchange on the
+    device.  ``forward`` is collective: every rank calls it equally often."""
+
+    def __init__(self, local_experts, n_experts: int, top_k: int, max_tokens: int,
+                 group: Optional[dist.ProcessGroup] = None, timeout_ms: int = 2000,
+                 nccl_comm: Optional[int] = None, workspace: Optional[torch.Tensor] = None):
+        """``workspace``: a uint8 device buffer to use (and grow) instead of a
+        private one, for layers that run one after another on one stream (a
+        stack); ``self.workspace`` is the buffer in use."""
+        self.lib = _lib.load()
+        self.experts = local_experts
+        self.device = local_experts.device
+        if self.device.type != "cuda":
+            raise RuntimeError("the expert-parallel layer runs on CUDA devices only")
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        if n_experts % self.world or local_experts.E != n_experts // self.world:
+            raise ValueError(f"{local_experts.E} local experts do not make {n_experts} over {self.world} ranks")
+        self.n_experts, self.top_k, self.max_tokens = int(n_experts), int(top_k), int(max_tokens)
+        desc = _lib.EpDesc(self.world, self.rank, self.n_experts, self.top_k, self.max_tokens,
+                           local_experts.H, local_experts.I, int(timeout_ms))
+        self.handle = C.c_void_p()
+        with torch.cuda.device(self.device):
+            _lib.check(self.lib.sb_ep_create(C.byref(desc), C.byref(self.handle)), "sb_ep_create")
+            try:
+                if self.world > 1:
+                    if nccl_comm is not None:
+                        s = torch.cuda.current_stream(self.device).cuda_stream
+                        _lib.check(self.lib.sb_ep_connect_nccl(self.handle, C.c_void_p(nccl_comm), C.c_void_p(s)),
+                                   "sb_ep_connect_nccl")
+                    else:
+                        buf = C.create_string_buffer(_lib.SB_EP_HANDLE_BYTES)
+                        _lib.check(self.lib.sb_ep_export(self.handle, buf), "sb_ep_export")
+                        allb = exchange_handles(buf.raw, group)
+                        _lib.check(self.lib.sb_ep_connect(self.handle, C.c_char_p(allb)), "sb_ep_connect")
+            except Exception:
+                self.lib.sb_ep_destroy(self.handle)
+                self.handle = None
+                raise
+            nbytes = int(self.lib.sb_ep_workspace_bytes(self.handle))
+            if workspace is not None and workspace.numel() >= nbytes + 1024:
+                self.workspace = workspace
+            else:
+                self.workspace = torch.empty(nbytes + 1024, dtype=torch.uint8, device=self.device)
+            base = self.workspace.data_ptr()
+            self._ws = (base + 1023) // 1024 * 1024
+            self._ws_bytes = nbytes
+
+    def forward(self, x: torch.Tensor, ids: torch.Tensor, weights: torch.Tensor,
+                out_dtype=torch.bfloat16, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if self.handle is None:
+            raise RuntimeError("the layer was closed")
+        if not (x.is_cuda and x.dtype == torch.bfloat16):
+            raise RuntimeError("activations must be bf16 CUDA tensors")
+        x = x.contiguous()
+        ids = ids.to(torch.int32).contiguous()
+        weights = weights.to(torch.float32).contiguous()
+        B = ids.shape[0]
+        if ids.shape[1] != self.top_k:
+            raise RuntimeError(f"ids carry {ids.shape[1]} slots, the layer was set up for {self.top_k}")
+        if out is None:
+            out = torch.empty(B, self.experts.H, dtype=out_dtype, device=x.device)
+        e = self.experts
+        s = torch.cuda.current_stream(x.device).cuda_stream
+        with torch.cuda.device(x.device):
+            rc = self.lib.sb_ep_forward(
+                self.handle, C.c_void_p(x.data_ptr()), _lib.SB_BF16, B, C.c_void_p(ids.data_ptr()),
+                C.c_void_p(weights.data_ptr()), C.c_void_p(e.gate.data_ptr()), C.c_void_p(e.up.data_ptr()),
+                C.c_void_p(e.down.data_ptr()), C.c_void_p(e.gate_scale.data_ptr()),
+                C.c_void_p(e.up_scale.data_ptr()), C.c_void_p(e.down_scale.data_ptr()),
+                C.c_void_p(out.data_ptr()), _lib.SB_BF16 if out.dtype == torch.bfloat16 else _lib.SB_F32,
+                C.c_void_p(self._ws), self._ws_bytes, C.c_void_p(s))
+        _lib.check(rc, "sb_ep_forward")
+        return out
+
+    __call__ = forward
+
+    def status(self) -> None:
+        """Raises if a wait for a peer ran out (synchronises the device)."""
+        _lib.check(self.lib.sb_ep_status(self.handle), "sb_ep_status")
+
+    def close(self) -> None:
+        """Collective: a barrier, then the buffers are released on every rank."""
+        if self.handle is None:
+            return
+        torch.cuda.synchronize(self.device)
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        self.lib.sb_ep_destroy(self.handle)
+        self.handle = None
+
+
+class AllToAllMoE:
+    """The same layer over the library collective: ``all_to_all_single``
+    (NCCL) of the counts, then of the token rows (one per slot), local expert
+    ids and weights; fp32 expert outputs back; the token's slots summed in slot
+    order.  Host-synchronised split sizes.  Kept as the baseline the fused
+    exchange is measured against."""
+
     def __init__(self, expert_fn: Callable, n_experts: int, group: Optional[dist.ProcessGroup] = None):
-        """expert_fn(x_rows [R,H], local_ids [R,1] int32, weights [R,1] fp32) -> fp32 [R,H]
-        runs this rank's experts (``TernaryExperts.forward`` on a GPU)."""
+        """expert_fn(x_rows [R,H], local_ids [R,1] int32, weights [R,1] fp32) -> fp32 [R,H]."""
         self.expert_fn = expert_fn
         self.group = group
         self.world = dist.get_world_size(group)
@@ -83,8 +199,32 @@ class ExpertParallelMoE:
         y_slots.index_copy_(0, order, y_send)
         y_slots = y_slots.view(B, k, H)
         out = torch.zeros(B, H, dtype=torch.float32, device=dev)
-        for j in range(k):   # 0 + y_0 + y_1 + ... in slot order, like the single-GPU combine
+        for j in range(k):
             out.add_(y_slots[:, j])
         return out.to(out_dtype or x.dtype)
+
+    __call__ = forward
+
+
+
+class EPMoELayer:
+    """The MoE layer with its experts sharded: the router's top-k on this rank's
+    tokens, then ``ExpertParallelMoE``.  Same call as ``sb200.moe.BVHMoELayer``
+    (``layer(x, out=...)``), so it can be replayed from a CUDA graph
+    (``sb200.moe.GraphedLayer``: the exchange's flags carry an epoch kept in
+    device memory, and no host work sits between the kernels)."""
+
+    def __init__(self, router, ep: ExpertParallelMoE, top_k: int = 8, select: str = "soft"):
+        self.router = router
+        self.ep = ep
+        self.top_k = int(top_k)
+        self.select = select
+
+    def route(self, x: torch.Tensor):
+        return self.router.forward_topk(x, k=self.top_k, select=self.select)
+
+    def forward(self, x: torch.Tensor, out_dtype=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        ids, w = self.route(x)
+        return self.ep(x, ids, w, out_dtype=out_dtype or x.dtype, out=out)
 
     __call__ = forward

@@ -27,18 +27,24 @@ import torch
 from sb200 import _lib
 from sb200 import ternary as _t
 
-# repacked weights per packed tensor object (weak keys: an entry dies with its
-# tensor, so a later tensor at the same address never sees a stale layout)
-_cache: "weakref.WeakKeyDictionary[torch.Tensor, tuple]" = weakref.WeakKeyDictionary()
+# repacked weights per packed tensor object, keyed by the object's id and
+# holding a weak reference to it: an entry whose tensor died (a later tensor may
+# reuse the id) is never taken for the new one, and dies with a finaliser.
+# (Tensors cannot be weak-dictionary keys: the lookup compares keys with ==,
+# which is elementwise for tensors.)
+_cache: dict = {}
 
 
 def _device_layout(packed: torch.Tensor, K: int) -> torch.Tensor:
     stamp = (packed.data_ptr(), tuple(packed.shape), packed._version, K, packed.device)
-    hit = _cache.get(packed)
-    if hit is not None and hit[0] == stamp:
-        return hit[1]
+    key = id(packed)
+    hit = _cache.get(key)
+    if hit is not None and hit[0]() is packed and hit[1] == stamp:
+        return hit[2]
     out = _t.repack_reference(packed.contiguous(), K)
-    _cache[packed] = (stamp, out)
+    if hit is None or hit[0]() is not packed:
+        weakref.finalize(packed, _cache.pop, key, None)
+    _cache[key] = (weakref.ref(packed), stamp, out)
     return out
 
 

@@ -23,6 +23,7 @@ from __future__ import annotations
 import argparse
 import glob
 import importlib.util
+import os
 import sys
 from pathlib import Path
 
@@ -349,8 +350,11 @@ def pipeline_case(ref_python: Path, name, H, seed, batch, x_seed, head_gain=20.0
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("SB_REFERENCE_ROOT"),
+                    help="root of the reference checkout (default: $SB_REFERENCE_ROOT)")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("pass --reference or set SB_REFERENCE_ROOT")
     ref_python = Path(a.reference) / "python"
     torch.set_num_threads(8)
     bvh = load_ref_router(ref_python)

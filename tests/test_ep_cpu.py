@@ -1,0 +1,79 @@
+"""The summation tree and the exchange protocol of the expert-parallel layer,
+on the CPU (oracle/ep.py; no GPU, one process).
+
+The device layer (csrc/ep.cu, csrc/tree_sum.cuh) relies on one property: the
+tree sum of a token's expert outputs splits over aligned blocks of experts, so
+per-GPU partial sums combined along the tree over the ranks give the single-GPU
+sum bit for bit.  These tests check that property in fp32 and that the
+device's stack schedule (ported line by line) builds the same tree.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import ep as oep
+
+
+def _case(seed, B, E, k, H, spread=3.0):
+    rng = np.random.default_rng(seed)
+    ids = np.stack([rng.choice(E, k, replace=False) for _ in range(B)]).astype(np.int32)
+    # magnitudes spread over decades so that the grouping changes the rounding
+    y = (rng.standard_normal((B, k, H)) * 10 ** rng.uniform(-spread, spread, (B, k, 1))).astype(np.float32)
+    return ids, y
+
+
+def test_grouping_matters_in_fp32():
+    """Sanity: slot order and tree order do differ in fp32 on these inputs, so
+    the bitwise checks below are not vacuous."""
+    ids, y = _case(0, 64, 64, 8, 16)
+    tree = oep.combine_single(ids, y)
+    slot = np.zeros_like(tree)
+    for j in range(8):
+        slot = (slot + y[:, j]).astype(np.float32)
+    assert not np.array_equal(tree, slot)
+    np.testing.assert_allclose(tree, slot, rtol=1e-5, atol=1e-5 * np.abs(y).max())
+
+
+@pytest.mark.parametrize("seed", range(5))
+def test_device_schedule_builds_the_recursive_tree(seed):
+    ids, y = _case(seed, 40, 64, 8, 8)
+    for t in range(len(ids)):
+        pos, vals = oep.token_entries(ids[t], list(y[t]))
+        merges = oep.tree_schedule(pos)
+        assert len(merges) == len(pos) - 1
+        assert np.array_equal(oep.tree_apply(vals, merges), oep.tree_sum(vals, pos))
+
+
+def test_schedule_with_repeated_positions():
+    """Equal ids (not produced by top-k, allowed by the API) merge deepest, right to left."""
+    vals = [np.float32(v) for v in (1e8, 1.0, -1e8, 3.0)]
+    pos = [5, 5, 5, 9]
+    assert oep.tree_apply(vals, oep.tree_schedule(pos)) == oep.tree_sum(vals, pos)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+@pytest.mark.parametrize("E,k", [(64, 8), (16, 4), (32, 16)])
+def test_sharded_sum_equals_single_gpu_bitwise(world, E, k):
+    if E % world:
+        pytest.skip("experts do not divide")
+    ids, y = _case(10 + world, 200, E, k, 12)
+    assert np.array_equal(oep.expert_parallel(ids, y, E, world), oep.combine_single(ids, y))
+
+
+def test_token_goes_once_per_destination():
+    """Dispatch is deduplicated per destination rank: a token is sent once to
+    each rank holding any of its experts (at most min(k, W) copies)."""
+    ids, _ = _case(3, 500, 64, 8, 1)
+    send_pos, lists = oep.plan_destinations(ids, 64, 8)
+    for t in range(len(ids)):
+        dests = {int(e) // 8 for e in ids[t]}
+        assert {g for g in range(8) if send_pos[t, g] >= 0} == dests
+    assert sum(len(l) for l in lists) == sum(len({int(e) // 8 for e in r}) for r in ids)
+    # rows of each destination are the tokens in ascending order, numbered 0..n-1
+    for g in range(8):
+        assert lists[g] == sorted(lists[g])
+        assert [send_pos[t, g] for t in lists[g]] == list(range(len(lists[g])))
+    # about 5.4 distinct ranks per token for 8 distinct experts over 8 blocks of 8
+    assert 5.0 < sum(len(l) for l in lists) / len(ids) < 5.8

@@ -119,3 +119,34 @@ def test_int8_accumulator_is_exact():
                     for i in range(5)])
     assert np.array_equal(acc, ref)
     assert np.abs(q).max() <= 127
+
+
+# ---------------------------------------------------------------------------
+# the torch restatement timed as the CPU baseline (oracle/torch_ref.py)
+# ---------------------------------------------------------------------------
+@pytest.mark.parametrize("mode", ["hard", "soft"])
+@pytest.mark.parametrize("name", ROUTER_GOLDENS)
+def test_torch_router_matches_reference(name, mode):
+    """Same torch operators in the reference's order: level probabilities equal
+    the reference's own outputs up to fp32 summation order."""
+    import torch
+    from oracle import torch_ref
+    w, x, g = golden_router_case(name)
+    r = torch_ref.TorchRouter(w, tuple(int(b) for b in g["branching"]))
+    with torch.no_grad():
+        p, path = r.forward(torch.from_numpy(np.asarray(x, np.float32)), soft=(mode == "soft"))
+    assert np.array_equal(path.numpy(), g[f"{mode}_route_path"])
+    np.testing.assert_allclose(p.numpy(), g[f"{mode}_expert_probs"], rtol=1e-5, atol=1e-8)
+
+
+def test_torch_moe_layer_matches_reference():
+    import torch
+    from oracle import torch_ref
+    g = load_golden("ternary_small")
+    experts = [torch_ref.TorchTernaryExpert({k: g[f"moe/{e}/{k}"] for k in (
+        "gate_ternary", "up_ternary", "down_ternary", "gate_scale", "up_scale", "down_scale")})
+        for e in range(6)]
+    with torch.no_grad():
+        y = torch_ref.forward_topk(torch.from_numpy(g["moe/x"]), torch.from_numpy(g["moe/probs"]),
+                                   torch.from_numpy(g["moe/ids"]), experts)
+    np.testing.assert_allclose(y.numpy(), g["moe/y"], rtol=1e-5, atol=1e-6)
