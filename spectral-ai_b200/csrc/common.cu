@@ -192,8 +192,16 @@ extern "C" int sb_device_status(int device) {
   cudaSetDevice(prev);
   if (e != cudaSuccess)
     return sb::fail(SB_ERR_CUDA, "status read failed: %s", cudaGetErrorString(e));
+  const unsigned waits = sb::ST_TIMEOUT_PRODUCER | sb::ST_TIMEOUT_MMA | sb::ST_TIMEOUT_EPILOGUE |
+                         sb::ST_TIMEOUT_UNPACK | sb::ST_TIMEOUT_EP;
+  if (v & waits)
+    return sb::fail(SB_ERR_DEVICE_TIMEOUT, "device %d kernel status 0x%x (bounded wait expired)", device, v);
+  if (v & sb::ST_RANGE)
+    return sb::fail(SB_ERR_INVALID,
+                    "device %d kernel status 0x%x (a hidden value beyond fp16's range was saturated; "
+                    "fp32 inputs take the bf16 hi/lo path, which has fp32's range)", device, v);
   if (v != 0)
-    return sb::fail(SB_ERR_DEVICE_TIMEOUT, "device %d kernel status 0x%x (bounded wait expired)",
+    return sb::fail(SB_ERR_INVALID, "device %d kernel status 0x%x (an out-of-range expert id was dropped)",
                     device, v);
   return SB_OK;
 }

@@ -66,7 +66,6 @@ namespace sb {
 constexpr int EP_MAX_WORLD = 8;
 constexpr int EP_KE = 16;  // metadata entries per received row (top_k <= 16)
 constexpr uint32_t EP_MAGIC = 0x53424550u;
-constexpr unsigned ST_TIMEOUT_EP = 32u;
 constexpr int EP_THREADS = 256;
 
 // Control block of a handle (device memory, zeroed at create).
@@ -430,12 +429,21 @@ __global__ void __launch_bounds__(EP_THREADS) ep_return_kernel(EpArgs a, const i
       return v;
     });
     float4* dst = reinterpret_cast<float4*>(ep_at(a, s, a.L.ret) + (((int64_t)a.rank * a.cap + i) * a.H) * 4);
-    for (int c = lane; c < n4; c += 32) {
-      float4 v[KC];
+    constexpr int CW = 2;
+    for (int c0 = lane; c0 < n4; c0 += 32 * CW) {
+      float4 v[KC][CW];
 #pragma unroll
       for (int q = 0; q < KC; ++q)
-        v[q] = q < n ? __ldg(reinterpret_cast<const float4*>(yp + row[q] * a.H) + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      dst[c] = n ? tree_apply<KC>(v, sched) : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int w = 0; w < CW; ++w) {
+          const int c = c0 + 32 * w;
+          v[q][w] = (q < n && c < n4) ? __ldg(reinterpret_cast<const float4*>(yp + row[q] * a.H) + c)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      tree_apply<KC, CW>(v, sched);
+#pragma unroll
+      for (int w = 0; w < CW; ++w)
+        if (c0 + 32 * w < n4) dst[c0 + 32 * w] = v[0][w];
     }
   }
   ep_last_block(&a.ctrl->done_ret, [&] {
@@ -489,13 +497,21 @@ __global__ void __launch_bounds__(EP_THREADS) ep_combine_kernel(EpArgs a, int64_
         if (j == q) v = gpos[j];
       return v;
     });
-    for (int c = lane; c < n4; c += 32) {
-      float4 v[EP_MAX_WORLD];
+    constexpr int CW = 2;
+    for (int c0 = lane; c0 < n4; c0 += 32 * CW) {
+      float4 v[EP_MAX_WORLD][CW];
 #pragma unroll
       for (int q = 0; q < EP_MAX_WORLD; ++q)
-        v[q] = (q < n && ok) ? reinterpret_cast<const float4*>(ret + row[q])[c] : make_float4(0.f, 0.f, 0.f, 0.f);
-      const float4 acc = n ? tree_apply<EP_MAX_WORLD>(v, sched) : make_float4(0.f, 0.f, 0.f, 0.f);
-      store4<TO>(out + t * a.H + 4 * c, acc);
+#pragma unroll
+        for (int w = 0; w < CW; ++w) {
+          const int c = c0 + 32 * w;
+          v[q][w] = (q < n && ok && c < n4) ? reinterpret_cast<const float4*>(ret + row[q])[c]
+                                            : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      tree_apply<EP_MAX_WORLD, CW>(v, sched);
+#pragma unroll
+      for (int w = 0; w < CW; ++w)
+        if (c0 + 32 * w < n4) store4<TO>(out + t * a.H + 4 * (c0 + 32 * w), v[0][w]);
     }
   }
 }

@@ -26,6 +26,8 @@ enum : unsigned int {
   ST_TIMEOUT_EPILOGUE = 4u,
   ST_TIMEOUT_UNPACK = 8u,
   ST_BAD_ARGUMENT = 16u,
+  ST_TIMEOUT_EP = 32u,  // a wait for a peer GPU ran out (expert-parallel layer)
+  ST_RANGE = 64u,  // a value beyond a 16-bit format's range was saturated
 };
 
 #ifndef SB_WAIT_LIMIT_NS

@@ -341,6 +341,42 @@ __global__ void moe_scatter_kernel(const TX* __restrict__ x, const int32_t* __re
   }
 }
 
+// The fp32-faithful dispatch: each fp32 row becomes two bf16 rows side by
+// side, hi = bf16(x) in columns [0, H) and lo = bf16(x - hi) in [H, 2H), so that
+// the GEMM over the doubled K sums T x_hi + T x_lo = T x to 2^-16 relative
+// (bf16 keeps fp32's exponent range).  H % 4 == 0 and 16-byte aligned rows.
+__global__ void moe_scatter_split_kernel(const float* __restrict__ x, const int32_t* __restrict__ ids,
+                                         const float* __restrict__ wts, int64_t B, int k, int H, int E,
+                                         const int* __restrict__ offsets, int* __restrict__ cursor,
+                                         __nv_bfloat16* __restrict__ xp, int64_t ldx, float* __restrict__ row_w,
+                                         int* __restrict__ inv) {
+  const int lane = threadIdx.x & 31;
+  const int64_t R = B * k;
+  for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; i < R;
+       i += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int e = ids[i];
+    int pos = -1;
+    if (lane == 0 && e >= 0 && e < E) pos = offsets[e] + atomicAdd(&cursor[e], 1);
+    pos = __shfl_sync(0xffffffffu, pos, 0);
+    if (lane == 0) inv[i] = pos;
+    if (pos < 0) continue;
+    if (lane == 0) row_w[pos] = wts ? wts[i] : 1.0f;
+    const float4* s4 = reinterpret_cast<const float4*>(x + (i / k) * (int64_t)H);
+    __nv_bfloat16* dst = xp + (int64_t)pos * ldx;
+    for (int c = lane; c < H / 4; c += 32) {
+      const float4 v = __ldg(s4 + c);
+      const __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y), h1 = __floats2bfloat162_rn(v.z, v.w);
+      const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+      const __nv_bfloat162 l0 = __floats2bfloat162_rn(v.x - f0.x, v.y - f0.y);
+      const __nv_bfloat162 l1 = __floats2bfloat162_rn(v.z - f1.x, v.w - f1.y);
+      *reinterpret_cast<uint2*>(dst + 4 * c) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+      *reinterpret_cast<uint2*>(dst + H + 4 * c) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&l0), *reinterpret_cast<const uint32_t*>(&l1));
+    }
+  }
+}
+
 template <typename TO>
 __device__ __forceinline__ TO cvt_out(float v);
 template <> __device__ __forceinline__ float cvt_out<float>(float v) { return v; }
@@ -390,22 +426,31 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int* __res
     int64_t row[KC];
 #pragma unroll
     for (int r = 0; r < KC; ++r) row[r] = (int64_t)__shfl_sync(0xffffffffu, crow, r < n ? tree_order(wt, r) : 0);
-    for (int c = lane; c < ncol; c += 32) {
-      float4 v[KC];
+    constexpr int CW = 2;  // column groups per pass of the schedule
+    for (int c0 = lane; c0 < ncol; c0 += 32 * CW) {
+      float4 v[KC][CW];
 #pragma unroll
-      for (int r = 0; r < KC; ++r) {
-        if (r < n) {
-          v[r] = vec ? __ldg(reinterpret_cast<const float4*>(y + row[r] * H) + c)
-                     : make_float4(__ldg(y + row[r] * H + c), 0.f, 0.f, 0.f);
-        } else {
-          v[r] = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int r = 0; r < KC; ++r)
+#pragma unroll
+        for (int w = 0; w < CW; ++w) {
+          const int c = c0 + 32 * w;
+          if (r < n && c < ncol)
+            v[r][w] = vec ? __ldg(reinterpret_cast<const float4*>(y + row[r] * H) + c)
+                          : make_float4(__ldg(y + row[r] * H + c), 0.f, 0.f, 0.f);
+          else
+            v[r][w] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      tree_apply<KC, CW>(v, wt.sched);
+#pragma unroll
+      for (int w = 0; w < CW; ++w) {
+        const int c = c0 + 32 * w;
+        if (c < ncol) {
+          if (vec)
+            store4<TO>(out + t * H + 4 * c, v[0][w]);
+          else
+            out[t * H + c] = cvt_out<TO>(v[0][w].x);
         }
       }
-      const float4 acc = tree_apply<KC>(v, wt.sched);
-      if (vec)
-        store4<TO>(out + t * H + 4 * c, acc);
-      else
-        out[t * H + c] = cvt_out<TO>(acc.x);
     }
   }
 }
@@ -455,12 +500,13 @@ struct MoeLayout {
       off_hp, off_yp, total;
 };
 
-MoeLayout moe_layout(int64_t B, int64_t H, int64_t I, int32_t E, int32_t k) {
+// split: the fp32-faithful form's rows, [hi | lo] (twice as wide)
+MoeLayout moe_layout(int64_t B, int64_t H, int64_t I, int32_t E, int32_t k, bool split = false) {
   MoeLayout L{};
   L.R = B * k;
   L.Rp = L.R + 32 * (int64_t)E;
-  L.ldx = round_up(H, 64);
-  L.ldh = round_up(I, 64);
+  L.ldx = split ? 2 * H : round_up(H, 64);
+  L.ldh = split ? 2 * I : round_up(I, 64);
   L.max_mt = L.Rp / 128 + E + 1;
   size_t o = 0;
   auto take = [&](size_t bytes) {
@@ -584,6 +630,10 @@ int launch_pair(const char* name, const CUtensorMap& tx, const CUtensorMap& tw0,
                              : launch_pair_s<MODE, FMT, 1>(name, tx, tw0, tw1, tout, p, stream);
 }
 
+bool split_form_fits(int64_t H, int64_t I, int engine) {
+  return engine == ENGINE_PAIR && H % TP_KB == 0 && I % TP_KB == 0;
+}
+
 int check_ternary_shapes(int64_t H, int64_t I) {
   SB_REQUIRE(H > 0 && I > 0, "hidden=%lld and intermediate=%lld must be positive", (long long)H, (long long)I);
   SB_REQUIRE(H <= (1 << 20) && I <= (1 << 20), "dimensions too large");
@@ -633,6 +683,10 @@ struct GroupedSwiGLU {
   const float *gs, *us, *ds;
   int fmt_gu;  // 1: bf16 activations, 0: fp16
   int engine;
+  // 1: fp32-faithful form (pair engine, H and I multiples of 128): the rows of
+  // xp are [x_hi | x_lo] (bf16, 2H wide), h is stored as [h_hi | h_lo] (bf16,
+  // 2I wide), and both GEMMs run over the doubled K with the weights read twice
+  int split = 0;
 };
 
 int grouped_swiglu(const GroupedSwiGLU& g, cudaStream_t stream) {
@@ -651,25 +705,25 @@ int grouped_swiglu(const GroupedSwiGLU& g, cudaStream_t stream) {
   // tensor maps: activations (SW128, 64 x 128 box) and packed weights (16 B x rows box)
   CUtensorMap tmx, tmg, tmu, tmh, tmd;
   const CUtensorMapDataType adt = fmt_gu ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const CUtensorMapDataType hdt = g.split ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  const int64_t xk = g.split ? 2 * H : H, hk = g.split ? 2 * I : I;  // activation columns the GEMMs run over
   const int64_t KWh = ternary_row_words(H), KWi = ternary_row_words(I);
   const bool pair = engine == ENGINE_PAIR;
   const uint32_t gu_box = pair ? 64 : 128, d_box = pair ? 128 : 256;
   const uint32_t p_words = pair ? TP_KB / 16 : 4;  // packed words per row in one weight box
   // token rows per activation box: two 48-row boxes per CTA with two MMA streams
   const uint32_t x_rows = pair ? (pair_streams() == 2 ? TP_QROWS : TP_HALF_ROWS) : 128;
-  if ((rc = make_tmap_2d(&tmx, xp, adt, 2, g.Rp, H, g.ldx, 64, x_rows, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+  if ((rc = make_tmap_2d(&tmx, xp, adt, 2, g.Rp, xk, g.ldx, 64, x_rows, CU_TENSOR_MAP_SWIZZLE_128B)) ||
       (rc = make_tmap_2d(&tmg, gate, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, p_words, gu_box,
                          CU_TENSOR_MAP_SWIZZLE_NONE)) ||
       (rc = make_tmap_2d(&tmu, up, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * I, KWh, KWh, p_words, gu_box,
                          CU_TENSOR_MAP_SWIZZLE_NONE)) ||
-      (rc = make_tmap_2d(&tmh, hp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.Rp, I, g.ldh, 64, x_rows,
-                         CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&tmh, hp, hdt, 2, g.Rp, hk, g.ldh, 64, x_rows, CU_TENSOR_MAP_SWIZZLE_128B)) ||
       (rc = make_tmap_2d(&tmd, down, CU_TENSOR_MAP_DATA_TYPE_UINT32, 4, (uint64_t)E * H, KWi, KWi, p_words, d_box,
                          CU_TENSOR_MAP_SWIZZLE_NONE)))
     return rc;
   CUtensorMap tmh_out{}, tmy_out{};
-  if (pair && ((rc = make_tmap_2d(&tmh_out, hp, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, g.Rp, I, g.ldh, 16, 32,
-                                  CU_TENSOR_MAP_SWIZZLE_NONE)) ||
+  if (pair && ((rc = make_tmap_2d(&tmh_out, hp, hdt, 2, g.Rp, hk, g.ldh, 16, 32, CU_TENSOR_MAP_SWIZZLE_NONE)) ||
                (rc = make_tmap_2d(&tmy_out, yp, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, g.Rp, H, H, 32, 32,
                                   CU_TENSOR_MAP_SWIZZLE_NONE))))
     return rc;
@@ -679,8 +733,12 @@ int grouped_swiglu(const GroupedSwiGLU& g, cudaStream_t stream) {
   pg.num_mtiles = nmt;
   pg.n_ntiles = (int)((I + 127) / 128);
   pg.N = (int)I;
-  pg.K = (int)H;
+  pg.K = (int)xk;
   pg.b_rows = (int)I;
+  if (g.split) {
+    pg.kb_wrap = (int)(H / TP_KB);
+    pg.h_lo_col = (int)I;
+  }
   pg.s0 = gs;
   pg.s1 = us;
   pg.out = hp;
@@ -700,14 +758,16 @@ int grouped_swiglu(const GroupedSwiGLU& g, cudaStream_t stream) {
   pd.num_mtiles = nmt;
   pd.n_ntiles = (int)((H + 255) / 256);
   pd.N = (int)H;
-  pd.K = (int)I;
+  pd.K = (int)hk;
   pd.b_rows = (int)H;
+  if (g.split) pd.kb_wrap = (int)(I / TP_KB);
   pd.s0 = ds;
   pd.row_w = row_w;
   pd.out = yp;
   pd.ldo = H;
   if (engine == ENGINE_PAIR)
-    rc = launch_pair<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, tmy_out, pd, stream);
+    rc = g.split ? launch_pair<TG_DOWN, 1>("ternary_down_tc", tmh, tmd, tmd, tmy_out, pd, stream)
+                 : launch_pair<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, tmy_out, pd, stream);
   else if (engine == ENGINE_TS)
     rc = launch_ts<TG_DOWN, 0>("ternary_down_tc", tmh, tmd, tmd, pd, stream);
   else
@@ -731,7 +791,14 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   if (B == 0) return SB_OK;
   SB_REQUIRE(x && ids && gate && up && down && gs && us && ds && out, "null pointer argument");
   SB_REQUIRE(B * k <= (int64_t)INT32_MAX / 2, "too many (token, slot) pairs");
-  const MoeLayout L = moe_layout(B, H, I, E, k);
+  // the pair engine stores y rows with TMA: its row pitch (H floats) must be a 16-byte multiple
+  int engine = ternary_engine();
+  if (engine == ENGINE_PAIR && (H % 4) != 0) engine = ENGINE_TS;
+  const bool x16 = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+  // fp32 inputs take the fp32-faithful split form where its shapes allow
+  // (otherwise they are rounded to fp16, as bf16 inputs' hidden state is)
+  const bool split = x_dtype == SB_F32 && split_form_fits(H, I, engine) && x16;
+  const MoeLayout L = moe_layout(B, H, I, E, k, split);
   if (!workspace || workspace_bytes < L.total)
     return fail(SB_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, L.total);
   SB_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 1023u) == 0, "workspace must be 1024-byte aligned");
@@ -749,11 +816,8 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   void* xp = ws + L.off_xp;
   __half* hp = reinterpret_cast<__half*>(ws + L.off_hp);
   float* yp = reinterpret_cast<float*>(ws + L.off_yp);
-  const int fmt_gu = (x_dtype == SB_BF16) ? 1 : 0;  // bf16 inputs stay bf16; fp32 inputs go to fp16
-  // the pair engine stores y rows with TMA: its row pitch (H floats) must be a 16-byte multiple
-  int engine = ternary_engine();
-  if (engine == ENGINE_PAIR && (H % 4) != 0) engine = ENGINE_TS;
-  const bool x16 = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+  // bf16 inputs stay bf16; fp32 inputs become bf16 hi/lo pairs (split) or fp16
+  const int fmt_gu = (x_dtype == SB_BF16 || split) ? 1 : 0;
 
   {
     const int64_t R = L.R;
@@ -766,7 +830,11 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
     ProfScope prof("moe_dispatch", stream);
     int64_t wblocks = (R * 32 + 255) / 256;
     if (wblocks > (int64_t)num_sms() * 16) wblocks = (int64_t)num_sms() * 16;
-    if (x_dtype == SB_BF16)
+    if (split)
+      moe_scatter_split_kernel<<<(unsigned)wblocks, 256, 0, stream>>>(
+          static_cast<const float*>(x), ids, weights, B, k, (int)H, E, offsets, cursor,
+          static_cast<__nv_bfloat16*>(xp), L.ldx, row_w, inv);
+    else if (x_dtype == SB_BF16)
       moe_scatter_kernel<__nv_bfloat16, __nv_bfloat16><<<(unsigned)wblocks, 256, 0, stream>>>(
           static_cast<const __nv_bfloat16*>(x), ids, weights, B, k, (int)H, E, offsets, cursor,
           static_cast<__nv_bfloat16*>(xp), L.ldx, row_w, inv, x16 && (H % 8) == 0);
@@ -778,7 +846,7 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   }
 
   GroupedSwiGLU g{xp, hp, yp, L.Rp, L.ldx, L.ldh, H, I, E, mtiles, nmt, row_w,
-                  gate, up, down, gs, us, ds, fmt_gu, engine};
+                  gate, up, down, gs, us, ds, fmt_gu, engine, split ? 1 : 0};
   if ((rc = grouped_swiglu(g, stream))) return rc;
   return moe_combine(yp, inv, ids, B, k, H, out, out_dtype, stream);
 }
@@ -788,7 +856,8 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
 
 extern "C" size_t sb_ternary_moe_workspace_bytes(int64_t B, int64_t H, int64_t I, int32_t E, int32_t k) {
   if (B < 0 || H <= 0 || I <= 0 || E <= 0 || k <= 0) return 0;
-  return sb::moe_layout(B, H, I, E, k).total;
+  // sized for the fp32-faithful form when the shapes allow it (it is the larger)
+  return sb::moe_layout(B, H, I, E, k, sb::split_form_fits(H, I, sb::ENGINE_PAIR)).total;
 }
 
 extern "C" int sb_ternary_moe_swiglu(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I,
@@ -807,7 +876,8 @@ extern "C" int sb_ternary_moe_swiglu(const void* x, int x_dtype, int64_t B, int6
 // the slot ids live at the end of the workspace.
 extern "C" size_t sb_ternary_gated_mlp_workspace_bytes(int64_t M, int64_t H, int64_t I) {
   if (M < 0 || H <= 0 || I <= 0) return 0;
-  return sb::moe_layout(M, H, I, 1, 1).total + sb::align_up(sizeof(int32_t) * (size_t)(M > 0 ? M : 1), 1024);
+  return sb::moe_layout(M, H, I, 1, 1, sb::split_form_fits(H, I, sb::ENGINE_PAIR)).total +
+         sb::align_up(sizeof(int32_t) * (size_t)(M > 0 ? M : 1), 1024);
 }
 
 extern "C" int sb_ternary_gated_mlp(const void* x, int x_dtype, int64_t M, int64_t H, int64_t I,
@@ -821,7 +891,7 @@ extern "C" int sb_ternary_gated_mlp(const void* x, int x_dtype, int64_t M, int64
   const size_t need = sb_ternary_gated_mlp_workspace_bytes(M, H, I);
   if (!workspace || workspace_bytes < need)
     return fail(SB_ERR_WORKSPACE, "workspace of %zu bytes is smaller than the %zu needed", workspace_bytes, need);
-  const size_t base = moe_layout(M, H, I, 1, 1).total;
+  const size_t base = moe_layout(M, H, I, 1, 1, split_form_fits(H, I, ENGINE_PAIR)).total;
   int32_t* ids = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + base);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   int64_t blocks = (M + 255) / 256;

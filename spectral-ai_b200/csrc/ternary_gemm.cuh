@@ -46,6 +46,13 @@ struct TernGemmParams {
   const float* row_w;  // DOWN: routing weight of each row
   void* out;
   int64_t ldo;
+  // Split activations (pair engine): K runs over two halves that share the
+  // weights — the packed weights' K-block index wraps after kb_wrap blocks —
+  // so [x_hi | x_lo] against [T | T] sums T x_hi + T x_lo.  0 = no wrap.
+  int kb_wrap;
+  // GATEUP (pair engine): 0 = h stored as fp16; > 0 = h stored as two bf16
+  // terms, hi = bf16(h) at column c and lo = bf16(h - hi) at c + h_lo_col.
+  int h_lo_col;
 };
 
 constexpr int TG_THREADS = 384;

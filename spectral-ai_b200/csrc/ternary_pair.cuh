@@ -177,11 +177,12 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
           if (!mbar_wait(&xp_empty[stage], phase ^ 1u, ST_TIMEOUT_PRODUCER)) goto done;
           uint8_t* st = smem + stage * TP_STAGE_BYTES;
           mbar_arrive_expect_tx(&full_p[stage], TP_P_BYTES);
+          const int wkb = (p.kb_wrap > 0 && kb >= p.kb_wrap) ? kb - p.kb_wrap : kb;  // weight K-block
           if (MODE == TG_GATEUP) {
-            tma_load_2d(st + TP_X_BYTES, &tmW0, &full_p[stage], kb * 8, wrow);
-            tma_load_2d(st + TP_X_BYTES + TP_P_BYTES / 2, &tmW1, &full_p[stage], kb * 8, wrow);
+            tma_load_2d(st + TP_X_BYTES, &tmW0, &full_p[stage], wkb * 8, wrow);
+            tma_load_2d(st + TP_X_BYTES + TP_P_BYTES / 2, &tmW1, &full_p[stage], wkb * 8, wrow);
           } else {
-            tma_load_2d(st + TP_X_BYTES, &tmW0, &full_p[stage], kb * 8, wrow);
+            tma_load_2d(st + TP_X_BYTES, &tmW0, &full_p[stage], wkb * 8, wrow);
           }
           if (rank == 0) mbar_arrive_expect_tx(&full_x[stage], 2 * TP_X_BYTES);
           const uint32_t fx = mapa_shared(smem_u32(&full_x[stage]), 0);
@@ -368,17 +369,40 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
         __syncwarp();
         const int t0 = mt.row0 + c * 32;
         if (MODE == TG_GATEUP) {
-          __half* hb = reinterpret_cast<__half*>(sb);  // [32 tokens][16 channels]
           const bool gate = lane < 16;
           const int ci = lane & 15;
+          if (p.h_lo_col > 0) {
+            // two bf16 terms: hi [32 tokens][16 channels] at sb, lo at sb + 1 KB
+            __nv_bfloat16* hi = reinterpret_cast<__nv_bfloat16*>(sb);
+            __nv_bfloat16* lo = hi + 32 * 16;
 #pragma unroll
-          for (int j = 0; j < 16; ++j) {
-            const float mine = __uint_as_float(gate ? v[j] : v[16 + j]);
-            const float other = __shfl_xor_sync(0xffffffffu, __uint_as_float(gate ? v[16 + j] : v[j]), 16);
-            // gate lane: token j (own gate, partner's up); up lane: token 16+j
-            const float g = (gate ? mine : other) * s_a;
-            const float u = (gate ? other : mine) * s_b;
-            hb[(gate ? j : 16 + j) * 16 + ci] = __float2half_rn(silu_fast(g) * u);
+            for (int j = 0; j < 16; ++j) {
+              const float mine = __uint_as_float(gate ? v[j] : v[16 + j]);
+              const float other = __shfl_xor_sync(0xffffffffu, __uint_as_float(gate ? v[16 + j] : v[j]), 16);
+              const float g = (gate ? mine : other) * s_a;
+              const float u = (gate ? other : mine) * s_b;
+              const float h = silu_fast(g) * u;
+              const __nv_bfloat16 hh = __float2bfloat16_rn(h);
+              hi[(gate ? j : 16 + j) * 16 + ci] = hh;
+              lo[(gate ? j : 16 + j) * 16 + ci] = __float2bfloat16_rn(h - __bfloat162float(hh));
+            }
+          } else {
+            __half* hb = reinterpret_cast<__half*>(sb);  // [32 tokens][16 channels]
+            bool over = false;
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float mine = __uint_as_float(gate ? v[j] : v[16 + j]);
+              const float other = __shfl_xor_sync(0xffffffffu, __uint_as_float(gate ? v[16 + j] : v[j]), 16);
+              // gate lane: token j (own gate, partner's up); up lane: token 16+j
+              const float g = (gate ? mine : other) * s_a;
+              const float u = (gate ? other : mine) * s_b;
+              const float h = silu_fast(g) * u;
+              // fp16 holds |h| <= 65504: larger values saturate and are reported
+              // (for the tile's tokens; its padding rows are never read)
+              over |= !(fabsf(h) <= 65504.f) && c * 32 + (gate ? j : 16 + j) < mt.rows;
+              hb[(gate ? j : 16 + j) * 16 + ci] = __float2half_rn(fminf(fmaxf(h, -65504.f), 65504.f));
+            }
+            if (__any_sync(0xffffffffu, over) && lane == 0) set_status(ST_RANGE);
           }
         } else {
           float* fb = reinterpret_cast<float*>(sb);  // [32 tokens][32 channels]
@@ -393,6 +417,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
         __syncwarp();
         if (lane == 0 && store) {
           tma_store_2d(&tmOut, sb, xcol, t0);
+          if (MODE == TG_GATEUP && p.h_lo_col > 0) tma_store_2d(&tmOut, sb + 32 * 16 * 2, xcol + p.h_lo_col, t0);
           bulk_commit_group();
         }
         nbuf ^= 1;

@@ -74,30 +74,41 @@ __device__ __forceinline__ int tree_code(const TreeSched& s, int m) {
   return (int)(((m < 8 ? s.s0 >> (8 * m) : s.s1 >> (8 * (m - 8)))) & 0xFFu);
 }
 
-// Applies the schedule to NV values (NV >= the tree's size; values past the
-// tree's size are never read); the sum ends in v[0].
-template <int NV>
-__device__ __forceinline__ float4 tree_apply(float4 (&v)[NV], const TreeSched& s) {
+// One merge v[d] += v[s] of the code dst * NV + src, found by a binary search
+// over the code range with compile-time indices at the leaves (the code is the
+// same in every lane, so the branches never diverge and the values stay in
+// registers).  CW column groups share the dispatch.
+template <int NV, int CW, int LO, int HI>
+__device__ __forceinline__ void tree_merge(float4 (&v)[NV][CW], int code) {
+  if constexpr (HI - LO == 1) {
+    constexpr int d = LO / NV, s = LO % NV;
+    if constexpr (d < s) {
 #pragma unroll
-  for (int m = 0; m < NV - 1; ++m) {
-    if (m < s.nm) {
-      const int code = tree_code(s, m);
-      const int dst = code >> 4, src = code & 15;
-      float4 t = v[NV - 1];
-#pragma unroll
-      for (int j = 1; j < NV - 1; ++j)
-        if (j == src) t = v[j];
-#pragma unroll
-      for (int j = 0; j < NV - 1; ++j)
-        if (j == dst) {
-          v[j].x += t.x;
-          v[j].y += t.y;
-          v[j].z += t.z;
-          v[j].w += t.w;
-        }
+      for (int c = 0; c < CW; ++c) {
+        v[d][c].x += v[s][c].x;
+        v[d][c].y += v[s][c].y;
+        v[d][c].z += v[s][c].z;
+        v[d][c].w += v[s][c].w;
+      }
     }
+  } else {
+    constexpr int MID = (LO + HI) / 2;
+    if (code < MID)
+      tree_merge<NV, CW, LO, MID>(v, code);
+    else
+      tree_merge<NV, CW, MID, HI>(v, code);
   }
-  return v[0];
+}
+
+// Applies the schedule to NV values of CW column groups (NV >= the tree's
+// size; values past it are never read); the sums end in v[0][*].
+template <int NV, int CW>
+__device__ __forceinline__ void tree_apply(float4 (&v)[NV][CW], const TreeSched& s) {
+#pragma unroll 1
+  for (int m = 0; m < s.nm; ++m) {
+    const int code = tree_code(s, m);
+    tree_merge<NV, CW, 0, NV * NV>(v, (code >> 4) * NV + (code & 15));
+  }
 }
 
 // A warp's k entries (lane j < n holds entry j with position `p` and a payload

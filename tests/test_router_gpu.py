@@ -15,7 +15,7 @@ import torch
 
 from conftest import ROUTER_GOLDENS, golden_router_case
 from oracle import router as orouter
-from parity import compare_paths, topk_ids_match
+from parity import TIE, compare_paths, topk_ids_match
 
 pytestmark = pytest.mark.gpu
 
@@ -78,22 +78,61 @@ def test_fast_engine_hard_mode(cuda_device, name):
     got = r.route(xb.to(cuda_device), select="hard", k=8, precision="fast")
     ref = orouter.router_forward(w, xb.float().numpy(), (4, 4, 4), mode="hard", k=8)
     check_against(ref, got, "hard", wtol=2e-2)
+    # against the oracle that rounds where the FAST engine rounds: the level
+    # probabilities (one-hot x refraction) within the FAST tie window
+    ref16 = orouter.router_forward(w, xb.float().numpy(), (4, 4, 4), mode="hard", k=8, arith="bf16")
+    check_against(ref16, got, "hard", wtol=FAST_TIE)
+
+
+# The FAST engine rounds the encoder's hidden state G and the spectral row to
+# bf16.  Two fp32-or-better summation orders of the same sums (the tensor
+# cores' and the oracle's float64) land on different sides of a bf16 rounding
+# boundary for about 1 in 4e4 elements, and one such flip moves a level
+# probability by up to 1.7e-3 relative (measured on the CPU between float64 and
+# float32 summation with the same roundings).  So FAST top-8 ids are identical
+# to the bf16-faithful oracle's except where two probabilities lie within
+# FAST_TIE of each other; the fp32 engine is held to the 1e-6 rule.
+FAST_TIE = 2e-3
+
+
+def _fast_soft_check(w, xb, got):
+    """FAST soft top-8 against the bf16-faithful oracle: ids identical except
+    within FAST_TIE, excused positions rare, weights within FAST_TIE; against
+    the fp32 (reference-arithmetic) oracle the weights stay within the bf16
+    contract's 2e-2."""
+    ref16 = orouter.router_forward(w, xb, (4, 4, 4), mode="soft", k=8, arith="bf16")
+    ids = got["topk_ids"].cpu().numpy()
+    bad = topk_ids_match(ref16["expert_probs"], ref16["topk_ids"], ids, FAST_TIE)
+    assert bad == 0, f"{bad} top-8 positions differ beyond {FAST_TIE} ties"
+    excused = topk_ids_match(ref16["expert_probs"], ref16["topk_ids"], ids, TIE)
+    print(f"top-8 positions differing within the FAST tie window: {excused} of {ids.size}")
+    assert excused <= max(4, ids.size // 500)
+    np.testing.assert_allclose(got["topk_weights"].cpu().numpy(), ref16["topk_weights"], rtol=FAST_TIE)
+    ref = orouter.router_forward(w, xb, (4, 4, 4), mode="soft", k=8)
+    np.testing.assert_allclose(got["topk_weights"].cpu().numpy(), ref["topk_weights"], rtol=2e-2)
 
 
 @pytest.mark.parametrize("name", ["router_cfg0", "router_cfg0_perturbed"])
 def test_fast_engine_soft_mode(cuda_device, name):
-    """bf16 encoder in soft mode: weights within the 2e-2 bf16 tolerance."""
+    """bf16 encoder in soft mode (the headline's selection)."""
     w, x, g = golden_router_case(name)
     H, S = int(g["H"]), int(g["S"])
     r = make_router(w, H, S, (4, 4, 4), cuda_device)
     xb = torch.from_numpy(x).to(torch.bfloat16)
     got = r.route(xb.to(cuda_device), select="soft", k=8, precision="fast")
-    ref = orouter.router_forward(w, xb.float().numpy(), (4, 4, 4), mode="soft", k=8)
-    # spec carries bf16 error, so soft probabilities move by up to ~2e-2 relative;
-    # the top-8 set is compared with a 2e-2 tie tolerance
-    ids = got["topk_ids"].cpu().numpy()
-    assert topk_ids_match(ref["expert_probs"], ref["topk_ids"], ids, 5e-2) == 0
-    np.testing.assert_allclose(got["topk_weights"].cpu().numpy(), ref["topk_weights"], rtol=2e-2)
+    _fast_soft_check(w, xb.float().numpy(), got)
+
+
+@pytest.mark.parametrize("B", [4096, 1])
+def test_fast_engine_soft_mode_headline_shape(cuda_device, B):
+    """The headline's router: seed-0 weights, unit-RMS bf16 tokens (seed 2), 4096 tokens and one."""
+    from sb200 import synth
+    H, S = 2048, 256
+    w = synth.router_weights(H, S, seed=0)
+    r = make_router(w, H, S, (4, 4, 4), cuda_device)
+    xb = synth.hidden_states(B, H, seed=2, dtype=torch.bfloat16)
+    got = r.route(xb.to(cuda_device), select="soft", k=8, precision="fast")
+    _fast_soft_check(w, xb.float().numpy(), got)
 
 
 @pytest.mark.parametrize("B", [300, 8500])

@@ -1,8 +1,20 @@
 """Ternary SwiGLU kernels against the CPU oracle (needs a B200).
 
-Contract: outputs after the fp32 scales within 1e-3 relative — held here
-row-normwise (||y - y_ref|| / ||y_ref|| <= 1e-3 per token); the elementwise
-error relative to |y_ref| + rms(row) is bounded too.
+Contract: outputs after the fp32 scales within 1e-3 relative.
+
+* fp32 inputs (the reference API's dtype) take the fp32-faithful form: x and
+  the SwiGLU hidden state h enter the tensor cores as bf16 hi/lo pairs (each
+  value to 2^-16, with fp32's exponent range), accumulation fp32.  Held to
+  1e-4 row-normwise and, elementwise, 1e-3 relative to |y_ref| + 0.1 rms(row):
+  1e-3 relative for every output of at least a tenth of its row's RMS, and
+  1e-4 of the row RMS absolutely for smaller ones (no elementwise bound can be
+  purely relative: any two fp32 summation orders, the reference's own CPU and
+  GPU paths included, differ by far more than 1e-3 of an output that cancels
+  to near zero).
+* bf16 inputs (the MoE layer's hot path) keep bf16 activations and round h to
+  fp16 (2^-11) before the down projection: 1e-3 row-normwise and 2e-3
+  elementwise relative to |y_ref| + rms(row).  An |h| beyond fp16's 65504
+  saturates and is reported through the device status word.
 """
 
 from __future__ import annotations
@@ -18,7 +30,10 @@ from parity import ternary_errors
 pytestmark = pytest.mark.gpu
 
 NORM_TOL = 1e-3
-ELEM_TOL = 5e-3
+ELEM_TOL = 2e-3
+FP32_NORM_TOL = 1e-4
+FP32_ELEM_TOL = 1e-3
+FP32_FLOOR = 0.1
 
 # the grouped GEMM engines (SB_TERNARY_ENGINE): CTA pairs (default), one CTA
 # with the weights in TMEM, one CTA with the weights in shared memory
@@ -41,6 +56,103 @@ def assert_close(got, ref, what):
     print(f"{what}: normwise {norm:.3e} elementwise {elem:.3e}")
     assert norm <= NORM_TOL, f"{what}: normwise {norm}"
     assert elem <= ELEM_TOL, f"{what}: elementwise {elem}"
+
+
+def assert_fp32_faithful(got, ref, what):
+    got = np.asarray(got, np.float64)
+    ref = np.asarray(ref, np.float64)
+    d = np.abs(got - ref)
+    rms = np.sqrt((ref * ref).mean(axis=1, keepdims=True)) + 1e-30
+    norm = float((np.sqrt((d * d).sum(axis=1)) / (np.sqrt((ref * ref).sum(axis=1)) + 1e-30)).max())
+    elem = float((d / (np.abs(ref) + FP32_FLOOR * rms)).max())
+    print(f"{what}: normwise {norm:.3e} elementwise {elem:.3e}")
+    assert norm <= FP32_NORM_TOL, f"{what}: normwise {norm}"
+    assert elem <= FP32_ELEM_TOL, f"{what}: elementwise {elem}"
+
+
+def _olmoe_expert(cuda_device, seed=21, H=2048, I=1024):
+    from sb200 import synth
+    ex = synth.ternary_experts(1, H, I, seed=seed)[0]
+    packs = [torch.from_numpy(otern.pack_ternary(ex[f"{n}_ternary"].T.copy())).to(cuda_device)
+             for n in ("gate", "up", "down")]
+    s = [torch.from_numpy(ex[f"{n}_scale"]).to(cuda_device) for n in ("gate", "up", "down")]
+    return ex, packs, s
+
+
+def _oracle(ex, x):
+    return otern.gated_mlp(np.asarray(x, np.float64), ex["gate_ternary"], ex["up_ternary"], ex["down_ternary"],
+                           ex["gate_scale"], ex["up_scale"], ex["down_scale"])
+
+
+@pytest.mark.parametrize("M", [1, 3, 130, 512])
+def test_gated_mlp_fp32_input_is_fp32_faithful(cuda_device, M):
+    from sb200 import synth
+    import ternary_expert_ext as ext
+    ex, packs, s = _olmoe_expert(cuda_device)
+    x = synth.hidden_states(M, 2048, seed=24, device=cuda_device)          # fp32
+    y = ext.ternary_gated_mlp(x, *packs, *s)
+    assert_fp32_faithful(y.cpu().numpy(), _oracle(ex, x.cpu().numpy()), f"fp32 expert M={M}")
+
+
+@pytest.mark.parametrize("scale", [1e3, 1e4])
+def test_large_magnitude_rows(cuda_device, scale):
+    """Rows scaled far past unit RMS: the fp32 path keeps fp32's range (bf16
+    hi/lo terms) and its accuracy; on the bf16 path the fp16 hidden state
+    saturates and the library reports it instead of returning inf."""
+    from sb200 import _lib, synth
+    from sb200.ternary import TernaryExperts
+    import ternary_expert_ext as ext
+    ex, packs, s = _olmoe_expert(cuda_device, seed=25)
+    x = synth.hidden_states(64, 2048, seed=26, device=cuda_device) * scale
+    y = ext.ternary_gated_mlp(x, *packs, *s)
+    torch.cuda.synchronize()
+    assert _lib.load().sb_device_status(0) == 0
+    assert_fp32_faithful(y.cpu().numpy(), _oracle(ex, x.cpu().numpy()), f"rows x{scale:g} fp32")
+    te = TernaryExperts([ex], cuda_device)
+    ids = torch.zeros(64, 1, dtype=torch.int32, device=cuda_device)
+    w = torch.ones(64, 1, device=cuda_device)
+    yb = te.forward(x.bfloat16(), ids, w)
+    torch.cuda.synchronize()
+    assert torch.isfinite(yb).all()
+    assert _lib.load().sb_device_status(0) == -1
+    assert "range" in _lib.last_error()
+
+
+def _reference_extension():
+    import glob
+    import importlib.util
+    from pathlib import Path
+    so = glob.glob(str(Path(__file__).resolve().parents[1] / "oracle" / "_ref" / "ternary_expert_ext_ref*.so"))
+    if not so:
+        return None
+    spec = importlib.util.spec_from_file_location("ternary_expert_ext_ref", so[0])
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+@pytest.mark.parametrize("M", [1, 3, 130, 512])
+def test_gated_mlp_matches_reference_kernel(cuda_device, M):
+    """The reference's own ternary_gated_mlp kernel (cuda/v5/ternary_torch_ext.cu,
+    compiled from its source into oracle/_ref) run on this GPU on the same
+    packed weights and fp32 tokens: the drop-in agrees with it to the fp32
+    contract, and both agree with the float64 oracle."""
+    ref = _reference_extension()
+    if ref is None:
+        pytest.skip("reference extension not built (oracle/build_ref.py)")
+    from sb200 import synth
+    import ternary_expert_ext as ext
+    ex = synth.ternary_experts(1, 2048, 1024, seed=27)[0]
+    packs = [ref.pack_ternary(torch.from_numpy(ex[f"{n}_ternary"].T.copy())).to(cuda_device)
+             for n in ("gate", "up", "down")]
+    s = [torch.from_numpy(ex[f"{n}_scale"]).to(cuda_device) for n in ("gate", "up", "down")]
+    x = synth.hidden_states(M, 2048, seed=28, device=cuda_device)
+    y_ref = ref.ternary_gated_mlp(x, *packs, *s)
+    y = ext.ternary_gated_mlp(x, *packs, *s)
+    torch.cuda.synchronize()
+    exact = _oracle(ex, x.cpu().numpy())
+    assert_fp32_faithful(y_ref.cpu().numpy(), exact, f"reference kernel M={M} vs oracle")
+    assert_fp32_faithful(y.cpu().numpy(), y_ref.cpu().numpy(), f"ours vs reference kernel M={M}")
 
 
 def test_repack_matches_host_layout(cuda_device):
@@ -87,6 +199,8 @@ def test_gated_mlp_olmoe_shape(cuda_device, M):
     ref = otern.gated_mlp(x.float().cpu().numpy(), ex["gate_ternary"], ex["up_ternary"],
                           ex["down_ternary"], ex["gate_scale"], ex["up_scale"], ex["down_scale"])
     assert_close(y.cpu().numpy(), ref, f"expert M={M}")
+    # a second call with the same packed tensors reuses their device layout
+    assert torch.equal(ext.ternary_gated_mlp(x, gp, up, dp, *s), y)
 
 
 def test_ternary_linear(cuda_device):
