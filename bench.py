@@ -542,7 +542,7 @@ def stack_workload(tokens: int, device, layers: int = 16, select: str = "soft", 
     rank = 0
     if world > 1:
         import torch.distributed as dist
-        from sb200.ep import EPMoELayer, ExpertParallelMoE
+        from sb200.ep import EPMoELayer
         rank = dist.get_rank()
     shared = None
     for l in range(layers):
@@ -553,9 +553,9 @@ def stack_workload(tokens: int, device, layers: int = 16, select: str = "soft", 
         if world > 1:
             el = E_EXPERTS // world
             local = TernaryExperts.random(el, H, I_INTER, seed=200 + 64 * l + rank, device=device)
-            ep = ExpertParallelMoE(local, E_EXPERTS, TOPK, tokens, workspace=shared)
-            shared = ep.workspace
-            stack.append(EPMoELayer(r, ep, top_k=TOPK, select=select))
+            layer = EPMoELayer(r, local, E_EXPERTS, TOPK, tokens, select=select, chunks=1, workspace=shared)
+            shared = layer.ep.workspace
+            stack.append(layer)
         else:
             stack.append(BVHMoELayer(r, TernaryExperts.random(E_EXPERTS, H, I_INTER, seed=200 + l, device=device),
                                      top_k=TOPK, select=select))
@@ -581,7 +581,7 @@ def ep_workload(batch: int, device, world: int, select: str = "soft"):
     import torch.distributed as dist
     from bvh_router import BVHRouter, RouterConfig
     from sb200 import synth
-    from sb200.ep import EPMoELayer, ExpertParallelMoE
+    from sb200.ep import EPMoELayer
     from sb200.moe import GraphedLayer, HostPipeline
     from sb200.ternary import TernaryExperts
     rank = dist.get_rank()
@@ -592,8 +592,8 @@ def ep_workload(batch: int, device, world: int, select: str = "soft"):
     e_local = E_EXPERTS // world
     allx = synth.ternary_experts(E_EXPERTS, H, I_INTER, seed=2)
     local = TernaryExperts(allx[rank * e_local:(rank + 1) * e_local], device)
-    ep = ExpertParallelMoE(local, E_EXPERTS, TOPK, batch)
-    layer = EPMoELayer(r, ep, top_k=TOPK, select=select)
+    chunks = int(os.environ.get("SB_EP_CHUNKS", "2"))
+    layer = EPMoELayer(r, local, E_EXPERTS, TOPK, batch, select=select, chunks=chunks)
     x = synth.hidden_states(batch, H, seed=2 + 1000 * rank, dtype=torch.bfloat16, device=device)
     out = torch.empty(batch, H, dtype=torch.bfloat16, device=device)
     ids, _ = layer.route(x)
@@ -643,7 +643,8 @@ def ep_workload(batch: int, device, world: int, select: str = "soft"):
                        "l2": "flushed (256 MiB write) before every timed step, outside the events"},
             "parallelism": (f"ep{world}: {e_local} experts per GPU; each token row sent once per GPU "
                             "holding one of its experts and one fp32 partial sum returned, by the "
-                            "layer's own kernels through peer memory (no host sync, no library collective)")}
+                            "layer's own kernels through peer memory (no host sync, no library collective); "
+                            f"{chunks} token ranges on their own streams so transfers overlap the GEMMs")}
     return step, (e2e_run, e2e_sequential, eager_step), meta
 
 

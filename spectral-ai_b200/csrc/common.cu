@@ -198,8 +198,9 @@ extern "C" int sb_device_status(int device) {
     return sb::fail(SB_ERR_DEVICE_TIMEOUT, "device %d kernel status 0x%x (bounded wait expired)", device, v);
   if (v & sb::ST_RANGE)
     return sb::fail(SB_ERR_INVALID,
-                    "device %d kernel status 0x%x (a hidden value beyond fp16's range was saturated; "
-                    "fp32 inputs take the bf16 hi/lo path, which has fp32's range)", device, v);
+                    "device %d kernel status 0x%x (a non-finite value in a layer's output: a non-finite "
+                    "input, or on the bf16 path a hidden value past fp16's 65504; fp32 inputs take the bf16 "
+                    "hi/lo path, which has fp32's range)", device, v);
   if (v != 0)
     return sb::fail(SB_ERR_INVALID, "device %d kernel status 0x%x (an out-of-range expert id was dropped)",
                     device, v);

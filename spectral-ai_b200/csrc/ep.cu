@@ -6,20 +6,21 @@
 // [r*El, (r+1)*El), El = E / W.  One forward on every rank (all ranks call it
 // the same number of times; it is collective):
 //
-//   ep_route        which ranks each token needs (its k expert ids) and the
-//                   token's row in each of those ranks' receive segments
-//                   (a block-wide scan per destination); a token is sent
-//                   once per destination rank, however many of its experts
-//                   live there (the reference sends one copy per slot through
-//                   its Python loop, python/olmoe_extract.py:146-155).
-//   ep_send         each (token, destination) row (bf16) and its metadata —
-//                   the destination's local expert ids of the token, ascending,
-//                   and their routing weights — stored straight into the
-//                   destination's receive buffer; the last block then stores
-//                   the row count and raises this rank's dispatch flag there.
-//   ep_recv_plan    waits (bounded) for every source's flag, histograms the
-//                   received (row, expert) entries, plans expert segments and
-//                   m-tiles as the single-GPU layer does.
+//   ep_send         a warp per token: the ranks its k expert ids live on, a
+//                   row claimed in each of those ranks' receive segment for
+//                   this rank (an atomic counter per destination), the token's
+//                   row (bf16, loaded once) and its metadata — the
+//                   destination's local expert ids of the token, ascending, and
+//                   their routing weights — stored straight into the
+//                   destination's receive buffer; a token goes once to each
+//                   rank holding any of its experts, however many live there
+//                   (the reference sends one copy per slot through its Python
+//                   loop, python/olmoe_extract.py:146-155).  The last block
+//                   stores the row counts and raises this rank's dispatch flag
+//                   at every destination.
+//   ep_wait         one block waits (bounded) for every source's flag;
+//   ep_recv_plan    histograms the received (row, expert) entries, plans expert
+//                   segments and m-tiles as the single-GPU layer does.
 //   ep_recv_scatter copies each received row into its experts' segments.
 //   grouped GEMMs   the same tcgen05 kernels as the single-GPU layer
 //                   (gate/up + SwiGLU, down + routing weight, fp32 per entry).
@@ -27,8 +28,8 @@
 //                   entries' outputs — the subtree of this rank's experts —
 //                   stored (fp32) into the source's return buffer; the last
 //                   block raises this rank's return flag at every source.
-//   ep_combine      waits for every destination's return flag, then per token
-//                   the tree sum of its destinations' partial sums -> out.
+//   ep_wait         one block waits for every destination's return flag;
+//   ep_combine      per token, the tree sum of its destinations' partial sums -> out.
 //
 // Because the partial sums follow the same tree as the single-GPU combine,
 // the layer's output equals the single-GPU layer's bit for bit whenever E/W is
@@ -40,16 +41,18 @@
 // fences them (fence.sc.sys) before it counts itself done, and the last block
 // fences again before its st.release.sys of the flag; a waiting thread reads
 // the flag with ld.acquire.sys.  Flags carry the forward's epoch (a counter
-// in device memory, bumped by ep_route), so they never need resetting and the
+// in device memory, bumped by ep_send), so they never need resetting and the
 // forward can be replayed from a CUDA graph.  Buffer reuse across forwards is
 // ordered by the protocol itself: a source writes forward t+1's rows only after
 // its combine of forward t saw every destination's return flag, which each
 // destination raises after its last read of forward t's rows.
 //
-// Waits are bounded (the handle's timeout); one that runs out records an error
-// in the handle's control word (sb_ep_status) and the kernels finish with what
-// they have.  Every wait is on a flag another rank's kernel raises without
-// waiting itself, so no wait depends on a kernel of the same GPU.
+// Waits are bounded (the handle's timeout) and happen in a one-block kernel
+// only (the heavy kernels never spin, so they never hold SMs that another
+// stream's kernels need); one that runs out records an error in the handle's
+// control word (sb_ep_status) and the kernels after it finish with what they
+// have.  Every wait is on a flag another rank's kernel raises without waiting
+// itself, so no wait depends on a kernel of the same GPU.
 //
 // No TMA or bulk copy touches peer memory: peer rows move with 16-byte
 // loads and stores from the SMs.
@@ -74,6 +77,7 @@ struct EpCtrl {
   uint32_t done_send;
   uint32_t done_ret;
   uint32_t error;  // bit 0: a dispatch wait ran out; bit 1: a return wait; bit 2: a bad expert id
+  uint32_t send_cnt[8];  // rows claimed at each destination by this forward (zeroed after it)
 };
 
 // One rank's peer-visible buffer (byte offsets; the same on every rank).
@@ -139,71 +143,18 @@ __device__ __forceinline__ int nth_bit(unsigned m, int q) {
 __device__ __forceinline__ uint8_t* ep_at(const EpArgs& a, int g, int64_t off) { return a.peer[g] + off; }
 
 // ---------------------------------------------------------------------------
-// ep_route: destinations and receive rows, one block
-// ---------------------------------------------------------------------------
-constexpr int EP_ROUTE_THREADS = 1024;
-
-__global__ void __launch_bounds__(EP_ROUTE_THREADS) ep_route_kernel(const int32_t* __restrict__ ids, int64_t B,
-                                                                    EpArgs a, int* __restrict__ send_pos,
-                                                                    int* __restrict__ send_cnt) {
-  __shared__ int wsum[EP_MAX_WORLD][32];
-  __shared__ int base[EP_MAX_WORLD], ctot[EP_MAX_WORLD];
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if (tid == 0) a.ctrl->epoch += 1u;  // this forward's epoch, read by the kernels after this one
-  if (tid < EP_MAX_WORLD) base[tid] = 0;
-  __syncthreads();
-  for (int64_t c0 = 0; c0 < B; c0 += EP_ROUTE_THREADS) {
-    const int64_t t = c0 + tid;
-    unsigned mask = 0;
-    if (t < B) {
-      for (int j = 0; j < a.k; ++j) {
-        const int e = __ldg(ids + t * a.k + j);
-        if (e >= 0 && e < a.E)
-          mask |= 1u << (e / a.El);
-        else
-          atomicOr(&a.ctrl->error, 4u);
-      }
-    }
-    int pre[EP_MAX_WORLD];
-#pragma unroll
-    for (int g = 0; g < EP_MAX_WORLD; ++g) {
-      const unsigned b = __ballot_sync(0xffffffffu, (mask >> g) & 1u);
-      pre[g] = __popc(b & ((1u << lane) - 1u));
-      if (lane == 0) wsum[g][warp] = __popc(b);
-    }
-    __syncthreads();
-    if (warp < a.W) {  // warp g scans destination g's 32 warp totals
-      const int v = wsum[warp][lane];
-      int inc = v;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int u = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += u;
-      }
-      wsum[warp][lane] = inc - v;
-      if (lane == 31) ctot[warp] = inc;
-    }
-    __syncthreads();
-    if (t < B) {
-      for (int g = 0; g < a.W; ++g)
-        send_pos[t * a.W + g] = ((mask >> g) & 1u) ? base[g] + wsum[g][warp] + pre[g] : -1;
-    }
-    __syncthreads();
-    if (tid < a.W) base[tid] += ctot[tid];
-    __syncthreads();
-  }
-  if (tid < a.W) send_cnt[tid] = base[tid];
-}
-
-// ---------------------------------------------------------------------------
 // ep_send: rows and metadata into the destinations' receive buffers
 // ---------------------------------------------------------------------------
-// The last block to finish (counted in ctrl->*done) runs `last()`.
+// The last block to finish (counted in ctrl->*done) runs `last()`.  Each
+// block orders its stores before its count with a GPU-scope fence; the last
+// block, having seen every count, fences at system scope before `last()`
+// raises flags that other GPUs acquire, so every block's stores (peer memory
+// included) happen before the flag in the memory model's causality order.
 template <typename F>
 __device__ __forceinline__ void ep_last_block(uint32_t* done, F last) {
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
+    __threadfence();
     const uint32_t prev = atomicAdd(done, 1u);
     if (prev == gridDim.x - 1) {
       __threadfence_system();
@@ -216,77 +167,115 @@ __device__ __forceinline__ void ep_last_block(uint32_t* done, F last) {
 __global__ void __launch_bounds__(EP_THREADS) ep_send_kernel(const __nv_bfloat16* __restrict__ x,
                                                              const int32_t* __restrict__ ids,
                                                              const float* __restrict__ wts, int64_t B, EpArgs a,
-                                                             const int* __restrict__ send_pos,
-                                                             const int* __restrict__ send_cnt) {
+                                                             int* __restrict__ send_pos) {
   const int lane = threadIdx.x & 31;
   const int n16 = (int)(a.H >> 3);  // 16-byte words per row
-  const int64_t pairs = B * a.W;
-  for (int64_t p = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; p < pairs;
-       p += ((int64_t)gridDim.x * blockDim.x) >> 5) {
-    const int pos = __ldg(send_pos + p);
-    if (pos < 0) continue;
-    const int64_t t = p / a.W;
-    const int g = (int)(p % a.W);
-    const int64_t row = (int64_t)a.rank * a.cap + pos;  // this rank's segment at g
-    // the row: 16-byte words, all loads before the stores
-    const uint4* src = reinterpret_cast<const uint4*>(x + t * a.H);
-    uint4* dst = reinterpret_cast<uint4*>(ep_at(a, g, a.L.rx) + row * a.H * 2);
-    for (int c0 = 0; c0 < n16; c0 += 32 * 8) {
-      uint4 v[8];
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (c0 + lane + 32 * u < n16) v[u] = __ldg(src + c0 + lane + 32 * u);
-#pragma unroll
-      for (int u = 0; u < 8; ++u)
-        if (c0 + lane + 32 * u < n16) dst[c0 + lane + 32 * u] = v[u];
-    }
-    // metadata: the token's experts on g, ascending local id (then slot)
-    int le = 0x7fffffff;
+  for (int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < B;
+       t += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    // the token's slots: lane j < k holds slot j
+    int e = -1;
     float w = 0.f;
     if (lane < a.k) {
-      const int e = __ldg(ids + t * a.k + lane);
-      if (e >= 0 && e < a.E && e / a.El == g) {
-        le = e - g * a.El;
-        w = wts ? __ldg(wts + t * a.k + lane) : 1.0f;
+      e = __ldg(ids + t * a.k + lane);
+      w = wts ? __ldg(wts + t * a.k + lane) : 1.0f;
+      if (e < 0 || e >= a.E) {
+        atomicOr(&a.ctrl->error, 4u);
+        e = -1;
       }
     }
-    const bool mine = le != 0x7fffffff;
-    int rank = 0;
-    for (int j = 0; j < a.k; ++j) {
-      const int q = __shfl_sync(0xffffffffu, le, j);
-      rank += (q < le || (q == le && j < lane)) ? 1 : 0;
-    }
-    uint32_t byte = 0xFFu;
-    float wq = 0.f;
+    const int dest = e >= 0 ? e / a.El : -1;
+    unsigned mask = 0;  // destination ranks of the token
 #pragma unroll
-    for (int q = 0; q < EP_KE; ++q) {
-      const unsigned m = __ballot_sync(0xffffffffu, mine && rank == q);
-      const int s = m ? __ffs(m) - 1 : 0;
-      const int lq = __shfl_sync(0xffffffffu, le, s);
-      const float wv = __shfl_sync(0xffffffffu, w, s);
-      if (lane == q && m) {
-        byte = (uint32_t)lq;
-        wq = wv;
-      }
+    for (int g = 0; g < EP_MAX_WORLD; ++g)
+      if (__ballot_sync(0xffffffffu, dest == g)) mask |= 1u << g;
+    if (lane < a.W) send_pos[t * a.W + lane] = -1;
+    if (!mask) continue;
+    // the row, loaded once for all its destinations (rows up to 4096 bf16 in registers)
+    const uint4* src = reinterpret_cast<const uint4*>(x + t * a.H);
+    const bool small = n16 <= 32 * 8;
+    uint4 v[8];
+    if (small) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (lane + 32 * u < n16) v[u] = __ldg(src + lane + 32 * u);
     }
-    // lanes 0..3 pack four bytes each; lanes 0..15 store one weight each
-    const uint32_t b0 = __shfl_sync(0xffffffffu, byte, (4 * lane) & 31), b1 = __shfl_sync(0xffffffffu, byte, (4 * lane + 1) & 31);
-    const uint32_t b2 = __shfl_sync(0xffffffffu, byte, (4 * lane + 2) & 31), b3 = __shfl_sync(0xffffffffu, byte, (4 * lane + 3) & 31);
-    if (lane < 4)
-      reinterpret_cast<uint32_t*>(ep_at(a, g, a.L.meta_e) + row * EP_KE)[lane] = b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
-    if (lane < EP_KE) reinterpret_cast<float*>(ep_at(a, g, a.L.meta_w))[row * EP_KE + lane] = wq;
+    for (unsigned mm = mask; mm; mm &= mm - 1) {
+      const int g = __ffs(mm) - 1;
+      // this token's row at g: a slot of g's receive segment for this rank
+      int pos = 0;
+      if (lane == 0) pos = atomicAdd(reinterpret_cast<int*>(&a.ctrl->send_cnt[g]), 1);
+      pos = __shfl_sync(0xffffffffu, pos, 0);
+      if (lane == 0) send_pos[t * a.W + g] = pos;
+      const int64_t row = (int64_t)a.rank * a.cap + pos;
+      uint4* dst = reinterpret_cast<uint4*>(ep_at(a, g, a.L.rx) + row * a.H * 2);
+      if (small) {
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          if (lane + 32 * u < n16) dst[lane + 32 * u] = v[u];
+      } else {
+        for (int c = lane; c < n16; c += 32) dst[c] = __ldg(src + c);
+      }
+      // metadata: the token's experts on g, ascending local id (then slot)
+      const bool mine = dest == g;
+      const int le = mine ? e - g * a.El : 0x7fffffff;
+      int rank = 0;
+      for (int j = 0; j < a.k; ++j) {
+        const int q = __shfl_sync(0xffffffffu, le, j);
+        rank += (q < le || (q == le && j < lane)) ? 1 : 0;
+      }
+      uint32_t byte = 0xFFu;
+      float wq = 0.f;
+#pragma unroll
+      for (int q = 0; q < EP_KE; ++q) {
+        const unsigned m = __ballot_sync(0xffffffffu, mine && rank == q);
+        const int s = m ? __ffs(m) - 1 : 0;
+        const int lq = __shfl_sync(0xffffffffu, le, s);
+        const float wv = __shfl_sync(0xffffffffu, w, s);
+        if (lane == q && m) {
+          byte = (uint32_t)lq;
+          wq = wv;
+        }
+      }
+      // lanes 0..3 pack four bytes each; lanes 0..15 store one weight each
+      const uint32_t b0 = __shfl_sync(0xffffffffu, byte, (4 * lane) & 31);
+      const uint32_t b1 = __shfl_sync(0xffffffffu, byte, (4 * lane + 1) & 31);
+      const uint32_t b2 = __shfl_sync(0xffffffffu, byte, (4 * lane + 2) & 31);
+      const uint32_t b3 = __shfl_sync(0xffffffffu, byte, (4 * lane + 3) & 31);
+      if (lane < 4)
+        reinterpret_cast<uint32_t*>(ep_at(a, g, a.L.meta_e) + row * EP_KE)[lane] =
+            b0 | (b1 << 8) | (b2 << 16) | (b3 << 24);
+      if (lane < EP_KE) reinterpret_cast<float*>(ep_at(a, g, a.L.meta_w))[row * EP_KE + lane] = wq;
+    }
   }
   ep_last_block(&a.ctrl->done_send, [&] {
-    const uint32_t epoch = ld_volatile(&a.ctrl->epoch);
+    // a new forward: its epoch tags every flag this and the later kernels use
+    const uint32_t epoch = a.ctrl->epoch + 1u;
+    a.ctrl->epoch = epoch;
     for (int g = 0; g < a.W; ++g)
-      reinterpret_cast<int*>(ep_at(a, g, a.L.rcount))[a.rank] = send_cnt[g];
+      reinterpret_cast<int*>(ep_at(a, g, a.L.rcount))[a.rank] = (int)atomicExch(&a.ctrl->send_cnt[g], 0u);
     __threadfence_system();
     for (int g = 0; g < a.W; ++g) st_release_sys(reinterpret_cast<uint32_t*>(ep_at(a, g, a.L.dflag)) + a.rank, epoch);
   });
 }
 
 // ---------------------------------------------------------------------------
-// ep_recv_plan: wait for the sources, plan the local expert segments
+// ep_wait: one block waits (bounded) until every rank raised its flag of this
+// forward; the kernels after it in the stream read what the flags cover, and
+// none of the heavy kernels ever spins
+// ---------------------------------------------------------------------------
+__global__ void ep_wait_kernel(EpArgs a, int64_t flag_off, unsigned err_bit) {
+  const int tid = threadIdx.x;
+  if (tid < a.W) {
+    const uint32_t epoch = ld_volatile(&a.ctrl->epoch);
+    if (!ep_wait(reinterpret_cast<const uint32_t*>(a.peer[a.rank] + flag_off) + tid, epoch, a.limit_ns)) {
+      atomicOr(&a.ctrl->error, err_bit);
+      set_status(ST_TIMEOUT_EP);
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// ep_recv_plan: plan the local expert segments
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(PLAN_THREADS) ep_recv_plan_kernel(EpArgs a, int* __restrict__ rcnt,
                                                                     int* __restrict__ counts, int* __restrict__ offsets,
@@ -299,18 +288,13 @@ __global__ void __launch_bounds__(PLAN_THREADS) ep_recv_plan_kernel(EpArgs a, in
   const uint8_t* own = a.peer[a.rank];
   for (int e = tid; e < a.El; e += PLAN_THREADS) sh_count[e] = 0;
   if (tid < a.W) {
-    const uint32_t epoch = ld_volatile(&a.ctrl->epoch);
-    int c = 0;
-    if (ep_wait(reinterpret_cast<const uint32_t*>(own + a.L.dflag) + tid, epoch, a.limit_ns)) {
-      c = reinterpret_cast<const volatile int*>(own + a.L.rcount)[tid];
-      if (c < 0 || c > a.cap) {
-        atomicOr(&a.ctrl->error, 4u);
-        c = 0;
-      }
-    } else {
-      atomicOr(&a.ctrl->error, 1u);
-      set_status(ST_TIMEOUT_EP);
+    // the counts landed before the flags ep_wait_kernel saw (it ran just before)
+    int c = reinterpret_cast<const volatile int*>(own + a.L.rcount)[tid];
+    if (c < 0 || c > a.cap) {
+      atomicOr(&a.ctrl->error, 4u);
+      c = 0;
     }
+    if (a.ctrl->error & 1u) c = 0;  // a dispatch wait ran out: nothing usable arrived
     srcnt[tid] = c;
     rcnt[tid] = c;
   }
@@ -458,22 +442,9 @@ __global__ void __launch_bounds__(EP_THREADS) ep_return_kernel(EpArgs a, const i
 template <typename TO>
 __global__ void __launch_bounds__(EP_THREADS) ep_combine_kernel(EpArgs a, int64_t B, const int* __restrict__ send_pos,
                                                                 TO* __restrict__ out) {
-  __shared__ int ok;
   const int lane = threadIdx.x & 31;
   const uint8_t* own = a.peer[a.rank];
-  if (threadIdx.x == 0) {
-    const uint32_t epoch = ld_volatile(&a.ctrl->epoch);
-    int good = 1;
-    for (int g = 0; g < a.W; ++g)
-      if (!ep_wait(reinterpret_cast<const uint32_t*>(own + a.L.rflag) + g, epoch, a.limit_ns)) {
-        atomicOr(&a.ctrl->error, 2u);
-        set_status(ST_TIMEOUT_EP);
-        good = 0;
-        break;
-      }
-    ok = good;
-  }
-  __syncthreads();
+  const bool ok = (a.ctrl->error & 2u) == 0;  // set by ep_wait_kernel when a return wait ran out
   const int n4 = (int)(a.H >> 2);
   const float* ret = reinterpret_cast<const float*>(own + a.L.ret);
   for (int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < B;
@@ -509,6 +480,11 @@ __global__ void __launch_bounds__(EP_THREADS) ep_combine_kernel(EpArgs a, int64_
                                             : make_float4(0.f, 0.f, 0.f, 0.f);
         }
       tree_apply<EP_MAX_WORLD, CW>(v, sched);
+      bool bad = false;
+#pragma unroll
+      for (int w = 0; w < CW; ++w)
+        bad |= !(isfinite(v[0][w].x) && isfinite(v[0][w].y) && isfinite(v[0][w].z) && isfinite(v[0][w].w));
+      if (__any_sync(0xffffffffu, bad) && lane == 0) set_status(ST_RANGE);
 #pragma unroll
       for (int w = 0; w < CW; ++w)
         if (c0 + 32 * w < n4) store4<TO>(out + t * a.H + 4 * (c0 + 32 * w), v[0][w]);
@@ -531,7 +507,7 @@ __global__ void ep_stale_wait_kernel(EpArgs a) {
 // ---------------------------------------------------------------------------
 struct EpWorkspace {
   int64_t R, Rp, ldx, ldh, max_mt;
-  size_t send_pos, send_cnt, rcnt, counts, offsets, cursor, nmt, mtiles, row_w, inv, xp, hp, yp, total;
+  size_t send_pos, rcnt, counts, offsets, cursor, nmt, mtiles, row_w, inv, xp, hp, yp, total;
 };
 
 }  // namespace sb
@@ -575,7 +551,6 @@ EpWorkspace ep_workspace(const sb_ep* h) {
     return at;
   };
   w.send_pos = take(sizeof(int) * (size_t)h->cap * h->W);
-  w.send_cnt = take(sizeof(int) * EP_MAX_WORLD);
   w.rcnt = take(sizeof(int) * EP_MAX_WORLD);
   w.counts = take(sizeof(int) * h->El);
   w.offsets = take(sizeof(int) * h->El);
@@ -843,7 +818,6 @@ extern "C" int sb_ep_forward(sb_ep* h, const void* x, int x_dtype, int64_t batch
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   int* send_pos = reinterpret_cast<int*>(ws + w.send_pos);
-  int* send_cnt = reinterpret_cast<int*>(ws + w.send_cnt);
   int* rcnt = reinterpret_cast<int*>(ws + w.rcnt);
   int* counts = reinterpret_cast<int*>(ws + w.counts);
   int* offsets = reinterpret_cast<int*>(ws + w.offsets);
@@ -861,23 +835,23 @@ extern "C" int sb_ep_forward(sb_ep* h, const void* x, int x_dtype, int64_t batch
   if (engine == ENGINE_PAIR && (h->H % 4) != 0) engine = ENGINE_TS;
   const int tile_rows = engine == ENGINE_PAIR ? TP_TILE_ROWS : 128;
   {
-    ProfScope prof("ep_route", st);
-    ep_route_kernel<<<1, EP_ROUTE_THREADS, 0, st>>>(ids, batch, a, send_pos, send_cnt);
-    SB_CUDA_TRY(cudaGetLastError());
-  }
-  {
     ProfScope prof("ep_send", st);
-    int64_t blocks = (batch * h->W * 32 + EP_THREADS - 1) / EP_THREADS;
+    int64_t blocks = (batch * 32 + EP_THREADS - 1) / EP_THREADS;
     if (blocks > (int64_t)sms * 4) blocks = (int64_t)sms * 4;
     if (blocks < 1) blocks = 1;
     ep_send_kernel<<<(unsigned)blocks, EP_THREADS, 0, st>>>(static_cast<const __nv_bfloat16*>(x), ids, weights,
-                                                             batch, a, send_pos, send_cnt);
+                                                             batch, a, send_pos);
+    SB_CUDA_TRY(cudaGetLastError());
+  }
+  {
+    ProfScope prof("ep_wait_dispatch", st);
+    ep_wait_kernel<<<1, 32, 0, st>>>(a, h->L.dflag, 1u);
     SB_CUDA_TRY(cudaGetLastError());
   }
   {
     ProfScope prof("ep_recv_plan", st);
-    ep_recv_plan_kernel<<<1, PLAN_THREADS, sizeof(int) * h->El, st>>>(a, rcnt, counts, offsets, cursor, mtiles, nmt,
-                                                                       (int)w.max_mt, tile_rows);
+    ep_recv_plan_kernel<<<1, PLAN_THREADS, sizeof(int) * h->El, st>>>(
+        a, rcnt, counts, offsets, cursor, mtiles, nmt, (int)w.max_mt, tile_rows);
     SB_CUDA_TRY(cudaGetLastError());
   }
   {
@@ -889,7 +863,8 @@ extern "C" int sb_ep_forward(sb_ep* h, const void* x, int x_dtype, int64_t batch
   }
   int rc;
   GroupedSwiGLU g{xp, hp, yp, w.Rp, w.ldx, w.ldh, h->H, h->I, h->El, mtiles, nmt, row_w,
-                  gate, up, down, gate_scale, up_scale, down_scale, 1, engine};
+                  gate, up, down, gate_scale, up_scale, down_scale, 1, engine, 0,
+                  poll_waits(batch * h->k)};
   if ((rc = grouped_swiglu(g, st))) return rc;
   {
     ProfScope prof("ep_return", st);
@@ -899,6 +874,11 @@ extern "C" int sb_ep_forward(sb_ep* h, const void* x, int x_dtype, int64_t batch
       ep_return_kernel<8><<<(unsigned)blocks, EP_THREADS, 0, st>>>(a, rcnt, inv, yp);
     else
       ep_return_kernel<16><<<(unsigned)blocks, EP_THREADS, 0, st>>>(a, rcnt, inv, yp);
+    SB_CUDA_TRY(cudaGetLastError());
+  }
+  {
+    ProfScope prof("ep_wait_return", st);
+    ep_wait_kernel<<<1, 32, 0, st>>>(a, h->L.rflag, 2u);
     SB_CUDA_TRY(cudaGetLastError());
   }
   {

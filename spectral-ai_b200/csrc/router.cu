@@ -313,7 +313,28 @@ struct TreeDev {
   int S;
   const float* refb;     // [total]
   const void* refw;      // [total,S], bf16 (FAST) or fp32 (EXACT)
+  int stage;             // 1: the kernel copies centers and portals into shared memory first
 };
+
+// Trees up to this many nodes are staged in shared memory by the descent
+// kernels (centers and portals, 60 bytes a node): one round of loads at the
+// block's start instead of dependent global loads level after level, which is
+// what a small batch waits on.
+constexpr int STAGE_MAX_NODES = 512;
+
+// Copies the tree's centers [total*3] and portals [total*12] into `sm` (when
+// t.stage) and returns the pointers the descent reads them from.
+__device__ __forceinline__ void stage_tree(const TreeDev& t, float* sm, const float*& cen, const float*& por) {
+  cen = t.centers;
+  por = t.portals;
+  if (!t.stage) return;
+  const int nc = t.total_nodes * 3, np = t.total_nodes * 12;
+  for (int i = threadIdx.x; i < nc; i += blockDim.x) sm[i] = __ldg(t.centers + i);
+  for (int i = threadIdx.x; i < np; i += blockDim.x) sm[nc + i] = __ldg(t.portals + i);
+  __syncthreads();
+  cen = sm;
+  por = sm + nc;
+}
 
 struct DescentOut {
   int32_t* topk_ids;
@@ -402,6 +423,10 @@ __global__ void __launch_bounds__(HARD_WARPS * 32) descent_hard_kernel(const flo
                                                                        const TS* __restrict__ spec,
                                                                        int64_t B, TreeDev t, DescentOut o) {
   constexpr int TPW = 32 / G;  // tokens per warp
+  extern __shared__ float hsm[];
+  const float* cen_all;
+  const float* por_all;
+  stage_tree(t, hsm, cen_all, por_all);
   const float m_out = logf(0.0f + 1e-10f);
   const TS* __restrict__ wr = static_cast<const TS*>(t.refw);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -422,15 +447,15 @@ __global__ void __launch_bounds__(HARD_WARPS * 32) descent_hard_kernel(const flo
       const int Nl = t.nodes[l], off = t.offset[l], nb = t.branching[l];
       const float m_in = logf(pc + 1e-10f);
       const int lo = l > 0 ? prev * nb : 0, hi = l > 0 ? lo + nb : Nl;
-      const float* cen = t.centers + (size_t)off * 3;
+      const float* cen = cen_all + (size_t)off * 3;
       float best = -INFINITY;
       int bi = 0x7fffffff;
       // a warp-uniform trip count (groups have the same nb; level 0 is whole)
       for (int j0 = 0; j0 < hi - lo; j0 += G) {
         const int j = lo + j0 + sub;
         if (j < hi) {
-          const float dx = cx - __ldg(cen + 3 * j), dy = cy - __ldg(cen + 3 * j + 1),
-                      dz = cz - __ldg(cen + 3 * j + 2);
+          const float dx = cx - cen[3 * j], dy = cy - cen[3 * j + 1],
+                      dz = cz - cen[3 * j + 2];
           const float d2 = (dx * dx + dy * dy) + dz * dz;
           float lg = -d2 / t.denom;
           if (l > 0) lg = lg + m_in;
@@ -454,8 +479,8 @@ __global__ void __launch_bounds__(HARD_WARPS * 32) descent_hard_kernel(const flo
           for (int j0 = 0; j0 < Nl; j0 += G) {
             const int j = j0 + sub;
             if (j < Nl) {
-              const float dx = cx - __ldg(cen + 3 * j), dy = cy - __ldg(cen + 3 * j + 1),
-                          dz = cz - __ldg(cen + 3 * j + 2);
+              const float dx = cx - cen[3 * j], dy = cy - cen[3 * j + 1],
+                          dz = cz - cen[3 * j + 2];
               const float d2 = (dx * dx + dy * dy) + dz * dz;
               const float lg = -d2 / t.denom + ((j >= lo && j < hi) ? m_in : m_out);
               if (lg > best) {
@@ -474,10 +499,10 @@ __global__ void __launch_bounds__(HARD_WARPS * 32) descent_hard_kernel(const flo
       pc = nv / (nv + 1e-8f);
       if (o.route_path && valid && sub == 0) o.route_path[tok * t.L + l] = choice;
       if (l < t.L - 1) {
-        const float* a = t.portals + (size_t)node * 12;
-        const float lx = fmaf(__ldg(a + 0), cx, fmaf(__ldg(a + 1), cy, fmaf(__ldg(a + 2), cz, __ldg(a + 3))));
-        const float ly = fmaf(__ldg(a + 4), cx, fmaf(__ldg(a + 5), cy, fmaf(__ldg(a + 6), cz, __ldg(a + 7))));
-        const float lz = fmaf(__ldg(a + 8), cx, fmaf(__ldg(a + 9), cy, fmaf(__ldg(a + 10), cz, __ldg(a + 11))));
+        const float* a = por_all + (size_t)node * 12;
+        const float lx = fmaf(a[0], cx, fmaf(a[1], cy, fmaf(a[2], cz, a[3])));
+        const float ly = fmaf(a[4], cx, fmaf(a[5], cy, fmaf(a[6], cz, a[7])));
+        const float lz = fmaf(a[8], cx, fmaf(a[9], cy, fmaf(a[10], cz, a[11])));
         cx = lx * pc;
         cy = ly * pc;
         cz = lz * pc;
@@ -527,6 +552,9 @@ __global__ void __launch_bounds__(SOFT_WARPS * 32)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* const pa0 = dsm + (size_t)warp * 2 * t.max_nodes;
   float* const pb0 = pa0 + t.max_nodes;
+  const float* cen_all;
+  const float* por_all;
+  stage_tree(t, dsm + (size_t)SOFT_WARPS * 2 * t.max_nodes, cen_all, por_all);
   for (int64_t tok = (int64_t)blockIdx.x * SOFT_WARPS + warp; tok < B; tok += (int64_t)gridDim.x * SOFT_WARPS) {
     const float4 p4 = reinterpret_cast<const float4*>(pos)[tok];
     float cx = p4.x, cy = p4.y, cz = p4.z;
@@ -535,11 +563,11 @@ __global__ void __launch_bounds__(SOFT_WARPS * 32)
     float* pb = pb0;
     for (int l = 0; l < t.L; ++l) {
       const int Nl = t.nodes[l], off = t.offset[l], nb = t.branching[l];
-      const float* cen = t.centers + (size_t)off * 3;
+      const float* cen = cen_all + (size_t)off * 3;
       float mx = -INFINITY;
       for (int j = lane; j < Nl; j += 32) {
-        const float dx = cx - __ldg(cen + 3 * j), dy = cy - __ldg(cen + 3 * j + 1),
-                    dz = cz - __ldg(cen + 3 * j + 2);
+        const float dx = cx - cen[3 * j], dy = cy - cen[3 * j + 1],
+                    dz = cz - cen[3 * j + 2];
         const float d2 = (dx * dx + dy * dy) + dz * dz;
         float lg = -d2 / t.denom;
         if (l > 0) lg = lg + logf(pa[j / nb] + 1e-10f);
@@ -576,14 +604,14 @@ __global__ void __launch_bounds__(SOFT_WARPS * 32)
       // route_path holds the level-global node index (bvh_router.py:322)
       if (o.route_path && lane == 0) o.route_path[tok * t.L + l] = bi;
       if (l < t.L - 1) {
-        const float* A = t.portals + (size_t)off * 12;
+        const float* A = por_all + (size_t)off * 12;
         float sx = 0.f, sy = 0.f, sz = 0.f;
         for (int j = lane; j < Nl; j += 32) {
           const float* a = A + (size_t)j * 12;
           const float pj = pb[j];
-          sx += pj * fmaf(__ldg(a + 0), cx, fmaf(__ldg(a + 1), cy, fmaf(__ldg(a + 2), cz, __ldg(a + 3))));
-          sy += pj * fmaf(__ldg(a + 4), cx, fmaf(__ldg(a + 5), cy, fmaf(__ldg(a + 6), cz, __ldg(a + 7))));
-          sz += pj * fmaf(__ldg(a + 8), cx, fmaf(__ldg(a + 9), cy, fmaf(__ldg(a + 10), cz, __ldg(a + 11))));
+          sx += pj * fmaf(a[0], cx, fmaf(a[1], cy, fmaf(a[2], cz, a[3])));
+          sy += pj * fmaf(a[4], cx, fmaf(a[5], cy, fmaf(a[6], cz, a[7])));
+          sz += pj * fmaf(a[8], cx, fmaf(a[9], cy, fmaf(a[10], cz, a[11])));
         }
         cx = warp_sum(sx);
         cy = warp_sum(sy);
@@ -678,6 +706,9 @@ struct sb_router {
   CUtensorMap tm_w1{}, tm_w2{}, tm_w3s{}, tm_wr{};
   // narrower boxes for small batches, where the wide tiles leave SMs idle
   CUtensorMap tm_w1_128{}, tm_w2_64{}, tm_wr_32{};
+  // 32-row boxes for batches of a few row blocks: the weights (W1 is 8 MB at
+  // hidden 2048) are then streamed by many SMs instead of a handful
+  CUtensorMap tm_w1_32{}, tm_w2_32{};
   // the position rows split over a CTA pair: 8 of the 16 rows per CTA; W2 in
   // 128-row boxes for the pair GEMM
   CUtensorMap tm_w3s_8{}, tm_w2_128{};
@@ -877,7 +908,11 @@ extern "C" int sb_router_upload(sb_router* h, const sb_router_weights* w) {
       (rc = make_tmap_2d(&h->tm_w3s_8, h->w3s_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 16, H, H,
                          GEMM_BK, 8, CU_TENSOR_MAP_SWIZZLE_128B)) ||
       (rc = make_tmap_2d(&h->tm_w2_128, h->w2_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, S, H, H,
-                         GEMM_BK, S < 128 ? S : 128, CU_TENSOR_MAP_SWIZZLE_128B))) {
+                         GEMM_BK, S < 128 ? S : 128, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&h->tm_w1_32, h->w1_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, H, H,
+                         GEMM_BK, 32, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (rc = make_tmap_2d(&h->tm_w2_32, h->w2_bf16, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, S, H, H,
+                         GEMM_BK, 32, CU_TENSOR_MAP_SWIZZLE_128B))) {
     free_router_buffers(h);
     return rc;
   }
@@ -1044,6 +1079,11 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
     else if (mblocks * ((H + 255) / 256 + 1) >= sms)
       rc = launch_gemm_tc<256, 4, EpiGeluBf16, true>("router_enc1_gelu_tc", ta, h->tm_w1, h->tm_w3s, M, H, H,
                                                       e1, stream);
+    else if (mblocks * ((H + 127) / 128 + 1) * 2 <= sms)
+      // 128-wide tiles would leave half the SMs idle: 32-wide tiles and a
+      // deeper ring, so the weight stream is spread over the GPU
+      rc = launch_gemm_tc<32, 8, EpiGeluBf16, true>("router_enc1_gelu_tc", ta, h->tm_w1_32, h->tm_w3s, M, H, H,
+                                                     e1, stream);
     else
       rc = launch_gemm_tc<128, 4, EpiGeluBf16, true>("router_enc1_gelu_tc", ta, h->tm_w1_128, h->tm_w3s, M, H,
                                                       H, e1, stream);
@@ -1054,6 +1094,9 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
       // tm_w1_128's twin for W2: a 128-row box per CTA of the pair
       if ((rc = launch_gemm_pair<EpiTanhBf16, false>("router_enc2_tanh_tc", tg, h->tm_w2_128, h->tm_w2_128, M, S, H,
                                                      e2, stream)))
+        return rc;
+    } else if (mblocks * ((S + 63) / 64) * 2 <= sms) {
+      if ((rc = launch_gemm_tc<32, 8>("router_enc2_tanh_tc", tg, h->tm_w2_32, h->tm_w2_32, M, S, H, e2, stream)))
         return rc;
     } else if (S > 64 && mblocks * ((S + 127) / 128) < sms) {
       if ((rc = launch_gemm_tc<64, 4>("router_enc2_tanh_tc", tg, h->tm_w2_64, h->tm_w2_64, M, S, H, e2, stream)))
@@ -1138,6 +1181,8 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
   t.S = S;
   t.refb = h->refb;
   t.refw = precision == SB_PREC_FAST ? static_cast<const void*>(h->wr_bf16) : static_cast<const void*>(h->refw);
+  t.stage = h->total_nodes <= STAGE_MAX_NODES ? 1 : 0;
+  const size_t stage_bytes = t.stage ? (size_t)h->total_nodes * 15 * sizeof(float) : 0;
   DescentOut o{out->topk_ids, out->topk_weights, out->expert_id, out->expert_probs,
                out->route_path, out->confidence, top_k};
   ProfScope prof("router_descent", stream);
@@ -1152,15 +1197,15 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
     const dim3 grid((unsigned)blocks), block(HARD_WARPS * 32);
     if (precision == SB_PREC_FAST) {
       const __nv_bfloat16* sp = static_cast<const __nv_bfloat16*>(spec);
-      if (wide) descent_hard_kernel<__nv_bfloat16, 32><<<grid, block, 0, stream>>>(pos, sp, batch, t, o);
-      else descent_hard_kernel<__nv_bfloat16, 8><<<grid, block, 0, stream>>>(pos, sp, batch, t, o);
+      if (wide) descent_hard_kernel<__nv_bfloat16, 32><<<grid, block, stage_bytes, stream>>>(pos, sp, batch, t, o);
+      else descent_hard_kernel<__nv_bfloat16, 8><<<grid, block, stage_bytes, stream>>>(pos, sp, batch, t, o);
     } else {
       const float* sp = static_cast<const float*>(spec);
-      if (wide) descent_hard_kernel<float, 32><<<grid, block, 0, stream>>>(pos, sp, batch, t, o);
-      else descent_hard_kernel<float, 8><<<grid, block, 0, stream>>>(pos, sp, batch, t, o);
+      if (wide) descent_hard_kernel<float, 32><<<grid, block, stage_bytes, stream>>>(pos, sp, batch, t, o);
+      else descent_hard_kernel<float, 8><<<grid, block, stage_bytes, stream>>>(pos, sp, batch, t, o);
     }
   } else {
-    if (dsm_soft > 48 * 1024) {
+    if (dsm_soft + stage_bytes > 48 * 1024) {
       // the opt-in limit is per device: set it once on each
       static PerDevice attr;
       int dev = 0, arc;
@@ -1175,7 +1220,8 @@ extern "C" int sb_router_forward(sb_router* h, const void* x, int x_dtype, int64
     int64_t blocks = (batch + SOFT_WARPS - 1) / SOFT_WARPS;
     const int64_t cap = (int64_t)num_sms() * 8;
     if (blocks > cap) blocks = cap;
-    descent_soft_kernel<<<(unsigned)blocks, SOFT_WARPS * 32, dsm_soft, stream>>>(pos, nbuf, batch, t, o);
+    descent_soft_kernel<<<(unsigned)blocks, SOFT_WARPS * 32, dsm_soft + stage_bytes, stream>>>(pos, nbuf, batch, t,
+                                                                                              o);
   }
   SB_CUDA_TRY(cudaGetLastError());
   return SB_OK;

@@ -21,6 +21,7 @@
 #include "ternary_ts.cuh"
 #include "ternary_pair.cuh"
 #include "tree_sum.cuh"
+#include "ternary_gemv.cuh"
 
 #include <cstdlib>
 #include <cstring>
@@ -441,6 +442,13 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int* __res
             v[r][w] = make_float4(0.f, 0.f, 0.f, 0.f);
         }
       tree_apply<KC, CW>(v, wt.sched);
+      // a non-finite output (non-finite input, or an fp16 hidden value past
+      // 65504 on the bf16 path) is reported through the status word
+      bool bad = false;
+#pragma unroll
+      for (int w = 0; w < CW; ++w)
+        bad |= !(isfinite(v[0][w].x) && isfinite(v[0][w].y) && isfinite(v[0][w].z) && isfinite(v[0][w].w));
+      if (__any_sync(0xffffffffu, bad) && lane == 0) set_status(ST_RANGE);
 #pragma unroll
       for (int w = 0; w < CW; ++w) {
         const int c = c0 + 32 * w;
@@ -687,7 +695,23 @@ struct GroupedSwiGLU {
   // xp are [x_hi | x_lo] (bf16, 2H wide), h is stored as [h_hi | h_lo] (bf16,
   // 2I wide), and both GEMMs run over the doubled K with the weights read twice
   int split = 0;
+  // 1: the tile kernels' waits poll instead of suspending (small batches)
+  int poll = 0;
 };
+
+// Polling waits for batches of at most this many (token, expert) pairs: the
+// tiles are then few and latency-bound, each stage is waited on, and a
+// suspended wait's wake-up is the time that counts; at larger batches the
+// polls would take issue slots from the working warps.  SB_TERNARY_POLL=0/1
+// forces either.
+constexpr int64_t POLL_MAX_PAIRS = 4096;
+int poll_waits(int64_t pairs) {
+  static const int force = [] {
+    const char* e = getenv("SB_TERNARY_POLL");
+    return e ? (e[0] == '1' ? 1 : 0) : -1;
+  }();
+  return force >= 0 ? force : (pairs <= POLL_MAX_PAIRS ? 1 : 0);
+}
 
 int grouped_swiglu(const GroupedSwiGLU& g, cudaStream_t stream) {
   int rc;
@@ -735,6 +759,7 @@ int grouped_swiglu(const GroupedSwiGLU& g, cudaStream_t stream) {
   pg.N = (int)I;
   pg.K = (int)xk;
   pg.b_rows = (int)I;
+  pg.poll = g.poll;
   if (g.split) {
     pg.kb_wrap = (int)(H / TP_KB);
     pg.h_lo_col = (int)I;
@@ -760,6 +785,7 @@ int grouped_swiglu(const GroupedSwiGLU& g, cudaStream_t stream) {
   pd.N = (int)H;
   pd.K = (int)hk;
   pd.b_rows = (int)H;
+  pd.poll = g.poll;
   if (g.split) pd.kb_wrap = (int)(I / TP_KB);
   pd.s0 = ds;
   pd.row_w = row_w;
@@ -846,7 +872,7 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   }
 
   GroupedSwiGLU g{xp, hp, yp, L.Rp, L.ldx, L.ldh, H, I, E, mtiles, nmt, row_w,
-                  gate, up, down, gs, us, ds, fmt_gu, engine, split ? 1 : 0};
+                  gate, up, down, gs, us, ds, fmt_gu, engine, split ? 1 : 0, poll_waits(B * k)};
   if ((rc = grouped_swiglu(g, stream))) return rc;
   return moe_combine(yp, inv, ids, B, k, H, out, out_dtype, stream);
 }
@@ -872,6 +898,51 @@ extern "C" int sb_ternary_moe_swiglu(const void* x, int x_dtype, int64_t B, int6
                          reinterpret_cast<cudaStream_t>(stream));
 }
 
+namespace sb {
+// The few-token path fits: K multiples of 64 up to GEMV_MAX_K.
+inline bool gemv_fits(int64_t H, int64_t I) {
+  return H % 64 == 0 && I % 64 == 0 && H <= GEMV_MAX_K && I <= GEMV_MAX_K;
+}
+
+int launch_gemv(const void* x, int x_dtype, int M, int H, int I, const uint32_t* gate, const uint32_t* up,
+                const uint32_t* down, const float* gs, const float* us, const float* ds, float* h, float* y,
+                cudaStream_t stream) {
+  static PerDevice attr;
+  int dev = 0, rc;
+  SB_CUDA_TRY(cudaGetDevice(&dev));
+  if ((rc = attr.once(dev, []() -> int {
+         const int cap = GEMV_ROWS * GEMV_MAX_K * (int)sizeof(float);
+         SB_CUDA_TRY(cudaFuncSetAttribute(ternary_gemv_gateup_kernel<float>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, cap));
+         SB_CUDA_TRY(cudaFuncSetAttribute(ternary_gemv_gateup_kernel<__nv_bfloat16>,
+                                          cudaFuncAttributeMaxDynamicSharedMemorySize, cap));
+         SB_CUDA_TRY(cudaFuncSetAttribute(ternary_gemv_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          cap));
+         return SB_OK;
+       })))
+    return rc;
+  const int per = GEMV_THREADS / 32;
+  {
+    ProfScope prof("ternary_gateup_gemv", stream);
+    const size_t smem = (size_t)M * H * sizeof(float);
+    if (x_dtype == SB_F32)
+      ternary_gemv_gateup_kernel<float><<<(I + per - 1) / per, GEMV_THREADS, smem, stream>>>(
+          static_cast<const float*>(x), M, gate, up, gs, us, H, I, h);
+    else
+      ternary_gemv_gateup_kernel<__nv_bfloat16><<<(I + per - 1) / per, GEMV_THREADS, smem, stream>>>(
+          static_cast<const __nv_bfloat16*>(x), M, gate, up, gs, us, H, I, h);
+    SB_CUDA_TRY(cudaGetLastError());
+  }
+  {
+    ProfScope prof("ternary_down_gemv", stream);
+    const size_t smem = (size_t)M * I * sizeof(float);
+    ternary_gemv_down_kernel<<<(H + per - 1) / per, GEMV_THREADS, smem, stream>>>(h, M, down, ds, H, I, y);
+    SB_CUDA_TRY(cudaGetLastError());
+  }
+  return SB_OK;
+}
+}  // namespace sb
+
 // Single expert = the grouped path with one expert and one slot per token;
 // the slot ids live at the end of the workspace.
 extern "C" size_t sb_ternary_gated_mlp_workspace_bytes(int64_t M, int64_t H, int64_t I) {
@@ -894,6 +965,14 @@ extern "C" int sb_ternary_gated_mlp(const void* x, int x_dtype, int64_t M, int64
   const size_t base = moe_layout(M, H, I, 1, 1, split_form_fits(H, I, ENGINE_PAIR)).total;
   int32_t* ids = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + base);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  if (M <= GEMV_ROWS && gemv_fits(H, I) && (reinterpret_cast<uintptr_t>(x) & 3u) == 0) {
+    // a handful of tokens: the weight stream over all SMs (ternary_gemv.cuh),
+    // the hidden state in fp32 in the workspace
+    SB_REQUIRE(gate && up && down && gate_scale && up_scale && down_scale && x && y, "null pointer argument");
+    float* h = reinterpret_cast<float*>(workspace);
+    return launch_gemv(x, x_dtype, (int)M, (int)H, (int)I, gate, up, down, gate_scale, up_scale, down_scale, h, y,
+                       st);
+  }
   int64_t blocks = (M + 255) / 256;
   if (blocks > 4096) blocks = 4096;
   fill_i32_kernel<<<(unsigned)blocks, 256, 0, st>>>(ids, M, 0);

@@ -209,22 +209,65 @@ class AllToAllMoE:
 
 class EPMoELayer:
     """The MoE layer with its experts sharded: the router's top-k on this rank's
-    tokens, then ``ExpertParallelMoE``.  Same call as ``sb200.moe.BVHMoELayer``
-    (``layer(x, out=...)``), so it can be replayed from a CUDA graph
-    (``sb200.moe.GraphedLayer``: the exchange's flags carry an epoch kept in
-    device memory, and no host work sits between the kernels)."""
+    tokens, then the expert-parallel exchange.  Same call as
+    ``sb200.moe.BVHMoELayer`` (``layer(x, out=...)``), so it can be replayed
+    from a CUDA graph (``sb200.moe.GraphedLayer``: the exchange's flags carry an
+    epoch kept in device memory, and no host work sits between the kernels).
 
-    def __init__(self, router, ep: ExpertParallelMoE, top_k: int = 8, select: str = "soft"):
+    ``chunks`` > 1 splits each batch into that many consecutive token ranges,
+    each with its own exchange handle and stream, so one range's transfers over
+    NVLink run while another range's grouped GEMMs hold the tensor cores (the
+    exchange kernels fit on the SMs beside a GEMM's persistent CTA)."""
+
+    def __init__(self, router, local_experts, n_experts: int, top_k: int, max_tokens: int,
+                 select: str = "soft", chunks: int = 1, group: Optional[dist.ProcessGroup] = None,
+                 timeout_ms: int = 2000, workspace: Optional[torch.Tensor] = None):
+        """``workspace``: a buffer shared with layers that run one after
+        another on the same stream (``chunks`` == 1 only)."""
         self.router = router
-        self.ep = ep
         self.top_k = int(top_k)
         self.select = select
+        self.chunks = max(1, int(chunks))
+        per = (int(max_tokens) + self.chunks - 1) // self.chunks
+        self.eps = [ExpertParallelMoE(local_experts, n_experts, top_k, per, group=group, timeout_ms=timeout_ms,
+                                      workspace=workspace if self.chunks == 1 else None)
+                    for _ in range(self.chunks)]
+        self.per = per
+        dev = local_experts.device
+        self.streams = [torch.cuda.Stream(dev) for _ in range(self.chunks)] if self.chunks > 1 else []
+
+    @property
+    def ep(self):
+        return self.eps[0]
 
     def route(self, x: torch.Tensor):
         return self.router.forward_topk(x, k=self.top_k, select=self.select)
 
     def forward(self, x: torch.Tensor, out_dtype=None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         ids, w = self.route(x)
-        return self.ep(x, ids, w, out_dtype=out_dtype or x.dtype, out=out)
+        B = x.shape[0]
+        if out is None:
+            out = torch.empty(B, x.shape[1], dtype=out_dtype or x.dtype, device=x.device)
+        if self.chunks == 1:
+            return self.eps[0](x, ids, w, out=out)
+        main = torch.cuda.current_stream(x.device)
+        for c, (ep, s) in enumerate(zip(self.eps, self.streams)):
+            lo, hi = min(c * self.per, B), min((c + 1) * self.per, B)
+            s.wait_stream(main)
+            with torch.cuda.stream(s):
+                ep(x[lo:hi], ids[lo:hi], w[lo:hi], out=out[lo:hi])
+            for t in (x, ids, w, out):
+                t.record_stream(s)
+        for s in self.streams:
+            main.wait_stream(s)
+        return out
 
     __call__ = forward
+
+    def status(self) -> None:
+        for ep in self.eps:
+            ep.status()
+
+    def close(self) -> None:
+        for ep in self.eps:
+            ep.close()

@@ -6,7 +6,8 @@
 * A wait that runs out: a bounded wait on a flag no rank writes is reported by
   sb_ep_status and the device status word, and the GPU keeps working.
 * Two GPUs (skipped on a 1-GPU box): every rank's output equals the single-GPU
-  layer over all experts bit for bit, over several forwards and with both
+  layer over all experts (run on both ranks' tokens at once, so that every
+  expert sees the same rows) bit for bit, over several forwards and with both
   set-up paths (handles exchanged by torch.distributed, or by the library over
   an NCCL communicator); then a rank that skips a forward makes the other's
   next forward report the timeout instead of hanging.
@@ -58,6 +59,41 @@ def test_single_rank_equals_single_gpu_layer(cuda_device, E, H, I, k):
         ep.status()
     finally:
         ep.close()
+
+
+@pytest.mark.parametrize("chunks", [1, 3])
+def test_sharded_layer_equals_single_gpu_layer(cuda_device, chunks):
+    """The whole layer (router top-k, then the exchange) against BVHMoELayer,
+    with the batch split into token ranges on their own streams, eagerly and
+    replayed from a CUDA graph."""
+    import numpy as np
+    from bvh_router import BVHRouter, RouterConfig
+    from sb200 import synth
+    from sb200.ep import EPMoELayer
+    from sb200.moe import BVHMoELayer, GraphedLayer
+    from sb200.ternary import TernaryExperts
+    H, S, E, I, k, B = 2048, 256, 64, 1024, 8, 1000
+    w = synth.router_weights(H, S, (4, 4, 4), seed=0)
+    r = BVHRouter(RouterConfig(embed_dim=H, spectral_dim=S))
+    r.load_state_dict({kk: torch.from_numpy(np.array(v)) for kk, v in w.items()})
+    r = r.to(cuda_device).eval()
+    experts = synth.ternary_experts(E, H, I, seed=2)
+    one = BVHMoELayer(r, TernaryExperts(experts, cuda_device), top_k=k)
+    sharded = EPMoELayer(r, TernaryExperts(experts, cuda_device), E, k, B, chunks=chunks)
+    try:
+        x = synth.hidden_states(B, H, seed=5, dtype=torch.bfloat16, device=cuda_device)
+        y1 = one(x)
+        y2 = sharded(x)
+        out = torch.empty_like(y1)
+        g = GraphedLayer(sharded)
+        g(x, out)
+        g(x, out)
+        torch.cuda.synchronize()
+        assert torch.equal(y1, y2)
+        assert torch.equal(y1, out)
+        sharded.status()
+    finally:
+        sharded.close()
 
 
 def test_stale_wait_is_reported_and_the_gpu_keeps_working(cuda_device):
@@ -157,15 +193,24 @@ def _worker(rank, world, port, q, use_nccl):
             comm = cp.value
         ep = ExpertParallelMoE(TernaryExperts(experts[rank * el:(rank + 1) * el], dev), E, k, 4096,
                                timeout_ms=1000, nccl_comm=comm)
-        for step, B in enumerate([700 + 37 * rank, 4096, 0 if rank == 1 else 5, 2000]):
-            x = synth.hidden_states(B, H, seed=70 + 10 * step + rank, dtype=torch.bfloat16, device=dev)
-            ids_np, w_np = synth.zipf_routing(B, E, k, seed=80 + 10 * step + rank)
-            ids, w = torch.from_numpy(ids_np).to(dev), torch.from_numpy(w_np).to(dev)
-            y_ep = ep(x, ids, w, out_dtype=torch.float32)
-            y_one = full.forward(x, ids, w, out_dtype=torch.float32)
+        sizes = [[700, 737], [4096, 4096], [5, 0], [2000, 2000]]
+        for step, Bs in enumerate(sizes):
+            # every rank's tokens of this step (each rank routes its own); the
+            # single-GPU layer runs them all at once, so every expert sees the
+            # same rows in both layers
+            xs, idss, ws = [], [], []
+            for r in range(world):
+                xs.append(synth.hidden_states(Bs[r], H, seed=70 + 10 * step + r, dtype=torch.bfloat16, device=dev))
+                ids_np, w_np = synth.zipf_routing(Bs[r], E, k, seed=80 + 10 * step + r)
+                idss.append(torch.from_numpy(ids_np).to(dev))
+                ws.append(torch.from_numpy(w_np).to(dev))
+            y_ep = ep(xs[rank], idss[rank], ws[rank], out_dtype=torch.float32)
+            y_all = full.forward(torch.cat(xs), torch.cat(idss), torch.cat(ws), out_dtype=torch.float32)
+            lo = sum(Bs[:rank])
+            y_one = y_all[lo:lo + Bs[rank]]
             torch.cuda.synchronize()
             results.append((step, bool(torch.equal(y_ep, y_one)),
-                            float((y_ep - y_one).abs().max()) if B else 0.0))
+                            float((y_ep - y_one).abs().max()) if Bs[rank] else 0.0))
         ep.status()
         # a rank that skips a forward: the other's waits run out and it says so
         dist.barrier()
