@@ -863,8 +863,7 @@ extern "C" int sb_ep_forward(sb_ep* h, const void* x, int x_dtype, int64_t batch
   }
   int rc;
   GroupedSwiGLU g{xp, hp, yp, w.Rp, w.ldx, w.ldh, h->H, h->I, h->El, mtiles, nmt, row_w,
-                  gate, up, down, gate_scale, up_scale, down_scale, 1, engine, 0,
-                  poll_waits(batch * h->k)};
+                  gate, up, down, gate_scale, up_scale, down_scale, 1, engine};
   if ((rc = grouped_swiglu(g, st))) return rc;
   {
     ProfScope prof("ep_return", st);

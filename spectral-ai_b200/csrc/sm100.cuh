@@ -119,22 +119,6 @@ __device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar_addr, uint32_t 
 }
 constexpr uint32_t SB_WAIT_SLEEP_NS = 1000000;  // one suspension: at most 1 ms
 
-// Bounded wait by polling with test_wait (never suspends): for pipelines that
-// wait on every stage (small tiles), where the wake-up of a suspended
-// try_wait is the latency that counts.
-__device__ __forceinline__ bool mbar_wait_poll(uint64_t* bar, uint32_t parity, unsigned int code) {
-  const uint32_t a = smem_u32(bar);
-  if (mbar_test_wait(a, parity)) return true;
-  const uint64_t t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_test_wait(a, parity)) return true;
-    if ((i & 255u) == 0 && globaltimer() - t0 > SB_WAIT_LIMIT_NS) {
-      set_status(code);
-      return false;
-    }
-  }
-}
-
 // Bounded wait for the phase with the given parity to complete.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, unsigned int code) {
   const uint32_t a = smem_u32(bar);

@@ -695,23 +695,7 @@ struct GroupedSwiGLU {
   // xp are [x_hi | x_lo] (bf16, 2H wide), h is stored as [h_hi | h_lo] (bf16,
   // 2I wide), and both GEMMs run over the doubled K with the weights read twice
   int split = 0;
-  // 1: the tile kernels' waits poll instead of suspending (small batches)
-  int poll = 0;
 };
-
-// Polling waits for batches of at most this many (token, expert) pairs: the
-// tiles are then few and latency-bound, each stage is waited on, and a
-// suspended wait's wake-up is the time that counts; at larger batches the
-// polls would take issue slots from the working warps.  SB_TERNARY_POLL=0/1
-// forces either.
-constexpr int64_t POLL_MAX_PAIRS = 4096;
-int poll_waits(int64_t pairs) {
-  static const int force = [] {
-    const char* e = getenv("SB_TERNARY_POLL");
-    return e ? (e[0] == '1' ? 1 : 0) : -1;
-  }();
-  return force >= 0 ? force : (pairs <= POLL_MAX_PAIRS ? 1 : 0);
-}
 
 int grouped_swiglu(const GroupedSwiGLU& g, cudaStream_t stream) {
   int rc;
@@ -759,7 +743,6 @@ int grouped_swiglu(const GroupedSwiGLU& g, cudaStream_t stream) {
   pg.N = (int)I;
   pg.K = (int)xk;
   pg.b_rows = (int)I;
-  pg.poll = g.poll;
   if (g.split) {
     pg.kb_wrap = (int)(H / TP_KB);
     pg.h_lo_col = (int)I;
@@ -785,7 +768,6 @@ int grouped_swiglu(const GroupedSwiGLU& g, cudaStream_t stream) {
   pd.N = (int)H;
   pd.K = (int)hk;
   pd.b_rows = (int)H;
-  pd.poll = g.poll;
   if (g.split) pd.kb_wrap = (int)(I / TP_KB);
   pd.s0 = ds;
   pd.row_w = row_w;
@@ -872,7 +854,7 @@ int moe_forward(const void* x, int x_dtype, int64_t B, int64_t H, int64_t I, int
   }
 
   GroupedSwiGLU g{xp, hp, yp, L.Rp, L.ldx, L.ldh, H, I, E, mtiles, nmt, row_w,
-                  gate, up, down, gs, us, ds, fmt_gu, engine, split ? 1 : 0, poll_waits(B * k)};
+                  gate, up, down, gs, us, ds, fmt_gu, engine, split ? 1 : 0};
   if ((rc = grouped_swiglu(g, stream))) return rc;
   return moe_combine(yp, inv, ids, B, k, H, out, out_dtype, stream);
 }
@@ -899,47 +881,44 @@ extern "C" int sb_ternary_moe_swiglu(const void* x, int x_dtype, int64_t B, int6
 }
 
 namespace sb {
-// The few-token path fits: K multiples of 64 up to GEMV_MAX_K.
+// The few-token path fits: K multiples of 64, at most GEMV_MAX_CHUNKS chunks.
 inline bool gemv_fits(int64_t H, int64_t I) {
-  return H % 64 == 0 && I % 64 == 0 && H <= GEMV_MAX_K && I <= GEMV_MAX_K;
+  return H % 64 == 0 && I % 64 == 0 && H <= GEMV_CHUNK * GEMV_MAX_CHUNKS && I <= GEMV_CHUNK * GEMV_MAX_CHUNKS;
+}
+
+template <int N>
+int launch_gemv_n(const void* x, int x_dtype, int M, int H, int I, const uint32_t* gate, const uint32_t* up,
+                  const uint32_t* down, const float* gs, const float* us, const float* ds, float* h, float* y,
+                  cudaStream_t stream) {
+  const int hch = (H + GEMV_CHUNK - 1) / GEMV_CHUNK, ich = (I + GEMV_CHUNK - 1) / GEMV_CHUNK;
+  const int cpb = GEMV_WARPS / (2 * hch) > 0 ? GEMV_WARPS / (2 * hch) : 1;  // channels per block
+  const int opb = GEMV_WARPS / ich > 0 ? GEMV_WARPS / ich : 1;              // output channels per block
+  {
+    ProfScope prof("ternary_gateup_gemv", stream);
+    const unsigned blocks = (unsigned)((I + cpb - 1) / cpb);
+    if (x_dtype == SB_F32)
+      ternary_gemv_gateup_kernel<N, float><<<blocks, GEMV_WARPS * 32, 0, stream>>>(
+          static_cast<const float*>(x), gate, up, gs, us, H, I, cpb, M, h);
+    else
+      ternary_gemv_gateup_kernel<N, __nv_bfloat16><<<blocks, GEMV_WARPS * 32, 0, stream>>>(
+          static_cast<const __nv_bfloat16*>(x), gate, up, gs, us, H, I, cpb, M, h);
+    SB_CUDA_TRY(cudaGetLastError());
+  }
+  {
+    ProfScope prof("ternary_down_gemv", stream);
+    const unsigned blocks = (unsigned)((H + opb - 1) / opb);
+    ternary_gemv_down_kernel<N><<<blocks, GEMV_WARPS * 32, 0, stream>>>(h, down, ds, H, I, opb, M, y);
+    SB_CUDA_TRY(cudaGetLastError());
+  }
+  return SB_OK;
 }
 
 int launch_gemv(const void* x, int x_dtype, int M, int H, int I, const uint32_t* gate, const uint32_t* up,
                 const uint32_t* down, const float* gs, const float* us, const float* ds, float* h, float* y,
                 cudaStream_t stream) {
-  static PerDevice attr;
-  int dev = 0, rc;
-  SB_CUDA_TRY(cudaGetDevice(&dev));
-  if ((rc = attr.once(dev, []() -> int {
-         const int cap = GEMV_ROWS * GEMV_MAX_K * (int)sizeof(float);
-         SB_CUDA_TRY(cudaFuncSetAttribute(ternary_gemv_gateup_kernel<float>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, cap));
-         SB_CUDA_TRY(cudaFuncSetAttribute(ternary_gemv_gateup_kernel<__nv_bfloat16>,
-                                          cudaFuncAttributeMaxDynamicSharedMemorySize, cap));
-         SB_CUDA_TRY(cudaFuncSetAttribute(ternary_gemv_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          cap));
-         return SB_OK;
-       })))
-    return rc;
-  const int per = GEMV_THREADS / 32;
-  {
-    ProfScope prof("ternary_gateup_gemv", stream);
-    const size_t smem = (size_t)M * H * sizeof(float);
-    if (x_dtype == SB_F32)
-      ternary_gemv_gateup_kernel<float><<<(I + per - 1) / per, GEMV_THREADS, smem, stream>>>(
-          static_cast<const float*>(x), M, gate, up, gs, us, H, I, h);
-    else
-      ternary_gemv_gateup_kernel<__nv_bfloat16><<<(I + per - 1) / per, GEMV_THREADS, smem, stream>>>(
-          static_cast<const __nv_bfloat16*>(x), M, gate, up, gs, us, H, I, h);
-    SB_CUDA_TRY(cudaGetLastError());
-  }
-  {
-    ProfScope prof("ternary_down_gemv", stream);
-    const size_t smem = (size_t)M * I * sizeof(float);
-    ternary_gemv_down_kernel<<<(H + per - 1) / per, GEMV_THREADS, smem, stream>>>(h, M, down, ds, H, I, y);
-    SB_CUDA_TRY(cudaGetLastError());
-  }
-  return SB_OK;
+  if (M <= 1) return launch_gemv_n<1>(x, x_dtype, M, H, I, gate, up, down, gs, us, ds, h, y, stream);
+  if (M <= 2) return launch_gemv_n<2>(x, x_dtype, M, H, I, gate, up, down, gs, us, ds, h, y, stream);
+  return launch_gemv_n<4>(x, x_dtype, M, H, I, gate, up, down, gs, us, ds, h, y, stream);
 }
 }  // namespace sb
 
@@ -965,7 +944,7 @@ extern "C" int sb_ternary_gated_mlp(const void* x, int x_dtype, int64_t M, int64
   const size_t base = moe_layout(M, H, I, 1, 1, split_form_fits(H, I, ENGINE_PAIR)).total;
   int32_t* ids = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + base);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  if (M <= GEMV_ROWS && gemv_fits(H, I) && (reinterpret_cast<uintptr_t>(x) & 3u) == 0) {
+  if (M <= GEMV_ROWS && gemv_fits(H, I) && (reinterpret_cast<uintptr_t>(x) & 7u) == 0) {
     // a handful of tokens: the weight stream over all SMs (ternary_gemv.cuh),
     // the hidden state in fp32 in the workspace
     SB_REQUIRE(gate && up && down && gate_scale && up_scale && down_scale && x && y, "null pointer argument");

@@ -53,9 +53,6 @@ struct TernGemmParams {
   // GATEUP (pair engine): 0 = h stored as fp16; > 0 = h stored as two bf16
   // terms, hi = bf16(h) at column c and lo = bf16(h - hi) at c + h_lo_col.
   int h_lo_col;
-  // 1: every wait polls (test_wait) instead of suspending (pair engine; set
-  // for launches with few tiles per CTA pair, where each stage is waited on)
-  int poll;
 };
 
 constexpr int TG_THREADS = 384;
@@ -85,22 +82,6 @@ __device__ __forceinline__ uint32_t tern_pair(uint32_t w, int j) {
 }
 
 // Bounded wait by a whole warp (the lanes leave together); sleeps while waiting.
-__device__ __forceinline__ bool mbar_wait_warp_poll(uint64_t* bar, uint32_t parity, unsigned code) {
-  const uint32_t a = smem_u32(bar);
-  if (__all_sync(0xffffffffu, mbar_test_wait(a, parity))) return true;
-  const uint64_t t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (__all_sync(0xffffffffu, mbar_test_wait(a, parity))) return true;
-    if ((i & 255u) == 0) {
-      const bool late = globaltimer() - t0 > SB_WAIT_LIMIT_NS;
-      if (__any_sync(0xffffffffu, late)) {
-        if ((threadIdx.x & 31) == 0) set_status(code);
-        return false;
-      }
-    }
-  }
-}
-
 __device__ __forceinline__ bool mbar_wait_warp_t(uint64_t* bar, uint32_t parity, unsigned code) {
   const uint32_t a = smem_u32(bar);
   if (__all_sync(0xffffffffu, mbar_try_wait(a, parity))) return true;

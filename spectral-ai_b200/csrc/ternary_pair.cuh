@@ -174,9 +174,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
         const int xrow0 = mt.row0 + (int)rank * q;
         const int xrow1 = mt.row0 + (mt.pad >> 1) + (int)rank * q;
         for (int kb = 0; kb < kblocks; ++kb) {
-          if (!(p.poll ? mbar_wait_poll(&xp_empty[stage], phase ^ 1u, ST_TIMEOUT_PRODUCER)
-                      : mbar_wait(&xp_empty[stage], phase ^ 1u, ST_TIMEOUT_PRODUCER)))
-            goto done;
+          if (!mbar_wait(&xp_empty[stage], phase ^ 1u, ST_TIMEOUT_PRODUCER)) goto done;
           uint8_t* st = smem + stage * TP_STAGE_BYTES;
           mbar_arrive_expect_tx(&full_p[stage], TP_P_BYTES);
           const int wkb = (p.kb_wrap > 0 && kb >= p.kb_wrap) ? kb - p.kb_wrap : kb;  // weight K-block
@@ -222,17 +220,13 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
         const int buf = local & 1;
         const uint32_t d_tmem = tmem_base + (uint32_t)(buf * TP_D_COLS) + (uint32_t)(sid * n);
         const uint32_t b_off = (uint32_t)(sid * TP_QROWS * 128) >> 4;  // stream's rows in the slot
-        const uint32_t tph = ((uint32_t)(local >> 1) & 1u) ^ 1u;
-        if (!(p.poll ? mbar_wait_poll(&tempty[buf], tph, ST_TIMEOUT_MMA) : mbar_wait_cluster(&tempty[buf], tph, ST_TIMEOUT_MMA)))
-          goto done;
+        if (!mbar_wait_cluster(&tempty[buf], ((uint32_t)(local >> 1) & 1u) ^ 1u, ST_TIMEOUT_MMA)) goto done;
         tc_fence_after();
         bool ready = false;  // this K-block's full_a was seen complete by the previous peek
         for (int kb = 0; kb < kblocks; ++kb) {
           // one wait per K-block: full_a completes only after the rank-0 unpack
           // warps have also seen this slot's token halves land (full_x)
-          if (!ready && !(p.poll ? mbar_wait_poll(&full_a[astage], aphase, ST_TIMEOUT_MMA)
-                                  : mbar_wait_cluster(&full_a[astage], aphase, ST_TIMEOUT_MMA)))
-            goto done;
+          if (!ready && !mbar_wait_cluster(&full_a[astage], aphase, ST_TIMEOUT_MMA)) goto done;
           tc_fence_after();
           // peek at the next K-block's barrier now: the poll's latency overlaps
           // the MMA issue below, and the result is only used in the next pass
@@ -280,9 +274,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
         const int stage = it % TP_STAGES;
         const uint32_t phase = (uint32_t)(it / TP_STAGES) & 1u;
         const int astage = it % TP_A_STAGES;
-        if (!(p.poll ? mbar_wait_warp_poll(&full_p[stage], phase, ST_TIMEOUT_UNPACK)
-                    : mbar_wait_warp_t(&full_p[stage], phase, ST_TIMEOUT_UNPACK)))
-          goto done;
+        if (!mbar_wait_warp_t(&full_p[stage], phase, ST_TIMEOUT_UNPACK)) goto done;
         // expand the row's eight words (128 K) into registers first: only the
         // stores into TMEM have to wait for the A stage to drain
         const uint8_t* pw = smem + stage * TP_STAGE_BYTES + TP_X_BYTES + prow * 32;
@@ -307,9 +299,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
         // next use of the slot needs this very pass), so the parity is exact.
         if (it >= TP_A_STAGES) {
           const int pj = it - TP_A_STAGES;
-          const uint32_t eph = (uint32_t)(pj / TP_STAGES) & 1u;
-          if (!(p.poll ? mbar_wait_warp_poll(&xp_empty[pj % TP_STAGES], eph, ST_TIMEOUT_UNPACK)
-                      : mbar_wait_warp_t(&xp_empty[pj % TP_STAGES], eph, ST_TIMEOUT_UNPACK)))
+          if (!mbar_wait_warp_t(&xp_empty[pj % TP_STAGES], (uint32_t)(pj / TP_STAGES) & 1u, ST_TIMEOUT_UNPACK))
             goto done;
         }
         tc_fence_after();
@@ -320,9 +310,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
         tc_fence_before();
         // rank 0 also waits for both token halves of this slot, so that the MMA
         // issuer needs a single barrier per K-block
-        if (rank == 0 && !(p.poll ? mbar_wait_warp_poll(&full_x[stage], phase, ST_TIMEOUT_UNPACK)
-                                   : mbar_wait_warp_t(&full_x[stage], phase, ST_TIMEOUT_UNPACK)))
-          goto done;
+        if (rank == 0 && !mbar_wait_warp_t(&full_x[stage], phase, ST_TIMEOUT_UNPACK)) goto done;
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&full_a[astage]), 0));
       }
@@ -355,9 +343,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
       }
       const int xcol = (MODE == TG_GATEUP) ? c0 + 16 * q : c0 + 32 * q;  // box column
       const bool store = xcol < p.N;
-      if (!(p.poll ? mbar_wait_warp_poll(&tfull[buf], ph, ST_TIMEOUT_EPILOGUE)
-                    : mbar_wait_warp_t(&tfull[buf], ph, ST_TIMEOUT_EPILOGUE)))
-        goto done;
+      if (!mbar_wait_warp_t(&tfull[buf], ph, ST_TIMEOUT_EPILOGUE)) goto done;
       tc_fence_after();
       const uint32_t tbase = tlanes + (uint32_t)(buf * TP_D_COLS);
       // this warp's last chunk (or none): the accumulator is released after its load
