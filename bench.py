@@ -888,13 +888,20 @@ def roofline_tensor(meta, prof, pk, steps_ms, steps):
     dom = prof.get(meta["dominant"], (0, 0.0))
     if not dom[0]:
         return None
+    # dominant_flop is per step; a chunked layer launches the kernel several
+    # times a step, each on a share of the step's rows
+    flop_launch = meta["dominant_flop"] * steps / dom[0]
     avg_s = dom[1] / dom[0] / 1e3
-    achieved = meta["dominant_flop"] / avg_s / 1e12
-    return {"kernel": meta["dominant"], "bound": "tensor", "achieved": round(achieved, 1),
-            "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4),
-            "peak_source": f"{pk['source']} bf16 burst (cuBLAS)",
-            "traffic": traffic_for(meta), "avg_launch_ms": round(dom[1] / dom[0], 4),
-            "algorithmic_flop_per_launch": meta["dominant_flop"]}
+    achieved = flop_launch / avg_s / 1e12
+    out = {"kernel": meta["dominant"], "bound": "tensor", "achieved": round(achieved, 1),
+           "peak": pk["bf16_tflops"], "unit": "TFLOP/s", "frac": round(achieved / pk["bf16_tflops"], 4),
+           "peak_source": f"{pk['source']} bf16 burst (cuBLAS)",
+           "traffic": scale_traffic(traffic_for(meta), steps / dom[0]), "avg_launch_ms": round(dom[1] / dom[0], 4),
+           "launches_per_step": round(dom[0] / steps, 2), "algorithmic_flop_per_launch": flop_launch}
+    if dom[0] > steps:
+        out["note"] = ("launches of different token ranges run on their own streams and may overlap; "
+                       "each launch's events include the time it shared the GPU")
+    return out
 
 
 def run_ours(a):
@@ -1124,6 +1131,10 @@ TRAFFIC_PROFILES = {
     "router_enc1_gelu_tc": "router_enc1_gelu_tc.json",
     "ternary_gateup_tc": "ternary_pair_gateup_moe4096.json",
 }
+
+
+def scale_traffic(t, f):
+    return None if t is None else int(t * f)
 
 
 def traffic_for(meta):

@@ -38,10 +38,11 @@
 // cuda/async_pipeline.cu:79-133 when the experts are spread over GPUs.
 //
 // Ordering: a source's rows are plain stores into peer memory; each block
-// fences them (fence.sc.sys) before it counts itself done, and the last block
-// fences again before its st.release.sys of the flag; a waiting thread reads
-// the flag with ld.acquire.sys.  Flags carry the forward's epoch (a counter
-// in device memory, bumped by ep_send), so they never need resetting and the
+// orders them before its done count with a GPU-scope fence, and the last block,
+// having seen every count, fences at system scope before its st.release.sys of
+// the flag; a waiting thread reads the flag with ld.acquire.sys.  Flags carry
+// the forward's epoch (a counter in device memory, bumped by ep_send), so they
+// never need resetting and the
 // forward can be replayed from a CUDA graph.  Buffer reuse across forwards is
 // ordered by the protocol itself: a source writes forward t+1's rows only after
 // its combine of forward t saw every destination's return flag, which each
@@ -414,7 +415,8 @@ __global__ void __launch_bounds__(EP_THREADS) ep_return_kernel(EpArgs a, const i
     });
     float4* dst = reinterpret_cast<float4*>(ep_at(a, s, a.L.ret) + (((int64_t)a.rank * a.cap + i) * a.H) * 4);
     constexpr int CW = 2;
-    for (int c0 = lane; c0 < n4; c0 += 32 * CW) {
+    for (int cb = 0; cb < n4; cb += 32 * CW) {  // warp-uniform bound
+      const int c0 = cb + lane;
       float4 v[KC][CW];
 #pragma unroll
       for (int q = 0; q < KC; ++q)
@@ -469,7 +471,8 @@ __global__ void __launch_bounds__(EP_THREADS) ep_combine_kernel(EpArgs a, int64_
       return v;
     });
     constexpr int CW = 2;
-    for (int c0 = lane; c0 < n4; c0 += 32 * CW) {
+    for (int cb = 0; cb < n4; cb += 32 * CW) {  // warp-uniform bound: every lane reaches the vote
+      const int c0 = cb + lane;
       float4 v[EP_MAX_WORLD][CW];
 #pragma unroll
       for (int q = 0; q < EP_MAX_WORLD; ++q)

@@ -428,7 +428,10 @@ __global__ void moe_combine_kernel(const float* __restrict__ y, const int* __res
 #pragma unroll
     for (int r = 0; r < KC; ++r) row[r] = (int64_t)__shfl_sync(0xffffffffu, crow, r < n ? tree_order(wt, r) : 0);
     constexpr int CW = 2;  // column groups per pass of the schedule
-    for (int c0 = lane; c0 < ncol; c0 += 32 * CW) {
+    // the loop bound is warp-uniform (lanes past the row's end load zeros and
+    // store nothing), so every lane reaches the warp vote below
+    for (int cb = 0; cb < ncol; cb += 32 * CW) {
+      const int c0 = cb + lane;
       float4 v[KC][CW];
 #pragma unroll
       for (int r = 0; r < KC; ++r)

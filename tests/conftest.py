@@ -20,6 +20,19 @@ def pytest_configure(config):
     config.addinivalue_line("markers", "gpu: needs a CUDA device (B200); run with -m gpu")
 
 
+def pytest_collection_modifyitems(config, items):
+    """A GPU test that has not finished in 10 minutes ends the run (pytest-timeout's
+    thread method, which also ends a process blocked inside a CUDA call) instead of
+    holding the GPU until an outer limit."""
+    try:
+        import pytest_timeout  # noqa: F401
+    except ImportError:
+        return
+    for item in items:
+        if item.get_closest_marker("gpu") is not None and item.get_closest_marker("timeout") is None:
+            item.add_marker(pytest.mark.timeout(600, method="thread"))
+
+
 def load_golden(name: str) -> dict:
     with np.load(GOLDEN / f"{name}.npz", allow_pickle=False) as z:
         return {k: z[k] for k in z.files}

@@ -5,12 +5,12 @@
   for bit, for empty, one-token and full batches, several forwards in a row.
 * A wait that runs out: a bounded wait on a flag no rank writes is reported by
   sb_ep_status and the device status word, and the GPU keeps working.
-* Two GPUs (skipped on a 1-GPU box): every rank's output equals the single-GPU
-  layer over all experts (run on both ranks' tokens at once, so that every
-  expert sees the same rows) bit for bit, over several forwards and with both
-  set-up paths (handles exchanged by torch.distributed, or by the library over
-  an NCCL communicator); then a rank that skips a forward makes the other's
-  next forward report the timeout instead of hanging.
+* All GPUs of the box, 2, 4 or 8 (skipped on a 1-GPU box): every rank's output
+  equals the single-GPU layer over all experts (run on all ranks' tokens at
+  once, so that every expert sees the same rows) bit for bit, over several
+  forwards and with both set-up paths (handles exchanged by torch.distributed,
+  or by the library over an NCCL communicator); then rank 0 runs a forward the
+  others skip, and its waits report the timeout instead of hanging.
 """
 
 from __future__ import annotations
@@ -150,7 +150,7 @@ def test_bad_arguments_are_rejected_on_the_host(cuda_device):
 
 
 # ---------------------------------------------------------------------------
-# two GPUs
+# several GPUs
 # ---------------------------------------------------------------------------
 def _free_port():
     s = socket.socket()
@@ -193,7 +193,8 @@ def _worker(rank, world, port, q, use_nccl):
             comm = cp.value
         ep = ExpertParallelMoE(TernaryExperts(experts[rank * el:(rank + 1) * el], dev), E, k, 4096,
                                timeout_ms=1000, nccl_comm=comm)
-        sizes = [[700, 737], [4096, 4096], [5, 0], [2000, 2000]]
+        sizes = [[700 + 37 * r for r in range(world)], [4096] * world, [5] + [0] * (world - 1),
+                 [2000] * world]
         for step, Bs in enumerate(sizes):
             # every rank's tokens of this step (each rank routes its own); the
             # single-GPU layer runs them all at once, so every expert sees the
@@ -235,10 +236,12 @@ def _worker(rank, world, port, q, use_nccl):
 
 
 @pytest.mark.parametrize("use_nccl", [False, True])
-def test_two_gpus_bitwise_and_a_skipped_forward(use_nccl):
-    if torch.cuda.device_count() < 2:
+def test_all_gpus_bitwise_and_a_skipped_forward(use_nccl):
+    """On every GPU of the box (the largest power of two, at most 8)."""
+    n = torch.cuda.device_count()
+    if n < 2:
         pytest.skip("needs 2 GPUs")
-    world = 2
+    world = 8 if n >= 8 else 4 if n >= 4 else 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
