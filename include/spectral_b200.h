@@ -177,9 +177,10 @@ int sb_ternary_pack_ref(const int8_t* w, int64_t K, int64_t N, int32_t* packed);
 /* Bytes of one matrix in the device layout used by the B200 kernels: row-major
  * [N, ceil(K/64)*4] uint32 words, one word per 16 consecutive K of one output
  * row n.  Inside a word, element 2j+e (j=0..7, e=0,1) is the biased code
- * value+1 in {0,1,2} at bits 16e+2j..16e+2j+1 (padding: code 1), so that two
- * elements expand to two 16-bit floats with a shift, an and-or and one packed
- * subtraction. */
+ * value+1 in {0,1,2} at bits 16e+p..16e+p+1 with p = 0,2,4,8,10,12,6,14 for
+ * j = 0..7 (padding: code 1), so that two elements expand to two 16-bit floats
+ * with an and-or and one packed subtraction (plus a shift for the pairs that
+ * lie beyond the format's mantissa). */
 size_t sb_ternary_matrix_bytes(int64_t K, int64_t N);
 
 /* Converts a reference-layout packed matrix (device int32 [ceil(K/16), N]) into

@@ -9,13 +9,16 @@
 // Device layout: uint32 [N, KW] with KW = ceil(K/64)*4 words per output row
 // (row n holds K contiguous, padded to a multiple of 64 with zeros).  Word w of
 // row n covers K indices 16w .. 16w+15; element 16w+2j+e (e = 0,1; j = 0..7)
-// is stored as the biased code value+1 in {0,1,2} at bits 16e+2j .. 16e+2j+1
-// (padding holds code 1, value 0).  A pair (2j, 2j+1) becomes two packed
-// 16-bit floats with one shift, one and-or and one packed subtraction:
-//   ((w >> 2j) & 0x00030003) | B  is the pair  (b + code_2j, b + code_2j+1)
-// with B the 16-bit float b = 128 (bf16 0x4300) or b = 1024 (fp16 0x6400),
-// whose unit in the last place is 1; subtracting b + 1 leaves code - 1 =
-// value exactly.
+// is stored as the biased code value+1 in {0,1,2} at bits 16e+p_j .. 16e+p_j+1
+// with p_j = tern_pos(j) = 0, 2, 4, 8, 10, 12, 6, 14 (padding holds code 1,
+// value 0).  A pair (2j, 2j+1) becomes two packed 16-bit floats with one and-or
+// and one packed subtraction: with E the exponent that makes bit p the
+// mantissa's unit (bf16: p <= 4, fp16: p <= 8),
+//   (w & (0x00030003 << p)) | E  is the pair  (b + code_2j, b + code_2j+1)
+// for b = 2^(7-p) (bf16) or 2^(10-p) (fp16), and subtracting b + 1 leaves
+// code - 1 = value exactly.  Pairs past the mantissa are first shifted down
+// (by 8, shared by three pairs, or to bit 0): 19 instructions per word of 16
+// weights in bf16 and 17 in fp16, against 24 with a shift for every pair.
 #include "common.cuh"
 #include "ternary_gemm.cuh"
 #include "ternary_ts.cuh"
@@ -55,7 +58,7 @@ __global__ void ternary_repack_kernel(const uint32_t* __restrict__ ref, int64_t 
         if (k >= K) break;
         const int s = ternary_code_to_sign((codes >> (2 * t)) & 3u);
         const int e = t & 1, j = t >> 1;
-        const int sh = 16 * e + 2 * j;
+        const int sh = 16 * e + tern_pos(j);
         out = (out & ~(3u << sh)) | ((uint32_t)(s + 1) << sh);
       }
     }
@@ -916,6 +919,97 @@ int launch_gemv_n(const void* x, int x_dtype, int M, int H, int I, const uint32_
   return SB_OK;
 }
 
+// One expert over every row (the drop-in ternary_gated_mlp past the few-token
+// sizes): the m-tile table of rows [0, M) — tiles of up to tile_rows rows from
+// row 0, the last padded to 32 — and a routing weight of 1 for every padded row.
+// The rows need no dispatch copy and the single slot no combine: the GEMMs read
+// the rows where they are (TMA fills rows past M with zeros and clips the
+// stores there), and the down GEMM stores y itself.
+__global__ void single_plan_kernel(int64_t M, int tile_rows, int max_mt, MTile* __restrict__ mtiles,
+                                   int* __restrict__ nmt, float* __restrict__ row_w) {
+  const int64_t cp = (M + 31) & ~(int64_t)31;
+  const int64_t nt = (cp + tile_rows - 1) / tile_rows;
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+  if (i == 0) *nmt = (int)(nt < max_mt ? nt : max_mt);
+  for (int64_t t = i; t < nt && t < max_mt; t += stride) {
+    MTile m;
+    m.expert = 0;
+    m.row0 = (int)(t * tile_rows);
+    m.rows = (int)(M - m.row0 < tile_rows ? M - m.row0 : tile_rows);
+    m.pad = (int)(cp - m.row0 < tile_rows ? cp - m.row0 : tile_rows);
+    mtiles[t] = m;
+  }
+  for (int64_t r = i; r < cp; r += stride) row_w[r] = 1.0f;
+}
+
+// The fp32-faithful rows of the single-expert form: row r of x becomes
+// [bf16(x) | bf16(x - bf16(x))] in place r of xs (the arithmetic of
+// moe_scatter_split_kernel).  A warp per row; H % 4 == 0, 16-byte rows.
+__global__ void split_rows_kernel(const float* __restrict__ x, int64_t M, int H, __nv_bfloat16* __restrict__ xs,
+                                  int64_t ldx) {
+  const int lane = threadIdx.x & 31;
+  for (int64_t r = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; r < M;
+       r += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const float4* s4 = reinterpret_cast<const float4*>(x + r * (int64_t)H);
+    __nv_bfloat16* dst = xs + r * ldx;
+    for (int c = lane; c < H / 4; c += 32) {
+      const float4 v = __ldg(s4 + c);
+      const __nv_bfloat162 h0 = __floats2bfloat162_rn(v.x, v.y), h1 = __floats2bfloat162_rn(v.z, v.w);
+      const float2 f0 = __bfloat1622float2(h0), f1 = __bfloat1622float2(h1);
+      const __nv_bfloat162 l0 = __floats2bfloat162_rn(v.x - f0.x, v.y - f0.y);
+      const __nv_bfloat162 l1 = __floats2bfloat162_rn(v.z - f1.x, v.w - f1.y);
+      *reinterpret_cast<uint2*>(dst + 4 * c) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+      *reinterpret_cast<uint2*>(dst + H + 4 * c) =
+          make_uint2(*reinterpret_cast<const uint32_t*>(&l0), *reinterpret_cast<const uint32_t*>(&l1));
+    }
+  }
+}
+
+// The single-expert form applies: the pair engine (its stores are TMA stores,
+// clipped at row M), y and the rows 16-byte aligned with 16-byte row pitches;
+// bf16 rows are read in place, fp32 rows take the fp32-faithful form.
+bool single_form_fits(const void* x, int x_dtype, int64_t H, int64_t I, const float* y) {
+  const bool a16 = (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && (reinterpret_cast<uintptr_t>(y) & 15u) == 0;
+  if (ternary_engine() != ENGINE_PAIR || !a16 || (H % 4) != 0) return false;
+  if (x_dtype == SB_BF16) return (H % 8) == 0;
+  return x_dtype == SB_F32 && split_form_fits(H, I, ENGINE_PAIR);
+}
+
+int single_expert_forward(const void* x, int x_dtype, int64_t M, int64_t H, int64_t I, const uint32_t* gate,
+                          const uint32_t* up, const uint32_t* down, const float* gs, const float* us,
+                          const float* ds, float* y, void* workspace, cudaStream_t stream) {
+  const bool split = x_dtype == SB_F32;
+  const MoeLayout L = moe_layout(M, H, I, 1, 1, split);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int* nmt = reinterpret_cast<int*>(ws + L.off_nmt);
+  MTile* mtiles = reinterpret_cast<MTile*>(ws + L.off_mtiles);
+  float* row_w = reinterpret_cast<float*>(ws + L.off_roww);
+  const void* xp = x;
+  int64_t ldx = H;
+  {
+    ProfScope prof("moe_plan", stream);
+    int64_t blocks = ((M + 31) / 32 + 255) / 256 * 32;
+    if (blocks < 1) blocks = 1;
+    if (blocks > (int64_t)num_sms() * 4) blocks = (int64_t)num_sms() * 4;
+    single_plan_kernel<<<(unsigned)blocks, 256, 0, stream>>>(M, TP_TILE_ROWS, (int)L.max_mt, mtiles, nmt, row_w);
+    SB_CUDA_TRY(cudaGetLastError());
+  }
+  if (split) {
+    ProfScope prof("moe_dispatch", stream);
+    __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(ws + L.off_xp);
+    int64_t blocks = (M * 32 + 255) / 256;
+    if (blocks > (int64_t)num_sms() * 16) blocks = (int64_t)num_sms() * 16;
+    split_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(static_cast<const float*>(x), M, (int)H, xs, L.ldx);
+    SB_CUDA_TRY(cudaGetLastError());
+    xp = xs;
+    ldx = L.ldx;
+  }
+  GroupedSwiGLU g{xp, reinterpret_cast<__half*>(ws + L.off_hp), y, M, ldx, L.ldh, H, I, 1, mtiles, nmt, row_w,
+                  gate, up, down, gs, us, ds, 1, ENGINE_PAIR, split ? 1 : 0};
+  return grouped_swiglu(g, stream);
+}
+
 int launch_gemv(const void* x, int x_dtype, int M, int H, int I, const uint32_t* gate, const uint32_t* up,
                 const uint32_t* down, const float* gs, const float* us, const float* ds, float* h, float* y,
                 cudaStream_t stream) {
@@ -954,6 +1048,15 @@ extern "C" int sb_ternary_gated_mlp(const void* x, int x_dtype, int64_t M, int64
     float* h = reinterpret_cast<float*>(workspace);
     return launch_gemv(x, x_dtype, (int)M, (int)H, (int)I, gate, up, down, gate_scale, up_scale, down_scale, h, y,
                        st);
+  }
+  SB_REQUIRE(gate && up && down && gate_scale && up_scale && down_scale && x && y, "null pointer argument");
+  if (single_form_fits(x, x_dtype, H, I, y)) {
+    SB_REQUIRE((reinterpret_cast<uintptr_t>(workspace) & 1023u) == 0, "workspace must be 1024-byte aligned");
+    SB_REQUIRE((reinterpret_cast<uintptr_t>(gate) & 15u) == 0 && (reinterpret_cast<uintptr_t>(up) & 15u) == 0 &&
+                   (reinterpret_cast<uintptr_t>(down) & 15u) == 0,
+               "packed weights must be 16-byte aligned");
+    return single_expert_forward(x, x_dtype, M, H, I, gate, up, down, gate_scale, up_scale, down_scale, y,
+                                 workspace, st);
   }
   int64_t blocks = (M + 255) / 256;
   if (blocks > 4096) blocks = 4096;

@@ -70,15 +70,62 @@ static_assert(TG_STAGE_BYTES % 1024 == 0, "stage alignment");
 //   FMT 1: bf16, FMT 0: fp16.  The biased codes c in {0,1,2} are placed in the
 //   mantissa of b = 128 (bf16) / 1024 (fp16), whose last place is 1, and b + 1
 //   is subtracted: (b + c) - (b + 1) = c - 1, exact in both formats.
+// Bit position, in each 16-bit half of a layout word, of pair j (elements
+// 2j and 2j+1 of the word's 16 K; the second element sits 16 bits above the
+// first).  The order puts six pairs (bf16) or seven (fp16) where the format's
+// mantissa can take the code in place (below).
+__host__ __device__ constexpr int tern_pos(int j) { return j < 3 ? 2 * j : j < 6 ? 2 * j + 2 : j == 6 ? 6 : 14; }
+
+// The codes at bit P of each half as 16-bit floats: OR-ing in the exponent
+// that makes bit P the mantissa's unit turns code c into base + c exactly, and
+// one packed subtraction of base + 1 leaves c - 1, the weight.  P must leave
+// both code bits inside the mantissa: at most 4 for bf16 (7 mantissa bits),
+// 8 for fp16 (10 bits).  base is 2^(7-P) (bf16) or 2^(10-P) (fp16).
+template <int FMT, int P>
+__device__ __forceinline__ uint32_t tern_decode_at(uint32_t w) {
+  static_assert(P >= 0 && P <= (FMT ? 4 : 8), "both code bits must lie inside the mantissa");
+  constexpr uint32_t base = FMT ? ((134u - P) << 7) : ((25u - P) << 10);
+  constexpr uint32_t one = base + (1u << P);
+  const uint32_t t = (w & (0x00030003u << P)) | (base | (base << 16));
+  uint32_t r;
+  if constexpr (FMT)
+    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(t), "r"(one | (one << 16)));
+  else
+    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(t), "r"(one | (one << 16)));
+  return r;
+}
+
+// Pair J of word w (J known at compile time): in place where the mantissa
+// allows, else from w >> 8 (shared by the pairs that use it), else shifted down.
+template <int FMT, int J>
+__device__ __forceinline__ uint32_t tern_pair_c(uint32_t w) {
+  constexpr int P = tern_pos(J);
+  constexpr int LIM = FMT ? 4 : 8;
+  if constexpr (P <= LIM)
+    return tern_decode_at<FMT, P>(w);
+  else if constexpr (P >= 8 && P - 8 <= LIM)
+    return tern_decode_at<FMT, P - 8>(w >> 8);
+  else
+    return tern_decode_at<FMT, 0>(w >> P);
+}
+
+// The word's eight pairs: out[j] holds elements 2j, 2j+1 (K order).
+template <int FMT>
+__device__ __forceinline__ void tern_word(uint32_t w, uint32_t* out) {
+  out[0] = tern_pair_c<FMT, 0>(w);
+  out[1] = tern_pair_c<FMT, 1>(w);
+  out[2] = tern_pair_c<FMT, 2>(w);
+  out[3] = tern_pair_c<FMT, 3>(w);
+  out[4] = tern_pair_c<FMT, 4>(w);
+  out[5] = tern_pair_c<FMT, 5>(w);
+  out[6] = tern_pair_c<FMT, 6>(w);
+  out[7] = tern_pair_c<FMT, 7>(w);
+}
+
+// Pair j of word w for a j known only at run time (the few-token kernels).
 template <int FMT>
 __device__ __forceinline__ uint32_t tern_pair(uint32_t w, int j) {
-  const uint32_t t = ((w >> (2 * j)) & 0x00030003u) | (FMT ? 0x43004300u : 0x64006400u);
-  uint32_t r;
-  if (FMT)
-    asm("sub.rn.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(t), "r"(0x43014301u));
-  else
-    asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(t), "r"(0x64016401u));
-  return r;
+  return tern_decode_at<FMT, 0>(w >> ((0xE6CA8420u >> (4 * j)) & 15u));
 }
 
 // Bounded wait by a whole warp (the lanes leave together); sleeps while waiting.
@@ -224,14 +271,10 @@ __global__ void __launch_bounds__(TG_THREADS, 1)
           for (int q = 0; q < 4; ++q) {
             const uint32_t w = words[q];
             uint4 lo, hi;
-            lo.x = tern_pair<FMT>(w, 0);
-            lo.y = tern_pair<FMT>(w, 1);
-            lo.z = tern_pair<FMT>(w, 2);
-            lo.w = tern_pair<FMT>(w, 3);
-            hi.x = tern_pair<FMT>(w, 4);
-            hi.y = tern_pair<FMT>(w, 5);
-            hi.z = tern_pair<FMT>(w, 6);
-            hi.w = tern_pair<FMT>(w, 7);
+            uint32_t pr[8];
+            tern_word<FMT>(w, pr);
+            lo = make_uint4(pr[0], pr[1], pr[2], pr[3]);
+            hi = make_uint4(pr[4], pr[5], pr[6], pr[7]);
             *reinterpret_cast<uint4*>(bu + sw128_offset(r, 2 * q)) = lo;
             *reinterpret_cast<uint4*>(bu + sw128_offset(r, 2 * q + 1)) = hi;
           }

@@ -33,7 +33,7 @@ constexpr int GEMV_CHUNK = 512;   // K per task
 constexpr int GEMV_MAX_CHUNKS = 16;
 
 // The pair of weights (elements 2j, 2j+1 of word w) as two floats, from the
-// bf16 pair tern_pair<1> makes (exact +-1/0).
+// bf16 pair tern_pair<1> makes (exact +-1/0; j known at run time).
 __device__ __forceinline__ float2 tern_pair_f2(uint32_t w, int j) {
   const uint32_t p = tern_pair<1>(w, j);
   return make_float2(__uint_as_float(p << 16), __uint_as_float(p & 0xFFFF0000u));

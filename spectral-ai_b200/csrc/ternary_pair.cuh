@@ -57,8 +57,9 @@ namespace sb {
 
 constexpr int TP_EPI_WARPS = 4;
 constexpr int TP_EPI_SETS = TP_EPI_WARPS / 4;        // epilogue warps per TMEM lane quarter
+constexpr int TP_UNPACK_WARPS = 4;                   // 4, or 8: two per TMEM lane quarter, one 64-K half each
 constexpr int TP_UNPACK_WARP0 = 4 + TP_EPI_WARPS;
-constexpr int TP_THREADS = 32 * (TP_UNPACK_WARP0 + 4);
+constexpr int TP_THREADS = 32 * (TP_UNPACK_WARP0 + TP_UNPACK_WARPS);
 constexpr int TP_STAGES = 4;
 constexpr int TP_A_STAGES = 2;
 constexpr int TP_KB = 128;                           // K per block
@@ -138,7 +139,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
       mbar_init(&full_p[s], 1);
       mbar_init(&xp_empty[s], STREAMS);  // one commit per MMA stream
     }
-    for (int s = 0; s < TP_A_STAGES; ++s) mbar_init(&full_a[s], 8);  // 4 unpack warps x 2 CTAs
+    for (int s = 0; s < TP_A_STAGES; ++s) mbar_init(&full_a[s], 2 * TP_UNPACK_WARPS);  // unpack warps x 2 CTAs
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], STREAMS);
       mbar_init(&tempty[b], 2 * TP_EPI_WARPS);
@@ -261,6 +262,7 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
   } else if (warp >= TP_UNPACK_WARP0) {
     // ------------------------------------------------------------ unpack warps
     const int q = warp & 3;
+    [[maybe_unused]] const int uh = (warp - TP_UNPACK_WARP0) >> 2;  // 8 unpack warps: this warp's 64-K half
     // the packed row this lane expands (TMEM lane 32q + lane)
     int prow;
     if (MODE == TG_GATEUP)
@@ -278,19 +280,23 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
         // expand the row's eight words (128 K) into registers first: only the
         // stores into TMEM have to wait for the A stage to drain
         const uint8_t* pw = smem + stage * TP_STAGE_BYTES + TP_X_BYTES + prow * 32;
-        const uint4 w0 = *reinterpret_cast<const uint4*>(pw);
-        const uint4 w1 = *reinterpret_cast<const uint4*>(pw + 16);
-        uint32_t a0[32], a1[32];
-        {
+        uint32_t a0[32];
+        [[maybe_unused]] uint32_t a1[TP_UNPACK_WARPS == 4 ? 32 : 1];
+        if constexpr (TP_UNPACK_WARPS == 4) {
+          const uint4 w0 = *reinterpret_cast<const uint4*>(pw);
+          const uint4 w1 = *reinterpret_cast<const uint4*>(pw + 16);
           const uint32_t words0[4] = {w0.x, w0.y, w0.z, w0.w};
           const uint32_t words1[4] = {w1.x, w1.y, w1.z, w1.w};
 #pragma unroll
-          for (int w = 0; w < 4; ++w)
+          for (int w = 0; w < 4; ++w) {
+            tern_word<FMT>(words0[w], a0 + 8 * w);
+            tern_word<FMT>(words1[w], a1 + 8 * w);
+          }
+        } else {
+          const uint4 w0 = *reinterpret_cast<const uint4*>(pw + 16 * uh);
+          const uint32_t words0[4] = {w0.x, w0.y, w0.z, w0.w};
 #pragma unroll
-            for (int j = 0; j < 8; ++j) {
-              a0[8 * w + j] = tern_pair<FMT>(words0[w], j);
-              a1[8 * w + j] = tern_pair<FMT>(words1[w], j);
-            }
+          for (int w = 0; w < 4; ++w) tern_word<FMT>(words0[w], a0 + 8 * w);
         }
         // The A stage is free once the MMAs of K-block it - TP_A_STAGES have
         // completed, which the commit on that block's slot barrier signals.
@@ -304,8 +310,12 @@ __global__ void __launch_bounds__(TP_THREADS, 1)
         }
         tc_fence_after();
         const uint32_t col = lane_base + (uint32_t)(astage * TP_A_COLS);
-        tmem_st_32x32b_x32_p(col, a0);
-        tmem_st_32x32b_x32_p(col + 32u, a1);
+        if constexpr (TP_UNPACK_WARPS == 4) {
+          tmem_st_32x32b_x32_p(col, a0);
+          tmem_st_32x32b_x32_p(col + 32u, a1);
+        } else {
+          tmem_st_32x32b_x32_p(col + 32u * (uint32_t)uh, a0);
+        }
         asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
         tc_fence_before();
         // rank 0 also waits for both token halves of this slot, so that the MMA

@@ -95,9 +95,7 @@ __device__ __forceinline__ void unpack_row_to_tmem(const uint4 wv, uint32_t tadd
   const uint32_t words[4] = {wv.x, wv.y, wv.z, wv.w};
   uint32_t a[32];
 #pragma unroll
-  for (int w = 0; w < 4; ++w)
-#pragma unroll
-    for (int j = 0; j < 8; ++j) a[8 * w + j] = tern_pair<FMT>(words[w], j);
+  for (int w = 0; w < 4; ++w) tern_word<FMT>(words[w], a + 8 * w);
   tmem_st_32x32b_x32(taddr, a);
 }
 

@@ -2,8 +2,9 @@
 
 Weights live on the device in the B200 layout: uint32 [N, KW], KW =
 ceil(K/64)*4, one word per 16 consecutive K of an output row; element 2j+e of
-a word (e = 0, 1) is stored as the biased code value+1 in bits 16e+2j ..
-16e+2j+1, and padding holds code 1 (value 0).  ``pack_device`` builds it on the host from int8 ternary
+a word (e = 0, 1) is stored as the biased code value+1 in bits 16e+p_j ..
+16e+p_j+1 with p_j = TERN_POS[j] (the order in which the kernels can expand
+most pairs without a shift), and padding holds code 1 (value 0).  ``pack_device`` builds it on the host from int8 ternary
 matrices in the PyTorch [out, in] layout; ``repack_reference`` converts the
 reference extension's packed layout (int32 [ceil(K/16), N],
 cuda/v5/ternary_torch_ext.cu:197-231) on the device.
@@ -20,6 +21,10 @@ import torch
 from . import _lib
 
 
+# bit position of pair j in each 16-bit half (csrc/ternary_gemm.cuh tern_pos)
+TERN_POS = (0, 2, 4, 8, 10, 12, 6, 14)
+
+
 def row_words(K: int) -> int:
     return (K + 63) // 64 * 4
 
@@ -32,8 +37,8 @@ def pack_device(T: np.ndarray) -> np.ndarray:
     pad = np.zeros((N, KW * 16), np.int8)
     pad[:, :K] = T
     code = (pad.reshape(N, KW, 8, 2).astype(np.int64) + 1).astype(np.uint32)  # [n, word, j, e]
-    j = np.arange(8, dtype=np.uint32)[None, None, :]
-    w = (code[..., 0] << (2 * j)) | (code[..., 1] << (16 + 2 * j))
+    p = np.array(TERN_POS, dtype=np.uint32)[None, None, :]
+    w = (code[..., 0] << p) | (code[..., 1] << (16 + p))
     return np.bitwise_or.reduce(w, axis=2).astype(np.uint32)
 
 
@@ -45,8 +50,8 @@ def pack_device_torch(T: torch.Tensor) -> torch.Tensor:
     pad = torch.zeros(N, KW * 16, dtype=torch.int8, device=T.device)
     pad[:, :K] = T
     code = pad.view(N, KW, 8, 2).to(torch.int64) + 1
-    j = torch.arange(8, device=T.device, dtype=torch.int64).view(1, 1, 8)
-    w = (code[..., 0] << (2 * j)) | (code[..., 1] << (16 + 2 * j))
+    p = torch.tensor(TERN_POS, device=T.device, dtype=torch.int64).view(1, 1, 8)
+    w = (code[..., 0] << p) | (code[..., 1] << (16 + p))
     words = w.sum(dim=2)  # the bit fields of the 8 pairs are disjoint
     return torch.where(words >= 2 ** 31, words - 2 ** 32, words).to(torch.int32)
 

@@ -9,15 +9,18 @@ import torch
 from conftest import load_golden
 
 
+POS = (0, 2, 4, 8, 10, 12, 6, 14)  # bit of pair j in each half (test-side restatement)
+
+
 def decode_device(words: np.ndarray, K: int) -> np.ndarray:
     """Inverse of the biased-code device layout (test-side restatement):
-    element 2j+e of a word is code value+1 at bits 16e+2j .. 16e+2j+1."""
+    element 2j+e of a word is code value+1 at bits 16e+POS[j] .. 16e+POS[j]+1."""
     w = np.asarray(words).view(np.uint32)
     N, KW = w.shape
-    j = np.arange(8, dtype=np.uint32)
+    p = np.array(POS, dtype=np.uint32)
     out = np.zeros((N, KW, 8, 2), np.int8)
     for e in range(2):
-        code = (w[:, :, None] >> (16 * e + 2 * j)) & 3
+        code = (w[:, :, None] >> (16 * e + p)) & 3
         assert (code <= 2).all(), "code 3 is not used"
         out[..., e] = code.astype(np.int8) - 1
     return out.reshape(N, KW * 16)[:, :K]
@@ -50,23 +53,40 @@ def test_device_layout_round_trip(shape):
 
 
 def test_device_layout_pair_expansion_formula():
-    """Two elements per word become 16-bit +-1/0 with shift, and-or and one packed
-    subtraction of b+1 (b = 128 in bf16, 1024 in fp16): (b + code) - (b + 1)."""
-    from sb200.ternary import pack_device
+    """Two elements per word become 16-bit +-1/0 with one and-or and one packed
+    subtraction: with the exponent that makes bit p the mantissa's unit,
+    (w & (3 << p)) | E is b + code, b = 2^(7-p) (bf16, p <= 4) or 2^(10-p)
+    (fp16, p <= 8), and (b + code) - (b + 1) is the weight.  Pairs past the
+    mantissa are first shifted by 8 (then sitting at p - 8) or down to bit 0,
+    as the kernels' tern_pair_c does."""
+    from sb200.ternary import pack_device, TERN_POS
+    assert tuple(TERN_POS) == POS
     rng = np.random.default_rng(5)
-    T = rng.integers(-1, 2, size=(1, 16), dtype=np.int8)
-    w = int(pack_device(T)[0, 0])
-    for fmt, (bias, bias1) in {"bf16": (0x4300, 0x4301), "f16": (0x6400, 0x6401)}.items():
-        def to_f(h):
-            if fmt == "f16":
-                return float(np.array([h], np.uint16).view(np.float16)[0])
-            return float(np.array([h << 16], np.uint32).view(np.float32)[0])
-        for j in range(8):
-            t = ((w >> (2 * j)) & 0x00030003) | (bias | (bias << 16))
-            for e in range(2):
-                half = (t >> (16 * e)) & 0xFFFF
-                # the subtraction is exact: both operands and the result are representable
-                assert to_f(half) - to_f(bias1) == T[0, 2 * j + e]
+    T = rng.integers(-1, 2, size=(4, 16), dtype=np.int8)
+    for row in range(4):
+        w = int(pack_device(T[row:row + 1])[0, 0])
+        for fmt, lim in (("bf16", 4), ("f16", 8)):
+            def to_f(h):
+                if fmt == "f16":
+                    return float(np.array([h], np.uint16).view(np.float16)[0])
+                return float(np.array([h << 16], np.uint32).view(np.float32)[0])
+            for j in range(8):
+                p = POS[j]
+                if p <= lim:
+                    src, q = w, p
+                elif p >= 8 and p - 8 <= lim:
+                    src, q = w >> 8, p - 8
+                else:
+                    src, q = w >> p, 0
+                base = ((134 - q) << 7) if fmt == "bf16" else ((25 - q) << 10)
+                t = (src & (0x00030003 << q)) | (base | (base << 16))
+                for e in range(2):
+                    half = (t >> (16 * e)) & 0xFFFF
+                    # the subtraction is exact: both operands and the result are representable
+                    assert to_f(half) - to_f(base + (1 << q)) == T[row, 2 * j + e], (fmt, j, e)
+                # the run-time form: shift to bit 0 by the nibble table
+                sh = (0xE6CA8420 >> (4 * j)) & 15
+                assert sh == p
 
 
 def test_padding_decodes_to_zero():

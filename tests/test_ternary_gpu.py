@@ -204,6 +204,27 @@ def test_gated_mlp_olmoe_shape(cuda_device, M):
     assert torch.equal(ext.ternary_gated_mlp(x, gp, up, dp, *s), y)
 
 
+@pytest.mark.parametrize("M", [5, 200, 4096])
+@pytest.mark.parametrize("xdtype", [torch.float32, torch.bfloat16])
+def test_gated_mlp_equals_the_routed_single_expert(cuda_device, M, xdtype):
+    """Past the few-token sizes ternary_gated_mlp reads the rows in place and
+    lets the down GEMM store y (no dispatch copy, no combine); it equals the
+    routed layer with one expert and weight 1 bit for bit."""
+    from sb200 import synth
+    from sb200 import ternary as T
+    from sb200.ternary import TernaryExperts
+    H, I = 2048, 1024
+    te = TernaryExperts(synth.ternary_experts(1, H, I, seed=23), cuda_device)
+    x = synth.hidden_states(M, H, seed=24, dtype=xdtype, device=cuda_device)
+    y = T.gated_mlp(x, te.gate, te.up, te.down, te.gate_scale[0], te.up_scale[0], te.down_scale[0], H, I)
+    ids = torch.zeros(M, 1, dtype=torch.int32, device=cuda_device)
+    w = torch.ones(M, 1, device=cuda_device)
+    y_routed = te.forward(x, ids, w, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert y.dtype == torch.float32 and y.shape == (M, H)
+    assert torch.equal(y, y_routed), f"max |diff| {(y - y_routed).abs().max()}"
+
+
 def test_ternary_linear(cuda_device):
     import ternary_expert_ext as ext
     rng = np.random.default_rng(3)
