@@ -531,7 +531,8 @@ def stack_workload(tokens: int, device, layers: int = 16, select: str = "soft", 
     """Config 3: a stack of MoE layers (router + 64 ternary experts each, own
     random weights per layer) with residual h <- h + MoE(h); attention omitted.
     At N > 1 every layer is expert-parallel (64/N experts per GPU, the
-    peer-memory exchange), the layers sharing one workspace."""
+    peer-memory exchange, a balanced expert placement per layer), the layers
+    sharing one workspace."""
     import numpy as np
     import torch
     from bvh_router import BVHRouter, RouterConfig
@@ -551,9 +552,18 @@ def stack_workload(tokens: int, device, layers: int = 16, select: str = "soft", 
         r.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in w.items()})
         r = r.to(device).eval()
         if world > 1:
+            from sb200.ep import balanced_placement
             el = E_EXPERTS // world
+            # this layer's placement from its router's loads on a calibration batch
+            xc = synth.hidden_states(tokens, H, seed=9 + 1000 * rank, dtype=torch.bfloat16, device=device)
+            ids_c, _ = r.forward_topk(xc, k=TOPK, select=select)
+            calib = torch.bincount(ids_c.long().flatten(), minlength=E_EXPERTS).float()
+            dist.all_reduce(calib)
+            placement = balanced_placement(calib.cpu().tolist(), world)
+            # the experts at this rank's positions (random weights either way)
             local = TernaryExperts.random(el, H, I_INTER, seed=200 + 64 * l + rank, device=device)
-            layer = EPMoELayer(r, local, E_EXPERTS, TOPK, tokens, select=select, chunks=1, workspace=shared)
+            layer = EPMoELayer(r, local, E_EXPERTS, TOPK, tokens, select=select, chunks=1, workspace=shared,
+                               placement=placement)
             shared = layer.ep.workspace
             stack.append(layer)
         else:
@@ -591,17 +601,31 @@ def ep_workload(batch: int, device, world: int, select: str = "soft"):
     r = r.to(device).eval()
     e_local = E_EXPERTS // world
     allx = synth.ternary_experts(E_EXPERTS, H, I_INTER, seed=2)
-    local = TernaryExperts(allx[rank * e_local:(rank + 1) * e_local], device)
+    # expert placement from routing statistics of a calibration batch (other
+    # tokens than the timed ones), summed over the ranks: the busy experts
+    # spread over the GPUs so that their GEMM work evens out
+    from sb200.ep import balanced_placement, experts_at
+    xc = synth.hidden_states(batch, H, seed=7 + 1000 * rank, dtype=torch.bfloat16, device=device)
+    ids_c, _ = r.forward_topk(xc, k=TOPK, select=select)
+    calib = torch.bincount(ids_c.long().flatten(), minlength=E_EXPERTS).float()
+    dist.all_reduce(calib)
+    placement = None if os.environ.get("SB_EP_PLACEMENT") == "contiguous" else \
+        balanced_placement(calib.cpu().tolist(), world)
+    held = experts_at(placement, rank, world) if placement else list(range(rank * e_local, (rank + 1) * e_local))
+    local = TernaryExperts([allx[e] for e in held], device)
     chunks = int(os.environ.get("SB_EP_CHUNKS", "2"))
-    layer = EPMoELayer(r, local, E_EXPERTS, TOPK, batch, select=select, chunks=chunks)
+    layer = EPMoELayer(r, local, E_EXPERTS, TOPK, batch, select=select, chunks=chunks, placement=placement)
     x = synth.hidden_states(batch, H, seed=2 + 1000 * rank, dtype=torch.bfloat16, device=device)
     out = torch.empty(batch, H, dtype=torch.bfloat16, device=device)
     ids, _ = layer.route(x)
     counts = torch.bincount(ids.long().flatten(), minlength=E_EXPERTS).float()
     dist.all_reduce(counts)                      # the whole job's expert loads
-    per_rank = counts.view(world, e_local).sum(dim=1)
+    perm_t = torch.tensor(placement if placement else list(range(E_EXPERTS)), device=device)
+    owner = perm_t // e_local                    # each expert's rank
+    per_rank = torch.zeros(world, device=device).index_add_(0, owner, counts)
+    contiguous = counts.view(world, e_local).sum(dim=1)
     dests = torch.zeros(batch, world, dtype=torch.bool, device=device)
-    dests.scatter_(1, (ids.long() // e_local), True)
+    dests.scatter_(1, owner[ids.long()], True)
     rows_sent = float(dests.sum()) / max(batch, 1)
 
     def eager_step():
@@ -636,6 +660,10 @@ def ep_workload(batch: int, device, world: int, select: str = "soft"):
                        "tokens_per_gpu": batch, "router_select": select,
                        "experts_per_gpu": e_local,
                        "entries_per_gpu_max_over_mean": round(float(per_rank.max() / per_rank.mean()), 3),
+                       "expert_placement": ("balanced from a calibration batch's routing (sb200.ep."
+                                            "balanced_placement)" if placement else "contiguous blocks"),
+                       "entries_per_gpu_max_over_mean_contiguous": round(
+                           float(contiguous.max() / contiguous.mean()), 3),
                        "expert_load_max_over_mean": round(float(counts.max() / counts.mean()), 3),
                        "rows_sent_per_token": round(rows_sent, 3),
                        "precision": "router bf16 tcgen05 + fp32 descent; ternary bf16 x {-1,0,1} "
@@ -983,7 +1011,7 @@ def run_ours(a):
                           "tokens_per_gpu": stok, "layers": 16, "steps": st_steps,
                           "scaling": "strong (16384 tokens in total, split over the GPUs)",
                           "parallelism": (f"ep{world} per layer ({E_EXPERTS // world} experts per GPU, "
-                                          "peer-memory exchange)" if world > 1 else "single GPU"),
+                                          "peer-memory exchange, balanced placement per layer)" if world > 1 else "single GPU"),
                           "l2": "weights of 16 layers (1.7 GB) stream every step; no flush"}
     # ---- config 4: 6-level 4096-expert router at hidden 4096 vs a dense gate
     if not a.skip_config4:

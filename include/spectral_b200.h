@@ -283,6 +283,16 @@ int sb_ep_export(const sb_ep* h, void* handle);
 int sb_ep_connect(sb_ep* h, const void* handles);
 int sb_ep_connect_nccl(sb_ep* h, void* nccl_comm, void* stream);
 size_t sb_ep_workspace_bytes(const sb_ep* h);
+/* Expert placement (optional, the same on every rank, before a forward;
+ * synchronous): perm[e] (host int32 [E], a permutation of [0,E)) is expert e's
+ * position, and rank r holds the experts at positions [r*E/W, (r+1)*E/W) —
+ * its local expert j being the one at position r*E/W + j, so the caller
+ * passes that rank's weights in position order.  The partial sums follow the
+ * tree over positions: the output equals sb_ternary_moe_swiglu on one GPU over
+ * the experts in position order with ids perm[ids], bit for bit.  Spreading
+ * the busy experts over the ranks evens out their GEMM work.  perm = NULL
+ * restores the identity. */
+int sb_ep_set_placement(sb_ep* h, const int32_t* perm);
 int sb_ep_forward(sb_ep* h, const void* x, int x_dtype, int64_t batch, const int32_t* ids,
                   const float* weights, const uint32_t* gate, const uint32_t* up, const uint32_t* down,
                   const float* gate_scale, const float* up_scale, const float* down_scale,

@@ -2,9 +2,11 @@
 // token exchange done by the layer's own kernels through peer memory (NVLink /
 // NVSwitch): no host round trip, no library collective on the data path.
 //
-// W ranks (one process per GPU), E experts, rank r holds experts
-// [r*El, (r+1)*El), El = E / W.  One forward on every rank (all ranks call it
-// the same number of times; it is collective):
+// W ranks (one process per GPU), E experts, rank r holds the experts at
+// positions [r*El, (r+1)*El), El = E / W; an expert's position is its id, or
+// perm[id] after sb_ep_set_placement (spreading the busy experts over the
+// ranks).  One forward on every rank (all ranks call it the same number of
+// times; it is collective):
 //
 //   ep_send         a warp per token: the ranks its k expert ids live on, a
 //                   row claimed in each of those ranks' receive segment for
@@ -59,6 +61,8 @@
 // loads and stores from the SMs.
 
 #include "common.cuh"
+
+#include <vector>
 #include "sm100.cuh"
 #include "tree_sum.cuh"
 
@@ -112,6 +116,7 @@ struct EpArgs {
   int64_t cap, H;
   uint64_t limit_ns;
   EpCtrl* ctrl;
+  const int32_t* perm;  // expert id -> position (null: the identity), sb_ep_set_placement
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -182,6 +187,8 @@ __global__ void __launch_bounds__(EP_THREADS) ep_send_kernel(const __nv_bfloat16
       if (e < 0 || e >= a.E) {
         atomicOr(&a.ctrl->error, 4u);
         e = -1;
+      } else if (a.perm) {
+        e = __ldg(a.perm + e);  // the expert's position: rank e / El, local id e % El
       }
     }
     const int dest = e >= 0 ? e / a.El : -1;
@@ -525,6 +532,7 @@ struct sb_ep {
   uint8_t* peer[sb::EP_MAX_WORLD] = {};
   bool connected = false;
   sb::EpCtrl* ctrl = nullptr;
+  int32_t* perm = nullptr;  // device [E], set by sb_ep_set_placement
 };
 
 namespace sb {
@@ -582,6 +590,7 @@ EpArgs ep_args(const sb_ep* h) {
   a.H = h->H;
   a.limit_ns = (uint64_t)h->timeout_ms * 1000000ull;
   a.ctrl = h->ctrl;
+  a.perm = h->perm;
   return a;
 }
 
@@ -930,7 +939,28 @@ extern "C" int sb_ep_destroy(sb_ep* h) {
       if (g != h->rank && h->peer[g]) cudaIpcCloseMemHandle(h->peer[g]);
     if (h->local) cudaFree(h->local);
     if (h->ctrl) cudaFree(h->ctrl);
+    if (h->perm) cudaFree(h->perm);
   }
   delete h;
+  return SB_OK;
+}
+
+extern "C" int sb_ep_set_placement(sb_ep* h, const int32_t* perm) {
+  using namespace sb;
+  SB_REQUIRE(h, "null handle");
+  DeviceGuard dg(h->device);
+  if (!perm) {  // back to the identity
+    if (h->perm) SB_CUDA_TRY(cudaFree(h->perm));
+    h->perm = nullptr;
+    return SB_OK;
+  }
+  std::vector<char> seen((size_t)h->E, 0);
+  for (int e = 0; e < h->E; ++e) {
+    SB_REQUIRE(perm[e] >= 0 && perm[e] < h->E && !seen[(size_t)perm[e]],
+               "placement must be a permutation of [0, %d): entry %d is %d", h->E, e, perm[e]);
+    seen[(size_t)perm[e]] = 1;
+  }
+  if (!h->perm) SB_CUDA_TRY(cudaMalloc(&h->perm, sizeof(int32_t) * (size_t)h->E));
+  SB_CUDA_TRY(cudaMemcpy(h->perm, perm, sizeof(int32_t) * (size_t)h->E, cudaMemcpyHostToDevice));
   return SB_OK;
 }

@@ -165,6 +165,7 @@ SIGNATURES = [
     ("sb_ep_connect", C.c_int, [C.c_void_p, C.c_void_p]),
     ("sb_ep_connect_nccl", C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p]),
     ("sb_ep_workspace_bytes", C.c_size_t, [C.c_void_p]),
+    ("sb_ep_set_placement", C.c_int, [C.c_void_p, C.c_void_p]),
     ("sb_ep_forward", C.c_int,
      [C.c_void_p, C.c_void_p, C.c_int, C.c_int64, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
       C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_size_t, C.c_void_p]),

@@ -25,7 +25,7 @@ of the fused exchange.
 from __future__ import annotations
 
 import ctypes as C
-from typing import Callable, Optional
+from typing import Callable, Optional, Sequence
 
 import torch
 import torch.distributed as dist
@@ -44,17 +44,57 @@ def exchange_handles(mine: bytes, group: Optional[dist.ProcessGroup] = None) -> 
     return b"".join(got)
 
 
+def balanced_placement(loads: Sequence[float], world: int) -> list:
+    """An expert placement (``perm[e]`` = expert e's position; rank r holds
+    positions [r*E/W, (r+1)*E/W)) that evens out the ranks' expert loads:
+    experts in falling order of load, each to the least-loaded rank that still
+    has room (longest-processing-time first, E/W experts per rank), then each
+    rank's experts in ascending id.  ``loads`` are per-expert entry counts from
+    routing statistics (a calibration batch)."""
+    E = len(loads)
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    el = E // world
+    order = sorted(range(E), key=lambda e: (-float(loads[e]), e))
+    bins = [[] for _ in range(world)]
+    tot = [0.0] * world
+    for e in order:
+        r = min((r for r in range(world) if len(bins[r]) < el), key=lambda r: (tot[r], r))
+        bins[r].append(e)
+        tot[r] += float(loads[e])
+    perm = [0] * E
+    for r in range(world):
+        for j, e in enumerate(sorted(bins[r])):
+            perm[e] = r * el + j
+    return perm
+
+
+def experts_at(perm: Sequence[int], rank: int, world: int) -> list:
+    """The expert ids rank ``rank`` holds under ``perm``, in position order."""
+    E = len(perm)
+    el = E // world
+    inv = [0] * E
+    for e, p in enumerate(perm):
+        inv[p] = e
+    return inv[rank * el:(rank + 1) * el]
+
+
 class ExpertParallelMoE:
-    """The grouped ternary SwiGLU with this rank's experts (``TernaryExperts``
-    holding experts [rank*E/W, (rank+1)*E/W)) and the token exchange on the
-    device.  ``forward`` is collective: every rank calls it equally often."""
+    """The grouped ternary SwiGLU with this rank's experts and the token
+    exchange on the device.  ``local_experts`` (``TernaryExperts``) holds the
+    experts at positions [rank*E/W, (rank+1)*E/W) in position order: experts
+    [rank*E/W, ...) themselves, or ``experts_at(placement, rank, W)`` with a
+    ``placement``.  ``forward`` is collective: every rank calls it equally
+    often."""
 
     def __init__(self, local_experts, n_experts: int, top_k: int, max_tokens: int,
                  group: Optional[dist.ProcessGroup] = None, timeout_ms: int = 2000,
-                 nccl_comm: Optional[int] = None, workspace: Optional[torch.Tensor] = None):
+                 nccl_comm: Optional[int] = None, workspace: Optional[torch.Tensor] = None,
+                 placement: Optional[Sequence[int]] = None):
         """``workspace``: a uint8 device buffer to use (and grow) instead of a
         private one, for layers that run one after another on one stream (a
-        stack); ``self.workspace`` is the buffer in use."""
+        stack); ``self.workspace`` is the buffer in use.  ``placement``: expert
+        id -> position (``balanced_placement``), the same on every rank."""
         self.lib = _lib.load()
         self.experts = local_experts
         self.device = local_experts.device
@@ -82,6 +122,11 @@ class ExpertParallelMoE:
                         _lib.check(self.lib.sb_ep_export(self.handle, buf), "sb_ep_export")
                         allb = exchange_handles(buf.raw, group)
                         _lib.check(self.lib.sb_ep_connect(self.handle, C.c_char_p(allb)), "sb_ep_connect")
+                if placement is not None:
+                    perm = (C.c_int32 * self.n_experts)(*[int(p) for p in placement])
+                    if len(placement) != self.n_experts:
+                        raise ValueError(f"placement names {len(placement)} experts, the layer has {self.n_experts}")
+                    _lib.check(self.lib.sb_ep_set_placement(self.handle, perm), "sb_ep_set_placement")
             except Exception:
                 self.lib.sb_ep_destroy(self.handle)
                 self.handle = None
@@ -221,16 +266,18 @@ class EPMoELayer:
 
     def __init__(self, router, local_experts, n_experts: int, top_k: int, max_tokens: int,
                  select: str = "soft", chunks: int = 1, group: Optional[dist.ProcessGroup] = None,
-                 timeout_ms: int = 2000, workspace: Optional[torch.Tensor] = None):
+                 timeout_ms: int = 2000, workspace: Optional[torch.Tensor] = None,
+                 placement: Optional[Sequence[int]] = None):
         """``workspace``: a buffer shared with layers that run one after
-        another on the same stream (``chunks`` == 1 only)."""
+        another on the same stream (``chunks`` == 1 only).  ``placement``: as
+        for ``ExpertParallelMoE`` (``local_experts`` in position order)."""
         self.router = router
         self.top_k = int(top_k)
         self.select = select
         self.chunks = max(1, int(chunks))
         per = (int(max_tokens) + self.chunks - 1) // self.chunks
         self.eps = [ExpertParallelMoE(local_experts, n_experts, top_k, per, group=group, timeout_ms=timeout_ms,
-                                      workspace=workspace if self.chunks == 1 else None)
+                                      workspace=workspace if self.chunks == 1 else None, placement=placement)
                     for _ in range(self.chunks)]
         self.per = per
         dev = local_experts.device

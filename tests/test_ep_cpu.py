@@ -77,3 +77,46 @@ def test_token_goes_once_per_destination():
         assert [send_pos[t, g] for t in lists[g]] == list(range(len(lists[g])))
     # about 5.4 distinct ranks per token for 8 distinct experts over 8 blocks of 8
     assert 5.0 < sum(len(l) for l in lists) / len(ids) < 5.8
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_balanced_placement_is_a_permutation_that_evens_the_ranks(world):
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "spectral-ai_b200"))
+    from sb200.ep import balanced_placement, experts_at
+    rng = np.random.default_rng(world)
+    # skewed loads like the router's (max/mean about 2.6), hot experts clustered
+    loads = np.sort(rng.gamma(1.2, 100.0, 64))[::-1].copy()
+    perm = balanced_placement(loads, world)
+    assert sorted(perm) == list(range(64))
+    el = 64 // world
+    held = [experts_at(perm, r, world) for r in range(world)]
+    assert sorted(e for h in held for e in h) == list(range(64))
+    for r, h in enumerate(held):
+        assert len(h) == el and h == sorted(h)                 # position order = ascending id
+        assert all(perm[e] // el == r for e in h)
+    per = np.array([loads[h].sum() for h in held])
+    contiguous = np.array([loads[r * el:(r + 1) * el].sum() for r in range(world)])
+    assert per.max() <= contiguous.max() + 1e-9
+    if world > 1:
+        # LPT bound: the busiest rank exceeds the mean by at most one expert's load
+        assert per.max() <= per.mean() + loads.max() + 1e-9
+
+
+def test_placement_keeps_the_sharded_sum_bitwise():
+    """Relabelling experts by a placement and sharding by position gives the
+    single-process tree sum over the relabelled ids (what csrc/ep.cu computes)."""
+    ids, y = _case(5, 40, 16, 4, 8)
+    perm = np.random.default_rng(3).permutation(16).astype(np.int32)
+    pos = perm[ids]
+    ref = oep.combine_single(pos, y)
+    for world in (2, 4):
+        send_pos, lists = oep.plan_destinations(pos, 16, world)
+        partials = []
+        for g in range(world):
+            rows = lists[g]
+            partials.append(oep.destination_partials(pos[rows], y[rows], g, 16, world) if len(rows)
+                            else np.zeros((0, y.shape[2]), np.float32))
+        got = oep.source_combine(send_pos, partials)
+        assert np.array_equal(got, ref)

@@ -9,8 +9,11 @@
   equals the single-GPU layer over all experts (run on all ranks' tokens at
   once, so that every expert sees the same rows) bit for bit, over several
   forwards and with both set-up paths (handles exchanged by torch.distributed,
-  or by the library over an NCCL communicator); then rank 0 runs a forward the
-  others skip, and its waits report the timeout instead of hanging.
+  or by the library over an NCCL communicator, the latter with an expert
+  placement); then rank 0 runs a forward the others skip, and its waits report
+  the timeout instead of hanging.
+* An expert placement on one rank: the layer equals the single-GPU layer over
+  the experts in position order fed ids perm[ids].
 """
 
 from __future__ import annotations
@@ -57,6 +60,37 @@ def test_single_rank_equals_single_gpu_layer(cuda_device, E, H, I, k):
                 assert y_ep.shape == (B, H) and y_ep.dtype == dt
                 assert torch.equal(y_ep, y_one), f"B={B} {dt}: max |diff| {(y_ep.float() - y_one.float()).abs().max()}"
         ep.status()
+    finally:
+        ep.close()
+
+
+def test_single_rank_placement_equals_the_relabelled_layer(cuda_device):
+    """With an expert placement (perm[e] = position), the layer equals the
+    single-GPU layer over the experts in position order fed ids perm[ids]."""
+    import numpy as np
+    from sb200 import synth
+    from sb200.ep import ExpertParallelMoE, experts_at
+    from sb200.ternary import TernaryExperts
+    E, H, I, k = 16, 512, 256, 4
+    experts = synth.ternary_experts(E, H, I, seed=62)
+    perm = [int(p) for p in np.random.default_rng(7).permutation(E)]
+    ordered = [experts[e] for e in experts_at(perm, 0, 1)]
+    full = TernaryExperts(ordered, cuda_device)
+    ep = ExpertParallelMoE(TernaryExperts(ordered, cuda_device), E, k, 1024, placement=perm)
+    try:
+        perm_t = torch.tensor(perm, dtype=torch.int64, device=cuda_device)
+        for call, B in enumerate([300, 1024, 1]):
+            x = synth.hidden_states(B, H, seed=63 + call, dtype=torch.bfloat16, device=cuda_device)
+            ids_np, w_np = synth.zipf_routing(B, E, k, seed=64 + call)
+            ids = torch.from_numpy(ids_np).to(cuda_device)
+            w = torch.from_numpy(w_np).to(cuda_device)
+            y_ep = ep(x, ids, w, out_dtype=torch.float32)
+            y_one = full.forward(x, perm_t[ids.long()].to(torch.int32), w, out_dtype=torch.float32)
+            torch.cuda.synchronize()
+            assert torch.equal(y_ep, y_one), f"B={B}: max |diff| {(y_ep - y_one).abs().max()}"
+        ep.status()
+        with pytest.raises(RuntimeError, match="permutation"):
+            ExpertParallelMoE(TernaryExperts(ordered, cuda_device), E, k, 64, placement=[0] * E)
     finally:
         ep.close()
 
@@ -178,10 +212,18 @@ def _worker(rank, world, port, q, use_nccl):
     comm = None
     results = []
     try:
+        import numpy as np
+        from sb200.ep import experts_at
         E, H, I, k = 64, 2048, 1024, 8
         experts = synth.ternary_experts(E, H, I, seed=61)
         el = E // world
-        full = TernaryExperts(experts, dev)
+        # the NCCL set-up path also runs with an expert placement (the same
+        # seeded permutation on every rank); the reference then takes the
+        # experts in position order and ids perm[ids]
+        perm = [int(p) for p in np.random.default_rng(11).permutation(E)] if use_nccl else list(range(E))
+        order = experts_at(perm, 0, 1)
+        full = TernaryExperts([experts[e] for e in order], dev)
+        perm_t = torch.tensor(perm, dtype=torch.int64, device=dev)
         if use_nccl:
             uid = C.create_string_buffer(128)
             if rank == 0:
@@ -191,8 +233,9 @@ def _worker(rank, world, port, q, use_nccl):
             cp = C.c_void_p()
             _lib.check(lib.sb_nccl_comm_init(world, rank, C.c_char_p(box[0]), C.byref(cp)), "sb_nccl_comm_init")
             comm = cp.value
-        ep = ExpertParallelMoE(TernaryExperts(experts[rank * el:(rank + 1) * el], dev), E, k, 4096,
-                               timeout_ms=1000, nccl_comm=comm)
+        mine = [experts[e] for e in experts_at(perm, rank, world)]
+        ep = ExpertParallelMoE(TernaryExperts(mine, dev), E, k, 4096, timeout_ms=1000, nccl_comm=comm,
+                               placement=perm if use_nccl else None)
         sizes = [[700 + 37 * r for r in range(world)], [4096] * world, [5] + [0] * (world - 1),
                  [2000] * world]
         for step, Bs in enumerate(sizes):
@@ -206,7 +249,8 @@ def _worker(rank, world, port, q, use_nccl):
                 idss.append(torch.from_numpy(ids_np).to(dev))
                 ws.append(torch.from_numpy(w_np).to(dev))
             y_ep = ep(xs[rank], idss[rank], ws[rank], out_dtype=torch.float32)
-            y_all = full.forward(torch.cat(xs), torch.cat(idss), torch.cat(ws), out_dtype=torch.float32)
+            ids_pos = perm_t[torch.cat(idss).long()].to(torch.int32)
+            y_all = full.forward(torch.cat(xs), ids_pos, torch.cat(ws), out_dtype=torch.float32)
             lo = sum(Bs[:rank])
             y_one = y_all[lo:lo + Bs[rank]]
             torch.cuda.synchronize()
