@@ -559,7 +559,8 @@ def stack_workload(tokens: int, device, layers: int = 16, select: str = "soft", 
             ids_c, _ = r.forward_topk(xc, k=TOPK, select=select)
             calib = torch.bincount(ids_c.long().flatten(), minlength=E_EXPERTS).float()
             dist.all_reduce(calib)
-            placement = balanced_placement(calib.cpu().tolist(), world)
+            g = BRANCHING[-1] if el % BRANCHING[-1] == 0 else 1
+            placement = balanced_placement(calib.cpu().tolist(), world, group=g)
             # the experts at this rank's positions (random weights either way)
             local = TernaryExperts.random(el, H, I_INTER, seed=200 + 64 * l + rank, device=device)
             layer = EPMoELayer(r, local, E_EXPERTS, TOPK, tokens, select=select, chunks=1, workspace=shared,
@@ -609,8 +610,13 @@ def ep_workload(batch: int, device, world: int, select: str = "soft"):
     ids_c, _ = r.forward_topk(xc, k=TOPK, select=select)
     calib = torch.bincount(ids_c.long().flatten(), minlength=E_EXPERTS).float()
     dist.all_reduce(calib)
-    placement = None if os.environ.get("SB_EP_PLACEMENT") == "contiguous" else \
-        balanced_placement(calib.cpu().tolist(), world)
+    # units of sibling leaves (the router's last branching factor) stay on one
+    # GPU: a token's experts cluster in the tree, so this keeps the GPUs a
+    # token visits near the contiguous placement's while the loads even out
+    group = BRANCHING[-1] if (E_EXPERTS // world) % BRANCHING[-1] == 0 else 1
+    mode = os.environ.get("SB_EP_PLACEMENT", "grouped")
+    placement = None if mode == "contiguous" else \
+        balanced_placement(calib.cpu().tolist(), world, group=1 if mode == "scattered" else group)
     held = experts_at(placement, rank, world) if placement else list(range(rank * e_local, (rank + 1) * e_local))
     local = TernaryExperts([allx[e] for e in held], device)
     chunks = int(os.environ.get("SB_EP_CHUNKS", "2"))
@@ -660,8 +666,9 @@ def ep_workload(batch: int, device, world: int, select: str = "soft"):
                        "tokens_per_gpu": batch, "router_select": select,
                        "experts_per_gpu": e_local,
                        "entries_per_gpu_max_over_mean": round(float(per_rank.max() / per_rank.mean()), 3),
-                       "expert_placement": ("balanced from a calibration batch's routing (sb200.ep."
-                                            "balanced_placement)" if placement else "contiguous blocks"),
+                       "expert_placement": (f"balanced from a calibration batch's routing (sb200.ep."
+                                            f"balanced_placement, units of {1 if mode == 'scattered' else group} "
+                                            "sibling experts)" if placement else "contiguous blocks"),
                        "entries_per_gpu_max_over_mean_contiguous": round(
                            float(contiguous.max() / contiguous.mean()), 3),
                        "expert_load_max_over_mean": round(float(counts.max() / counts.mean()), 3),

@@ -44,28 +44,38 @@ def exchange_handles(mine: bytes, group: Optional[dist.ProcessGroup] = None) -> 
     return b"".join(got)
 
 
-def balanced_placement(loads: Sequence[float], world: int) -> list:
+def balanced_placement(loads: Sequence[float], world: int, group: int = 1) -> list:
     """An expert placement (``perm[e]`` = expert e's position; rank r holds
     positions [r*E/W, (r+1)*E/W)) that evens out the ranks' expert loads:
-    experts in falling order of load, each to the least-loaded rank that still
-    has room (longest-processing-time first, E/W experts per rank), then each
-    rank's experts in ascending id.  ``loads`` are per-expert entry counts from
-    routing statistics (a calibration batch)."""
+    units of ``group`` consecutive experts, in falling order of load, each to
+    the least-loaded rank that still has room (longest-processing-time first,
+    E/W experts per rank), each rank's experts then in ascending id.
+    ``loads`` are per-expert entry counts from routing statistics (a
+    calibration batch).  Keeping groups of experts that a router tends to
+    select together (the BVH router's sibling leaves) on one rank keeps the
+    number of ranks a token visits close to contiguous blocks' while the
+    loads even out; ``group=1`` balances best and scatters most."""
     E = len(loads)
     if E % world:
         raise ValueError(f"{E} experts do not split over {world} ranks")
     el = E // world
-    order = sorted(range(E), key=lambda e: (-float(loads[e]), e))
+    if group < 1 or el % group:
+        raise ValueError(f"group {group} does not divide the {el} experts of a rank")
+    units = E // group
+    uload = [sum(float(loads[u * group + j]) for j in range(group)) for u in range(units)]
+    order = sorted(range(units), key=lambda u: (-uload[u], u))
+    cap = el // group
     bins = [[] for _ in range(world)]
     tot = [0.0] * world
-    for e in order:
-        r = min((r for r in range(world) if len(bins[r]) < el), key=lambda r: (tot[r], r))
-        bins[r].append(e)
-        tot[r] += float(loads[e])
+    for u in order:
+        r = min((r for r in range(world) if len(bins[r]) < cap), key=lambda r: (tot[r], r))
+        bins[r].append(u)
+        tot[r] += uload[u]
     perm = [0] * E
     for r in range(world):
-        for j, e in enumerate(sorted(bins[r])):
-            perm[e] = r * el + j
+        for j, u in enumerate(sorted(bins[r])):
+            for i in range(group):
+                perm[u * group + i] = r * el + j * group + i
     return perm
 
 

@@ -79,8 +79,9 @@ def test_token_goes_once_per_destination():
     assert 5.0 < sum(len(l) for l in lists) / len(ids) < 5.8
 
 
+@pytest.mark.parametrize("group", [1, 4])
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
-def test_balanced_placement_is_a_permutation_that_evens_the_ranks(world):
+def test_balanced_placement_is_a_permutation_that_evens_the_ranks(world, group):
     import sys
     from pathlib import Path
     sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "spectral-ai_b200"))
@@ -88,8 +89,11 @@ def test_balanced_placement_is_a_permutation_that_evens_the_ranks(world):
     rng = np.random.default_rng(world)
     # skewed loads like the router's (max/mean about 2.6), hot experts clustered
     loads = np.sort(rng.gamma(1.2, 100.0, 64))[::-1].copy()
-    perm = balanced_placement(loads, world)
+    perm = balanced_placement(loads, world, group=group)
     assert sorted(perm) == list(range(64))
+    for u in range(64 // group):   # a unit of `group` consecutive experts stays together, in order
+        ps = [perm[u * group + i] for i in range(group)]
+        assert ps == list(range(ps[0], ps[0] + group)) and ps[0] // (64 // world) == ps[-1] // (64 // world)
     el = 64 // world
     held = [experts_at(perm, r, world) for r in range(world)]
     assert sorted(e for h in held for e in h) == list(range(64))
@@ -100,8 +104,9 @@ def test_balanced_placement_is_a_permutation_that_evens_the_ranks(world):
     contiguous = np.array([loads[r * el:(r + 1) * el].sum() for r in range(world)])
     assert per.max() <= contiguous.max() + 1e-9
     if world > 1:
-        # LPT bound: the busiest rank exceeds the mean by at most one expert's load
-        assert per.max() <= per.mean() + loads.max() + 1e-9
+        # LPT bound: the busiest rank exceeds the mean by at most one unit's load
+        unit = loads.reshape(-1, group).sum(axis=1)
+        assert per.max() <= per.mean() + unit.max() + 1e-9
 
 
 def test_placement_keeps_the_sharded_sum_bitwise():
