@@ -531,8 +531,8 @@ def stack_workload(tokens: int, device, layers: int = 16, select: str = "soft", 
     """Config 3: a stack of MoE layers (router + 64 ternary experts each, own
     random weights per layer) with residual h <- h + MoE(h); attention omitted.
     At N > 1 every layer is expert-parallel (64/N experts per GPU, the
-    peer-memory exchange, a balanced expert placement per layer), the layers
-    sharing one workspace."""
+    peer-memory exchange, an expert placement per layer from its router's
+    routing of a calibration batch), the layers sharing one workspace."""
     import numpy as np
     import torch
     from bvh_router import BVHRouter, RouterConfig
@@ -552,15 +552,10 @@ def stack_workload(tokens: int, device, layers: int = 16, select: str = "soft", 
         r.load_state_dict({k: torch.from_numpy(np.array(v)) for k, v in w.items()})
         r = r.to(device).eval()
         if world > 1:
-            from sb200.ep import balanced_placement
             el = E_EXPERTS // world
-            # this layer's placement from its router's loads on a calibration batch
+            # this layer's placement from its router on a calibration batch
             xc = synth.hidden_states(tokens, H, seed=9 + 1000 * rank, dtype=torch.bfloat16, device=device)
-            ids_c, _ = r.forward_topk(xc, k=TOPK, select=select)
-            calib = torch.bincount(ids_c.long().flatten(), minlength=E_EXPERTS).float()
-            dist.all_reduce(calib)
-            g = BRANCHING[-1] if el % BRANCHING[-1] == 0 else 1
-            placement = balanced_placement(calib.cpu().tolist(), world, group=g)
+            placement, _ = ep_placement(r, xc, world, select, iters=1000)
             # the experts at this rank's positions (random weights either way)
             local = TernaryExperts.random(el, H, I_INTER, seed=200 + 64 * l + rank, device=device)
             layer = EPMoELayer(r, local, E_EXPERTS, TOPK, tokens, select=select, chunks=1, workspace=shared,
@@ -579,6 +574,35 @@ def stack_workload(tokens: int, device, layers: int = 16, select: str = "soft", 
         return h
 
     return step
+
+
+def ep_placement(router, xc, world: int, select: str, iters: int = 3000):
+    """The expert placement of an expert-parallel layer from a calibration
+    batch (other tokens than the timed ones): every rank routes its own
+    batch, the ids are gathered so that every rank sees the same statistics,
+    units of sibling experts are balanced over the ranks (sb200.ep.
+    balanced_placement) and swaps then lower the modelled step time (sb200.ep.
+    refine_placement, the same seeded search on every rank).  SB_EP_PLACEMENT=
+    contiguous | grouped | scattered selects a simpler form for comparison."""
+    import torch
+    import torch.distributed as dist
+    from sb200.ep import balanced_placement, refine_placement
+    mode = os.environ.get("SB_EP_PLACEMENT", "refined")
+    if mode == "contiguous":
+        return None, mode
+    ids_c, _ = router.forward_topk(xc, k=TOPK, select=select)
+    ids_c = ids_c.to(torch.int32).contiguous()
+    allc = torch.empty(world * ids_c.shape[0], ids_c.shape[1], dtype=ids_c.dtype, device=ids_c.device)
+    dist.all_gather_into_tensor(allc, ids_c)
+    allc = allc.cpu().numpy()
+    import numpy as np
+    loads = np.bincount(allc.ravel(), minlength=E_EXPERTS).astype(float)
+    el = E_EXPERTS // world
+    group = 1 if mode == "scattered" else (BRANCHING[-1] if el % BRANCHING[-1] == 0 else 1)
+    perm = balanced_placement(loads.tolist(), world, group=group)
+    if mode == "refined":
+        perm = refine_placement(perm, allc, world, iters=iters)
+    return perm, mode
 
 
 def ep_workload(batch: int, device, world: int, select: str = "soft"):
@@ -602,21 +626,10 @@ def ep_workload(batch: int, device, world: int, select: str = "soft"):
     r = r.to(device).eval()
     e_local = E_EXPERTS // world
     allx = synth.ternary_experts(E_EXPERTS, H, I_INTER, seed=2)
-    # expert placement from routing statistics of a calibration batch (other
-    # tokens than the timed ones), summed over the ranks: the busy experts
-    # spread over the GPUs so that their GEMM work evens out
-    from sb200.ep import balanced_placement, experts_at
+    # expert placement from routing statistics of a calibration batch
+    from sb200.ep import experts_at
     xc = synth.hidden_states(batch, H, seed=7 + 1000 * rank, dtype=torch.bfloat16, device=device)
-    ids_c, _ = r.forward_topk(xc, k=TOPK, select=select)
-    calib = torch.bincount(ids_c.long().flatten(), minlength=E_EXPERTS).float()
-    dist.all_reduce(calib)
-    # units of sibling leaves (the router's last branching factor) stay on one
-    # GPU: a token's experts cluster in the tree, so this keeps the GPUs a
-    # token visits near the contiguous placement's while the loads even out
-    group = BRANCHING[-1] if (E_EXPERTS // world) % BRANCHING[-1] == 0 else 1
-    mode = os.environ.get("SB_EP_PLACEMENT", "grouped")
-    placement = None if mode == "contiguous" else \
-        balanced_placement(calib.cpu().tolist(), world, group=1 if mode == "scattered" else group)
+    placement, mode = ep_placement(r, xc, world, select)
     held = experts_at(placement, rank, world) if placement else list(range(rank * e_local, (rank + 1) * e_local))
     local = TernaryExperts([allx[e] for e in held], device)
     chunks = int(os.environ.get("SB_EP_CHUNKS", "2"))
@@ -666,9 +679,13 @@ def ep_workload(batch: int, device, world: int, select: str = "soft"):
                        "tokens_per_gpu": batch, "router_select": select,
                        "experts_per_gpu": e_local,
                        "entries_per_gpu_max_over_mean": round(float(per_rank.max() / per_rank.mean()), 3),
-                       "expert_placement": (f"balanced from a calibration batch's routing (sb200.ep."
-                                            f"balanced_placement, units of {1 if mode == 'scattered' else group} "
-                                            "sibling experts)" if placement else "contiguous blocks"),
+                       "expert_placement": {"refined": "balanced units of sibling experts, then swaps that "
+                                                       "lower the modelled step time (sb200.ep.balanced_placement "
+                                                       "+ refine_placement), from a calibration batch's routing",
+                                            "grouped": "balanced units of sibling experts (sb200.ep."
+                                                       "balanced_placement), from a calibration batch's routing",
+                                            "scattered": "balanced single experts (sb200.ep.balanced_placement)",
+                                            "contiguous": "contiguous blocks"}.get(mode, mode),
                        "entries_per_gpu_max_over_mean_contiguous": round(
                            float(contiguous.max() / contiguous.mean()), 3),
                        "expert_load_max_over_mean": round(float(counts.max() / counts.mean()), 3),
@@ -1018,7 +1035,7 @@ def run_ours(a):
                           "tokens_per_gpu": stok, "layers": 16, "steps": st_steps,
                           "scaling": "strong (16384 tokens in total, split over the GPUs)",
                           "parallelism": (f"ep{world} per layer ({E_EXPERTS // world} experts per GPU, "
-                                          "peer-memory exchange, balanced placement per layer)" if world > 1 else "single GPU"),
+                                          "peer-memory exchange, expert placement per layer)" if world > 1 else "single GPU"),
                           "l2": "weights of 16 layers (1.7 GB) stream every step; no flush"}
     # ---- config 4: 6-level 4096-expert router at hidden 4096 vs a dense gate
     if not a.skip_config4:

@@ -125,3 +125,36 @@ def test_placement_keeps_the_sharded_sum_bitwise():
                             else np.zeros((0, y.shape[2]), np.float32))
         got = oep.source_combine(send_pos, partials)
         assert np.array_equal(got, ref)
+
+
+def _model_cost(perm, ids, world, entry_ns=12.0, row_ns=37.0):
+    perm = np.asarray(perm)
+    el = len(perm) // world
+    owner = perm[ids] // el
+    ent = np.bincount(owner.ravel(), minlength=world)
+    rows = sum(len(set(o)) for o in owner)
+    return entry_ns * ent.max() + row_ns * rows / world
+
+
+@pytest.mark.parametrize("world", [2, 8])
+def test_refine_placement_lowers_the_modelled_step_time(world):
+    import sys
+    from pathlib import Path
+    sys.path.insert(0, str(Path(__file__).resolve().parents[1] / "spectral-ai_b200"))
+    from sb200.ep import balanced_placement, refine_placement
+    rng = np.random.default_rng(world)
+    # clustered routing like a tree router's: a token's experts come mostly
+    # from one group of 8 neighbouring experts, with skewed group popularity
+    T, E, k = 3000, 64, 8
+    groups = rng.choice(8, size=T, p=np.array([8, 6, 5, 4, 3, 2, 1, 1]) / 30)
+    ids = np.stack([np.concatenate([rng.choice(8, 6, replace=False) + 8 * g,
+                                    rng.choice(E, 2, replace=False)]) for g in groups]).astype(np.int32)
+    loads = np.bincount(ids.ravel(), minlength=E).astype(float)
+    p0 = balanced_placement(loads, world, group=4)
+    p1 = refine_placement(p0, ids, world, iters=1500, seed=1)
+    assert sorted(p1) == list(range(E))
+    el = E // world
+    assert all(sum(1 for p in p1 if p // el == r) == el for r in range(world))
+    assert _model_cost(p1, ids, world) <= _model_cost(p0, ids, world)
+    # the same inputs give the same placement (every rank computes it alone)
+    assert refine_placement(p0, ids, world, iters=1500, seed=1) == p1
